@@ -1,0 +1,452 @@
+"""Benchmark: fused selected-quant paged decode on B200 (sm_100a).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload c2|c3|c5|c1] [--impl b200|reference]
+
+One "step" is one decode step of the workload's whole batch (all sequences,
+all heads) over its router-selected pages.  ``value`` is the selected-KV HBM
+throughput in GB/s (algorithmic bytes: K+V codes + the scales they need, of
+every selected page, divided by the device time of the step) summed over all
+ranks; ``ms_per_step`` / ``us_per_step`` give the step time.  Multi-GPU runs
+shard the batch (weak scaling: every rank decodes its own full-size batch,
+no collective on the data path) and take the max time over ranks.
+
+Default workload: Llama-3-8B-shape GQA decode, batch 32,
+32 q heads / 8 kv heads, head_dim 128, 32768-token context in 16-token
+pages; the router keeps the first 512 and last 1024 tokens plus the top
+ATTEND blocks by seeded score (1024 of 2048 pages per sequence and kv head);
+selected pages are 30% FP16 / 40% FP8-e4m3 / 30% INT8 with per-page,
+per-head scales.  Synthetic seeded data (no dataset is involved).
+
+``--impl reference`` times the reference algorithm's CPU implementation (the
+numpy restatement in oracle/, which the tests pin to the reference's own
+outputs) on the host cores, on a bounded sample of the same workload, and
+reports the same metric.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "intent-attention-kernel_b200"))
+
+METRIC = "decode-attn µs/step & selected-KV HBM GB/s (vs 8 TB/s) at 1/2/4/8 B200 vs CPU ref"
+FALLBACK_HBM_GBS = 6650.0
+
+# name -> [IAK format code, K+V code bytes per page per head-dim element pair]
+FMT_CODE = {"F16": 1, "FP8": 2, "INT8": 3, "INT4": 4, "INT4R": 5}
+
+
+# --------------------------------------------------------------------------- #
+#  Workloads
+# --------------------------------------------------------------------------- #
+
+def workload(name: str) -> dict:
+    if name == "c2":
+        return dict(name="C2 Llama-3-8B-shape GQA decode", B=32, Hq=32, Hkv=8, D=128, T=32768, PS=16,
+                    head_tokens=512, tail_tokens=1024, attend_block_pages=4, select_pages=1024,
+                    mix={"F16": 0.3, "FP8": 0.4, "INT8": 0.3}, scale_mode="page", q_std=1.0, outliers=0.01,
+                    seed=1002)
+    if name == "c3":
+        return dict(name="C3 Llama-3-70B-shape low-bit decode", B=64, Hq=64, Hkv=8, D=128, T=8192, PS=16,
+                    head_tokens=8192, tail_tokens=0, attend_block_pages=4, select_pages=512,
+                    mix={"F16": 0.2, "INT4": 0.4, "INT4R": 0.4}, scale_mode="group32", q_std=0.5, outliers=0.0,
+                    seed=1003)
+    if name == "c5":
+        return dict(name="C5 long-context decode (single GPU)", B=8, Hq=32, Hkv=8, D=128, T=524288, PS=16,
+                    head_tokens=512, tail_tokens=1024, attend_block_pages=4, select_pages=8192,
+                    mix={"F16": 0.1, "FP8": 0.3, "INT8": 0.3, "INT4": 0.3}, scale_mode="page", q_std=1.0,
+                    outliers=0.0, seed=1005)
+    if name == "c1":
+        return dict(name="C1 CPU-runnable MHA decode", B=1, Hq=8, Hkv=8, D=64, T=1440, PS=16,
+                    head_tokens=128, tail_tokens=160, attend_block_pages=56, select_pages=74,
+                    mix={"F16": 0.5, "INT8": 0.5}, scale_mode="page", q_std=1.0, outliers=0.0, seed=1001)
+    raise SystemExit(f"unknown workload {name}")
+
+
+def select_pages(w: dict):
+    """Router-selected logical pages (shared by every (b, kv head)) + their formats."""
+    from intent_attention import BlockLayout, BlockPolicy, BlockRouter, RouterConfig, SemanticBlock
+    from intent_attention import routing_to_kernel_metadata
+    PS, T = w["PS"], w["T"]
+    rng = np.random.default_rng(w["seed"])
+    blocks = []
+    if w["head_tokens"]:
+        blocks.append(SemanticBlock("system", 0, w["head_tokens"], BlockPolicy.ALWAYS))
+    mid_start, mid_end = w["head_tokens"], T - w["tail_tokens"]
+    bt = w["attend_block_pages"] * PS
+    n_mid = (mid_end - mid_start) // bt
+    for i in range(n_mid):
+        blocks.append(SemanticBlock(f"doc{i}", mid_start + i * bt, mid_start + (i + 1) * bt, BlockPolicy.ATTEND,
+                                    score=float(rng.random())))
+    if w["tail_tokens"]:
+        blocks.append(SemanticBlock("recent", mid_end, T, BlockPolicy.RECENT))
+    fixed = (w["head_tokens"] + w["tail_tokens"]) // PS
+    top_k = max(0, (w["select_pages"] - fixed) // w["attend_block_pages"])
+    router = BlockRouter(RouterConfig(top_k_blocks=top_k, memory_pressure=0.0))
+    meta = routing_to_kernel_metadata(router.route_layout(BlockLayout(blocks), T), PS)
+    ids = np.asarray(meta["selected_page_ids"], dtype=np.int32)
+    n = ids.size
+    names = list(w["mix"].keys())
+    counts = [int(round(w["mix"][k] * n)) for k in names]
+    counts[-1] = n - sum(counts[:-1])
+    fmt = np.concatenate([np.full(c, FMT_CODE[k], np.uint8) for k, c in zip(names, counts)])
+    fmt = fmt[rng.permutation(n)]
+    return ids, fmt
+
+
+def page_bytes(fmt_code: int, PS: int, D: int, ns: int) -> int:
+    """Algorithmic bytes of one selected page (K and V planes + their scales)."""
+    code = {1: 2 * D, 2: D, 3: D, 4: D // 2, 5: D}[fmt_code] * PS
+    scales = {1: 0, 2: 1, 3: 1, 4: 1, 5: 2}[fmt_code] * ns * 4
+    return 2 * (code + scales)
+
+
+def n_scales(mode: str, D: int) -> int:
+    return {"page": 1, "group32": D // 32, "channel": D}[mode]
+
+
+def step_bytes(w: dict, fmt: np.ndarray) -> int:
+    ns = n_scales(w["scale_mode"], w["D"])
+    per_unit = sum(page_bytes(int(f), w["PS"], w["D"], ns) for f in fmt)
+    return per_unit * w["B"] * w["Hkv"]
+
+
+# --------------------------------------------------------------------------- #
+#  CPU (reference algorithm) timing on a bounded sample
+# --------------------------------------------------------------------------- #
+
+def cpu_reference_step(w: dict, ids: np.ndarray, fmt: np.ndarray, budget_s: float = 12.0, max_units: int = 64):
+    """Time the numpy oracle decode over sampled (b, kv head) units; extrapolate
+    to the full step.  Returns (seconds per full step, units timed, cores)."""
+    import concurrent.futures as cf
+    from oracle import decode as odec
+    from oracle import quant as oq
+    cores = len(os.sched_getaffinity(0))
+    D, PS, G = w["D"], w["PS"], w["Hq"] // w["Hkv"]
+    n = ids.size
+    rng = np.random.default_rng(w["seed"] + 7)
+    tag_map = {1: "F16", 2: "FP8", 3: "INT8", 4: "INT4", 5: "INT4R"}
+
+    def build_unit():
+        k = rng.standard_normal((n, PS, D)).astype(np.float32)
+        v = rng.standard_normal((n, PS, D)).astype(np.float32)
+        pools = {"k_f16": k.astype(np.float16), "v_f16": v.astype(np.float16)}
+        sc = {}
+        for plane, x in (("k", k), ("v", v)):
+            if any(f in (2, 3, 4, 5) for f in fmt):
+                r8 = oq.quantize_pages(x, "INT8", w["scale_mode"])
+                pools[f"{plane}_i8"] = r8["codes"]
+                sc[f"{plane}_scale"] = r8["scale"]
+                pools[f"{plane}_fp8"] = oq.f32_to_e4m3(x / oq.expand_scales(r8["scale"], w["scale_mode"], D))
+                r4 = oq.quantize_pages(x, "INT4_RESIDUAL", w["scale_mode"])
+                pools[f"{plane}_i4"] = oq.pack_int4(r4["codes"])
+                pools[f"{plane}_i4r"] = oq.pack_int4(r4["res_codes"])
+                sc[f"{plane}_res_scale"] = r4["res_scale"]
+        q = rng.standard_normal((G, D)).astype(np.float32) * w["q_std"]
+        return q, pools, sc
+
+    units_total = w["B"] * w["Hkv"]
+    data = [build_unit() for _ in range(min(4, units_total))]
+    tags = fmt.astype(np.int64)
+    pids = np.arange(n)
+
+    def one(i):
+        q, pools, sc = data[i % len(data)]
+        return odec.unit_partial(q, pids, tags, tag_map, "SKIP", pools, sc, w["scale_mode"], 1.0 / math.sqrt(D))
+
+    # numpy's BLAS uses every core for the matmuls; a thread pool overlaps the
+    # per-unit gather / dequantisation work across cores as well
+    done = 0
+    t0 = time.perf_counter()
+    with cf.ThreadPoolExecutor(max_workers=cores) as ex:
+        while done < min(units_total, max_units) and time.perf_counter() - t0 < budget_s:
+            batch = min(cores, units_total - done)
+            list(ex.map(one, range(done, done + batch)))
+            done += batch
+    dt = time.perf_counter() - t0
+    return dt * units_total / done, done, cores
+
+
+# --------------------------------------------------------------------------- #
+#  GPU arm
+# --------------------------------------------------------------------------- #
+
+class ClockSampler:
+    """Samples nvidia-smi SM clocks and throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.rows = []
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([c.strip() for c in line.split(",")])
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["clocks not sampled"]}
+        sm = [float(r[1]) for r in self.rows if len(r) > 8 and r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if len(r) > 8 and r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows if len(r) > 8 for i in range(4) if r[5 + i] == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.rows)}
+
+
+def measured_hbm_peak():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def build_gpu_workload(w: dict, ids: np.ndarray, fmt: np.ndarray, device, rank: int):
+    import torch
+    from intent_attention import PagePool
+    B, Hq, Hkv, D, PS, T = w["B"], w["Hq"], w["Hkv"], w["D"], w["PS"], w["T"]
+    NLP = T // PS
+    units = B * Hkv
+    NP = units * NLP
+    n = ids.size
+    formats = sorted({k for k in w["mix"]})
+    pool = PagePool.allocate(NP, PS, D, formats, w["scale_mode"], device)
+    g = torch.Generator(device=device).manual_seed(w["seed"] * 131 + rank)
+    ids_t = torch.from_numpy(ids).to(device)
+    fmt_t = torch.from_numpy(fmt).to(device)
+    tags = torch.zeros(NP, dtype=torch.uint8, device=device)
+    chunk = max(1, (1 << 27) // (PS * D * n))       # ~512 MB of fp32 per plane per chunk
+    for u0 in range(0, units, chunk):
+        u1 = min(units, u0 + chunk)
+        dst = (torch.arange(u0, u1, device=device, dtype=torch.int32)[:, None] * NLP + ids_t[None, :]).reshape(-1)
+        P = dst.numel()
+        k = torch.randn((P, PS, D), generator=g, device=device)
+        v = torch.randn((P, PS, D), generator=g, device=device)
+        if w["outliers"]:
+            k = torch.where(torch.rand(k.shape, generator=g, device=device) < w["outliers"], k * 8, k)
+            v = torch.where(torch.rand(v.shape, generator=g, device=device) < w["outliers"], v * 8, v)
+        f = fmt_t.repeat(u1 - u0)
+        pool.quantize_(k, v, f, dst_ids=dst)
+        tags[dst.long()] = f
+        del k, v
+    table = (torch.arange(units, device=device, dtype=torch.int32)[:, None] * NLP + ids_t[None, :]).reshape(B, Hkv, n)
+    counts = torch.full((B, Hkv), n, dtype=torch.int32, device=device)
+    q = (torch.randn((B, Hq, D), generator=g, device=device) * w["q_std"]).to(torch.bfloat16)
+    torch.cuda.synchronize(device)
+    return pool, table.contiguous(), counts, tags, q
+
+
+def run_gpu(args):
+    import torch
+    import torch.distributed as dist
+    from intent_attention import paged_decode
+    from intent_attention.paged import make_tag_map, reserve_workspace
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
+    w = workload(args.workload)
+    ids, fmt = select_pages(w)
+    nbytes = step_bytes(w, fmt)
+    pool, table, counts, tags, q = build_gpu_workload(w, ids, fmt, device, rank)
+    tag_map = make_tag_map({c: (f if f in w["mix"] else "SKIP") for f, c in FMT_CODE.items()})
+    out = torch.empty(q.shape, dtype=torch.bfloat16, device=device)
+
+    def step():
+        paged_decode(q, pool, table, counts, tags, tag_map, 0, out=out, num_splits=args.splits)
+
+    step()
+    torch.cuda.synchronize(device)
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(device)
+    if world > 1:
+        dist.barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        torch.cuda.synchronize(device)
+        ev0.record()
+        for _ in range(args.steps):
+            step()
+        ev1.record()
+        torch.cuda.synchronize(device)
+    t_ms = ev0.elapsed_time(ev1) / args.steps
+    if world > 1:
+        t = torch.tensor([t_ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        t_ms = float(t.item())
+        dist.barrier()
+
+    # ---- end to end through the public API: host buffers in, host buffer out
+    q_host = q.cpu().pin_memory()
+    table_host = table.cpu().pin_memory()
+    counts_host = counts.cpu().pin_memory()
+    out_host = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+    q_dev, table_dev, counts_dev = torch.empty_like(q), torch.empty_like(table), torch.empty_like(counts)
+    h2d = q_host.numel() * q_host.element_size() + table_host.numel() * 4 + counts_host.numel() * 4
+    d2h = out_host.numel() * out_host.element_size()
+
+    def e2e_step():
+        q_dev.copy_(q_host, non_blocking=True)
+        table_dev.copy_(table_host, non_blocking=True)
+        counts_dev.copy_(counts_host, non_blocking=True)
+        paged_decode(q_dev, pool, table_dev, counts_dev, tags, tag_map, 0, out=out, num_splits=args.splits)
+        out_host.copy_(out, non_blocking=True)
+
+    for _ in range(args.warmup):
+        e2e_step()
+    torch.cuda.synchronize(device)
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize(device)
+    e2e_ms = e0.elapsed_time(e1) / args.steps
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+
+    from intent_attention import _native as N
+    launches_per_step = 1 + (1 if _num_splits(pool, q, table, counts, tags, tag_map, args.splits) > 1 else 0)
+
+    if rank == 0:
+        peak, peak_kind = measured_hbm_peak()
+        gbs = nbytes / (t_ms * 1e-3) / 1e9
+        value = gbs * world
+        rec = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(t_ms, 5), "us_per_step": round(t_ms * 1e3, 2),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp16/fp8/int8 pages, fp32 acc",
+            "data": "synthetic (seeded N(0,1) K/V with 1% x8 outliers, bf16 Q)",
+            "config": {"workload": w["name"], "batch_per_gpu": w["B"], "global_batch": w["B"] * world,
+                       "q_heads": w["Hq"], "kv_heads": w["Hkv"], "head_dim": w["D"], "ctx": w["T"],
+                       "page_size": w["PS"], "selected_pages_per_seq_head": int(ids.size),
+                       "format_mix": w["mix"], "scale_mode": w["scale_mode"],
+                       "selected_kv_bytes_per_step_per_gpu": nbytes,
+                       "l2": f"inputs larger than L2 ({nbytes / 1e9:.2f} GB of selected KV per step)",
+                       "parallelism": f"dp{world} (batch shards, no collective on the data path)"},
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(gbs / peak, 4), "traffic": None,
+                         "note": f"peak = {peak_kind} HBM copy bandwidth; achieved = algorithmic selected-KV bytes "
+                                 "per step / device time of the step (decode + merge launches)"},
+            "e2e": {"value": round(nbytes * world / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+                    "ms_per_step": round(e2e_ms, 5), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "api": "intent_attention.paged_decode with pinned host q / page table / counts in, output out"},
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": clocks.summary(),
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            sec, units, cores = cpu_reference_step(w, ids, fmt, budget_s=args.cpu_budget)
+            rec["cpu_baseline"] = {"value": round(nbytes / sec / 1e9, 4), "unit": "GB/s", "cores": cores,
+                                   "kind": "port", "seconds_per_step": round(sec, 3),
+                                   "sample": f"{units} of {w['B'] * w['Hkv']} (sequence, kv-head) units timed with the "
+                                             "numpy oracle decode, extrapolated linearly to the full step"}
+        print(json.dumps(rec), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def _num_splits(pool, q, table, counts, tags, tag_map, splits):
+    import ctypes
+    from intent_attention import _native as N
+    from intent_attention.paged import _decode_structs
+    P, A = _decode_structs(q, pool, table, counts, tags, tag_map, 0, None, q, None, splits)
+    nb = ctypes.c_size_t(0)
+    N.check(N.lib().iak_decode_workspace_size(ctypes.byref(P), ctypes.byref(A), ctypes.byref(nb)), "ws")
+    return 2 if nb.value > 0 else 1
+
+
+def run_reference(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    w = workload(args.workload)
+    ids, fmt = select_pages(w)
+    nbytes = step_bytes(w, fmt)
+    vals = []
+    cores = units = None
+    for i in range(args.warmup + args.steps):
+        sec, units, cores = cpu_reference_step(w, ids, fmt, budget_s=args.cpu_budget / max(1, args.steps),
+                                               max_units=64)
+        if i >= args.warmup:
+            vals.append(sec)
+    sec = statistics.median(vals)
+    v = nbytes / sec / 1e9
+    rec = {"impl": "reference", "metric": METRIC, "value": round(v, 4), "unit": "GB/s", "n_gpus": world,
+           "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(sec * 1e3, 3),
+           "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32 (numpy)",
+           "data": "synthetic", "config": {"workload": w["name"], "batch": w["B"], "q_heads": w["Hq"],
+                                           "kv_heads": w["Hkv"], "head_dim": w["D"], "ctx": w["T"]},
+           "cpu_baseline": {"value": round(v, 4), "unit": "GB/s", "cores": cores, "kind": "port",
+                            "sample": f"{units} (sequence, kv-head) units per step, extrapolated to the full step"},
+           "e2e": {"value": round(v, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(rec), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--workload", default="c2", choices=["c1", "c2", "c3", "c5"])
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--splits", type=int, default=0)
+    ap.add_argument("--cpu-budget", type=float, default=12.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_gpu(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,181 @@
+/*
+ * intent_attention_b200.h -- C ABI of the B200 (sm_100a) fused selected-quant
+ * paged decode attention library (libiak_b200.so).
+ *
+ * Plain C: device pointers, sizes, strides and POD descriptors; no torch or
+ * CUDA types (a CUDA stream is passed as `void*`, NULL = legacy default
+ * stream).  Every entry point returns an iak_status; on failure
+ * iak_last_error() returns a thread-local message.  Entry points never
+ * allocate device memory and never synchronise the stream; they are
+ * reentrant across devices (the current CUDA device is used).
+ *
+ * Reference interfaces replaced (manishklach/intent-attention-kernel,
+ * paths inside src/intent_attention/):
+ *   iak_decode / iak_decode_workspace_size
+ *       fused_selected_quant_decode.py:408-464  fused_selected_quant_decode()
+ *       fused_selected_quant_decode.py:472-513  _launch_triton_kernel()
+ *       triton_intent_quant_attention.py:342-457 intent_quant_decode_attention_triton()
+ *       triton_adaptive_format_attention.py:237-329 adaptive_format_decode_attention_triton()
+ *     (one decode for all three: each Python entry point fills tag_map with
+ *      its own enum, so FusedKVPrecision / TritonKVPrecision /
+ *      AdaptivePageFormat tags are translated at the boundary, never globally)
+ *   iak_merge_partials
+ *       the (m, l, acc) online-softmax recurrence of
+ *       fused_selected_quant_decode.py:323-334, applied across KV splits
+ *   iak_pack_metadata
+ *       fused_selected_quant_decode.py:344-400  metadata_to_kernel_tensors()
+ *       triton_intent_quant_attention.py:126-203 make_page_tables_from_selected_pages()
+ *   iak_quantize_pages
+ *       intent_quant.py:221-312 _absmax_scale() / fake_quantize_tensor()
+ *       fused_selected_quant_decode.py:521-542 fake_int8_pages_from_fp16()
+ *       (real packed page formats instead of fake quantisation)
+ *   iak_mla_decode
+ *       triton_mla_decode.py:110-152 mla_decode_triton(), mla.py:95-136
+ */
+#ifndef INTENT_ATTENTION_B200_H
+#define INTENT_ATTENTION_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define IAK_ABI_VERSION 1
+
+typedef enum iak_status {
+  IAK_OK = 0,
+  IAK_ERR_INVALID_ARG = 1,   /* maps to ValueError in the Python layer   */
+  IAK_ERR_UNSUPPORTED = 2,   /* shape / format combination not built      */
+  IAK_ERR_CUDA = 3,          /* a CUDA runtime / driver call failed       */
+  IAK_ERR_WORKSPACE = 4,     /* workspace missing or too small            */
+  IAK_ERR_TIMEOUT = 5        /* a bounded device-side wait gave up        */
+} iak_status;
+
+/* element types of q / out / dense inputs */
+enum { IAK_DT_F32 = 0, IAK_DT_F16 = 1, IAK_DT_BF16 = 2 };
+
+/* page formats a tag can map to */
+enum {
+  IAK_FMT_SKIP = 0,    /* no load, no contribution                                */
+  IAK_FMT_F16 = 1,     /* [NP, PS, D] float16                                     */
+  IAK_FMT_FP8 = 2,     /* [NP, PS, D] e4m3fn codes, value = code * scale          */
+  IAK_FMT_INT8 = 3,    /* [NP, PS, D] int8 codes, value = code * scale            */
+  IAK_FMT_INT4 = 4,    /* [NP, PS, D/2] packed nibbles, value = code * scale      */
+  IAK_FMT_INT4R = 5,   /* INT4 base plane + INT4 residual plane, two scale sets   */
+  IAK_FMT_SPARSE = 6   /* adaptive SPARSE: contributes nothing (reference kernel) */
+};
+
+/* scale granularity of the quantised formats (one scale set per page) */
+enum {
+  IAK_SCALE_PAGE = 0,     /* 1 scale per page                    */
+  IAK_SCALE_GROUP32 = 1,  /* head_dim / 32 scales per page       */
+  IAK_SCALE_CHANNEL = 2   /* head_dim scales per page            */
+};
+
+/* Paged KV storage.  Pages are single-head: page p of every pool is one
+ * (sequence, kv-head, logical page) slot, addressed by the page table.
+ * Pools that are not used by any tag may be NULL.  Packed INT4 rows hold
+ * channel d of nibble n in 32-bit word w at
+ *   d = 32*(w/4) + 4*(w%4) + {0,2,16,18,1,3,17,19}[n],  stored as code + 8.
+ * Base pointers must be 16-byte aligned. */
+typedef struct iak_page_pools {
+  void* k_f16;  void* v_f16;
+  void* k_fp8;  void* v_fp8;
+  void* k_i8;   void* v_i8;
+  void* k_i4;   void* v_i4;
+  void* k_i4r;  void* v_i4r;      /* INT4_RESIDUAL residual planes        */
+  float* k_scale;     float* v_scale;      /* [NP, n_scales]              */
+  float* k_res_scale; float* v_res_scale;  /* [NP, n_scales] (INT4R)      */
+  int64_t num_pages;
+  int32_t page_size;
+  int32_t head_dim;
+  int32_t scale_mode;             /* IAK_SCALE_*                           */
+} iak_page_pools;
+
+/* One decode step: B sequences, Hq query heads, Ht page-table heads
+ * (G = Hq / Ht query heads share one page list: G = 1 is the reference's
+ * per-head table, G > 1 is grouped-query attention). */
+typedef struct iak_decode_args {
+  const void* q;  int32_t q_dtype;  int64_t q_stride_b, q_stride_h;    /* elements */
+  void* out;      int32_t out_dtype; int64_t out_stride_b, out_stride_h;
+  int32_t batch, num_q_heads, num_table_heads;
+  const int32_t* page_table;      /* [B, Ht, W]; ids < 0 are unused slots */
+  int64_t pt_stride_b, pt_stride_h;
+  int32_t table_width;            /* W                                     */
+  const int32_t* page_counts;     /* [B, Ht] (row stride pc_stride_b) or NULL = W */
+  int64_t pc_stride_b;
+  const void* page_tags;          /* [NP] tag per page                      */
+  int32_t tag_bytes;              /* 1 (uint8) or 4 (int32)                 */
+  uint8_t tag_map[16];            /* tag -> IAK_FMT_*                       */
+  uint8_t tag_default;            /* format of tags outside 0..15           */
+  float sm_scale;                 /* softmax scale (1/sqrt(D) in the reference) */
+  /* Optional split-KV export: when partial_l != NULL the decode writes the
+   * unnormalised partial (m natural-log max, l, acc) of every query row
+   * ([B*Hq], [B*Hq], [B*Hq, D] fp32) instead of `out`; iak_merge_partials
+   * combines partials of several devices. */
+  float* partial_m; float* partial_l; float* partial_acc;
+  int32_t num_splits;             /* 0 = choose automatically               */
+} iak_decode_args;
+
+int iak_version(void);
+const char* iak_last_error(void);
+
+/* Workspace (device bytes) iak_decode needs for these arguments. */
+int iak_decode_workspace_size(const iak_page_pools* pools, const iak_decode_args* args,
+                              size_t* bytes);
+
+/* Fused selected-quant paged decode: gather the selected pages, dequantise
+ * in registers, split-KV online softmax, LSE merge. */
+int iak_decode(const iak_page_pools* pools, const iak_decode_args* args,
+               void* workspace, size_t workspace_bytes, void* stream);
+
+/* LSE merge of S partials per row: m/l [rows, S], acc [rows, S, D] (fp32,
+ * contiguous).  Writes normalised rows to out (dtype, row stride in
+ * elements); rows with no contribution become 0. */
+int iak_merge_partials(const float* m, const float* l, const float* acc,
+                       int64_t rows, int32_t splits, int32_t head_dim,
+                       void* out, int32_t out_dtype, int64_t out_row_stride, void* stream);
+
+/* Metadata packing on the device.  Logical page ids (one list shared by
+ * every (b, h), the router's selected_page_ids order) are mapped to
+ * physical ids base[b*Ht + h] + logical, written -1 padded into
+ * page_table [B, Ht, W] with counts min(n, W); when tags_in is non-NULL the
+ * per-logical-page tags are scattered to page_tags[physical]. */
+typedef struct iak_pack_args {
+  const int32_t* logical_ids; int32_t num_ids;
+  const uint8_t* logical_tags;    /* [num_logical_pages] or NULL            */
+  int32_t num_logical_pages;
+  const int32_t* bases;           /* [B*Ht] physical base per (b, h) or NULL = 0 */
+  int32_t batch, num_table_heads, table_width;
+  int32_t* page_table; int32_t* page_counts; uint8_t* page_tags;
+  int64_t num_tag_pages;          /* length of page_tags; writes outside it are dropped */
+  int32_t pad_value;              /* -1 (6-tag / adaptive) or 0 (fused API)  */
+} iak_pack_args;
+int iak_pack_metadata(const iak_pack_args* args, void* stream);
+
+/* Quantise dense pages x [P, PS, D] (f32 / f16 / bf16) into the pool
+ * formats, one plane (K or V) per call, with the reference's arithmetic:
+ * scale = max(absmax/127, 1e-8) over the scale span, INT8/INT4 codes =
+ * round_half_even(clamp(x/scale, +-127 / +-7)), FP8 = e4m3(x/scale),
+ * INT4R = INT4 base + INT4 residual with its own scale, FP16 = half(x).
+ * Source page i goes to pool page dst_ids[i] (NULL = i) in format
+ * formats[i] (IAK_FMT_*).  given_scale / given_res_scale ([P, n_scales],
+ * optional) replace the computed scales. */
+typedef struct iak_quant_args {
+  const void* x; int32_t x_dtype; int64_t num_src_pages;
+  const int32_t* dst_ids;
+  const uint8_t* formats;
+  const float* given_scale; const float* given_res_scale;
+  void* f16; void* fp8; void* i8; void* i4; void* i4r;   /* plane pools */
+  float* scale; float* res_scale;
+  int64_t num_pages;
+  int32_t page_size, head_dim, scale_mode;
+} iak_quant_args;
+int iak_quantize_pages(const iak_quant_args* args, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* INTENT_ATTENTION_B200_H */

@@ -1,0 +1,215 @@
+// C ABI entry points: argument validation, split planning, dispatch.
+#include <algorithm>
+#include <cstdarg>
+#include <cstring>
+#include <mutex>
+
+#include "iak_internal.cuh"
+
+namespace iak {
+
+static thread_local std::string g_last_error;
+
+void set_error(const char* fmt, ...) {
+  char buf[1024];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+}
+
+int fail(int status, const char* fmt, ...) {
+  char buf[1024];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return status;
+}
+
+int check_cuda(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return IAK_OK;
+  return fail(IAK_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+int device_sm_count() {
+  static std::mutex mu;
+  static int cache[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  std::lock_guard<std::mutex> lock(mu);
+  if (cache[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    cache[dev] = n;
+  }
+  return cache[dev];
+}
+
+static bool fmt_reachable(const iak_decode_args* a, int fmt) {
+  for (int i = 0; i < 16; ++i)
+    if (a->tag_map[i] == fmt) return true;
+  return a->tag_default == fmt;
+}
+
+static size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+// Validate pools + args and fill the flattened kernel parameters (without
+// workspace pointers).  Returns IAK_OK or an error status.
+static int prepare(const iak_page_pools* P, const iak_decode_args* a, DecodeParams* p) {
+  if (!P || !a) return fail(IAK_ERR_INVALID_ARG, "null pools/args");
+  if (a->batch < 0 || a->num_q_heads <= 0 || a->num_table_heads <= 0)
+    return fail(IAK_ERR_INVALID_ARG, "batch/heads must be positive (batch=%d, Hq=%d, Ht=%d)", a->batch,
+                a->num_q_heads, a->num_table_heads);
+  if (a->num_q_heads % a->num_table_heads)
+    return fail(IAK_ERR_INVALID_ARG, "num_q_heads %d is not a multiple of num_table_heads %d", a->num_q_heads,
+                a->num_table_heads);
+  const int D = P->head_dim, PS = P->page_size;
+  if (D <= 0 || D > 256 || D % 16) return fail(IAK_ERR_UNSUPPORTED, "head_dim %d unsupported (16..256, multiple of 16)", D);
+  if (PS <= 0 || PS > 1024) return fail(IAK_ERR_INVALID_ARG, "page_size %d out of range", PS);
+  if (P->num_pages < 0) return fail(IAK_ERR_INVALID_ARG, "num_pages < 0");
+  if (P->scale_mode < 0 || P->scale_mode > 2) return fail(IAK_ERR_INVALID_ARG, "bad scale_mode %d", P->scale_mode);
+  if (P->scale_mode == IAK_SCALE_GROUP32 && D % 32)
+    return fail(IAK_ERR_INVALID_ARG, "group32 scales need head_dim %% 32 == 0");
+  if (a->table_width < 0) return fail(IAK_ERR_INVALID_ARG, "table_width < 0");
+  if (a->tag_bytes != 1 && a->tag_bytes != 4) return fail(IAK_ERR_INVALID_ARG, "tag_bytes must be 1 or 4");
+  if (a->q_dtype < 0 || a->q_dtype > 2 || a->out_dtype < 0 || a->out_dtype > 2)
+    return fail(IAK_ERR_INVALID_ARG, "bad q/out dtype");
+  const int G = a->num_q_heads / a->num_table_heads;
+  if (G > 8) return fail(IAK_ERR_UNSUPPORTED, "more than 8 query heads per page table (%d)", G);
+  for (int i = 0; i < 16; ++i)
+    if (a->tag_map[i] > IAK_FMT_SPARSE) return fail(IAK_ERR_INVALID_ARG, "tag_map[%d]=%d is not a format", i, a->tag_map[i]);
+  if (a->tag_default > IAK_FMT_SPARSE) return fail(IAK_ERR_INVALID_ARG, "bad tag_default");
+  const bool any_work = a->batch > 0 && a->table_width > 0;
+  if (any_work) {
+    if (!a->q || !a->page_table || !a->page_tags) return fail(IAK_ERR_INVALID_ARG, "q/page_table/page_tags is NULL");
+    if (!a->out && !a->partial_l) return fail(IAK_ERR_INVALID_ARG, "out is NULL");
+    struct { int fmt; const void* k; const void* v; const char* name; } need[] = {
+        {IAK_FMT_F16, P->k_f16, P->v_f16, "f16"},   {IAK_FMT_FP8, P->k_fp8, P->v_fp8, "fp8"},
+        {IAK_FMT_INT8, P->k_i8, P->v_i8, "int8"},    {IAK_FMT_INT4, P->k_i4, P->v_i4, "int4"},
+        {IAK_FMT_INT4R, P->k_i4, P->v_i4, "int4"},   {IAK_FMT_INT4R, P->k_i4r, P->v_i4r, "int4 residual"}};
+    for (auto& n : need)
+      if (fmt_reachable(a, n.fmt) && (!n.k || !n.v))
+        return fail(IAK_ERR_INVALID_ARG, "a tag maps to format %d but the %s K/V pool is NULL", n.fmt, n.name);
+    const bool quant = fmt_reachable(a, IAK_FMT_FP8) || fmt_reachable(a, IAK_FMT_INT8) ||
+                       fmt_reachable(a, IAK_FMT_INT4) || fmt_reachable(a, IAK_FMT_INT4R);
+    if (quant && (!P->k_scale || !P->v_scale)) return fail(IAK_ERR_INVALID_ARG, "quantised formats need k_scale/v_scale");
+    if (fmt_reachable(a, IAK_FMT_INT4R) && (!P->k_res_scale || !P->v_res_scale))
+      return fail(IAK_ERR_INVALID_ARG, "INT4_RESIDUAL needs k_res_scale/v_res_scale");
+    if ((fmt_reachable(a, IAK_FMT_INT4) || fmt_reachable(a, IAK_FMT_INT4R)) && D % 32)
+      return fail(IAK_ERR_UNSUPPORTED, "INT4 pages need head_dim %% 32 == 0");
+  }
+  std::memset(p, 0, sizeof(*p));
+  p->k_f16 = static_cast<const __half*>(P->k_f16); p->v_f16 = static_cast<const __half*>(P->v_f16);
+  p->k_fp8 = static_cast<const uint8_t*>(P->k_fp8); p->v_fp8 = static_cast<const uint8_t*>(P->v_fp8);
+  p->k_i8 = static_cast<const int8_t*>(P->k_i8); p->v_i8 = static_cast<const int8_t*>(P->v_i8);
+  p->k_i4 = static_cast<const uint8_t*>(P->k_i4); p->v_i4 = static_cast<const uint8_t*>(P->v_i4);
+  p->k_i4r = static_cast<const uint8_t*>(P->k_i4r); p->v_i4r = static_cast<const uint8_t*>(P->v_i4r);
+  p->k_scale = P->k_scale; p->v_scale = P->v_scale; p->k_rscale = P->k_res_scale; p->v_rscale = P->v_res_scale;
+  p->num_pages = P->num_pages; p->PS = PS; p->D = D; p->scale_mode = P->scale_mode;
+  p->n_scales = n_scales_of(P->scale_mode, D);
+  p->q = a->q; p->q_dtype = a->q_dtype; p->q_sb = a->q_stride_b; p->q_sh = a->q_stride_h;
+  p->out = a->out; p->out_dtype = a->out_dtype; p->o_sb = a->out_stride_b; p->o_sh = a->out_stride_h;
+  p->B = a->batch; p->Hq = a->num_q_heads; p->Ht = a->num_table_heads; p->G = G;
+  p->pt = a->page_table; p->pt_sb = a->pt_stride_b; p->pt_sh = a->pt_stride_h; p->W = a->table_width;
+  p->pc = a->page_counts; p->pc_sb = a->pc_stride_b;
+  p->tags = a->page_tags; p->tag_bytes = a->tag_bytes;
+  std::memcpy(p->tag_map, a->tag_map, 16); p->tag_default = a->tag_default;
+  p->sm_scale = a->sm_scale;
+  p->ex_m = a->partial_m; p->ex_l = a->partial_l; p->ex_acc = a->partial_acc;
+  if (p->ex_l && (!p->ex_m || !p->ex_acc)) return fail(IAK_ERR_INVALID_ARG, "partial export needs m, l and acc");
+  // split planning: aim for ~4 CTAs per SM, at least 8 slots per split
+  const int64_t units = static_cast<int64_t>(a->batch) * a->num_table_heads;
+  int splits = a->num_splits;
+  if (splits <= 0) {
+    const int64_t target = 4LL * device_sm_count();
+    int64_t s = units > 0 ? (target + units - 1) / units : 1;
+    const int64_t max_s = std::max<int64_t>(1, (a->table_width + 7) / 8);
+    splits = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(s, max_s)));
+  }
+  splits = std::max(1, std::min(splits, std::max(1, a->table_width)));
+  int pps = a->table_width > 0 ? (a->table_width + splits - 1) / splits : 1;
+  splits = a->table_width > 0 ? (a->table_width + pps - 1) / pps : 1;
+  if (units * splits > 0x7FFFFFFFLL) return fail(IAK_ERR_UNSUPPORTED, "too many work units");
+  p->num_splits = splits; p->pages_per_split = pps;
+  return IAK_OK;
+}
+
+static size_t workspace_bytes_for(const DecodeParams& p) {
+  if (p.num_splits <= 1) return 0;
+  const size_t rows = static_cast<size_t>(p.B) * p.Hq * p.num_splits;
+  return align_up(rows * 4, 256) * 2 + align_up(rows * p.D * 4, 256);
+}
+
+}  // namespace iak
+
+using namespace iak;
+
+extern "C" {
+
+int iak_version(void) { return IAK_ABI_VERSION; }
+
+const char* iak_last_error(void) { return g_last_error.c_str(); }
+
+int iak_decode_workspace_size(const iak_page_pools* pools, const iak_decode_args* args, size_t* bytes) {
+  if (!bytes) return fail(IAK_ERR_INVALID_ARG, "bytes is NULL");
+  DecodeParams p;
+  int st = prepare(pools, args, &p);
+  if (st) return st;
+  *bytes = workspace_bytes_for(p);
+  return IAK_OK;
+}
+
+int iak_decode(const iak_page_pools* pools, const iak_decode_args* args, void* workspace, size_t ws_bytes,
+               void* stream) {
+  DecodeParams p;
+  int st = prepare(pools, args, &p);
+  if (st) return st;
+  if (p.B == 0) return IAK_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const size_t need = workspace_bytes_for(p);
+  if (need > 0) {
+    if (!workspace || ws_bytes < need)
+      return fail(IAK_ERR_WORKSPACE, "workspace of %zu bytes needed, %zu given", need, workspace ? ws_bytes : 0);
+    if (reinterpret_cast<uintptr_t>(workspace) % 256) return fail(IAK_ERR_WORKSPACE, "workspace must be 256-byte aligned");
+    const size_t rows = static_cast<size_t>(p.B) * p.Hq * p.num_splits;
+    char* w = static_cast<char*>(workspace);
+    p.ws_m = reinterpret_cast<float*>(w);
+    p.ws_l = reinterpret_cast<float*>(w + align_up(rows * 4, 256));
+    p.ws_acc = reinterpret_cast<float*>(w + 2 * align_up(rows * 4, 256));
+  }
+  if (p.W == 0) {
+    // nothing selected anywhere: every output row is zero (or an empty partial)
+    DecodeParams z = p;
+    z.num_splits = 1; z.pages_per_split = 1;
+    return launch_decode_generic(z, s);
+  }
+  bool launched = false;
+  st = launch_decode_mma(p, *pools, s, &launched);
+  if (st) return st;
+  if (!launched) {
+    st = launch_decode_generic(p, s);
+    if (st) return st;
+  }
+  if (p.num_splits > 1) {
+    st = launch_merge(p.ws_m, p.ws_l, p.ws_acc, static_cast<int64_t>(p.B) * p.Hq, p.num_splits, p.D, p.out,
+                      p.out_dtype, 0, &p, p.ex_m, p.ex_l, p.ex_acc, s);
+    if (st) return st;
+  }
+  return IAK_OK;
+}
+
+int iak_merge_partials(const float* m, const float* l, const float* acc, int64_t rows, int32_t splits,
+                       int32_t head_dim, void* out, int32_t out_dtype, int64_t out_row_stride, void* stream) {
+  if (rows < 0 || splits <= 0 || head_dim <= 0) return fail(IAK_ERR_INVALID_ARG, "bad merge sizes");
+  if (rows == 0) return IAK_OK;
+  if (!m || !l || !acc || !out) return fail(IAK_ERR_INVALID_ARG, "null merge pointer");
+  if (out_dtype < 0 || out_dtype > 2) return fail(IAK_ERR_INVALID_ARG, "bad out dtype");
+  if (out_row_stride < head_dim) return fail(IAK_ERR_INVALID_ARG, "out_row_stride < head_dim");
+  return launch_merge(m, l, acc, rows, splits, head_dim, out, out_dtype, out_row_stride, nullptr, nullptr, nullptr,
+                      nullptr, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

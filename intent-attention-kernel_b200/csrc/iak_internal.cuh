@@ -1,0 +1,96 @@
+// Internal declarations shared by the libiak_b200 translation units.
+#pragma once
+
+#include <cstdint>
+#include <cstdio>
+#include <string>
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_fp8.h>
+#include <cuda_runtime.h>
+
+#include "intent_attention_b200.h"
+
+namespace iak {
+
+// ---------------------------------------------------------------- errors ---
+void set_error(const char* fmt, ...);
+int fail(int status, const char* fmt, ...);
+int check_cuda(cudaError_t e, const char* what);
+int device_sm_count();
+
+// --------------------------------------------------------- device params ---
+// Flattened, by-value kernel parameters of one decode launch.
+struct DecodeParams {
+  const __half* k_f16; const __half* v_f16;
+  const uint8_t* k_fp8; const uint8_t* v_fp8;
+  const int8_t* k_i8; const int8_t* v_i8;
+  const uint8_t* k_i4; const uint8_t* v_i4;
+  const uint8_t* k_i4r; const uint8_t* v_i4r;
+  const float* k_scale; const float* v_scale;
+  const float* k_rscale; const float* v_rscale;
+  int64_t num_pages;
+  int PS, D, scale_mode, n_scales;
+  const void* q; int q_dtype; int64_t q_sb, q_sh;
+  void* out; int out_dtype; int64_t o_sb, o_sh;
+  int B, Hq, Ht, G;
+  const int32_t* pt; int64_t pt_sb, pt_sh; int W;
+  const int32_t* pc; int64_t pc_sb;
+  const void* tags; int tag_bytes;
+  uint8_t tag_map[16]; uint8_t tag_default;
+  float sm_scale;
+  int num_splits, pages_per_split;
+  // split partials, [unit][split][g] and [unit][split][g][D]
+  float* ws_m; float* ws_l; float* ws_acc;
+  // optional export of final per-row partials (rows = B*Hq)
+  float* ex_m; float* ex_l; float* ex_acc;
+};
+
+// Launchers (return IAK_OK or a status; errors recorded with set_error).
+int launch_decode_generic(const DecodeParams& p, cudaStream_t s);
+int launch_decode_mma(const DecodeParams& p, const iak_page_pools& pools, cudaStream_t s, bool* launched);
+int launch_merge(const float* m, const float* l, const float* acc, int64_t rows, int splits, int D,
+                 void* out, int out_dtype, int64_t out_row_stride,
+                 const DecodeParams* rowmap, float* ex_m, float* ex_l, float* ex_acc, cudaStream_t s);
+
+// ------------------------------------------------------- device helpers ---
+__host__ __device__ inline int n_scales_of(int mode, int D) {
+  return mode == IAK_SCALE_PAGE ? 1 : (mode == IAK_SCALE_GROUP32 ? D / 32 : D);
+}
+
+__device__ __forceinline__ float load_as_float(const void* base, int dtype, int64_t idx) {
+  if (dtype == IAK_DT_F32) return static_cast<const float*>(base)[idx];
+  if (dtype == IAK_DT_F16) return __half2float(static_cast<const __half*>(base)[idx]);
+  return __bfloat162float(static_cast<const __nv_bfloat16*>(base)[idx]);
+}
+
+__device__ __forceinline__ void store_from_float(void* base, int dtype, int64_t idx, float v) {
+  if (dtype == IAK_DT_F32) static_cast<float*>(base)[idx] = v;
+  else if (dtype == IAK_DT_F16) static_cast<__half*>(base)[idx] = __float2half_rn(v);
+  else static_cast<__nv_bfloat16*>(base)[idx] = __float2bfloat16_rn(v);
+}
+
+__device__ __forceinline__ float e4m3_to_float(uint8_t c) {
+  __half_raw h = __nv_cvt_fp8_to_halfraw(static_cast<__nv_fp8_storage_t>(c), __NV_E4M3);
+  return __half2float(__half(h));
+}
+
+// Packed INT4 layout: channel d lives in word 4*(d/32) + (d%16)/4 at nibble
+// NIB[(d%4)] + 2*((d%32) >= 16), stored as code + 8.
+__device__ __forceinline__ int int4_code(const uint8_t* row, int d) {
+  const int r = d & 31;
+  const int o = r & 3;
+  const int n = ((o & 1) << 2) + (o >> 1) + ((r >> 4) << 1);  // {0,4,1,5}[o] + 2*hi
+  const int w = ((d >> 5) << 2) + ((r & 15) >> 2);
+  const uint8_t byte = row[w * 4 + (n >> 1)];
+  return static_cast<int>((n & 1) ? (byte >> 4) : (byte & 0xF)) - 8;
+}
+
+__device__ __forceinline__ int page_format(const DecodeParams& p, int64_t pid) {
+  int tag = p.tag_bytes == 1 ? static_cast<int>(static_cast<const uint8_t*>(p.tags)[pid])
+                             : static_cast<const int32_t*>(p.tags)[pid];
+  return (tag >= 0 && tag < 16) ? p.tag_map[tag] : p.tag_default;
+}
+
+}  // namespace iak

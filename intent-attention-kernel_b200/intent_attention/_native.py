@@ -1,0 +1,136 @@
+"""ctypes binding of libiak_b200.so (the C ABI in include/intent_attention_b200.h).
+
+The library is loaded lazily; every product entry point calls ``lib()``, which
+raises ``RuntimeError`` when the CUDA extension is missing.  There is no CPU
+fallback anywhere on the decode path.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+from typing import Optional
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.environ.get("IAK_LIB", os.path.join(_HERE, "libiak_b200.so"))
+
+IAK_OK, IAK_ERR_INVALID_ARG, IAK_ERR_UNSUPPORTED, IAK_ERR_CUDA, IAK_ERR_WORKSPACE, IAK_ERR_TIMEOUT = range(6)
+DT_F32, DT_F16, DT_BF16 = 0, 1, 2
+FMT_SKIP, FMT_F16, FMT_FP8, FMT_INT8, FMT_INT4, FMT_INT4R, FMT_SPARSE = range(7)
+SCALE_PAGE, SCALE_GROUP32, SCALE_CHANNEL = 0, 1, 2
+SCALE_MODES = {"page": SCALE_PAGE, "group32": SCALE_GROUP32, "channel": SCALE_CHANNEL}
+
+c_void_p = ctypes.c_void_p
+c_i32 = ctypes.c_int32
+c_i64 = ctypes.c_int64
+
+
+class PagePools(ctypes.Structure):
+    _fields_ = [
+        ("k_f16", c_void_p), ("v_f16", c_void_p), ("k_fp8", c_void_p), ("v_fp8", c_void_p),
+        ("k_i8", c_void_p), ("v_i8", c_void_p), ("k_i4", c_void_p), ("v_i4", c_void_p),
+        ("k_i4r", c_void_p), ("v_i4r", c_void_p),
+        ("k_scale", c_void_p), ("v_scale", c_void_p), ("k_res_scale", c_void_p), ("v_res_scale", c_void_p),
+        ("num_pages", c_i64), ("page_size", c_i32), ("head_dim", c_i32), ("scale_mode", c_i32),
+    ]
+
+
+class DecodeArgs(ctypes.Structure):
+    _fields_ = [
+        ("q", c_void_p), ("q_dtype", c_i32), ("q_stride_b", c_i64), ("q_stride_h", c_i64),
+        ("out", c_void_p), ("out_dtype", c_i32), ("out_stride_b", c_i64), ("out_stride_h", c_i64),
+        ("batch", c_i32), ("num_q_heads", c_i32), ("num_table_heads", c_i32),
+        ("page_table", c_void_p), ("pt_stride_b", c_i64), ("pt_stride_h", c_i64), ("table_width", c_i32),
+        ("page_counts", c_void_p), ("pc_stride_b", c_i64),
+        ("page_tags", c_void_p), ("tag_bytes", c_i32), ("tag_map", ctypes.c_uint8 * 16), ("tag_default", ctypes.c_uint8),
+        ("sm_scale", ctypes.c_float),
+        ("partial_m", c_void_p), ("partial_l", c_void_p), ("partial_acc", c_void_p),
+        ("num_splits", c_i32),
+    ]
+
+
+class PackArgs(ctypes.Structure):
+    _fields_ = [
+        ("logical_ids", c_void_p), ("num_ids", c_i32),
+        ("logical_tags", c_void_p), ("num_logical_pages", c_i32),
+        ("bases", c_void_p), ("batch", c_i32), ("num_table_heads", c_i32), ("table_width", c_i32),
+        ("page_table", c_void_p), ("page_counts", c_void_p), ("page_tags", c_void_p),
+        ("num_tag_pages", c_i64), ("pad_value", c_i32),
+    ]
+
+
+class QuantArgs(ctypes.Structure):
+    _fields_ = [
+        ("x", c_void_p), ("x_dtype", c_i32), ("num_src_pages", c_i64),
+        ("dst_ids", c_void_p), ("formats", c_void_p),
+        ("given_scale", c_void_p), ("given_res_scale", c_void_p),
+        ("f16", c_void_p), ("fp8", c_void_p), ("i8", c_void_p), ("i4", c_void_p), ("i4r", c_void_p),
+        ("scale", c_void_p), ("res_scale", c_void_p),
+        ("num_pages", c_i64), ("page_size", c_i32), ("head_dim", c_i32), ("scale_mode", c_i32),
+    ]
+
+
+# name -> (restype, argtypes); mirrors every declaration of the public header
+SIGNATURES = {
+    "iak_version": (ctypes.c_int, []),
+    "iak_last_error": (ctypes.c_char_p, []),
+    "iak_decode_workspace_size": (ctypes.c_int, [ctypes.POINTER(PagePools), ctypes.POINTER(DecodeArgs),
+                                                 ctypes.POINTER(ctypes.c_size_t)]),
+    "iak_decode": (ctypes.c_int, [ctypes.POINTER(PagePools), ctypes.POINTER(DecodeArgs), c_void_p,
+                                  ctypes.c_size_t, c_void_p]),
+    "iak_merge_partials": (ctypes.c_int, [c_void_p, c_void_p, c_void_p, c_i64, c_i32, c_i32, c_void_p, c_i32,
+                                          c_i64, c_void_p]),
+    "iak_pack_metadata": (ctypes.c_int, [ctypes.POINTER(PackArgs), c_void_p]),
+    "iak_quantize_pages": (ctypes.c_int, [ctypes.POINTER(QuantArgs), c_void_p]),
+}
+
+_lock = threading.Lock()
+_lib: Optional[ctypes.CDLL] = None
+_load_error: Optional[str] = None
+
+
+def _load() -> Optional[ctypes.CDLL]:
+    global _lib, _load_error
+    with _lock:
+        if _lib is not None or _load_error is not None:
+            return _lib
+        if not os.path.exists(LIB_PATH):
+            _load_error = (f"the CUDA extension {LIB_PATH} is not built "
+                           "(run: python intent-attention-kernel_b200/build.py)")
+            return None
+        try:
+            lib = ctypes.CDLL(LIB_PATH)
+        except OSError as e:  # pragma: no cover - depends on the machine
+            _load_error = f"cannot load {LIB_PATH}: {e}"
+            return None
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(lib, name, None)
+            if fn is None:
+                _load_error = f"{LIB_PATH} does not export {name}"
+                return None
+            fn.restype = res
+            fn.argtypes = args
+        _lib = lib
+        return _lib
+
+
+def available() -> bool:
+    return _load() is not None
+
+
+def lib() -> ctypes.CDLL:
+    """The loaded library; raises RuntimeError if the extension is missing."""
+    l = _load()
+    if l is None:
+        raise RuntimeError(_load_error)
+    return l
+
+
+def check(status: int, what: str) -> None:
+    if status == IAK_OK:
+        return
+    msg = lib().iak_last_error().decode(errors="replace")
+    if status == IAK_ERR_INVALID_ARG:
+        raise ValueError(f"{what}: {msg}")
+    raise RuntimeError(f"{what} failed (status {status}): {msg}")
