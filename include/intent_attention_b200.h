@@ -117,7 +117,11 @@ typedef struct iak_decode_args {
    * combines partials of several devices. */
   float* partial_m; float* partial_l; float* partial_acc;
   int32_t num_splits;             /* 0 = choose automatically               */
+  int32_t kernel;                 /* IAK_KERNEL_*: 0 auto, 1 generic, 2 tensor core */
 } iak_decode_args;
+
+/* decode kernel selection (iak_decode_args.kernel) */
+enum { IAK_KERNEL_AUTO = 0, IAK_KERNEL_GENERIC = 1, IAK_KERNEL_TENSOR = 2 };
 
 int iak_version(void);
 const char* iak_last_error(void);

@@ -131,9 +131,15 @@ static int prepare(const iak_page_pools* P, const iak_decode_args* a, DecodePara
   }
   splits = std::max(1, std::min(splits, std::max(1, a->table_width)));
   int pps = a->table_width > 0 ? (a->table_width + splits - 1) / splits : 1;
+  if (pps > 512) pps = 512;  // the tensor-core kernel stages at most 512 table slots per CTA
   splits = a->table_width > 0 ? (a->table_width + pps - 1) / pps : 1;
   if (units * splits > 0x7FFFFFFFLL) return fail(IAK_ERR_UNSUPPORTED, "too many work units");
   p->num_splits = splits; p->pages_per_split = pps;
+  p->kernel = a->kernel;
+  if (a->kernel < 0 || a->kernel > 2) return fail(IAK_ERR_INVALID_ARG, "bad kernel selector %d", a->kernel);
+  if (a->kernel == IAK_KERNEL_TENSOR && !mma_path_eligible(*p))
+    return fail(IAK_ERR_UNSUPPORTED, "the tensor-core decode needs page_size 16, head_dim 64/128, fp16/bf16 q and "
+                "page (or, at head_dim 128, group32) scales");
   return IAK_OK;
 }
 
@@ -187,7 +193,7 @@ int iak_decode(const iak_page_pools* pools, const iak_decode_args* args, void* w
     return launch_decode_generic(z, s);
   }
   bool launched = false;
-  st = launch_decode_mma(p, *pools, s, &launched);
+  if (p.kernel != IAK_KERNEL_GENERIC) st = launch_decode_mma(p, *pools, s, &launched);
   if (st) return st;
   if (!launched) {
     st = launch_decode_generic(p, s);

@@ -41,6 +41,7 @@ struct DecodeParams {
   uint8_t tag_map[16]; uint8_t tag_default;
   float sm_scale;
   int num_splits, pages_per_split;
+  int kernel;  // IAK_KERNEL_*
   // split partials, [unit][split][g] and [unit][split][g][D]
   float* ws_m; float* ws_l; float* ws_acc;
   // optional export of final per-row partials (rows = B*Hq)
@@ -50,6 +51,7 @@ struct DecodeParams {
 // Launchers (return IAK_OK or a status; errors recorded with set_error).
 int launch_decode_generic(const DecodeParams& p, cudaStream_t s);
 int launch_decode_mma(const DecodeParams& p, const iak_page_pools& pools, cudaStream_t s, bool* launched);
+bool mma_path_eligible(const DecodeParams& p);
 int launch_merge(const float* m, const float* l, const float* acc, int64_t rows, int splits, int D,
                  void* out, int out_dtype, int64_t out_row_stride,
                  const DecodeParams* rowmap, float* ex_m, float* ex_l, float* ex_acc, cudaStream_t s);

@@ -20,6 +20,8 @@ DT_F32, DT_F16, DT_BF16 = 0, 1, 2
 FMT_SKIP, FMT_F16, FMT_FP8, FMT_INT8, FMT_INT4, FMT_INT4R, FMT_SPARSE = range(7)
 SCALE_PAGE, SCALE_GROUP32, SCALE_CHANNEL = 0, 1, 2
 SCALE_MODES = {"page": SCALE_PAGE, "group32": SCALE_GROUP32, "channel": SCALE_CHANNEL}
+KERNEL_AUTO, KERNEL_GENERIC, KERNEL_TENSOR = 0, 1, 2
+KERNELS = {"auto": KERNEL_AUTO, "generic": KERNEL_GENERIC, "tensor": KERNEL_TENSOR}
 
 c_void_p = ctypes.c_void_p
 c_i32 = ctypes.c_int32
@@ -46,7 +48,7 @@ class DecodeArgs(ctypes.Structure):
         ("page_tags", c_void_p), ("tag_bytes", c_i32), ("tag_map", ctypes.c_uint8 * 16), ("tag_default", ctypes.c_uint8),
         ("sm_scale", ctypes.c_float),
         ("partial_m", c_void_p), ("partial_l", c_void_p), ("partial_acc", c_void_p),
-        ("num_splits", c_i32),
+        ("num_splits", c_i32), ("kernel", c_i32),
     ]
 
 

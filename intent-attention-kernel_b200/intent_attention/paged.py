@@ -216,7 +216,7 @@ def make_tag_map(mapping: Mapping[int, str]) -> Tuple[int, ...]:
 
 
 def _decode_structs(q, pool, page_table, page_counts, page_tags, tag_map, tag_default, sm_scale, out,
-                    partial, num_splits):
+                    partial, num_splits, kernel="auto"):
     B, Hq, D = q.shape
     if page_table.dim() != 3 or page_table.shape[0] != B:
         raise ValueError(f"page_table must be [B, Ht, W] with B={B}, got {tuple(page_table.shape)}")
@@ -244,6 +244,7 @@ def _decode_structs(q, pool, page_table, page_counts, page_tags, tag_map, tag_de
         m, l, acc = partial
         args.partial_m, args.partial_l, args.partial_acc = m.data_ptr(), l.data_ptr(), acc.data_ptr()
     args.num_splits = int(num_splits)
+    args.kernel = N.KERNELS[kernel]
     return pool.struct(), args
 
 
@@ -251,13 +252,15 @@ def paged_decode(q: torch.Tensor, pool: PagePool, page_table: torch.Tensor, page
                  page_tags: torch.Tensor, tag_map: Sequence[int], tag_default: int = N.FMT_SKIP,
                  sm_scale: Optional[float] = None, out: Optional[torch.Tensor] = None,
                  out_dtype: Optional[torch.dtype] = None, num_splits: int = 0,
-                 partial: Optional[Tuple[torch.Tensor, torch.Tensor, torch.Tensor]] = None) -> torch.Tensor:
+                 partial: Optional[Tuple[torch.Tensor, torch.Tensor, torch.Tensor]] = None,
+                 kernel: str = "auto") -> torch.Tensor:
     """Single-query paged decode over selected pages -> out [B, Hq, D].
 
     ``tag_map`` (16 IAK_FMT codes, see ``make_tag_map``) translates the
     caller's precision enum; tags outside 0..15 use ``tag_default``.  With
     ``partial=(m, l, acc)`` ([B*Hq], [B*Hq], [B*Hq, D] fp32) the unnormalised
-    split-KV partials are written instead of ``out``.
+    split-KV partials are written instead of ``out``.  ``kernel`` selects
+    "auto" (tensor-core path when the shape allows it), "generic" or "tensor".
     """
     _require_cuda(q, "q")
     if q.dim() != 3:
@@ -290,7 +293,7 @@ def paged_decode(q: torch.Tensor, pool: PagePool, page_table: torch.Tensor, page
         if out.shape != q.shape or out.stride(-1) != 1 or out.dtype not in _DT:
             raise ValueError(f"out must be a {tuple(q.shape)} float tensor with a contiguous last dim")
     pools, args = _decode_structs(q, pool, page_table, page_counts, page_tags, tag_map, tag_default, sm_scale,
-                                  out, partial, num_splits)
+                                  out, partial, num_splits, kernel)
     L = N.lib()
     nbytes = ctypes.c_size_t(0)
     N.check(L.iak_decode_workspace_size(ctypes.byref(pools), ctypes.byref(args), ctypes.byref(nbytes)),

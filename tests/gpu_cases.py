@@ -63,10 +63,10 @@ def tag_map_for(formats):
     return make_tag_map({t: (f if f in formats else "SKIP") for t, f in TAG_MAP.items()})
 
 
-def run_gpu(case, out_dtype=torch.float32, num_splits=0, sm_scale=None):
+def run_gpu(case, out_dtype=torch.float32, num_splits=0, sm_scale=None, kernel="auto"):
     return paged_decode(case["q"], case["pool"], case["table"], case["counts"], case["tags"],
                         tag_map_for(case["formats"]), 0, sm_scale=sm_scale, out_dtype=out_dtype,
-                        num_splits=num_splits)
+                        num_splits=num_splits, kernel=kernel)
 
 
 def run_oracle(case, sm_scale=None):

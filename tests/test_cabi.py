@@ -60,7 +60,7 @@ int main(void) {
   printf("iak_pack_args %zu\n", sizeof(iak_pack_args));
   printf("iak_quant_args %zu\n", sizeof(iak_quant_args));
   P(iak_page_pools, num_pages) P(iak_page_pools, scale_mode)
-  P(iak_decode_args, tag_map) P(iak_decode_args, sm_scale) P(iak_decode_args, partial_acc) P(iak_decode_args, num_splits)
+  P(iak_decode_args, tag_map) P(iak_decode_args, sm_scale) P(iak_decode_args, partial_acc) P(iak_decode_args, num_splits) P(iak_decode_args, kernel)
   P(iak_pack_args, pad_value) P(iak_quant_args, scale_mode) P(iak_quant_args, num_pages)
   return 0;
 }

@@ -77,6 +77,31 @@ def test_decode_all_formats_matches_oracle(D, G, mode):
     _close(run_gpu(case), run_oracle(case))
 
 
+@pytest.mark.parametrize("kernel", ["generic", "tensor"])
+@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("G", [1, 4, 8])
+@pytest.mark.parametrize("mode", ["page", "group32"])
+def test_both_kernels_match_oracle(kernel, D, G, mode):
+    if mode == "group32" and D == 64 and kernel == "tensor":
+        pytest.skip("group32 scales at head_dim 64 run on the generic kernel")
+    case = make_case(300 + D + G + len(mode), B=2, Hq=2 * G, Ht=2, D=D, W=40, NP=160, scale_mode=mode)
+    _close(run_gpu(case, kernel=kernel), run_oracle(case))
+
+
+@pytest.mark.parametrize("kernel", ["generic", "tensor"])
+@pytest.mark.parametrize("fmt", ["F16"] + FORMATS)
+def test_single_format_each_kernel(kernel, fmt):
+    case = make_case(77, B=2, Hq=8, Ht=2, D=128, W=48, NP=160, formats=[fmt], skip_frac=0.0, pad_frac=0.0,
+                     counts="full", q_dtype=torch.float16)
+    _close(run_gpu(case, kernel=kernel), run_oracle(case))
+
+
+def test_tensor_kernel_rejects_ineligible_shapes():
+    case = make_case(5, scale_mode="channel")
+    with pytest.raises(RuntimeError, match="tensor-core decode needs"):
+        run_gpu(case, kernel="tensor")
+
+
 @pytest.mark.parametrize("fmt", ["F16"] + FORMATS)
 def test_decode_single_format(fmt):
     case = make_case(7, B=3, Hq=12, Ht=3, D=128, W=32, NP=160, formats=[fmt], skip_frac=0.0, pad_frac=0.0,
