@@ -135,6 +135,27 @@ int iak_decode_workspace_size(const iak_page_pools* pools, const iak_decode_args
 int iak_decode(const iak_page_pools* pools, const iak_decode_args* args,
                void* workspace, size_t workspace_bytes, void* stream);
 
+/* Decode without any device allocation.  No counterpart in the reference.
+ *
+ * For callers that cannot call cudaMalloc: serving engines that reserve all
+ * device memory up front (most of it for the KV cache) and forbid allocation
+ * while decoding, hosts that reach this library through an FFI holding only
+ * borrowed device pointers and no allocator, and latency-critical loops that
+ * cannot afford an allocation's implicit device synchronisation.
+ *
+ * Same arguments and results as iak_decode, but the split-KV scratch is a
+ * file-scope device array of IAK_NOALLOC_SCRATCH_BYTES (8 MiB) that every GPU
+ * loading the library holds until the process exits; decodes whose
+ * iak_decode_workspace_size exceeds it are rejected with IAK_ERR_WORKSPACE
+ * (pass fewer num_splits, or use iak_decode).  The first call on a device
+ * looks up the array's device address with that device current, so make that
+ * first call before any stream capture.  All calls share the one array and it
+ * keeps the last call's contents (nothing in it needs to start at zero):
+ * calls that overlap on the GPU, on any streams, race.  Calls no cudaMalloc,
+ * cudaFree or allocating library routine. */
+#define IAK_NOALLOC_SCRATCH_BYTES (8 << 20)
+int iak_decode_noalloc(const iak_page_pools* pools, const iak_decode_args* args, void* stream);
+
 /* LSE merge of S partials per row: m/l [rows, S], acc [rows, S, D] (fp32,
  * contiguous).  Writes normalised rows to out (dtype, row stride in
  * elements); rows with no contribution become 0. */

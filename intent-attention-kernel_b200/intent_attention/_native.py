@@ -85,7 +85,9 @@ SIGNATURES = {
                                           c_i64, c_void_p]),
     "iak_pack_metadata": (ctypes.c_int, [ctypes.POINTER(PackArgs), c_void_p]),
     "iak_quantize_pages": (ctypes.c_int, [ctypes.POINTER(QuantArgs), c_void_p]),
+    "iak_decode_noalloc": (ctypes.c_int, [ctypes.POINTER(PagePools), ctypes.POINTER(DecodeArgs), c_void_p]),
 }
+NOALLOC_SCRATCH_BYTES = 8 << 20
 
 _lock = threading.Lock()
 _lib: Optional[ctypes.CDLL] = None
