@@ -120,33 +120,65 @@ static int prepare(const iak_page_pools* P, const iak_decode_args* a, DecodePara
   p->sm_scale = a->sm_scale;
   p->ex_m = a->partial_m; p->ex_l = a->partial_l; p->ex_acc = a->partial_acc;
   if (p->ex_l && (!p->ex_m || !p->ex_acc)) return fail(IAK_ERR_INVALID_ARG, "partial export needs m, l and acc");
-  // split planning: aim for ~4 CTAs per SM, at least 8 slots per split
   const int64_t units = static_cast<int64_t>(a->batch) * a->num_table_heads;
-  int splits = a->num_splits;
-  if (splits <= 0) {
-    const int64_t target = 4LL * device_sm_count();
-    int64_t s = units > 0 ? (target + units - 1) / units : 1;
-    const int64_t max_s = std::max<int64_t>(1, (a->table_width + 7) / 8);
-    splits = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(s, max_s)));
-  }
-  splits = std::max(1, std::min(splits, std::max(1, a->table_width)));
-  int pps = a->table_width > 0 ? (a->table_width + splits - 1) / splits : 1;
-  if (pps > 512) pps = 512;  // the tensor-core kernel stages at most 512 table slots per CTA
-  splits = a->table_width > 0 ? (a->table_width + pps - 1) / pps : 1;
-  if (units * splits > 0x7FFFFFFFLL) return fail(IAK_ERR_UNSUPPORTED, "too many work units");
-  p->num_splits = splits; p->pages_per_split = pps;
-  p->kernel = a->kernel;
   if (a->kernel < 0 || a->kernel > 2) return fail(IAK_ERR_INVALID_ARG, "bad kernel selector %d", a->kernel);
-  if (a->kernel == IAK_KERNEL_TENSOR && !mma_path_eligible(*p))
+  p->kernel = a->kernel;
+  const bool shape_ok = mma_shape_eligible(*p);
+  if (a->kernel == IAK_KERNEL_TENSOR && !shape_ok)
     return fail(IAK_ERR_UNSUPPORTED, "the tensor-core decode needs page_size 16, head_dim 64/128, fp16/bf16 q and "
                 "page (or, at head_dim 128, group32) scales");
+  p->tensor = shape_ok && a->kernel != IAK_KERNEL_GENERIC;
+  const int W = a->table_width;
+  int splits = a->num_splits, pps;
+  if (p->tensor) {
+    // persistent kernel over (unit, split) items of <= kTensorItemSlots slots;
+    // aim for ~8 items per resident CTA so the static item striding balances
+    if (splits <= 0) {
+      // Static item striding over ~2 resident CTAs per SM: minimise
+      // waves * (slots per item + a fixed per-item cost of ~16 slots).
+      const int64_t ctas = 2LL * device_sm_count();
+      int64_t best = -1, best_cost = 0;
+      const int max_s = std::max(1, std::min(W, 256));
+      for (int cand = 1; cand <= max_s; ++cand) {
+        const int64_t slots = (W + cand - 1) / cand;
+        if (slots > kTensorItemSlots) continue;
+        const int64_t items = units * cand;
+        const int64_t waves = (items + ctas - 1) / ctas;
+        const int64_t cost = waves * (slots + 16);
+        if (best < 0 || cost < best_cost) { best = cand; best_cost = cost; }
+      }
+      splits = static_cast<int>(best < 0 ? 1 : best);
+    }
+    splits = std::max(1, std::min(splits, std::max(1, W)));
+    pps = W > 0 ? (W + splits - 1) / splits : 1;
+    if (pps > kTensorItemSlots) pps = kTensorItemSlots;
+  } else {
+    // one CTA per (unit, split): aim for ~4 CTAs per SM, at least 8 slots per split
+    if (splits <= 0) {
+      const int64_t target = 4LL * device_sm_count();
+      const int64_t s = units > 0 ? (target + units - 1) / units : 1;
+      const int64_t max_s = std::max<int64_t>(1, (W + 7) / 8);
+      splits = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(s, max_s)));
+    }
+    splits = std::max(1, std::min(splits, std::max(1, W)));
+    pps = W > 0 ? (W + splits - 1) / splits : 1;
+  }
+  splits = W > 0 ? (W + pps - 1) / pps : 1;
+  if (units * splits > 0x7FFFFFFFLL) return fail(IAK_ERR_UNSUPPORTED, "too many work units");
+  p->num_splits = splits; p->pages_per_split = pps;
+  p->ws_slots = p->tensor ? splits * kTensorConsumerWarps : splits;
   return IAK_OK;
 }
 
+static size_t qtab_bytes_for(const DecodeParams& p) {
+  return p.tensor ? align_up(static_cast<size_t>(p.B) * p.Ht * kQueryTableBytes, 256) : 0;
+}
+
+// Workspace: [query tables (tensor path)] [m: rows x slots] [l] [acc: rows x slots x D]
 static size_t workspace_bytes_for(const DecodeParams& p) {
-  if (p.num_splits <= 1) return 0;
-  const size_t rows = static_cast<size_t>(p.B) * p.Hq * p.num_splits;
-  return align_up(rows * 4, 256) * 2 + align_up(rows * p.D * 4, 256);
+  if (!p.tensor && p.num_splits <= 1) return 0;
+  const size_t n = static_cast<size_t>(p.B) * p.Hq * p.ws_slots;
+  return qtab_bytes_for(p) + align_up(n * 4, 256) * 2 + align_up(n * p.D * 4, 256);
 }
 
 }  // namespace iak
@@ -180,27 +212,24 @@ int iak_decode(const iak_page_pools* pools, const iak_decode_args* args, void* w
     if (!workspace || ws_bytes < need)
       return fail(IAK_ERR_WORKSPACE, "workspace of %zu bytes needed, %zu given", need, workspace ? ws_bytes : 0);
     if (reinterpret_cast<uintptr_t>(workspace) % 256) return fail(IAK_ERR_WORKSPACE, "workspace must be 256-byte aligned");
-    const size_t rows = static_cast<size_t>(p.B) * p.Hq * p.num_splits;
+    const size_t n = static_cast<size_t>(p.B) * p.Hq * p.ws_slots;
     char* w = static_cast<char*>(workspace);
+    p.ws_qtab = p.tensor ? w : nullptr;
+    w += qtab_bytes_for(p);
     p.ws_m = reinterpret_cast<float*>(w);
-    p.ws_l = reinterpret_cast<float*>(w + align_up(rows * 4, 256));
-    p.ws_acc = reinterpret_cast<float*>(w + 2 * align_up(rows * 4, 256));
+    p.ws_l = reinterpret_cast<float*>(w + align_up(n * 4, 256));
+    p.ws_acc = reinterpret_cast<float*>(w + 2 * align_up(n * 4, 256));
   }
   if (p.W == 0) {
     // nothing selected anywhere: every output row is zero (or an empty partial)
     DecodeParams z = p;
-    z.num_splits = 1; z.pages_per_split = 1;
+    z.num_splits = 1; z.pages_per_split = 1; z.tensor = 0; z.ws_slots = 1;
     return launch_decode_generic(z, s);
   }
-  bool launched = false;
-  if (p.kernel != IAK_KERNEL_GENERIC) st = launch_decode_mma(p, *pools, s, &launched);
+  st = p.tensor ? launch_decode_mma(p, *pools, s) : launch_decode_generic(p, s);
   if (st) return st;
-  if (!launched) {
-    st = launch_decode_generic(p, s);
-    if (st) return st;
-  }
-  if (p.num_splits > 1) {
-    st = launch_merge(p.ws_m, p.ws_l, p.ws_acc, static_cast<int64_t>(p.B) * p.Hq, p.num_splits, p.D, p.out,
+  if (p.ws_slots > 1 || p.tensor) {
+    st = launch_merge(p.ws_m, p.ws_l, p.ws_acc, static_cast<int64_t>(p.B) * p.Hq, p.ws_slots, p.D, p.out,
                       p.out_dtype, 0, &p, p.ex_m, p.ex_l, p.ex_acc, s);
     if (st) return st;
   }

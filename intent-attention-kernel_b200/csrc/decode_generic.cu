@@ -193,7 +193,7 @@ __global__ void __launch_bounds__(kWarps * 32) decode_generic_kernel(const Decod
     const int hq = hk * G + g;
     const int64_t r = static_cast<int64_t>(b) * p.Hq + hq;
     if (p.num_splits > 1) {
-      const int64_t wi = r * p.num_splits + split;
+      const int64_t wi = r * p.ws_slots + split;
       if (d == 0) {
         p.ws_m[wi] = M;
         p.ws_l[wi] = L;

@@ -30,6 +30,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <cstring>
 #include <mutex>
 #include <unordered_map>
@@ -44,28 +45,58 @@ namespace {
 
 constexpr int kPS = 16;
 constexpr int kConsumerWarps = 4;
-constexpr int kThreads = (kConsumerWarps + 1) * 32;
-constexpr int kChunkMax = 512;
-constexpr int kStages = 8;
+constexpr int kTmaWarp = kConsumerWarps;          // issues the TMA page loads
+constexpr int kPrepWarp = kConsumerWarps + 1;     // prepares the next work item
+constexpr int kThreads = (kConsumerWarps + 2) * 32;
+constexpr int kChunkMax = 256;                    // table slots per work item
+#ifndef IAK_STAGES
+#define IAK_STAGES 8
+#endif
+#ifndef IAK_MIN_BLOCKS
+#define IAK_MIN_BLOCKS 2
+#endif
+constexpr int kStages = IAK_STAGES;     // power of two, multiple of the consumer warp count
 constexpr int kStageBytes = 9216;   // K region 4 KB | V region 4 KB | scale rows 1 KB
 constexpr int kVOff = 4096;
 constexpr int kResOff = 1024;       // INT4 residual plane inside a K or V region
 constexpr int kScaleOff = 8192;
 constexpr long long kWaitCycles = 4000000000LL;  // ~2 s at boost clock, then give up
+#ifndef IAK_PRODUCER_LANES
+#define IAK_PRODUCER_LANES 4
+#endif
+#ifndef IAK_F16_ONE_BOX
+#define IAK_F16_ONE_BOX 1
+#endif
+constexpr float kLazyLog2 = 8.f;                  // rescale O only when the max grows by > 2^8
+constexpr int kProducerLanes = IAK_PRODUCER_LANES; // producer lanes issuing TMA for consecutive pages
+// F16 pages at D = 128: one TMA box of 32 half-rows (token-major, 256-byte
+// token rows) instead of two 64-channel boxes
+constexpr bool kF16OneBox = IAK_F16_ONE_BOX != 0;
 
 enum MapIdx { M_KF16 = 0, M_VF16, M_KFP8, M_VFP8, M_KI8, M_VI8, M_KI4, M_VI4, M_KI4R, M_VI4R, M_COUNT };
 struct TmaMaps {
   CUtensorMap m[M_COUNT];
 };
 
-struct SmemLayout {
-  static constexpr int stages = 0;
-  static constexpr int bars = kStages * kStageBytes;                 // full[kStages], empty[kStages]
-  static constexpr int pid = bars + 2 * kStages * 8;
-  static constexpr int scal = pid + kChunkMax * 4;                   // ks, vs, krs, vrs
+// Per-unit query table (built by decode_prep_kernel, bulk-copied per work item):
+// fp16 fragments [D/16][32] uint4 | int8 terms [D/32][32] uint4 | the same in
+// INT4 order | 128 floats: term scales s1[8], s2[8], int4 biases [4][8] x 2.
+constexpr int kQFrag = 0, kQI8 = 4096, kQI4 = 6144, kQSc = 8192, kQTab = 8704;
+
+// One work-item buffer: query table | page ids | 4 scale scalars | formats | meta.
+struct ItemLayout {
+  static constexpr int qtab = 0;
+  static constexpr int pid = kQTab;
+  static constexpr int scal = pid + kChunkMax * 4;
   static constexpr int fmt = scal + 4 * kChunkMax * 4;
-  static constexpr int misc = fmt + kChunkMax;
-  static constexpr int total = misc + 64;
+  static constexpr int meta = fmt + kChunkMax;                     // n_valid, unit, split
+  static constexpr int bytes = (meta + 16 + 127) / 128 * 128;
+};
+
+struct SmemLayout {
+  static constexpr int items = kStages * kStageBytes;              // two ItemLayout buffers
+  static constexpr int bars = items + 2 * ItemLayout::bytes;       // full[S], empty[S], ifull[2], iempty[2]
+  static constexpr int total = bars + (2 * kStages + 4) * 8;
 };
 
 // ----------------------------------------------------------------- PTX ---
@@ -116,6 +147,19 @@ __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1
       "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+// integer MMA m16n8k32: s32 += A(16x32, s8 or u8) * B(32x8, s8)
+__device__ __forceinline__ void imma_s8(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void imma_u8(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
@@ -251,6 +295,13 @@ __device__ __forceinline__ void v_table_int4(const char* tile, int r, int c, uin
   }
 }
 
+// shared-memory offset of fp16 channel d (multiple of 4) of token t
+template <int D>
+__device__ __forceinline__ uint32_t f16_off(int t, int d) {
+  if constexpr (D == 128 && kF16OneBox) return sw128(t * 256 + 2 * d);
+  return sw128((d >> 6) * 2048 + t * 128 + ((2 * d) & 127));
+}
+
 template <int D>
 __device__ __forceinline__ void v_table_f16(const char* tile, int r, int c, uint32_t (&vh)[2][D / 64][8]) {
 #pragma unroll
@@ -262,8 +313,8 @@ __device__ __forceinline__ void v_table_f16(const char* tile, int r, int c, uint
 #pragma unroll
       for (int part = 0; part < 2; ++part) {     // channels d0+{0..3}, d0+16+{0..3}
         const int d = d0 + 16 * part;
-        const uint32_t o0 = sw128((d >> 6) * 2048 + t0 * 128 + ((2 * d) & 127));
-        const uint32_t o1 = sw128((d >> 6) * 2048 + t1 * 128 + ((2 * d) & 127));
+        const uint32_t o0 = f16_off<D>(t0, d);
+        const uint32_t o1 = f16_off<D>(t1, d);
         const uint2 x0 = lds64(tile, o0), x1 = lds64(tile, o1);
         // nibble order: part 0 -> (0, 4, 1, 5), part 1 -> (2, 6, 3, 7)
         vh[tp][ws][0 + 2 * part] = __byte_perm(x0.x, x1.x, 0x5410);
@@ -276,10 +327,19 @@ __device__ __forceinline__ void v_table_f16(const char* tile, int r, int c, uint
 }
 
 // ------------------------------------------------ per-format QK A frags ---
-template <int D>
-__device__ __forceinline__ void k_frag_8bit(const char* tile, int r, int c, int kk, bool fp8, uint32_t (&a)[4]) {
-  const uint32_t x0 = lds32(tile, sw128(r * D + 16 * kk + 4 * c));
-  const uint32_t x1 = lds32(tile, sw128((r + 8) * D + 16 * kk + 4 * c));
+// (fp16 and e4m3 pages use fp16 MMAs; INT8 / INT4 pages use the integer MMA
+// on the raw codes, see the consumer loop)
+// Raw code words of two consecutive 16-byte chunks (ch, ch+1) of the 16 token
+// rows: x[0] = (row r, chunk ch), x[1] = (row r+8, ch), x[2] = (r, ch+1),
+// x[3] = (r+8, ch+1), each the 4 bytes 4c..4c+3 of that chunk (ldmatrix of
+// 8x16-byte matrices hands lane (r, c) exactly those bytes).
+__device__ __forceinline__ void ldsm_rows(uint32_t tile_u32, int row_bytes, int lane, int ch, uint32_t (&x)[4]) {
+  const int row = (lane & 7) + 8 * ((lane >> 3) & 1);
+  const int chunk = ch + (lane >> 4);
+  ldsm_x4(tile_u32 + sw128(row * row_bytes + 16 * chunk), x[0], x[1], x[2], x[3]);
+}
+
+__device__ __forceinline__ void k_frag_8bit_from(uint32_t x0, uint32_t x1, bool fp8, uint32_t (&a)[4]) {
   if (fp8) {
     a[0] = e4m3x2_f16x2(x0); a[2] = e4m3x2_f16x2(x0 >> 16);
     a[1] = e4m3x2_f16x2(x1); a[3] = e4m3x2_f16x2(x1 >> 16);
@@ -290,259 +350,486 @@ __device__ __forceinline__ void k_frag_8bit(const char* tile, int r, int c, int 
   }
 }
 
-// two k-steps (2p, 2p+1) of an INT4 plane
-template <int D>
-__device__ __forceinline__ void k_frag_int4(const char* tile, int r, int c, int p, uint32_t (&a)[2][4]) {
-  constexpr int RB = D / 2;
-  const uint32_t x0 = lds32(tile, sw128(r * RB + 16 * p + 4 * c));
-  const uint32_t x1 = lds32(tile, sw128((r + 8) * RB + 16 * p + 4 * c));
-  a[0][0] = i4pair_lo(x0); a[0][2] = i4pair_hi(x0);
-  a[0][1] = i4pair_lo(x1); a[0][3] = i4pair_hi(x1);
-  a[1][0] = i4pair_lo(x0 >> 8); a[1][2] = i4pair_hi(x0 >> 8);
-  a[1][1] = i4pair_lo(x1 >> 8); a[1][3] = i4pair_hi(x1 >> 8);
-}
-
 template <int D>
 __device__ __forceinline__ void k_frag_f16(uint32_t tile_u32, int lane, int kk, uint32_t (&a)[4]) {
   const int mi = lane >> 3, rr = lane & 7;
   const int tok = rr + 8 * (mi & 1);
   const int d = 16 * kk + 8 * (mi >> 1);
-  const uint32_t off = sw128((d >> 6) * 2048 + tok * 128 + ((2 * d) & 127));
-  ldsm_x4(tile_u32 + off, a[0], a[1], a[2], a[3]);
+  ldsm_x4(tile_u32 + f16_off<D>(tok, d), a[0], a[1], a[2], a[3]);
 }
 
-// ------------------------------------------------------------- kernel ---
-template <int D, bool GROUP>
-__global__ void __launch_bounds__(kThreads, 2)
-    decode_mma_kernel(const DecodeParams p, const __grid_constant__ TmaMaps maps) {
-  constexpr int KT = D / 16;   // k-steps of QK, m-tiles of PV
-  constexpr int NG = GROUP ? D / 32 : 1;
-  extern __shared__ __align__(1024) char smem_raw[];
-  char* smem = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SmemLayout::bars);
-  int32_t* pid_s = reinterpret_cast<int32_t*>(smem + SmemLayout::pid);
-  float* scal_s = reinterpret_cast<float*>(smem + SmemLayout::scal);
-  uint8_t* fmt_s = reinterpret_cast<uint8_t*>(smem + SmemLayout::fmt);
-  int* misc = reinterpret_cast<int*>(smem + SmemLayout::misc);
-
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int unit = blockIdx.y, split = blockIdx.x;
+// ------------------------------------------------------------- kernels ---
+// Query table of one (sequence, page-table head) unit: fp16 fragments for the
+// fp16 / e4m3 pages and the two int8 terms q = s1*i1 + s2*i2 (per query head;
+// |error| <= s2/2 ~ absmax/32258) for the integer MMA of INT8 / INT4 pages,
+// plus the per-32-channel sums of the terms that undo the INT4 +8 offset.
+template <int D>
+__global__ void __launch_bounds__(128) decode_prep_kernel(const DecodeParams p, char* __restrict__ qtab) {
+  constexpr int KT = D / 16;
+  __shared__ float qs[8 * D];
+  __shared__ int8_t i1s[8 * D], i2s[8 * D];
+  __shared__ float qsc[128];
+  const int unit = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int b = unit / p.Ht, hk = unit % p.Ht;
+  for (int idx = tid; idx < 8 * D; idx += 128) {
+    const int g = idx / D, d = idx % D;
+    const int64_t off = static_cast<int64_t>(b) * p.q_sb + static_cast<int64_t>(hk * p.G + g) * p.q_sh + d;
+    qs[idx] = g < p.G ? load_as_float(p.q, p.q_dtype, off) : 0.f;
+  }
+  for (int i = tid; i < 128; i += 128) qsc[i] = 0.f;
+  __syncthreads();
+  if (tid < 64) {
+    const int g = tid >> 3, sub = tid & 7;
+    const float* qr = qs + g * D;
+    float am = 0.f;
+    for (int d = sub; d < D; d += 8) am = fmaxf(am, fabsf(qr[d]));
+    for (int off = 1; off < 8; off <<= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, off));
+    const float s1 = am > 0.f ? am / 127.f : 1.f;
+    float am2 = 0.f;
+    for (int d = sub; d < D; d += 8) {
+      const float t = fminf(fmaxf(rintf(qr[d] / s1), -127.f), 127.f);
+      am2 = fmaxf(am2, fabsf(qr[d] - t * s1));
+    }
+    for (int off = 1; off < 8; off <<= 1) am2 = fmaxf(am2, __shfl_xor_sync(0xffffffffu, am2, off));
+    const float s2 = am2 > 0.f ? am2 / 127.f : 1.f;
+    int sum1[4] = {0, 0, 0, 0}, sum2[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int j = 0; j < D / 32; ++j)
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int d = 32 * j + sub + 8 * k;
+        const float t1 = fminf(fmaxf(rintf(qr[d] / s1), -127.f), 127.f);
+        const float t2 = fminf(fmaxf(rintf((qr[d] - t1 * s1) / s2), -127.f), 127.f);
+        i1s[g * D + d] = static_cast<int8_t>(t1);
+        i2s[g * D + d] = static_cast<int8_t>(t2);
+        sum1[j] += static_cast<int>(t1);
+        sum2[j] += static_cast<int>(t2);
+      }
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      for (int off = 1; off < 8; off <<= 1) {
+        sum1[j] += __shfl_xor_sync(0xffffffffu, sum1[j], off);
+        sum2[j] += __shfl_xor_sync(0xffffffffu, sum2[j], off);
+      }
+    if (sub == 0) {
+      qsc[g] = s1;
+      qsc[8 + g] = s2;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        qsc[16 + j * 8 + g] = static_cast<float>(sum1[j]);
+        qsc[48 + j * 8 + g] = static_cast<float>(sum2[j]);
+      }
+    }
+  }
+  __syncthreads();
+  char* out = qtab + static_cast<int64_t>(unit) * kQTab;
+  if (warp == 0) {
+    const int r = lane >> 2, c = lane & 3;
+    const float* qr = qs + r * D;
+    uint4* qfrag = reinterpret_cast<uint4*>(out + kQFrag);
+    uint4* qi8 = reinterpret_cast<uint4*>(out + kQI8);
+    uint4* qi4 = reinterpret_cast<uint4*>(out + kQI4);
+#pragma unroll
+    for (int kk = 0; kk < KT; ++kk) {
+      const int b0 = 16 * kk + 2 * c, b1 = 16 * kk + 4 * c;
+      qfrag[kk * 32 + lane] = make_uint4(pack_f16x2(qr[b0], qr[b0 + 1]), pack_f16x2(qr[b0 + 8], qr[b0 + 9]),
+                                         pack_f16x2(qr[b1], qr[b1 + 1]), pack_f16x2(qr[b1 + 2], qr[b1 + 3]));
+    }
+    auto pack4 = [&](const int8_t* t, int d0, int d1, int d2, int d3) {
+      return static_cast<uint32_t>(static_cast<uint8_t>(t[d0])) |
+             (static_cast<uint32_t>(static_cast<uint8_t>(t[d1])) << 8) |
+             (static_cast<uint32_t>(static_cast<uint8_t>(t[d2])) << 16) |
+             (static_cast<uint32_t>(static_cast<uint8_t>(t[d3])) << 24);
+    };
+    const int8_t* t1 = i1s + r * D;
+    const int8_t* t2 = i2s + r * D;
+#pragma unroll
+    for (int j = 0; j < D / 32; ++j) {
+      const int e = 32 * j + 4 * c;   // k = 4c..4c+3 and 16+4c..16+4c+3 of k-step j
+      qi8[j * 32 + lane] = make_uint4(pack4(t1, e, e + 1, e + 2, e + 3), pack4(t1, e + 16, e + 17, e + 18, e + 19),
+                                      pack4(t2, e, e + 1, e + 2, e + 3), pack4(t2, e + 16, e + 17, e + 18, e + 19));
+      // INT4 word 4j+c expands to bytes of channels e+{0,16,1,17} (low nibbles) and e+{2,18,3,19}
+      qi4[j * 32 + lane] = make_uint4(pack4(t1, e, e + 16, e + 1, e + 17), pack4(t1, e + 2, e + 18, e + 3, e + 19),
+                                      pack4(t2, e, e + 16, e + 1, e + 17), pack4(t2, e + 2, e + 18, e + 3, e + 19));
+    }
+  }
+  if (tid < 128) reinterpret_cast<float*>(out + kQSc)[tid] = qsc[tid];
+}
+
+// Work item -> (unit, split) and its table-slot range [lo, hi).
+__device__ __forceinline__ void item_range(const DecodeParams& p, int item, int& unit, int& split, int& lo, int& hi) {
+  unit = item / p.num_splits;
+  split = item - unit * p.num_splits;
+  const int b = unit / p.Ht, hk = unit - (unit / p.Ht) * p.Ht;
   int count = p.W;
   if (p.pc) {
     const int cc = p.pc[b * p.pc_sb + hk];
     count = cc < 0 ? 0 : (cc > p.W ? p.W : cc);
   }
-  const int lo = split * p.pages_per_split;
-  const int hi = min(lo + p.pages_per_split, count);
+  lo = split * p.pages_per_split;
+  hi = min(lo + p.pages_per_split, count);
+}
+
+// Persistent split-KV decode.  CTA c processes work items c, c + gridDim.x, ...
+// (item = (unit, split) of <= kChunkMax table slots).  Warp kPrepWarp fills
+// one of two item buffers (query table by bulk copy, compacted page list)
+// ahead of use; warp kTmaWarp streams every item's pages through the stage
+// ring without draining between items; each consumer warp writes its own
+// (m, l, acc) partial per item, merged afterwards by merge_kernel.
+template <int D, bool GROUP>
+__global__ void __launch_bounds__(kThreads, IAK_MIN_BLOCKS)
+    decode_mma_kernel(const DecodeParams p, const __grid_constant__ TmaMaps maps, const char* __restrict__ qtab,
+                      int n_items) {
+  constexpr int KT = D / 16;   // k-steps of QK, m-tiles of PV
+  constexpr int NG = GROUP ? D / 32 : 1;
+  extern __shared__ __align__(1024) char smem_raw[];
+  char* smem = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SmemLayout::bars);   // full | empty | ifull | iempty
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int r = lane >> 2, c = lane & 3;
+  auto full_bar = [&](int s) { return smem_u32(&bars[s]); };
+  auto empty_bar = [&](int s) { return smem_u32(&bars[kStages + s]); };
+  auto ifull_bar = [&](int buf) { return smem_u32(&bars[2 * kStages + buf]); };
+  auto iempty_bar = [&](int buf) { return smem_u32(&bars[2 * kStages + 2 + buf]); };
+  auto item_buf = [&](int buf) { return smem + SmemLayout::items + buf * ItemLayout::bytes; };
 
   if (tid == 0) {
     for (int s = 0; s < 2 * kStages; ++s) mbar_init(smem_u32(&bars[s]), 1);
+    // item-ready: the preparer's arrive.expect_tx (query-table bytes) + its
+    // arrive after the page list is written; item-free: one per consumer warp
+    for (int s = 0; s < 2; ++s) mbar_init(ifull_bar(s), 2);
+    for (int s = 0; s < 2; ++s) mbar_init(iempty_bar(s), kConsumerWarps);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    misc[0] = 0;
   }
   __syncthreads();
-
-  // ---- compact the split's valid pages (order preserving) + page-scale scalars
-  const int32_t* table = p.pt + b * p.pt_sb + hk * p.pt_sh;
-  for (int base = lo; base < hi; base += kThreads) {
-    const int j = base + tid;
-    int pid = -1, fmt = IAK_FMT_SKIP;
-    if (j < hi) {
-      pid = table[j];
-      if (pid >= 0 && pid < p.num_pages) fmt = page_format(p, pid);
-    }
-    const bool valid = fmt != IAK_FMT_SKIP && fmt != IAK_FMT_SPARSE;
-    const unsigned bal = __ballot_sync(0xffffffffu, valid);
-    if (lane == 0) misc[8 + warp] = __popc(bal);
-    __syncthreads();
-    int off = misc[0];
-    for (int w = 0; w < warp; ++w) off += misc[8 + w];
-    if (valid) {
-      const int idx = off + __popc(bal & ((1u << lane) - 1u));
-      pid_s[idx] = pid;
-      fmt_s[idx] = static_cast<uint8_t>(fmt);
-      if (!GROUP) {
-        const bool q = fmt != IAK_FMT_F16;
-        scal_s[idx] = q ? p.k_scale[pid] : 1.f;
-        scal_s[kChunkMax + idx] = q ? p.v_scale[pid] : 1.f;
-        scal_s[2 * kChunkMax + idx] = fmt == IAK_FMT_INT4R ? p.k_rscale[pid] : 0.f;
-        scal_s[3 * kChunkMax + idx] = fmt == IAK_FMT_INT4R ? p.v_rscale[pid] : 0.f;
-      }
-    }
-    __syncthreads();
-    if (tid == 0) {
-      int tot = misc[0];
-      for (int w = 0; w < kConsumerWarps + 1; ++w) tot += misc[8 + w];
-      misc[0] = tot;
-    }
-    __syncthreads();
-  }
-  const int n_valid = misc[0];
-
   bool timed_out = false;
-  const float qk_log2 = p.sm_scale * 1.4426950408889634f;
-  // per-lane running state: query columns g = 2c, 2c+1
-  float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
-  float oacc[KT][4];
-#pragma unroll
-  for (int mt = 0; mt < KT; ++mt) oacc[mt][0] = oacc[mt][1] = oacc[mt][2] = oacc[mt][3] = 0.f;
-  const int r = lane >> 2, c = lane & 3;
 
-  if (warp == kConsumerWarps) {
-    // ------------------------------------------------------------ producer
-    if (lane == 0) {
-      for (int i = 0; i < n_valid; ++i) {
-        const int s = i & (kStages - 1), round = i / kStages;
-        const uint32_t full = smem_u32(&bars[s]), empty = smem_u32(&bars[kStages + s]);
-        if (round > 0 && !mbar_wait(empty, (round - 1) & 1)) {
-          timed_out = true;
-          break;
-        }
-        const int fmt = fmt_s[i];
-        const int pid = pid_s[i];
-        const uint32_t st = smem_u32(smem + s * kStageBytes);
-        uint32_t bytes;
-        if (fmt == IAK_FMT_F16) bytes = 2 * kPS * D * 2;
-        else if (fmt == IAK_FMT_INT4) bytes = 2 * kPS * D / 2;
-        else bytes = 2 * kPS * D;   // FP8, INT8, INT4R (two half-size planes)
-        const bool gs = GROUP && fmt != IAK_FMT_F16;
-        if (gs) bytes += (fmt == IAK_FMT_INT4R ? 4 : 2) * NG * 4;
-        mbar_arrive_expect_tx(full, bytes);
-        const int y16 = pid * kPS;  // first token row of the page
-        if (fmt == IAK_FMT_F16) {
-          tma_load_2d(st, &maps.m[M_KF16], 0, y16, full);
-          tma_load_2d(st + kVOff, &maps.m[M_VF16], 0, y16, full);
-          if constexpr (D == 128) {
-            tma_load_2d(st + 2048, &maps.m[M_KF16], 64, y16, full);
-            tma_load_2d(st + kVOff + 2048, &maps.m[M_VF16], 64, y16, full);
-          }
-        } else if (fmt == IAK_FMT_FP8 || fmt == IAK_FMT_INT8) {
-          const int y = pid * (kPS * D / 128);   // 128-byte lines of 8-bit token rows
-          const int mk = fmt == IAK_FMT_FP8 ? M_KFP8 : M_KI8;
-          tma_load_2d(st, &maps.m[mk], 0, y, full);
-          tma_load_2d(st + kVOff, &maps.m[mk + 1], 0, y, full);
-        } else {
-          const int y = pid * (kPS * D / 256);   // 128-byte lines of packed int4 token rows
-          tma_load_2d(st, &maps.m[M_KI4], 0, y, full);
-          tma_load_2d(st + kVOff, &maps.m[M_VI4], 0, y, full);
-          if (fmt == IAK_FMT_INT4R) {
-            tma_load_2d(st + kResOff, &maps.m[M_KI4R], 0, y, full);
-            tma_load_2d(st + kVOff + kResOff, &maps.m[M_VI4R], 0, y, full);
-          }
-        }
-        if (gs) {
-          bulk_load(st + kScaleOff, p.k_scale + static_cast<int64_t>(pid) * NG, NG * 4, full);
-          bulk_load(st + kScaleOff + 16 * 4, p.v_scale + static_cast<int64_t>(pid) * NG, NG * 4, full);
-          if (fmt == IAK_FMT_INT4R) {
-            bulk_load(st + kScaleOff + 32 * 4, p.k_rscale + static_cast<int64_t>(pid) * NG, NG * 4, full);
-            bulk_load(st + kScaleOff + 48 * 4, p.v_rscale + static_cast<int64_t>(pid) * NG, NG * 4, full);
-          }
-        }
-      }
-    }
-  } else {
-    // ------------------------------------------------------------ consumers
-    // Q^T B fragments (row n = r is query head g = r), both channel orders
-    uint32_t qstd[KT][2], qperm[KT][2];
-    {
-      const bool live = r < p.G;
-      const int64_t qoff = static_cast<int64_t>(b) * p.q_sb + static_cast<int64_t>(hk * p.G + (live ? r : 0)) * p.q_sh;
-#pragma unroll
-      for (int kk = 0; kk < KT; ++kk) {
-        float v[8];
-        const int ds[8] = {16 * kk + 2 * c, 16 * kk + 2 * c + 1, 16 * kk + 2 * c + 8, 16 * kk + 2 * c + 9,
-                           16 * kk + 4 * c, 16 * kk + 4 * c + 1, 16 * kk + 4 * c + 2, 16 * kk + 4 * c + 3};
-#pragma unroll
-        for (int e = 0; e < 8; ++e) v[e] = live ? load_as_float(p.q, p.q_dtype, qoff + ds[e]) : 0.f;
-        qstd[kk][0] = pack_f16x2(v[0], v[1]); qstd[kk][1] = pack_f16x2(v[2], v[3]);
-        qperm[kk][0] = pack_f16x2(v[4], v[5]); qperm[kk][1] = pack_f16x2(v[6], v[7]);
-      }
-    }
-    for (int i = warp; i < n_valid; i += kConsumerWarps) {
-      const int s = i & (kStages - 1), round = i / kStages;
-      if (!mbar_wait(smem_u32(&bars[s]), round & 1)) {
+  if (warp == kPrepWarp) {
+    // -------------------------------------------------------------- preparer
+    constexpr int kPer = kChunkMax / 32;
+    for (int k = 0, item = blockIdx.x; item < n_items; ++k, item += gridDim.x) {
+      const int buf = k & 1;
+      char* ib = item_buf(buf);
+      if (k >= 2 && !mbar_wait(iempty_bar(buf), ((k >> 1) - 1) & 1)) {
         timed_out = true;
         break;
       }
+      int unit, split, lo, hi;
+      item_range(p, item, unit, split, lo, hi);
+      if (lane == 0) {
+        mbar_arrive_expect_tx(ifull_bar(buf), kQTab);
+        bulk_load(smem_u32(ib + ItemLayout::qtab), qtab + static_cast<int64_t>(unit) * kQTab, kQTab, ifull_bar(buf));
+      }
+      const int bb = unit / p.Ht, hk = unit - bb * p.Ht;
+      const int32_t* table = p.pt + bb * p.pt_sb + hk * p.pt_sh;
+      int32_t* pid_s = reinterpret_cast<int32_t*>(ib + ItemLayout::pid);
+      float* scal_s = reinterpret_cast<float*>(ib + ItemLayout::scal);
+      uint8_t* fmt_s = reinterpret_cast<uint8_t*>(ib + ItemLayout::fmt);
+      // all loads of the item first (three dependent rounds), then compaction
+      int pids[kPer], fmts[kPer];
+#pragma unroll
+      for (int t = 0; t < kPer; ++t) {
+        const int j = lo + 32 * t + lane;
+        pids[t] = j < hi ? table[j] : -1;
+      }
+#pragma unroll
+      for (int t = 0; t < kPer; ++t)
+        fmts[t] = (pids[t] >= 0 && pids[t] < p.num_pages) ? page_format(p, pids[t]) : IAK_FMT_SKIP;
+      int n = 0;
+#pragma unroll
+      for (int t = 0; t < kPer; ++t) {
+        const int fmt = fmts[t], pid = pids[t];
+        const bool valid = fmt != IAK_FMT_SKIP && fmt != IAK_FMT_SPARSE;
+        const unsigned bal = __ballot_sync(0xffffffffu, valid);
+        if (valid) {
+          const int idx = n + __popc(bal & ((1u << lane) - 1u));
+          pid_s[idx] = pid;
+          fmt_s[idx] = static_cast<uint8_t>(fmt);
+          if (!GROUP) {
+            const bool q = fmt != IAK_FMT_F16;
+            scal_s[idx] = q ? p.k_scale[pid] : 1.f;
+            scal_s[kChunkMax + idx] = q ? p.v_scale[pid] : 1.f;
+            scal_s[2 * kChunkMax + idx] = fmt == IAK_FMT_INT4R ? p.k_rscale[pid] : 0.f;
+            scal_s[3 * kChunkMax + idx] = fmt == IAK_FMT_INT4R ? p.v_rscale[pid] : 0.f;
+          }
+        }
+        n += __popc(bal);
+      }
+      if (lane == 0) {
+        int* meta = reinterpret_cast<int*>(ib + ItemLayout::meta);
+        meta[0] = n;
+        meta[1] = unit;
+        meta[2] = split;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(ifull_bar(buf));
+    }
+  } else if (warp == kTmaWarp) {
+    // -------------------------------------------------------------- TMA producer
+    int ctr = 0;   // pages issued before the current item
+    for (int k = 0, item = blockIdx.x; item < n_items && !timed_out; ++k, item += gridDim.x) {
+      const int buf = k & 1;
+      const char* ib = item_buf(buf);
+      if (!mbar_wait(ifull_bar(buf), (k >> 1) & 1)) {
+        timed_out = true;
+        break;
+      }
+      const int n = reinterpret_cast<const int*>(ib + ItemLayout::meta)[0];
+      const int n_pad = (n + kStages - 1) & ~(kStages - 1);
+      const int32_t* pid_s = reinterpret_cast<const int32_t*>(ib + ItemLayout::pid);
+      const uint8_t* fmt_s = reinterpret_cast<const uint8_t*>(ib + ItemLayout::fmt);
+      if (lane < kProducerLanes) {
+        for (int i = lane; i < n_pad; i += kProducerLanes) {
+          const int gi = ctr + i;
+          const int s = gi & (kStages - 1), round = gi / kStages;
+          const uint32_t full = full_bar(s);
+          if (round > 0 && !mbar_wait(empty_bar(s), (round - 1) & 1)) {
+            timed_out = true;
+            break;
+          }
+          if (i >= n) {            // padding slot: completes the stage's phase without data
+            mbar_arrive(full);
+            continue;
+          }
+          const int fmt = fmt_s[i], pid = pid_s[i];
+          const uint32_t st = smem_u32(smem + s * kStageBytes);
+          uint32_t bytes;
+          if (fmt == IAK_FMT_F16) bytes = 2 * kPS * D * 2;
+          else if (fmt == IAK_FMT_INT4) bytes = 2 * kPS * D / 2;
+          else bytes = 2 * kPS * D;   // FP8, INT8, INT4R (two half-size planes)
+          if (GROUP && fmt != IAK_FMT_F16) bytes += (fmt == IAK_FMT_INT4R ? 4 : 2) * NG * 4;
+          mbar_arrive_expect_tx(full, bytes);
+          if (fmt == IAK_FMT_F16) {
+            if constexpr (D == 128 && kF16OneBox) {
+              tma_load_2d(st, &maps.m[M_KF16], 0, pid * kPS * 2, full);
+              tma_load_2d(st + kVOff, &maps.m[M_VF16], 0, pid * kPS * 2, full);
+            } else {
+              tma_load_2d(st, &maps.m[M_KF16], 0, pid * kPS, full);
+              tma_load_2d(st + kVOff, &maps.m[M_VF16], 0, pid * kPS, full);
+              if constexpr (D == 128) {
+                tma_load_2d(st + 2048, &maps.m[M_KF16], 64, pid * kPS, full);
+                tma_load_2d(st + kVOff + 2048, &maps.m[M_VF16], 64, pid * kPS, full);
+              }
+            }
+          } else if (fmt == IAK_FMT_FP8 || fmt == IAK_FMT_INT8) {
+            const int y = pid * (kPS * D / 128);   // 128-byte lines of 8-bit token rows
+            const int mk = fmt == IAK_FMT_FP8 ? M_KFP8 : M_KI8;
+            tma_load_2d(st, &maps.m[mk], 0, y, full);
+            tma_load_2d(st + kVOff, &maps.m[mk + 1], 0, y, full);
+          } else {
+            const int y = pid * (kPS * D / 256);   // 128-byte lines of packed int4 token rows
+            tma_load_2d(st, &maps.m[M_KI4], 0, y, full);
+            tma_load_2d(st + kVOff, &maps.m[M_VI4], 0, y, full);
+            if (fmt == IAK_FMT_INT4R) {
+              tma_load_2d(st + kResOff, &maps.m[M_KI4R], 0, y, full);
+              tma_load_2d(st + kVOff + kResOff, &maps.m[M_VI4R], 0, y, full);
+            }
+          }
+          if (GROUP && fmt != IAK_FMT_F16) {
+            bulk_load(st + kScaleOff, p.k_scale + static_cast<int64_t>(pid) * NG, NG * 4, full);
+            bulk_load(st + kScaleOff + 16 * 4, p.v_scale + static_cast<int64_t>(pid) * NG, NG * 4, full);
+            if (fmt == IAK_FMT_INT4R) {
+              bulk_load(st + kScaleOff + 32 * 4, p.k_rscale + static_cast<int64_t>(pid) * NG, NG * 4, full);
+              bulk_load(st + kScaleOff + 48 * 4, p.v_rscale + static_cast<int64_t>(pid) * NG, NG * 4, full);
+            }
+          }
+        }
+      }
+      __syncwarp();
+      ctr += n_pad;
+    }
+  } else {
+    // -------------------------------------------------------------- consumers
+    const float qk_log2 = p.sm_scale * 1.4426950408889634f;
+    const int S = p.num_splits * kConsumerWarps;   // partial slots per query row
+    int ctr = 0;
+    for (int k = 0, item = blockIdx.x; item < n_items; ++k, item += gridDim.x) {
+      const int buf = k & 1;
+      const char* ib = item_buf(buf);
+      if (!mbar_wait(ifull_bar(buf), (k >> 1) & 1)) {
+        timed_out = true;
+        break;
+      }
+      const int* meta = reinterpret_cast<const int*>(ib + ItemLayout::meta);
+      const int n_valid = meta[0], unit = meta[1], split = meta[2];
+      const float* scal_s = reinterpret_cast<const float*>(ib + ItemLayout::scal);
+      const uint8_t* fmt_s = reinterpret_cast<const uint8_t*>(ib + ItemLayout::fmt);
+      const uint4* qfrag = reinterpret_cast<const uint4*>(ib + kQFrag);
+      const uint4* qi8 = reinterpret_cast<const uint4*>(ib + kQI8);
+      const uint4* qi4 = reinterpret_cast<const uint4*>(ib + kQI4);
+      const float* qsc = reinterpret_cast<const float*>(ib + kQSc);
+      float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
+      float oacc[KT][4];
+#pragma unroll
+      for (int mt = 0; mt < KT; ++mt) oacc[mt][0] = oacc[mt][1] = oacc[mt][2] = oacc[mt][3] = 0.f;
+      // Every item occupies a multiple of kStages ring slots (the tail is
+      // padding), so stage s is always filled by TMA lane s % kProducerLanes and
+      // drained by consumer warp s % kConsumerWarps, one phase at a time: a
+      // parity wait can never be two phases ahead of its barrier.
+      const int n_pad = (n_valid + kStages - 1) & ~(kStages - 1);
+      for (int i = warp; i < n_pad; i += kConsumerWarps) {
+        const int gi = ctr + i;
+        const int s = gi & (kStages - 1), round = gi / kStages;
+        if (!mbar_wait(full_bar(s), round & 1)) {
+          timed_out = true;
+          break;
+        }
+        if (i >= n_valid) {
+          __syncwarp();
+          if (lane == 0) mbar_arrive(empty_bar(s));
+          continue;
+        }
       const char* st = smem + s * kStageBytes;
       const uint32_t st_u32 = smem_u32(st);
       const int fmt = fmt_s[i];
       const float* gsc = reinterpret_cast<const float*>(st + kScaleOff);
       // ---------------- S^T = K Q^T
-      float sacc[NG][4], racc[NG][4];
+      // accumulator of k-step kk: its 32-channel group (group scales) or its
+      // parity (two independent MMA chains per page)
+      constexpr int NA = GROUP ? NG : 2;
+      float sacc[NA][4];
 #pragma unroll
-      for (int g = 0; g < NG; ++g)
+      for (int g = 0; g < NA; ++g)
 #pragma unroll
-        for (int e = 0; e < 4; ++e) sacc[g][e] = racc[g][e] = 0.f;
+        for (int e = 0; e < 4; ++e) sacc[g][e] = 0.f;
       if (fmt == IAK_FMT_F16) {
 #pragma unroll
         for (int kk = 0; kk < KT; ++kk) {
           uint32_t a[4];
           k_frag_f16<D>(st_u32, lane, kk, a);
-          mma16816(sacc[GROUP ? kk / 2 : 0], a[0], a[1], a[2], a[3], qstd[kk][0], qstd[kk][1]);
+          const uint4 qf = qfrag[kk * 32 + lane];
+          mma16816(sacc[GROUP ? kk / 2 : (kk & 1)], a[0], a[1], a[2], a[3], qf.x, qf.y);
         }
-      } else if (fmt == IAK_FMT_FP8 || fmt == IAK_FMT_INT8) {
-        const bool fp8 = fmt == IAK_FMT_FP8;
+      } else if (fmt == IAK_FMT_FP8) {
 #pragma unroll
-        for (int kk = 0; kk < KT; ++kk) {
-          uint32_t a[4];
-          k_frag_8bit<D>(st, r, c, kk, fp8, a);
-          mma16816(sacc[GROUP ? kk / 2 : 0], a[0], a[1], a[2], a[3], qperm[kk][0], qperm[kk][1]);
-        }
-      } else {
+        for (int kk = 0; kk < KT; kk += 2) {
+          uint32_t x[4];
+          ldsm_rows(st_u32, D, lane, kk, x);
 #pragma unroll
-        for (int pp = 0; pp < KT / 2; ++pp) {
-          uint32_t a[2][4];
-          k_frag_int4<D>(st, r, c, pp, a);
-          mma16816(sacc[GROUP ? pp : 0], a[0][0], a[0][1], a[0][2], a[0][3], qperm[2 * pp][0], qperm[2 * pp][1]);
-          mma16816(sacc[GROUP ? pp : 0], a[1][0], a[1][1], a[1][2], a[1][3], qperm[2 * pp + 1][0],
-                   qperm[2 * pp + 1][1]);
-          if (fmt == IAK_FMT_INT4R) {
-            k_frag_int4<D>(st + kResOff, r, c, pp, a);
-            mma16816(racc[GROUP ? pp : 0], a[0][0], a[0][1], a[0][2], a[0][3], qperm[2 * pp][0], qperm[2 * pp][1]);
-            mma16816(racc[GROUP ? pp : 0], a[1][0], a[1][1], a[1][2], a[1][3], qperm[2 * pp + 1][0],
-                     qperm[2 * pp + 1][1]);
+          for (int h = 0; h < 2; ++h) {
+            uint32_t a[4];
+            k_frag_8bit_from(x[2 * h], x[2 * h + 1], true, a);
+            const uint4 qf = qfrag[(kk + h) * 32 + lane];
+            mma16816(sacc[GROUP ? (kk + h) / 2 : h], a[0], a[1], a[2], a[3], qf.z, qf.w);
           }
         }
       }
-      // ---------------- scale + online softmax (log2 domain)
-      float sc[4];
-      if (!GROUP) {
-        const float ks = scal_s[i], krs = scal_s[2 * kChunkMax + i];
+      // ---------------- scores (times the K scale; INT8 / INT4 on the integer tensor path)
+      float sc[4] = {0.f, 0.f, 0.f, 0.f};
+      const float s1a = qsc[2 * c], s1b = qsc[2 * c + 1], s2a = qsc[8 + 2 * c], s2b = qsc[8 + 2 * c + 1];
+      if (fmt == IAK_FMT_F16 || fmt == IAK_FMT_FP8) {
+        if (!GROUP) {
+          const float ks = scal_s[i];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) sc[e] = (sacc[0][e] * ks + racc[0][e] * krs) * qk_log2;
-      } else {
+          for (int e = 0; e < 4; ++e) sc[e] = (sacc[0][e] + sacc[1][e]) * ks;
+        } else {
+          const bool q = fmt != IAK_FMT_F16;
 #pragma unroll
-        for (int e = 0; e < 4; ++e) sc[e] = 0.f;
-        const bool q = fmt != IAK_FMT_F16;
+          for (int g = 0; g < NA; ++g) {
+            const float ks = q ? gsc[g] : 1.f;
 #pragma unroll
-        for (int g = 0; g < NG; ++g) {
-          const float ks = q ? gsc[g] : 1.f, krs = fmt == IAK_FMT_INT4R ? gsc[32 + g] : 0.f;
-#pragma unroll
-          for (int e = 0; e < 4; ++e) sc[e] += sacc[g][e] * ks + racc[g][e] * krs;
+            for (int e = 0; e < 4; ++e) sc[e] = fmaf(sacc[g][e], ks, sc[e]);
+          }
         }
+      } else if (fmt == IAK_FMT_INT8) {
+        int i1[4] = {0, 0, 0, 0}, i2[4] = {0, 0, 0, 0};
 #pragma unroll
-        for (int e = 0; e < 4; ++e) sc[e] *= qk_log2;
+        for (int j = 0; j < D / 32; ++j) {
+          uint32_t x[4];
+          ldsm_rows(st_u32, D, lane, 2 * j, x);
+          const uint4 qi = qi8[j * 32 + lane];
+          imma_s8(i1, x, qi.x, qi.y);
+          imma_s8(i2, x, qi.z, qi.w);
+          if (GROUP) {
+            const float ks = gsc[j];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              sc[e] = fmaf(ks, fmaf((e & 1) ? s1b : s1a, static_cast<float>(i1[e]),
+                                    ((e & 1) ? s2b : s2a) * static_cast<float>(i2[e])), sc[e]);
+              i1[e] = i2[e] = 0;
+            }
+          }
+        }
+        if (!GROUP) {
+          const float ks = scal_s[i];
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            sc[e] = ks * fmaf((e & 1) ? s1b : s1a, static_cast<float>(i1[e]),
+                              ((e & 1) ? s2b : s2a) * static_cast<float>(i2[e]));
+        }
+      } else {
+        // INT4 / INT4R: nibbles -> bytes (code + 8) on the u8 x s8 path; the +8
+        // offset is removed exactly with the per-group sums of the q terms
+        const int nplanes = fmt == IAK_FMT_INT4R ? 2 : 1;
+        for (int pl = 0; pl < nplanes; ++pl) {
+          int i1[4] = {0, 0, 0, 0}, i2[4] = {0, 0, 0, 0};
+          float bias1a = 0.f, bias1b = 0.f, bias2a = 0.f, bias2b = 0.f;
+#pragma unroll
+          for (int jj = 0; jj < D / 64; ++jj) {
+            uint32_t x[4];
+            ldsm_rows(st_u32 + pl * kResOff, D / 2, lane, 2 * jj, x);
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const int j = 2 * jj + h;
+              const uint32_t a[4] = {x[2 * h] & 0x0F0F0F0Fu, x[2 * h + 1] & 0x0F0F0F0Fu,
+                                     (x[2 * h] >> 4) & 0x0F0F0F0Fu, (x[2 * h + 1] >> 4) & 0x0F0F0F0Fu};
+              const uint4 qi = qi4[j * 32 + lane];
+              imma_u8(i1, a, qi.x, qi.y);
+              imma_u8(i2, a, qi.z, qi.w);
+              const float b1a = qsc[16 + j * 8 + 2 * c], b1b = qsc[16 + j * 8 + 2 * c + 1];
+              const float b2a = qsc[48 + j * 8 + 2 * c], b2b = qsc[48 + j * 8 + 2 * c + 1];
+              if (GROUP) {
+                const float ks = gsc[32 * pl + j];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  const float t1 = static_cast<float>(i1[e]) - 8.f * ((e & 1) ? b1b : b1a);
+                  const float t2 = static_cast<float>(i2[e]) - 8.f * ((e & 1) ? b2b : b2a);
+                  sc[e] = fmaf(ks, fmaf((e & 1) ? s1b : s1a, t1, ((e & 1) ? s2b : s2a) * t2), sc[e]);
+                  i1[e] = i2[e] = 0;
+                }
+              } else {
+                bias1a += b1a; bias1b += b1b; bias2a += b2a; bias2b += b2b;
+              }
+            }
+          }
+          if (!GROUP) {
+            const float ks = scal_s[(pl == 0 ? 0 : 2) * kChunkMax + i];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float t1 = static_cast<float>(i1[e]) - 8.f * ((e & 1) ? bias1b : bias1a);
+              const float t2 = static_cast<float>(i2[e]) - 8.f * ((e & 1) ? bias2b : bias2a);
+              sc[e] = fmaf(ks, fmaf((e & 1) ? s1b : s1a, t1, ((e & 1) ? s2b : s2a) * t2), sc[e]);
+            }
+          }
+        }
       }
+#pragma unroll
+      for (int e = 0; e < 4; ++e) sc[e] *= qk_log2;
+      // ---------------- online softmax (log2 domain)
       float pm0 = fmaxf(sc[0], sc[2]), pm1 = fmaxf(sc[1], sc[3]);
 #pragma unroll
       for (int off = 4; off < 32; off <<= 1) {
         pm0 = fmaxf(pm0, __shfl_xor_sync(0xffffffffu, pm0, off));
         pm1 = fmaxf(pm1, __shfl_xor_sync(0xffffffffu, pm1, off));
       }
-      const float mn0 = fmaxf(m_run[0], pm0), mn1 = fmaxf(m_run[1], pm1);
-      const float al0 = exp2f(m_run[0] - mn0), al1 = exp2f(m_run[1] - mn1);
-      m_run[0] = mn0; m_run[1] = mn1;
-      const float p0 = exp2f(sc[0] - mn0), p1 = exp2f(sc[1] - mn1);
-      const float p2 = exp2f(sc[2] - mn0), p3 = exp2f(sc[3] - mn1);
-      l_run[0] = l_run[0] * al0 + p0 + p2;
-      l_run[1] = l_run[1] * al1 + p1 + p3;
+      // Lazy rescaling: the running max only moves (and O, l are rescaled)
+      // when some query's page max exceeds it by more than kLazyLog2; until
+      // then p <= 2^kLazyLog2, far inside fp16 / fp32 range.  Warp-uniform.
+      if (__any_sync(0xffffffffu, pm0 > m_run[0] + kLazyLog2 || pm1 > m_run[1] + kLazyLog2)) {
+        const float mn0 = fmaxf(m_run[0], pm0), mn1 = fmaxf(m_run[1], pm1);
+        const float al0 = exp2f(m_run[0] - mn0), al1 = exp2f(m_run[1] - mn1);
+        m_run[0] = mn0; m_run[1] = mn1;
+        l_run[0] *= al0; l_run[1] *= al1;
 #pragma unroll
-      for (int mt = 0; mt < KT; ++mt) {
-        oacc[mt][0] *= al0; oacc[mt][1] *= al1; oacc[mt][2] *= al0; oacc[mt][3] *= al1;
+        for (int mt = 0; mt < KT; ++mt) {
+          oacc[mt][0] *= al0; oacc[mt][1] *= al1; oacc[mt][2] *= al0; oacc[mt][3] *= al1;
+        }
       }
+      const float p0 = exp2f(sc[0] - m_run[0]), p1 = exp2f(sc[1] - m_run[1]);
+      const float p2 = exp2f(sc[2] - m_run[0]), p3 = exp2f(sc[3] - m_run[1]);
+      l_run[0] += p0 + p2;
+      l_run[1] += p1 + p3;
       // ---------------- O^T += V^T P^T
       uint32_t vh[2][D / 64][8];
       if (!GROUP) {
@@ -596,77 +883,41 @@ __global__ void __launch_bounds__(kThreads, 2)
           }
         }
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&bars[kStages + s]));
-    }
-    // full l per query column: sum the 8 lanes that share c
+        __syncwarp();
+        if (lane == 0) mbar_arrive(empty_bar(s));
+      }
+      // ---- this warp's partial of the item
 #pragma unroll
-    for (int off = 4; off < 32; off <<= 1) {
-      l_run[0] += __shfl_xor_sync(0xffffffffu, l_run[0], off);
-      l_run[1] += __shfl_xor_sync(0xffffffffu, l_run[1], off);
+      for (int off = 4; off < 32; off <<= 1) {
+        l_run[0] += __shfl_xor_sync(0xffffffffu, l_run[0], off);
+        l_run[1] += __shfl_xor_sync(0xffffffffu, l_run[1], off);
+      }
+      const int bb = unit / p.Ht, hk = unit - bb * p.Ht;
+      const int slot = split * kConsumerWarps + warp;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int g = 2 * c + h;
+        if (g < p.G) {
+          const int64_t row = static_cast<int64_t>(bb) * p.Hq + hk * p.G + g;
+          const int64_t wi = row * S + slot;
+          if (r == 0) {
+            p.ws_m[wi] = l_run[h] > 0.f ? m_run[h] * 0.6931471805599453f : -INFINITY;  // natural-log max
+            p.ws_l[wi] = l_run[h];
+          }
+          float* acc = p.ws_acc + wi * D;
+#pragma unroll
+          for (int mt = 0; mt < KT; ++mt) {
+            acc[pv_channel<D>(mt, r)] = oacc[mt][h];
+            acc[pv_channel<D>(mt, r + 8)] = oacc[mt][2 + h];
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(iempty_bar(buf));
+      ctr += n_pad;
     }
   }
   if (timed_out) atomicAdd(&g_decode_timeouts, 1u);
-  __syncthreads();  // every stage consumed: the ring is free for the epilogue
-
-  // ---------------------------------------------------------------- epilogue
-  float* red_m = reinterpret_cast<float*>(smem);          // [4][8]
-  float* red_l = red_m + 32;                               // [4][8]
-  float* red_o = red_m + 64;                               // [4][8][D]
-  if (warp < kConsumerWarps) {
-    if (r == 0) {
-      red_m[warp * 8 + 2 * c] = m_run[0]; red_m[warp * 8 + 2 * c + 1] = m_run[1];
-      red_l[warp * 8 + 2 * c] = l_run[0]; red_l[warp * 8 + 2 * c + 1] = l_run[1];
-    }
-#pragma unroll
-    for (int mt = 0; mt < KT; ++mt) {
-      const int d0 = pv_channel<D>(mt, r), d1 = pv_channel<D>(mt, r + 8);
-      float* o0 = red_o + (warp * 8 + 2 * c) * D;
-      float* o1 = o0 + D;
-      o0[d0] = oacc[mt][0]; o1[d0] = oacc[mt][1];
-      o0[d1] = oacc[mt][2]; o1[d1] = oacc[mt][3];
-    }
-  }
-  __syncthreads();
-  const int G = p.G;
-  for (int idx = tid; idx < G * D; idx += kThreads) {
-    const int g = idx / D, d = idx % D;
-    float M = -INFINITY;
-#pragma unroll
-    for (int w = 0; w < kConsumerWarps; ++w)
-      if (red_l[w * 8 + g] > 0.f) M = fmaxf(M, red_m[w * 8 + g]);
-    float L = 0.f, A = 0.f;
-    if (M != -INFINITY) {
-#pragma unroll
-      for (int w = 0; w < kConsumerWarps; ++w) {
-        const float lw = red_l[w * 8 + g];
-        if (lw > 0.f) {
-          const float e = exp2f(red_m[w * 8 + g] - M);
-          L += lw * e;
-          A += red_o[(w * 8 + g) * D + d] * e;
-        }
-      }
-    }
-    const float Mn = M * 0.6931471805599453f;  // partials carry the natural-log max
-    const int hq = hk * G + g;
-    const int64_t row = static_cast<int64_t>(b) * p.Hq + hq;
-    if (p.num_splits > 1) {
-      const int64_t wi = row * p.num_splits + split;
-      if (d == 0) {
-        p.ws_m[wi] = Mn;
-        p.ws_l[wi] = L;
-      }
-      p.ws_acc[wi * D + d] = A;
-    } else if (p.ex_l) {
-      if (d == 0) {
-        p.ex_m[row] = Mn;
-        p.ex_l[row] = L;
-      }
-      p.ex_acc[row * D + d] = A;
-    } else {
-      store_from_float(p.out, p.out_dtype, b * p.o_sb + hq * p.o_sh + d, L > 0.f ? A / L : 0.f);
-    }
-  }
 }
 
 // --------------------------------------------------------- tensor maps ---
@@ -717,7 +968,10 @@ int cached_map(CUtensorMap* out, const void* base, int kind, int D, int64_t num_
   CUtensorMapDataType dt = CU_TENSOR_MAP_DATA_TYPE_UINT8;
   int eb = 1;
   const uint64_t tokens = static_cast<uint64_t>(num_pages) * kPS;
-  if (kind == 0) {
+  if (kind == 0 && D == 128 && kF16OneBox) {
+    // 256-byte token rows viewed as two 128-byte half-rows; one box = one page
+    dt = CU_TENSOR_MAP_DATA_TYPE_FLOAT16; eb = 2; inner = 64; rows = tokens * 2; box_rows = 2 * kPS;
+  } else if (kind == 0) {
     dt = CU_TENSOR_MAP_DATA_TYPE_FLOAT16; eb = 2; inner = D; rows = tokens; box_rows = kPS;
   } else {
     const uint64_t row_bytes = kind == 1 ? D : D / 2;      // bytes per token row
@@ -744,18 +998,32 @@ int cached_map(CUtensorMap* out, const void* base, int kind, int D, int64_t num_
 
 }  // namespace
 
-bool mma_path_eligible(const DecodeParams& p) {
+bool mma_shape_eligible(const DecodeParams& p) {
   if (p.PS != kPS || (p.D != 64 && p.D != 128)) return false;
   if (p.q_dtype != IAK_DT_F16 && p.q_dtype != IAK_DT_BF16) return false;
   if (p.scale_mode == IAK_SCALE_CHANNEL) return false;
   if (p.scale_mode == IAK_SCALE_GROUP32 && p.D != 128) return false;
-  if (p.pages_per_split > kChunkMax) return false;
   return true;
 }
 
-int launch_decode_mma(const DecodeParams& p, const iak_page_pools& P, cudaStream_t s, bool* launched) {
-  *launched = false;
-  if (!mma_path_eligible(p)) return IAK_OK;
+template <int D, bool GROUP>
+static int launch_persistent(const DecodeParams& p, const TmaMaps& maps, int n_items, cudaStream_t s) {
+  const size_t smem = SmemLayout::total + 1024;
+  auto kern = decode_mma_kernel<D, GROUP>;
+  cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (err != cudaSuccess) return check_cuda(err, "decode_mma smem attribute");
+  int per_sm = 0;
+  err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem);
+  if (err != cudaSuccess) return check_cuda(err, "decode_mma occupancy");
+  const int ctas = std::max(1, std::min(n_items, std::max(1, per_sm) * device_sm_count()));
+  decode_prep_kernel<D><<<p.B * p.Ht, 128, 0, s>>>(p, p.ws_qtab);
+  err = cudaGetLastError();
+  if (err != cudaSuccess) return check_cuda(err, "decode_prep launch");
+  kern<<<ctas, kThreads, smem, s>>>(p, maps, p.ws_qtab, n_items);
+  return check_cuda(cudaGetLastError(), "decode_mma launch");
+}
+
+int launch_decode_mma(const DecodeParams& p, const iak_page_pools& P, cudaStream_t s) {
   TmaMaps maps;
   std::memset(&maps, 0, sizeof(maps));
   struct { const void* ptr; int idx; int kind; } pools[] = {
@@ -768,23 +1036,11 @@ int launch_decode_mma(const DecodeParams& p, const iak_page_pools& P, cudaStream
     int st = cached_map(&maps.m[e.idx], e.ptr, e.kind, p.D, P.num_pages);
     if (st) return st;
   }
-  const size_t smem = SmemLayout::total + 1024;
-  const int units = p.B * p.Ht;
-  dim3 grid(p.num_splits, units);
-  cudaError_t err;
-  if (p.D == 128 && p.scale_mode == IAK_SCALE_GROUP32) {
-    err = cudaFuncSetAttribute(decode_mma_kernel<128, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (err == cudaSuccess) decode_mma_kernel<128, true><<<grid, kThreads, smem, s>>>(p, maps);
-  } else if (p.D == 128) {
-    err = cudaFuncSetAttribute(decode_mma_kernel<128, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (err == cudaSuccess) decode_mma_kernel<128, false><<<grid, kThreads, smem, s>>>(p, maps);
-  } else {
-    err = cudaFuncSetAttribute(decode_mma_kernel<64, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (err == cudaSuccess) decode_mma_kernel<64, false><<<grid, kThreads, smem, s>>>(p, maps);
-  }
-  if (err != cudaSuccess) return check_cuda(err, "decode_mma smem attribute");
-  *launched = true;
-  return check_cuda(cudaGetLastError(), "decode_mma launch");
+  if (!p.ws_qtab) return fail(IAK_ERR_WORKSPACE, "tensor-core decode needs a workspace");
+  const int n_items = p.B * p.Ht * p.num_splits;
+  if (p.D == 128 && p.scale_mode == IAK_SCALE_GROUP32) return launch_persistent<128, true>(p, maps, n_items, s);
+  if (p.D == 128) return launch_persistent<128, false>(p, maps, n_items, s);
+  return launch_persistent<64, false>(p, maps, n_items, s);
 }
 
 }  // namespace iak

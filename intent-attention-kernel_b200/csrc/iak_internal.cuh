@@ -41,7 +41,10 @@ struct DecodeParams {
   uint8_t tag_map[16]; uint8_t tag_default;
   float sm_scale;
   int num_splits, pages_per_split;
-  int kernel;  // IAK_KERNEL_*
+  int kernel;    // IAK_KERNEL_*
+  int tensor;    // 1: the tensor-core path runs (per-warp partial slots, query tables)
+  int ws_slots;  // partial slots per query row in the workspace
+  char* ws_qtab; // per-unit query tables (tensor path)
   // split partials, [unit][split][g] and [unit][split][g][D]
   float* ws_m; float* ws_l; float* ws_acc;
   // optional export of final per-row partials (rows = B*Hq)
@@ -50,8 +53,11 @@ struct DecodeParams {
 
 // Launchers (return IAK_OK or a status; errors recorded with set_error).
 int launch_decode_generic(const DecodeParams& p, cudaStream_t s);
-int launch_decode_mma(const DecodeParams& p, const iak_page_pools& pools, cudaStream_t s, bool* launched);
-bool mma_path_eligible(const DecodeParams& p);
+int launch_decode_mma(const DecodeParams& p, const iak_page_pools& pools, cudaStream_t s);
+bool mma_shape_eligible(const DecodeParams& p);
+constexpr int kQueryTableBytes = 8704;   // per-unit query table of the tensor path
+constexpr int kTensorItemSlots = 256;    // max table slots per tensor-path work item
+constexpr int kTensorConsumerWarps = 4;  // partial slots per work item
 int launch_merge(const float* m, const float* l, const float* acc, int64_t rows, int splits, int D,
                  void* out, int out_dtype, int64_t out_row_stride,
                  const DecodeParams* rowmap, float* ex_m, float* ex_l, float* ex_acc, cudaStream_t s);

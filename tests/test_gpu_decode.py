@@ -146,6 +146,16 @@ def test_decode_first_slot_skip_does_not_poison():
     _close(run_gpu(case), ref)
 
 
+@pytest.mark.parametrize("splits", [7, 0])
+def test_persistent_items_of_ragged_sizes(splits):
+    """Several work items per CTA whose page counts are not multiples of the
+    stage ring (ragged counts, -1 slots, SKIP pages): the ring phases must stay
+    aligned across item boundaries."""
+    case = make_case(4321, B=16, Hq=32, Ht=8, D=128, W=150, NP=2000, counts="ragged", pad_frac=0.07,
+                     skip_frac=0.05)
+    _close(run_gpu(case, num_splits=splits, kernel="tensor"), run_oracle(case))
+
+
 def test_decode_large_width_many_splits():
     case = make_case(29, B=1, Hq=4, Ht=1, W=2000, NP=2400, counts="full", pad_frac=0.0)
     _close(run_gpu(case), run_oracle(case))
