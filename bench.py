@@ -225,7 +225,26 @@ class ClockSampler:
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = sorted({names[i] for r in self.rows if len(r) > 8 for i in range(4) if r[5 + i] == "Active"})
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(self.rows)}
+                "reasons": reasons, "samples": len(self.rows),
+                "window": "nvidia-smi every 100 ms over the load window ending with the timed region"}
+
+
+# DRAM bytes (read + write) of one decode_mma_kernel launch from an ncu capture of a
+# smaller batch of the same workload (profiles/decode_mma_c2_b4.md), and the units
+# (sequences) that capture processed.  Traffic grows in proportion to the sequences
+# decoded, so it is scaled to the benched batch.
+NCU_TRAFFIC = {"c2": {"bytes": 179_515_392, "batch": 4, "algorithmic": 174_640_384,
+                      "source": "profiles/decode_mma_c2_b4.md"}}
+
+
+def ncu_traffic(workload_name, batch, nbytes):
+    rec = NCU_TRAFFIC.get(workload_name)
+    if rec is None:
+        return None, "null (no ncu capture of this workload)"
+    scaled = rec["bytes"] * batch / rec["batch"]
+    return int(scaled), (f"dram__bytes_read.sum + dram__bytes_write.sum of one launch at batch {rec['batch']} "
+                         f"({rec['source']}), scaled x{batch / rec['batch']:g} to this batch; "
+                         f"{scaled / nbytes:.3f}x the algorithmic bytes")
 
 
 def measured_hbm_peak():
@@ -272,6 +291,7 @@ def build_gpu_workload(w: dict, ids: np.ndarray, fmt: np.ndarray, device, rank: 
 
 
 def run_gpu(args):
+    from intent_attention._native import KernelTimer
     import torch
     import torch.distributed as dist
     from intent_attention import paged_decode
@@ -286,6 +306,8 @@ def run_gpu(args):
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
     w = workload(args.workload)
+    if args.batch:
+        w["B"] = args.batch
     ids, fmt = select_pages(w)
     nbytes = step_bytes(w, fmt)
     pool, table, counts, tags, q = build_gpu_workload(w, ids, fmt, device, rank)
@@ -293,24 +315,34 @@ def run_gpu(args):
     out = torch.empty(q.shape, dtype=torch.bfloat16, device=device)
 
     def step():
-        paged_decode(q, pool, table, counts, tags, tag_map, 0, out=out, num_splits=args.splits)
+        paged_decode(q, pool, table, counts, tags, tag_map, 0, out=out, num_splits=args.splits, kernel="tensor")
 
     step()
     torch.cuda.synchronize(device)
-    for _ in range(args.warmup):
-        step()
-    torch.cuda.synchronize(device)
-    if world > 1:
-        dist.barrier()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks:
-        torch.cuda.synchronize(device)
-        ev0.record()
-        for _ in range(args.steps):
+        # nvidia-smi needs ~0.5 s to start sampling: keep the GPU under the same
+        # load until samples arrive, so the clock record covers the load window
+        # that ends with the timed region
+        t_probe = time.perf_counter()
+        while len(clocks.rows) < 3 and time.perf_counter() - t_probe < 3.0:
+            for _ in range(20):
+                step()
+            torch.cuda.synchronize(device)
+        for _ in range(args.warmup):
             step()
-        ev1.record()
         torch.cuda.synchronize(device)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(device)
+        with KernelTimer(args.steps) as ktimer:
+            ev0.record()
+            for _ in range(args.steps):
+                step()
+            ev1.record()
+            torch.cuda.synchronize(device)
     t_ms = ev0.elapsed_time(ev1) / args.steps
+    kernel_ms = ktimer.total_ms / max(1, ktimer.launches)
     if world > 1:
         t = torch.tensor([t_ms], device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -330,7 +362,8 @@ def run_gpu(args):
         q_dev.copy_(q_host, non_blocking=True)
         table_dev.copy_(table_host, non_blocking=True)
         counts_dev.copy_(counts_host, non_blocking=True)
-        paged_decode(q_dev, pool, table_dev, counts_dev, tags, tag_map, 0, out=out, num_splits=args.splits)
+        paged_decode(q_dev, pool, table_dev, counts_dev, tags, tag_map, 0, out=out, num_splits=args.splits,
+                     kernel="tensor")
         out_host.copy_(out, non_blocking=True)
 
     for _ in range(args.warmup):
@@ -350,13 +383,20 @@ def run_gpu(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_ms = float(t.item())
 
-    from intent_attention import _native as N
-    launches_per_step = 1 + (1 if _num_splits(pool, q, table, counts, tags, tag_map, args.splits) > 1 else 0)
+    # tensor-core path (forced above, so an ineligible shape fails loudly): query-table preparation,
+    # the persistent decode kernel and the LSE merge
+    launches_per_step = 3
+    if world > 1:
+        t = torch.tensor([kernel_ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        kernel_ms = float(t.item())
 
     if rank == 0:
         peak, peak_kind = measured_hbm_peak()
         gbs = nbytes / (t_ms * 1e-3) / 1e9
+        kernel_gbs = nbytes / (kernel_ms * 1e-3) / 1e9
         value = gbs * world
+        traffic, traffic_note = ncu_traffic(args.workload, w["B"], nbytes)
         rec = {
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(t_ms, 5), "us_per_step": round(t_ms * 1e3, 2),
@@ -369,10 +409,14 @@ def run_gpu(args):
                        "selected_kv_bytes_per_step_per_gpu": nbytes,
                        "l2": f"inputs larger than L2 ({nbytes / 1e9:.2f} GB of selected KV per step)",
                        "parallelism": f"dp{world} (batch shards, no collective on the data path)"},
-            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
-                         "frac": round(gbs / peak, 4), "traffic": None,
+            "roofline": {"bound": "hbm", "achieved": round(kernel_gbs, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(kernel_gbs / peak, 4), "traffic": traffic,
+                         "kernel": "decode_mma_kernel", "kernel_us": round(kernel_ms * 1e3, 2),
+                         "step_frac": round(gbs / peak, 4),
                          "note": f"peak = {peak_kind} HBM copy bandwidth; achieved = algorithmic selected-KV bytes "
-                                 "per step / device time of the step (decode + merge launches)"},
+                                 "per launch / average CUDA-event duration of the persistent decode kernel over the "
+                                 "timed region; step_frac uses the whole step (prep + decode + merge); traffic = "
+                                 + traffic_note},
             "e2e": {"value": round(nbytes * world / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
                     "ms_per_step": round(e2e_ms, 5), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "api": "intent_attention.paged_decode with pinned host q / page table / counts in, output out"},
@@ -389,16 +433,6 @@ def run_gpu(args):
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
-
-
-def _num_splits(pool, q, table, counts, tags, tag_map, splits):
-    import ctypes
-    from intent_attention import _native as N
-    from intent_attention.paged import _decode_structs
-    P, A = _decode_structs(q, pool, table, counts, tags, tag_map, 0, None, q, None, splits)
-    nb = ctypes.c_size_t(0)
-    N.check(N.lib().iak_decode_workspace_size(ctypes.byref(P), ctypes.byref(A), ctypes.byref(nb)), "ws")
-    return 2 if nb.value > 0 else 1
 
 
 def run_reference(args):
@@ -437,6 +471,7 @@ def main():
     ap.add_argument("--workload", default="c2", choices=["c1", "c2", "c3", "c5"])
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--splits", type=int, default=0)
+    ap.add_argument("--batch", type=int, default=0, help="override the workload's batch (profiling runs)")
     ap.add_argument("--cpu-budget", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()

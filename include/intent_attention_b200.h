@@ -156,6 +156,17 @@ int iak_decode(const iak_page_pools* pools, const iak_decode_args* args,
 #define IAK_NOALLOC_SCRATCH_BYTES (8 << 20)
 int iak_decode_noalloc(const iak_page_pools* pools, const iak_decode_args* args, void* stream);
 
+/* Kernel timer (measurement only; no counterpart in the reference).  While
+ * enabled, each iak_decode / iak_decode_noalloc call records a CUDA event
+ * pair on the caller's stream around its main decode kernel (not the query
+ * preparation or merge launches), for the first max_launches calls.
+ * iak_kernel_timer_read waits for the recorded events and returns the summed
+ * kernel time and the number of timed launches; iak_kernel_timer_disable
+ * releases the events.  Process-wide; do not enable during stream capture. */
+int iak_kernel_timer_enable(int32_t max_launches);
+int iak_kernel_timer_read(double* total_ms, int32_t* launches);
+int iak_kernel_timer_disable(void);
+
 /* LSE merge of S partials per row: m/l [rows, S], acc [rows, S, D] (fp32,
  * contiguous).  Writes normalised rows to out (dtype, row stride in
  * elements); rows with no contribution become 0. */

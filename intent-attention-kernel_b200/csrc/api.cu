@@ -3,6 +3,8 @@
 #include <cstdarg>
 #include <cstring>
 #include <mutex>
+#include <string>
+#include <vector>
 
 #include "iak_internal.cuh"
 
@@ -46,6 +48,36 @@ int device_sm_count() {
     cache[dev] = n;
   }
   return cache[dev];
+}
+
+// Process-wide kernel timer: event pairs recorded around the main decode launch.
+struct KernelTimer {
+  std::mutex mu;
+  std::vector<cudaEvent_t> start, stop;
+  int used = 0;
+  bool on = false;
+  bool open = false;  // a begin without its end yet
+};
+static KernelTimer g_timer;
+
+void kernel_timer_begin(cudaStream_t s) {
+  std::lock_guard<std::mutex> lock(g_timer.mu);
+  if (!g_timer.on || g_timer.used >= static_cast<int>(g_timer.start.size())) return;
+  if (cudaEventRecord(g_timer.start[g_timer.used], s) == cudaSuccess) g_timer.open = true;
+}
+
+void kernel_timer_end(cudaStream_t s) {
+  std::lock_guard<std::mutex> lock(g_timer.mu);
+  if (!g_timer.open) return;
+  g_timer.open = false;
+  if (cudaEventRecord(g_timer.stop[g_timer.used], s) == cudaSuccess) ++g_timer.used;
+}
+
+static void timer_release_locked() {
+  for (auto e : g_timer.start) cudaEventDestroy(e);
+  for (auto e : g_timer.stop) cudaEventDestroy(e);
+  g_timer.start.clear(); g_timer.stop.clear();
+  g_timer.used = 0; g_timer.on = false; g_timer.open = false;
 }
 
 static bool fmt_reachable(const iak_decode_args* a, int fmt) {
@@ -233,6 +265,47 @@ int iak_decode(const iak_page_pools* pools, const iak_decode_args* args, void* w
                       p.out_dtype, 0, &p, p.ex_m, p.ex_l, p.ex_acc, s);
     if (st) return st;
   }
+  return IAK_OK;
+}
+
+int iak_kernel_timer_enable(int32_t max_launches) {
+  if (max_launches <= 0 || max_launches > (1 << 20)) return fail(IAK_ERR_INVALID_ARG, "max_launches out of range");
+  std::lock_guard<std::mutex> lock(g_timer.mu);
+  timer_release_locked();
+  g_timer.start.resize(max_launches); g_timer.stop.resize(max_launches);
+  for (int i = 0; i < max_launches; ++i) {
+    cudaError_t e0 = cudaEventCreate(&g_timer.start[i]);
+    cudaError_t e1 = cudaEventCreate(&g_timer.stop[i]);
+    if (e0 != cudaSuccess || e1 != cudaSuccess) {
+      g_timer.start.resize(e0 == cudaSuccess ? i + 1 : i);
+      g_timer.stop.resize(e1 == cudaSuccess ? i + 1 : i);
+      timer_release_locked();
+      return check_cuda(e0 != cudaSuccess ? e0 : e1, "kernel timer events");
+    }
+  }
+  g_timer.on = true;
+  return IAK_OK;
+}
+
+int iak_kernel_timer_read(double* total_ms, int32_t* launches) {
+  if (!total_ms || !launches) return fail(IAK_ERR_INVALID_ARG, "null output pointer");
+  std::lock_guard<std::mutex> lock(g_timer.mu);
+  double t = 0.0;
+  for (int i = 0; i < g_timer.used; ++i) {
+    cudaError_t e = cudaEventSynchronize(g_timer.stop[i]);
+    float ms = 0.f;
+    if (e == cudaSuccess) e = cudaEventElapsedTime(&ms, g_timer.start[i], g_timer.stop[i]);
+    if (e != cudaSuccess) return check_cuda(e, "kernel timer read");
+    t += ms;
+  }
+  *total_ms = t;
+  *launches = g_timer.used;
+  return IAK_OK;
+}
+
+int iak_kernel_timer_disable(void) {
+  std::lock_guard<std::mutex> lock(g_timer.mu);
+  timer_release_locked();
   return IAK_OK;
 }
 

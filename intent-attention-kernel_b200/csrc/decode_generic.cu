@@ -276,11 +276,14 @@ int launch_decode_generic(const DecodeParams& p, cudaStream_t s) {
   if (units == 0) return IAK_OK;
   dim3 grid(p.num_splits, units);
   const int dpl = (p.D + 31) / 32;
+  kernel_timer_begin(s);
   if (dpl <= 1) decode_generic_kernel<1><<<grid, kWarps * 32, 0, s>>>(p);
   else if (dpl <= 2) decode_generic_kernel<2><<<grid, kWarps * 32, 0, s>>>(p);
   else if (dpl <= 4) decode_generic_kernel<4><<<grid, kWarps * 32, 0, s>>>(p);
   else decode_generic_kernel<8><<<grid, kWarps * 32, 0, s>>>(p);
-  return check_cuda(cudaGetLastError(), "decode_generic launch");
+  const cudaError_t err = cudaGetLastError();
+  kernel_timer_end(s);
+  return check_cuda(err, "decode_generic launch");
 }
 
 int launch_merge(const float* m, const float* l, const float* acc, int64_t rows, int splits, int D, void* out,

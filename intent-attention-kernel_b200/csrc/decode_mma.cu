@@ -1010,17 +1010,34 @@ template <int D, bool GROUP>
 static int launch_persistent(const DecodeParams& p, const TmaMaps& maps, int n_items, cudaStream_t s) {
   const size_t smem = SmemLayout::total + 1024;
   auto kern = decode_mma_kernel<D, GROUP>;
-  cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-  if (err != cudaSuccess) return check_cuda(err, "decode_mma smem attribute");
+  // the smem attribute and occupancy are per (device, instantiation): look them up once
+  static std::mutex mu;
+  static int per_sm_cache[64] = {0};
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return check_cuda(err, "cudaGetDevice");
   int per_sm = 0;
-  err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem);
-  if (err != cudaSuccess) return check_cuda(err, "decode_mma occupancy");
-  const int ctas = std::max(1, std::min(n_items, std::max(1, per_sm) * device_sm_count()));
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    per_sm = (dev >= 0 && dev < 64) ? per_sm_cache[dev] : 0;
+    if (per_sm == 0) {
+      err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+      if (err != cudaSuccess) return check_cuda(err, "decode_mma smem attribute");
+      err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem);
+      if (err != cudaSuccess) return check_cuda(err, "decode_mma occupancy");
+      if (per_sm <= 0) return fail(IAK_ERR_UNSUPPORTED, "decode_mma does not fit on an SM");
+      if (dev >= 0 && dev < 64) per_sm_cache[dev] = per_sm;
+    }
+  }
+  const int ctas = std::max(1, std::min(n_items, per_sm * device_sm_count()));
   decode_prep_kernel<D><<<p.B * p.Ht, 128, 0, s>>>(p, p.ws_qtab);
   err = cudaGetLastError();
   if (err != cudaSuccess) return check_cuda(err, "decode_prep launch");
+  kernel_timer_begin(s);
   kern<<<ctas, kThreads, smem, s>>>(p, maps, p.ws_qtab, n_items);
-  return check_cuda(cudaGetLastError(), "decode_mma launch");
+  err = cudaGetLastError();
+  kernel_timer_end(s);
+  return check_cuda(err, "decode_mma launch");
 }
 
 int launch_decode_mma(const DecodeParams& p, const iak_page_pools& P, cudaStream_t s) {

@@ -19,6 +19,9 @@ void set_error(const char* fmt, ...);
 int fail(int status, const char* fmt, ...);
 int check_cuda(cudaError_t e, const char* what);
 int device_sm_count();
+// kernel timer hooks around the main decode launch (no-ops unless enabled)
+void kernel_timer_begin(cudaStream_t s);
+void kernel_timer_end(cudaStream_t s);
 
 // --------------------------------------------------------- device params ---
 // Flattened, by-value kernel parameters of one decode launch.

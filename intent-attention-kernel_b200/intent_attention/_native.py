@@ -86,6 +86,9 @@ SIGNATURES = {
     "iak_pack_metadata": (ctypes.c_int, [ctypes.POINTER(PackArgs), c_void_p]),
     "iak_quantize_pages": (ctypes.c_int, [ctypes.POINTER(QuantArgs), c_void_p]),
     "iak_decode_noalloc": (ctypes.c_int, [ctypes.POINTER(PagePools), ctypes.POINTER(DecodeArgs), c_void_p]),
+    "iak_kernel_timer_enable": (ctypes.c_int, [c_i32]),
+    "iak_kernel_timer_read": (ctypes.c_int, [ctypes.POINTER(ctypes.c_double), ctypes.POINTER(c_i32)]),
+    "iak_kernel_timer_disable": (ctypes.c_int, []),
 }
 NOALLOC_SCRATCH_BYTES = 8 << 20
 
@@ -138,3 +141,28 @@ def check(status: int, what: str) -> None:
     if status == IAK_ERR_INVALID_ARG:
         raise ValueError(f"{what}: {msg}")
     raise RuntimeError(f"{what} failed (status {status}): {msg}")
+
+
+class KernelTimer:
+    """CUDA-event timing of the main decode kernel of each decode call
+    (measurement only).  ``with KernelTimer(n) as t: ...`` then ``t.total_ms``,
+    ``t.launches`` (read after the block, which waits for the events)."""
+
+    def __init__(self, max_launches: int):
+        self.max_launches = int(max_launches)
+        self.total_ms = 0.0
+        self.launches = 0
+
+    def __enter__(self):
+        check(lib().iak_kernel_timer_enable(self.max_launches), "iak_kernel_timer_enable")
+        return self
+
+    def __exit__(self, *exc):
+        try:
+            if exc[0] is None:
+                ms, n = ctypes.c_double(0.0), c_i32(0)
+                check(lib().iak_kernel_timer_read(ctypes.byref(ms), ctypes.byref(n)), "iak_kernel_timer_read")
+                self.total_ms, self.launches = ms.value, n.value
+        finally:
+            lib().iak_kernel_timer_disable()
+        return False
