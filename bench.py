@@ -8,7 +8,11 @@ throughput in GB/s (algorithmic bytes: K+V codes + the scales they need, of
 every selected page, divided by the device time of the step) summed over all
 ranks; ``ms_per_step`` / ``us_per_step`` give the step time.  Multi-GPU runs
 shard the batch (weak scaling: every rank decodes its own full-size batch,
-no collective on the data path) and take the max time over ranks.
+no collective on the data path) and take the max time over ranks; with
+``--workload c5`` they instead cut every sequence's selected pages into one
+range per rank (strong scaling: the whole C5 step is shared), each rank
+decodes its range into partial (m, l, acc) blocks, one NCCL all-gather
+exchanges them and every rank LSE-merges the result.
 
 Default workload: Llama-3-8B-shape GQA decode, batch 32,
 32 q heads / 8 kv heads, head_dim 128, 32768-token context in 16-token
@@ -309,13 +313,33 @@ def run_gpu(args):
     if args.batch:
         w["B"] = args.batch
     ids, fmt = select_pages(w)
-    nbytes = step_bytes(w, fmt)
-    pool, table, counts, tags, q = build_gpu_workload(w, ids, fmt, device, rank)
+    n_sel_total = int(ids.size)
+    # C5 on several GPUs shards every sequence's selected pages by sequence range
+    # (strong scaling, one all-gather of partial blocks per step); the other
+    # workloads shard the batch (weak scaling, no collective on the data path)
+    seq_shard = args.workload == "c5" and world > 1
+    nbytes_total = step_bytes(w, fmt) * (1 if seq_shard else world)
+    if seq_shard:
+        from intent_attention.split_kv import SequenceShardedDecoder, shard_bounds
+        a, b = shard_bounds(ids.size, rank, world)
+        ids, fmt = ids[a:b], fmt[a:b]
+        w["name"] = "C5 long-context decode, sequence-sharded split-KV"
+    nbytes = step_bytes(w, fmt)                     # this rank's selected-KV bytes per step
+    pool, table, counts, tags, q = build_gpu_workload(w, ids, fmt, device, 0 if seq_shard else rank)
     tag_map = make_tag_map({c: (f if f in w["mix"] else "SKIP") for f, c in FMT_CODE.items()})
     out = torch.empty(q.shape, dtype=torch.bfloat16, device=device)
+    decoder = SequenceShardedDecoder() if seq_shard else None
+
+    def decode(q_, table_, counts_):
+        if decoder is not None:
+            decoder.decode(q_, pool, table_, counts_, tags, tag_map, 0, out=out, num_splits=args.splits,
+                           kernel="tensor")
+        else:
+            paged_decode(q_, pool, table_, counts_, tags, tag_map, 0, out=out, num_splits=args.splits,
+                         kernel="tensor")
 
     def step():
-        paged_decode(q, pool, table, counts, tags, tag_map, 0, out=out, num_splits=args.splits, kernel="tensor")
+        decode(q, table, counts)
 
     step()
     torch.cuda.synchronize(device)
@@ -323,12 +347,20 @@ def run_gpu(args):
     with ClockSampler(local) as clocks:
         # nvidia-smi needs ~0.5 s to start sampling: keep the GPU under the same
         # load until samples arrive, so the clock record covers the load window
-        # that ends with the timed region
+        # that ends with the timed region.  Every rank runs the same number of
+        # probe rounds (steps may hold a collective).
         t_probe = time.perf_counter()
-        while len(clocks.rows) < 3 and time.perf_counter() - t_probe < 3.0:
+        while True:
             for _ in range(20):
                 step()
             torch.cuda.synchronize(device)
+            done = len(clocks.rows) >= 3 or time.perf_counter() - t_probe >= 3.0
+            if world > 1:
+                flag = torch.tensor([1 if done else 0], device=device)
+                dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+                done = bool(flag.item())
+            if done:
+                break
         for _ in range(args.warmup):
             step()
         torch.cuda.synchronize(device)
@@ -362,8 +394,7 @@ def run_gpu(args):
         q_dev.copy_(q_host, non_blocking=True)
         table_dev.copy_(table_host, non_blocking=True)
         counts_dev.copy_(counts_host, non_blocking=True)
-        paged_decode(q_dev, pool, table_dev, counts_dev, tags, tag_map, 0, out=out, num_splits=args.splits,
-                     kernel="tensor")
+        decode(q_dev, table_dev, counts_dev)
         out_host.copy_(out, non_blocking=True)
 
     for _ in range(args.warmup):
@@ -385,7 +416,7 @@ def run_gpu(args):
 
     # tensor-core path (forced above, so an ineligible shape fails loudly): query-table preparation,
     # the persistent decode kernel and the LSE merge
-    launches_per_step = 3
+    launches_per_step = 3 + (1 if seq_shard else 0)   # + merge of the gathered partial blocks
     if world > 1:
         t = torch.tensor([kernel_ms], device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -395,20 +426,23 @@ def run_gpu(args):
         peak, peak_kind = measured_hbm_peak()
         gbs = nbytes / (t_ms * 1e-3) / 1e9
         kernel_gbs = nbytes / (kernel_ms * 1e-3) / 1e9
-        value = gbs * world
+        value = nbytes_total / (t_ms * 1e-3) / 1e9
         traffic, traffic_note = ncu_traffic(args.workload, w["B"], nbytes)
         rec = {
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(t_ms, 5), "us_per_step": round(t_ms * 1e3, 2),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp16/fp8/int8 pages, fp32 acc",
+            "higher_is_better": True, "scaling": "strong" if seq_shard else "weak", "vs_baseline": None, "dtype": "fp16/fp8/int8 pages, fp32 acc",
             "data": "synthetic (seeded N(0,1) K/V with 1% x8 outliers, bf16 Q)",
-            "config": {"workload": w["name"], "batch_per_gpu": w["B"], "global_batch": w["B"] * world,
+            "config": {"workload": w["name"], "batch_per_gpu": w["B"], "global_batch": w["B"] * (1 if seq_shard else world),
                        "q_heads": w["Hq"], "kv_heads": w["Hkv"], "head_dim": w["D"], "ctx": w["T"],
-                       "page_size": w["PS"], "selected_pages_per_seq_head": int(ids.size),
+                       "page_size": w["PS"], "selected_pages_per_seq_head": n_sel_total,
+                       "selected_pages_per_seq_head_per_gpu": int(ids.size),
                        "format_mix": w["mix"], "scale_mode": w["scale_mode"],
                        "selected_kv_bytes_per_step_per_gpu": nbytes,
                        "l2": f"inputs larger than L2 ({nbytes / 1e9:.2f} GB of selected KV per step)",
-                       "parallelism": f"dp{world} (batch shards, no collective on the data path)"},
+                       "parallelism": (f"sp{world} (each sequence's selected pages cut into {world} ranges; partial "
+                                       "(m, l, acc) blocks all-gathered over NCCL, LSE-merged on every rank)")
+                       if seq_shard else f"dp{world} (batch shards, no collective on the data path)"},
             "roofline": {"bound": "hbm", "achieved": round(kernel_gbs, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(kernel_gbs / peak, 4), "traffic": traffic,
                          "kernel": "decode_mma_kernel", "kernel_us": round(kernel_ms * 1e3, 2),
@@ -417,9 +451,11 @@ def run_gpu(args):
                                  "per launch / average CUDA-event duration of the persistent decode kernel over the "
                                  "timed region; step_frac uses the whole step (prep + decode + merge); traffic = "
                                  + traffic_note},
-            "e2e": {"value": round(nbytes * world / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+            "e2e": {"value": round(nbytes_total / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
                     "ms_per_step": round(e2e_ms, 5), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "api": "intent_attention.paged_decode with pinned host q / page table / counts in, output out"},
+                    "api": ("intent_attention.SequenceShardedDecoder.decode" if seq_shard else
+                            "intent_attention.paged_decode") +
+                           " with pinned host q / page table / counts in, output out"},
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clocks.summary(),
         }

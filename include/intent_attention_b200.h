@@ -174,6 +174,25 @@ int iak_merge_partials(const float* m, const float* l, const float* acc,
                        int64_t rows, int32_t splits, int32_t head_dim,
                        void* out, int32_t out_dtype, int64_t out_row_stride, void* stream);
 
+/* Partial blocks: merging decodes of disjoint page ranges (sequence shards
+ * on several GPUs, or any split of the page lists).  No counterpart in the
+ * reference, which decodes on one device.  A block holds
+ * rows * (head_dim + 2) fp32 values laid out
+ *     [m: rows][l: rows][acc: rows x head_dim]
+ * with rows = batch * num_q_heads and row = b * num_q_heads + h.
+ * iak_decode writes one when partial_m / partial_l / partial_acc point at
+ * block, block + rows and block + 2 * rows.  m is the running max of the
+ * scaled scores (natural-log domain), l the softmax denominator, acc the
+ * unnormalised weighted sum of values; l = 0 marks a row without pages. */
+#define IAK_PARTIAL_BLOCK_FLOATS(rows, head_dim) ((rows) * ((head_dim) + 2))
+
+/* LSE merge of num_parts consecutive partial blocks (e.g. the result of an
+ * all-gather over ranks) into normalised rows of out (dtype, row stride in
+ * elements): m = max m_i, l = sum l_i e^(m_i - m), o = sum acc_i e^(m_i - m) / l;
+ * rows without pages anywhere become 0. */
+int iak_merge_partial_blocks(const float* blocks, int32_t num_parts, int64_t rows, int32_t head_dim,
+                             void* out, int32_t out_dtype, int64_t out_row_stride, void* stream);
+
 /* Metadata packing on the device.  Logical page ids (one list shared by
  * every (b, h), the router's selected_page_ids order) are mapped to
  * physical ids base[b*Ht + h] + logical, written -1 padded into

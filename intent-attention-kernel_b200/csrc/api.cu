@@ -320,4 +320,17 @@ int iak_merge_partials(const float* m, const float* l, const float* acc, int64_t
                       nullptr, static_cast<cudaStream_t>(stream));
 }
 
+int iak_merge_partial_blocks(const float* blocks, int32_t num_parts, int64_t rows, int32_t head_dim, void* out,
+                             int32_t out_dtype, int64_t out_row_stride, void* stream) {
+  if (rows < 0 || num_parts <= 0 || head_dim <= 0) return fail(IAK_ERR_INVALID_ARG, "bad merge sizes");
+  if (rows == 0) return IAK_OK;
+  if (!blocks || !out) return fail(IAK_ERR_INVALID_ARG, "null merge pointer");
+  if (out_dtype < 0 || out_dtype > 2) return fail(IAK_ERR_INVALID_ARG, "bad out dtype");
+  if (out_row_stride < head_dim) return fail(IAK_ERR_INVALID_ARG, "out_row_stride < head_dim");
+  const int64_t blk = rows * (static_cast<int64_t>(head_dim) + 2);
+  return launch_merge_strided(blocks, blocks + rows, blocks + 2 * rows, 1, blk, head_dim, blk, rows, num_parts,
+                              head_dim, out, out_dtype, out_row_stride, nullptr, nullptr, nullptr, nullptr,
+                              static_cast<cudaStream_t>(stream));
+}
+
 }  // extern "C"

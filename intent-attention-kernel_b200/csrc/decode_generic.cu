@@ -213,25 +213,28 @@ __global__ void __launch_bounds__(kWarps * 32) decode_generic_kernel(const Decod
 
 // LSE merge over splits: rows x splits partials -> normalised rows (or a
 // merged partial when ex_l != nullptr).
+// Partial (s) of row r: m/l at [r * ms_r + s * ms_s], acc at [r * as_r + s * as_s + d].
 __global__ void merge_kernel(const float* __restrict__ m, const float* __restrict__ l, const float* __restrict__ acc,
+                             int64_t ms_r, int64_t ms_s, int64_t as_r, int64_t as_s,
                              int64_t rows, int S, int D, void* out, int out_dtype, int64_t out_row_stride, int Hq,
                              int64_t o_sb, int64_t o_sh, float* ex_m, float* ex_l, float* ex_acc) {
   extern __shared__ float w_s[];
   __shared__ float stat[2];
   for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
-    const float* mr = m + r * S;
-    const float* lr = l + r * S;
+    const float* mr = m + r * ms_r;
+    const float* lr = l + r * ms_r;
     if (threadIdx.x < 32) {
       float M = -INFINITY;
       for (int s = threadIdx.x; s < S; s += 32)
-        if (lr[s] > 0.f) M = fmaxf(M, mr[s]);
+        if (lr[s * ms_s] > 0.f) M = fmaxf(M, mr[s * ms_s]);
 #pragma unroll
       for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
       float L = 0.f;
       for (int s = threadIdx.x; s < S; s += 32) {
-        const float w = (lr[s] > 0.f && M != -INFINITY) ? expf(mr[s] - M) : 0.f;
+        const float ls = lr[s * ms_s];
+        const float w = (ls > 0.f && M != -INFINITY) ? expf(mr[s * ms_s] - M) : 0.f;
         w_s[s] = w;
-        L += lr[s] * w;
+        L += ls * w;
       }
 #pragma unroll
       for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
@@ -246,7 +249,7 @@ __global__ void merge_kernel(const float* __restrict__ m, const float* __restric
       float A = 0.f;
       for (int s = 0; s < S; ++s) {
         const float w = w_s[s];
-        if (w != 0.f) A = fmaf(acc[(r * S + s) * D + d], w, A);
+        if (w != 0.f) A = fmaf(acc[r * as_r + s * as_s + d], w, A);
       }
       if (ex_l) {
         ex_acc[r * D + d] = A;
@@ -289,6 +292,14 @@ int launch_decode_generic(const DecodeParams& p, cudaStream_t s) {
 int launch_merge(const float* m, const float* l, const float* acc, int64_t rows, int splits, int D, void* out,
                  int out_dtype, int64_t out_row_stride, const DecodeParams* rowmap, float* ex_m, float* ex_l,
                  float* ex_acc, cudaStream_t s) {
+  return launch_merge_strided(m, l, acc, splits, 1, static_cast<int64_t>(splits) * D, D, rows, splits, D, out,
+                              out_dtype, out_row_stride, rowmap, ex_m, ex_l, ex_acc, s);
+}
+
+int launch_merge_strided(const float* m, const float* l, const float* acc, int64_t ms_r, int64_t ms_s, int64_t as_r,
+                         int64_t as_s, int64_t rows, int splits, int D, void* out, int out_dtype,
+                         int64_t out_row_stride, const DecodeParams* rowmap, float* ex_m, float* ex_l, float* ex_acc,
+                         cudaStream_t s) {
   if (rows == 0) return IAK_OK;
   if (splits > 12288) return fail(IAK_ERR_UNSUPPORTED, "too many splits to merge (%d)", splits);
   const int threads = D >= 128 ? 128 : (D >= 64 ? 64 : 32);
@@ -299,7 +310,8 @@ int launch_merge(const float* m, const float* l, const float* acc, int64_t rows,
     if (e != cudaSuccess) return check_cuda(e, "merge smem attribute");
   }
   merge_kernel<<<static_cast<unsigned>(blocks), threads, smem, s>>>(
-      m, l, acc, rows, splits, D, out, out_dtype, out_row_stride, rowmap ? rowmap->Hq : 0, rowmap ? rowmap->o_sb : 0,
+      m, l, acc, ms_r, ms_s, as_r, as_s, rows, splits, D, out, out_dtype, out_row_stride, rowmap ? rowmap->Hq : 0,
+      rowmap ? rowmap->o_sb : 0,
       rowmap ? rowmap->o_sh : 0, ex_m, ex_l, ex_acc);
   return check_cuda(cudaGetLastError(), "merge launch");
 }

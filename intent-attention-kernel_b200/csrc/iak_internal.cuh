@@ -64,6 +64,11 @@ constexpr int kTensorConsumerWarps = 4;  // partial slots per work item
 int launch_merge(const float* m, const float* l, const float* acc, int64_t rows, int splits, int D,
                  void* out, int out_dtype, int64_t out_row_stride,
                  const DecodeParams* rowmap, float* ex_m, float* ex_l, float* ex_acc, cudaStream_t s);
+// partial (s) of row r: m/l at [r * ms_r + s * ms_s], acc at [r * as_r + s * as_s + d]
+int launch_merge_strided(const float* m, const float* l, const float* acc, int64_t ms_r, int64_t ms_s, int64_t as_r,
+                         int64_t as_s, int64_t rows, int splits, int D, void* out, int out_dtype,
+                         int64_t out_row_stride, const DecodeParams* rowmap, float* ex_m, float* ex_l, float* ex_acc,
+                         cudaStream_t s);
 
 // ------------------------------------------------------- device helpers ---
 __host__ __device__ inline int n_scales_of(int mode, int D) {

@@ -43,6 +43,13 @@ from .triton_adaptive_format_attention import (
     make_adaptive_page_tables,
 )
 from .paged import PagePool, merge_partials, pack_metadata, paged_decode
+from .split_kv import (
+    SequenceShardedDecoder,
+    decode_partial_block,
+    merge_partial_blocks,
+    shard_bounds,
+    shard_page_lists,
+)
 
 __all__ = [
     "BlockLayout", "BlockPolicy", "SemanticBlock",
@@ -56,4 +63,5 @@ __all__ = [
     "AdaptiveFormatKernelConfig", "AdaptivePageFormat", "adaptive_format_decode_attention_triton",
     "make_adaptive_page_tables",
     "PagePool", "merge_partials", "pack_metadata", "paged_decode",
+    "SequenceShardedDecoder", "decode_partial_block", "merge_partial_blocks", "shard_bounds", "shard_page_lists",
 ]

@@ -1,0 +1,83 @@
+"""GPU parity of the sequence-sharded split-KV decode.
+
+One GPU emulates N ranks: every rank's page range (``shard_page_lists``) is
+decoded into its own partial block through the C ABI, the blocks are stacked
+as an all-gather would leave them and merged with ``iak_merge_partial_blocks``;
+the result must match the oracle's unsharded decode (atol 2e-3 / rtol 1e-2).
+With two or more GPUs the same path also runs as real ranks over NCCL
+(``split_kv_nccl_worker.py``, launched with torch.distributed.run).
+"""
+
+import os
+import subprocess
+import sys
+
+import numpy as np
+import pytest
+import torch
+
+from gpu_cases import make_case, run_gpu, run_oracle, tag_map_for
+from intent_attention.split_kv import (SequenceShardedDecoder, block_floats, decode_partial_block,
+                                       merge_partial_blocks, shard_page_lists)
+
+pytestmark = pytest.mark.gpu
+ATOL, RTOL = 2e-3, 1e-2
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def _sharded(case, world, kernel="auto", out_dtype=torch.float32):
+    q = case["q"]
+    B, Hq, D = q.shape
+    rows = B * Hq
+    blocks = torch.empty((world, block_floats(rows, D)), dtype=torch.float32, device=q.device)
+    for r in range(world):
+        lt, lc = shard_page_lists(case["table"], case["counts"], r, world)
+        decode_partial_block(q, case["pool"], lt, lc, case["tags"], tag_map_for(case["formats"]), block=blocks[r],
+                             kernel=kernel)
+    return merge_partial_blocks(blocks, rows, D, out_dtype=out_dtype).view(B, Hq, D)
+
+
+@pytest.mark.parametrize("world", [1, 2, 3, 8])
+@pytest.mark.parametrize("kernel", ["tensor", "generic"])
+def test_sharded_blocks_merge_to_unsharded(world, kernel):
+    case = make_case(900 + world, B=3, Hq=32, Ht=8, W=120, NP=1500, formats=("F16", "FP8", "INT8", "INT4"))
+    got = _sharded(case, world, kernel)
+    np.testing.assert_allclose(got.cpu().numpy(), run_oracle(case), atol=ATOL, rtol=RTOL)
+
+
+def test_sharded_rows_with_empty_shards_are_zero_or_exact():
+    # counts 0 / 1 rows: most ranks hold no page of the row, their blocks carry l = 0
+    case = make_case(911, B=2, Hq=16, Ht=4, W=9, NP=300, formats=("F16", "INT8"), counts="ragged")
+    case["counts"][0, 1] = 0
+    case["counts"][1, 2] = 1
+    case["np_counts"] = case["counts"].cpu().numpy()
+    got = _sharded(case, 8)
+    ref = run_oracle(case)
+    np.testing.assert_allclose(got.cpu().numpy(), ref, atol=ATOL, rtol=RTOL)
+    assert (got[0, 4:8] == 0).all()
+
+
+def test_sharded_matches_single_device_decode_bf16_out():
+    case = make_case(921, B=4, Hq=32, Ht=8, W=200, NP=2500, formats=("F16", "FP8", "INT8", "INT4"), counts="full")
+    got = _sharded(case, 4, out_dtype=torch.bfloat16)
+    ref = run_gpu(case, out_dtype=torch.float32)
+    np.testing.assert_allclose(got.float().cpu().numpy(), ref.cpu().numpy(), atol=1e-2, rtol=1e-2)
+
+
+def test_single_rank_decoder_is_plain_decode():
+    case = make_case(931, B=2, Hq=8, Ht=2, W=64, NP=400)
+    dec = SequenceShardedDecoder()
+    assert dec.world == 1
+    out = dec.decode(case["q"], case["pool"], case["table"], case["counts"], case["tags"],
+                     tag_map_for(case["formats"]))
+    np.testing.assert_allclose(out.float().cpu().numpy(), run_oracle(case), atol=1e-2, rtol=1e-2)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_nccl_two_ranks_match_oracle(tmp_path):
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", RESULT_DIR=str(tmp_path))
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
+           "--master-addr=127.0.0.1", "--master-port=29631", os.path.join(HERE, "split_kv_nccl_worker.py")]
+    subprocess.run(["timeout", "-k", "30", "300"] + cmd, check=True, env=env, cwd=os.path.dirname(HERE))
+    for r in range(2):
+        assert float(np.load(os.path.join(tmp_path, f"rank{r}.npy"))[0]) == 0.0
