@@ -156,6 +156,53 @@ int iak_decode(const iak_page_pools* pools, const iak_decode_args* args,
 #define IAK_NOALLOC_SCRATCH_BYTES (8 << 20)
 int iak_decode_noalloc(const iak_page_pools* pools, const iak_decode_args* args, void* stream);
 
+/* ------------------------------------------------------------------------
+ * MLA (absorbed multi-head latent attention) decode.
+ *
+ * Replaces triton_mla_decode.py:110-152 mla_decode_triton() and its CPU path
+ * _mla_decode_cpu() (:155-186), and the decode step of mla.py:95-136
+ * mla_triton_decode().  The reference collapses heads into one absorbed
+ * query row per (batch, position) and uses the whole latent vector as key
+ * and value; here every query row r = (b, h) attends over its own sequence's
+ * selected latent pages: score = sm_scale * q[b,h,:d_qk] . c[:d_qk],
+ * context[b,h,:] = softmax-weighted sum of c[:d_v] (d_v <= d_qk; the rope
+ * channels d_v..d_qk-1 are key-only).  The W_VO projection that follows in
+ * the reference is a plain GEMM left to the caller.
+ *
+ * Latent pages are [NP, page_size, d_qk], one pool per format: dense
+ * (f32 / f16 / bf16) and FP8-e4m3 codes with one fp32 scale per page
+ * (value = code * scale).  page_tags + tag_map pick a page's format.
+ * ------------------------------------------------------------------------ */
+enum { IAK_MLA_SKIP = 0, IAK_MLA_DENSE = 1, IAK_MLA_FP8 = 2 };
+
+typedef struct iak_mla_args {
+  const void* q; int32_t q_dtype; int64_t q_stride_b, q_stride_h;     /* [B, H, d_qk], elements */
+  void* out; int32_t out_dtype; int64_t out_stride_b, out_stride_h;    /* [B, H, d_v] context    */
+  int32_t batch, num_heads, d_qk, d_v;
+  const void* dense_pages; int32_t dense_dtype;   /* [NP, page_size, d_qk] IAK_DT_*, or NULL   */
+  const uint8_t* fp8_pages; const float* fp8_scale; /* [NP, page_size, d_qk] e4m3 codes, [NP]  */
+  int64_t num_pages;
+  int32_t page_size;
+  const int32_t* page_table;      /* [B, W]; pt_stride_b = 0 shares one list; ids < 0 unused  */
+  int64_t pt_stride_b;
+  int32_t table_width;
+  const int32_t* page_counts;     /* [B] or NULL = W                                          */
+  const void* page_tags;          /* [NP] or NULL = every page IAK_MLA_DENSE                  */
+  int32_t tag_bytes;              /* 1 or 4                                                   */
+  uint8_t tag_map[16];            /* tag -> IAK_MLA_*                                         */
+  uint8_t tag_default;
+  float sm_scale;                 /* 1/sqrt(d_qk) in the reference                            */
+  /* optional export of per-row partials (rows = B*H: m [rows], l [rows],
+   * acc [rows, d_v], the layout of a partial block with head_dim = d_v)
+   * instead of `out` */
+  float* partial_m; float* partial_l; float* partial_acc;
+  int32_t num_splits;             /* 0 = choose automatically                                 */
+  int32_t kernel;                 /* IAK_KERNEL_*: auto, generic (CUDA cores), tensor (tcgen05) */
+} iak_mla_args;
+
+int iak_mla_workspace_size(const iak_mla_args* args, size_t* bytes);
+int iak_mla_decode(const iak_mla_args* args, void* workspace, size_t workspace_bytes, void* stream);
+
 /* Kernel timer (measurement only; no counterpart in the reference).  While
  * enabled, each iak_decode / iak_decode_noalloc call records a CUDA event
  * pair on the caller's stream around its main decode kernel (not the query

@@ -73,6 +73,26 @@ class QuantArgs(ctypes.Structure):
     ]
 
 
+class MlaArgs(ctypes.Structure):
+    _fields_ = [
+        ("q", c_void_p), ("q_dtype", c_i32), ("q_stride_b", c_i64), ("q_stride_h", c_i64),
+        ("out", c_void_p), ("out_dtype", c_i32), ("out_stride_b", c_i64), ("out_stride_h", c_i64),
+        ("batch", c_i32), ("num_heads", c_i32), ("d_qk", c_i32), ("d_v", c_i32),
+        ("dense_pages", c_void_p), ("dense_dtype", c_i32),
+        ("fp8_pages", c_void_p), ("fp8_scale", c_void_p),
+        ("num_pages", c_i64), ("page_size", c_i32),
+        ("page_table", c_void_p), ("pt_stride_b", c_i64), ("table_width", c_i32),
+        ("page_counts", c_void_p),
+        ("page_tags", c_void_p), ("tag_bytes", c_i32), ("tag_map", ctypes.c_uint8 * 16), ("tag_default", ctypes.c_uint8),
+        ("sm_scale", ctypes.c_float),
+        ("partial_m", c_void_p), ("partial_l", c_void_p), ("partial_acc", c_void_p),
+        ("num_splits", c_i32), ("kernel", c_i32),
+    ]
+
+
+MLA_SKIP, MLA_DENSE, MLA_FP8 = 0, 1, 2
+
+
 # name -> (restype, argtypes); mirrors every declaration of the public header
 SIGNATURES = {
     "iak_version": (ctypes.c_int, []),
@@ -87,6 +107,8 @@ SIGNATURES = {
     "iak_quantize_pages": (ctypes.c_int, [ctypes.POINTER(QuantArgs), c_void_p]),
     "iak_decode_noalloc": (ctypes.c_int, [ctypes.POINTER(PagePools), ctypes.POINTER(DecodeArgs), c_void_p]),
     "iak_merge_partial_blocks": (ctypes.c_int, [c_void_p, c_i32, c_i64, c_i32, c_void_p, c_i32, c_i64, c_void_p]),
+    "iak_mla_workspace_size": (ctypes.c_int, [ctypes.POINTER(MlaArgs), ctypes.POINTER(ctypes.c_size_t)]),
+    "iak_mla_decode": (ctypes.c_int, [ctypes.POINTER(MlaArgs), c_void_p, ctypes.c_size_t, c_void_p]),
     "iak_kernel_timer_enable": (ctypes.c_int, [c_i32]),
     "iak_kernel_timer_read": (ctypes.c_int, [ctypes.POINTER(ctypes.c_double), ctypes.POINTER(c_i32)]),
     "iak_kernel_timer_disable": (ctypes.c_int, []),
