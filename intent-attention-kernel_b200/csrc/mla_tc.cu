@@ -15,6 +15,8 @@
 //     P (f16) is written back into the S columns and is the TMEM A operand
 //     of O_h += P . C[:, h*256 : h*256+256] (M=128, N=256, K=16, the tile
 //     read MN-major from the same shared-memory bytes), O_h in TMEM;
+//   * FP8 tiles stay codes: the page scale multiplies the scores and P
+//     (so O accumulates code x scale x weight); l sums unscaled weights;
 //   * the O accumulator is rescaled lazily (only when a row max grows by
 //     more than 2^8), in TMEM.
 // TMEM: O_h 256 columns + 3 x 16 S/P columns (512 allocated: one CTA per SM).
@@ -408,7 +410,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_ld16(lane_addr + kSCol + k * kTile, sr);
       tmem_wait_ld();
       const int pg = j / tpp;
-      const float sc = s_fmt[pg] == IAK_MLA_FP8 ? base_scale * p.fp8_scale[s_pid[pg]] : base_scale;
+      // FP8 tiles hold codes: the page scale multiplies the scores (key side)
+      // and P (value side); l stays in unscaled softmax weights
+      const float vs = s_fmt[pg] == IAK_MLA_FP8 ? p.fp8_scale[s_pid[pg]] : 1.f;
+      const float sc = base_scale * vs;
       float x[16], tmax = -INFINITY;
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
@@ -447,9 +452,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       float lsum = 0.f;
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        const __half2 h = __floats2half2_rn(exp2f(x[2 * i] - m_used), exp2f(x[2 * i + 1] - m_used));
-        const float2 back = __half22float2(h);
-        lsum += back.x + back.y;
+        const float p0 = exp2f(x[2 * i] - m_used), p1 = exp2f(x[2 * i + 1] - m_used);
+        lsum += p0 + p1;
+        const __half2 h = __floats2half2_rn(p0 * vs, p1 * vs);
         pk[i] = *reinterpret_cast<const uint32_t*>(&h);
       }
       l += lsum;
