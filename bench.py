@@ -1,6 +1,6 @@
 """Benchmark: fused selected-quant paged decode on B200 (sm_100a).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload c2|c3|c5|c1] [--impl b200|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload c2|c3|c4|c5|c1] [--impl b200|reference]
 
 One "step" is one decode step of the workload's whole batch (all sequences,
 all heads) over its router-selected pages.  ``value`` is the selected-KV HBM
@@ -476,6 +476,8 @@ def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
+    if args.workload == "c4":
+        return run_reference_mla(args, world)
     w = workload(args.workload)
     ids, fmt = select_pages(w)
     nbytes = step_bytes(w, fmt)
@@ -499,12 +501,273 @@ def run_reference(args):
     print(json.dumps(rec), flush=True)
 
 
+# --------------------------------------------------------------------------- #
+#  C4: DeepSeek-V2-shape MLA absorbed decode (tcgen05 / TMEM kernel)
+# --------------------------------------------------------------------------- #
+
+C4 = dict(name="C4 DeepSeek-V2-shape MLA absorbed decode", B=64, H=128, Dqk=576, Dv=512, T=16384, PS=64,
+          recent_tokens=2048, select_pages=154, seed=1004)
+
+
+def select_mla_pages(w: dict):
+    """Router-selected latent pages (one-page ATTEND blocks with seeded scores
+    plus the RECENT tail) and their formats: the last ``recent_tokens`` stay
+    BF16 (tag 0), the rest are FP8 (tag 1)."""
+    from intent_attention import BlockLayout, BlockPolicy, BlockRouter, RouterConfig, SemanticBlock
+    from intent_attention import routing_to_kernel_metadata
+    PS, T = w["PS"], w["T"]
+    rng = np.random.default_rng(w["seed"])
+    tail = T - w["recent_tokens"]
+    blocks = [SemanticBlock(f"lat{i}", i * PS, (i + 1) * PS, BlockPolicy.ATTEND, score=float(rng.random()))
+              for i in range(tail // PS)]
+    blocks.append(SemanticBlock("recent", tail, T, BlockPolicy.RECENT))
+    top_k = w["select_pages"] - w["recent_tokens"] // PS
+    router = BlockRouter(RouterConfig(top_k_blocks=top_k, memory_pressure=0.0))
+    meta = routing_to_kernel_metadata(router.route_layout(BlockLayout(blocks), T), PS)
+    ids = np.asarray(meta["selected_page_ids"], dtype=np.int32)
+    tags = np.where(ids >= tail // PS, 0, 1).astype(np.uint8)
+    return ids, tags
+
+
+def mla_bytes_flops(w: dict, tags: np.ndarray):
+    """Algorithmic bytes (latent codes + FP8 page scales of every selected
+    page) and FLOPs (QK over d_qk + PV over d_v per head and token) per step."""
+    PS, Dqk = w["PS"], w["Dqk"]
+    per_seq = sum(PS * Dqk * 2 if t == 0 else PS * Dqk + 4 for t in tags)
+    tokens = tags.size * PS
+    flops = 2 * (w["Dqk"] + w["Dv"]) * w["H"] * tokens * w["B"]
+    return per_seq * w["B"], flops
+
+
+def build_mla_workload(w: dict, ids: np.ndarray, tags_sel: np.ndarray, device, rank: int):
+    import torch
+    B, H, Dqk, PS, T = w["B"], w["H"], w["Dqk"], w["PS"], w["T"]
+    NLP = T // PS
+    NP = B * NLP
+    dense = torch.empty((NP, PS, Dqk), dtype=torch.bfloat16, device=device)
+    fp8 = torch.empty((NP, PS, Dqk), dtype=torch.uint8, device=device)
+    scale = torch.ones(NP, dtype=torch.float32, device=device)
+    tags = torch.full((NP,), 2, dtype=torch.uint8, device=device)   # unselected pages: SKIP
+    g = torch.Generator(device=device).manual_seed(w["seed"] * 131 + rank)
+    ids_t = torch.from_numpy(ids).to(device).long()
+    is_dense = torch.from_numpy(tags_sel).to(device) == 0
+    for b in range(B):
+        dst = b * NLP + ids_t
+        x = torch.randn((ids.size, PS, Dqk), generator=g, device=device)
+        dense[dst[is_dense]] = x[is_dense].to(torch.bfloat16)
+        xf = x[~is_dense]
+        sc = torch.clamp(xf.abs().amax(dim=(1, 2)) / 127.0, min=1e-8)
+        fp8[dst[~is_dense]] = (xf / sc[:, None, None]).to(torch.float8_e4m3fn).view(torch.uint8)
+        scale[dst[~is_dense]] = sc
+        tags[dst] = torch.where(is_dense, 0, 1).to(torch.uint8)
+    table = (torch.arange(B, device=device, dtype=torch.int32)[:, None] * NLP + ids_t[None, :].int()).contiguous()
+    q = torch.randn((B, H, Dqk), generator=g, device=device).to(torch.bfloat16)
+    torch.cuda.synchronize(device)
+    return dense, fp8, scale, tags, table, q
+
+
+def cpu_mla_step(w: dict, ids: np.ndarray, tags_sel: np.ndarray, budget_s: float = 12.0, max_seqs: int = 16):
+    """Time the numpy oracle's per-head MLA decode over sampled sequences and
+    extrapolate to the batch.  Returns (seconds per step, sequences timed, cores)."""
+    import concurrent.futures as cf
+    from oracle import mla as omla
+    from oracle import quant as oq
+    cores = len(os.sched_getaffinity(0))
+    PS, Dqk, Dv, H = w["PS"], w["Dqk"], w["Dv"], w["H"]
+    n = ids.size
+    rng = np.random.default_rng(w["seed"] + 7)
+    lat = rng.standard_normal((n, PS, Dqk)).astype(np.float32)
+    scale = np.maximum(np.abs(lat).reshape(n, -1).max(1) / 127.0, 1e-8).astype(np.float32)
+    pools = {"bf16": lat, "fp8": oq.f32_to_e4m3(lat / scale[:, None, None])}
+    q = rng.standard_normal((1, H, Dqk)).astype(np.float32)
+    table = np.arange(n)[None, :]
+    tags = tags_sel.astype(np.int64)
+
+    def one(_):
+        return omla.mla_paged_decode(q, table, None, tags, pools, scale, Dv, 1.0 / math.sqrt(Dqk))
+
+    done = 0
+    t0 = time.perf_counter()
+    with cf.ThreadPoolExecutor(max_workers=cores) as ex:
+        while done < min(w["B"], max_seqs) and time.perf_counter() - t0 < budget_s:
+            k = min(cores, w["B"] - done)
+            list(ex.map(one, range(k)))
+            done += k
+    dt = time.perf_counter() - t0
+    return dt * w["B"] / done, done, cores
+
+
+def run_reference_mla(args, world):
+    w = dict(C4)
+    ids, tags_sel = select_mla_pages(w)
+    nbytes, _ = mla_bytes_flops(w, tags_sel)
+    vals = []
+    seqs = cores = None
+    for i in range(args.warmup + args.steps):
+        sec, seqs, cores = cpu_mla_step(w, ids, tags_sel, budget_s=args.cpu_budget / max(1, args.steps), max_seqs=4)
+        if i >= args.warmup:
+            vals.append(sec)
+    sec = statistics.median(vals)
+    v = nbytes / sec / 1e9
+    rec = {"impl": "reference", "metric": METRIC, "value": round(v, 4), "unit": "GB/s", "n_gpus": world,
+           "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(sec * 1e3, 3),
+           "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp64 (numpy)",
+           "data": "synthetic", "config": {"workload": w["name"], "batch": w["B"], "q_heads": w["H"],
+                                           "d_qk": w["Dqk"], "d_v": w["Dv"], "ctx": w["T"]},
+           "cpu_baseline": {"value": round(v, 4), "unit": "GB/s", "cores": cores, "kind": "port",
+                            "sample": f"{seqs} sequences per step, extrapolated to the full batch"},
+           "e2e": {"value": round(v, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(rec), flush=True)
+
+
+def measured_tensor_peak():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 1590.0, "fallback"
+
+
+def run_gpu_mla(args):
+    import torch
+    import torch.distributed as dist
+    from intent_attention._native import KernelTimer
+    from intent_attention.triton_mla_decode import make_mla_tag_map, mla_paged_decode
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
+    w = dict(C4)
+    if args.batch:
+        w["B"] = args.batch
+    ids, tags_sel = select_mla_pages(w)
+    nbytes, flops = mla_bytes_flops(w, tags_sel)
+    dense, fp8, scale, tags, table, q = build_mla_workload(w, ids, tags_sel, device, rank)
+    tag_map = make_mla_tag_map({0: "DENSE", 1: "FP8", 2: "SKIP"})
+    out = torch.empty((w["B"], w["H"], w["Dv"]), dtype=torch.bfloat16, device=device)
+
+    def decode(q_, table_):
+        mla_paged_decode(q_, table_, None, dense_pages=dense, fp8_pages=fp8, fp8_scale=scale, page_tags=tags,
+                         tag_map=tag_map, d_v=w["Dv"], out=out, num_splits=args.splits, kernel="tensor")
+
+    decode(q, table)
+    torch.cuda.synchronize(device)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        t_probe = time.perf_counter()
+        while True:
+            for _ in range(10):
+                decode(q, table)
+            torch.cuda.synchronize(device)
+            done = len(clocks.rows) >= 3 or time.perf_counter() - t_probe >= 3.0
+            if world > 1:
+                flag = torch.tensor([1 if done else 0], device=device)
+                dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+                done = bool(flag.item())
+            if done:
+                break
+        for _ in range(args.warmup):
+            decode(q, table)
+        torch.cuda.synchronize(device)
+        if world > 1:
+            dist.barrier()
+        with KernelTimer(args.steps) as ktimer:
+            ev0.record()
+            for _ in range(args.steps):
+                decode(q, table)
+            ev1.record()
+            torch.cuda.synchronize(device)
+    t_ms = ev0.elapsed_time(ev1) / args.steps
+    kernel_ms = ktimer.total_ms / max(1, ktimer.launches)
+
+    q_host, table_host = q.cpu().pin_memory(), table.cpu().pin_memory()
+    out_host = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+    q_dev, table_dev = torch.empty_like(q), torch.empty_like(table)
+    h2d = q_host.numel() * q_host.element_size() + table_host.numel() * 4
+    d2h = out_host.numel() * out_host.element_size()
+
+    def e2e_step():
+        q_dev.copy_(q_host, non_blocking=True)
+        table_dev.copy_(table_host, non_blocking=True)
+        decode(q_dev, table_dev)
+        out_host.copy_(out, non_blocking=True)
+
+    for _ in range(args.warmup):
+        e2e_step()
+    torch.cuda.synchronize(device)
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize(device)
+    e2e_ms = e0.elapsed_time(e1) / args.steps
+    if world > 1:
+        t = torch.tensor([t_ms, kernel_ms, e2e_ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        t_ms, kernel_ms, e2e_ms = (float(x) for x in t.tolist())
+
+    if rank == 0:
+        hbm_peak, hbm_kind = measured_hbm_peak()
+        tc_peak, tc_kind = measured_tensor_peak()
+        tflops = flops / (kernel_ms * 1e-3) / 1e12
+        kernel_gbs = nbytes / (kernel_ms * 1e-3) / 1e9
+        gbs = nbytes / (t_ms * 1e-3) / 1e9
+        n_sel = int(ids.size)
+        rec = {
+            "metric": METRIC, "value": round(gbs * world, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(t_ms, 5), "us_per_step": round(t_ms * 1e3, 2),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16/fp8-e4m3 latent pages, f16 tensor-core operands, fp32 acc",
+            "data": "synthetic (seeded N(0,1) latents and bf16 Q)",
+            "config": {"workload": w["name"], "batch_per_gpu": w["B"], "global_batch": w["B"] * world,
+                       "q_heads": w["H"], "d_qk": w["Dqk"], "d_v": w["Dv"], "ctx": w["T"], "page_size": w["PS"],
+                       "selected_pages_per_seq": n_sel, "bf16_pages_per_seq": int((tags_sel == 0).sum()),
+                       "fp8_pages_per_seq": int((tags_sel == 1).sum()),
+                       "selected_kv_bytes_per_step_per_gpu": nbytes, "flops_per_step_per_gpu": flops,
+                       "l2": f"inputs larger than L2 ({nbytes / 1e9:.2f} GB of selected latents per step)",
+                       "parallelism": f"dp{world} (batch shards, no collective on the data path)"},
+            "roofline": {"bound": "tensor", "achieved": round(tflops, 1), "peak": tc_peak, "unit": "TFLOP/s",
+                         "frac": round(tflops / tc_peak, 4), "traffic": None, "kernel": "mla_tc_kernel",
+                         "kernel_us": round(kernel_ms * 1e3, 2),
+                         "hbm": {"achieved": round(kernel_gbs, 1), "peak": hbm_peak, "unit": "GB/s",
+                                 "frac": round(kernel_gbs / hbm_peak, 4)},
+                         "note": f"peak = {tc_kind} cuBLAS bf16 GEMM (burst); achieved = useful FLOPs per launch "
+                                 "(2*(d_qk+d_v) per head and selected token; the two value halves recompute "
+                                 "Q.C^T, 1.53x the useful tensor work) / CUDA-event kernel time; hbm = selected "
+                                 f"latent bytes / the same time vs the {hbm_kind} copy bandwidth"},
+            "e2e": {"value": round(nbytes * world / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+                    "ms_per_step": round(e2e_ms, 5), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "api": "intent_attention.triton_mla_decode.mla_paged_decode with pinned host q / page table "
+                           "in, context out"},
+            "gpu_launches": args.steps,
+            "clocks": clocks.summary(),
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            sec, seqs, cores = cpu_mla_step(w, ids, tags_sel, budget_s=args.cpu_budget)
+            rec["cpu_baseline"] = {"value": round(nbytes / sec / 1e9, 4), "unit": "GB/s", "cores": cores,
+                                   "kind": "port", "seconds_per_step": round(sec, 3),
+                                   "sample": f"{seqs} of {w['B']} sequences timed with the numpy oracle's per-head "
+                                             "MLA decode, extrapolated linearly to the full step"}
+        print(json.dumps(rec), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--workload", default="c2", choices=["c1", "c2", "c3", "c5"])
+    ap.add_argument("--workload", default="c2", choices=["c1", "c2", "c3", "c4", "c5"])
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--splits", type=int, default=0)
     ap.add_argument("--batch", type=int, default=0, help="override the workload's batch (profiling runs)")
@@ -515,6 +778,8 @@ def main():
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "c4":
+        run_gpu_mla(args)
     else:
         run_gpu(args)
 
