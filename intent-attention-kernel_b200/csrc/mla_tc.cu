@@ -1,37 +1,41 @@
 // Tensor-core (tcgen05 / TMEM) MLA decode for the absorbed DeepSeek-V2 shape:
 // d_qk = 576 (512 latent + 64 rope channels), d_v = 512, up to 128 query
-// heads per sequence, latent pages of a multiple of 16 tokens, dense BF16 /
+// heads per sequence, latent pages of a multiple of 64 tokens, dense BF16 /
 // F16 or FP8-e4m3 (per-page scale) pages.
 //
 // One CTA = one work item (sequence b, page range `split`, value half h):
-//   * the 128 head rows are the M = 128 rows of every MMA; Q (f16, K-major,
-//     128-byte swizzle) stays in shared memory for the whole item;
-//   * 16-token page tiles stream through a 4-stage TMA ring; FP8 and BF16
-//     tiles are converted to f16 in place by a converter warpgroup (FP8 via
-//     cvt.e4m3x2, exact; BF16 via f32, exact inside the f16 range);
-//   * S = Q . C^T (M=128, N=16, K=576: 36 tcgen05.mma, f32 in TMEM, three
-//     S buffers); the softmax warpgroup owns one TMEM lane (= one head) per
-//     thread, so the online softmax needs no cross-thread reduction;
-//     P (f16) is written back into the S columns and is the TMEM A operand
-//     of O_h += P . C[:, h*256 : h*256+256] (M=128, N=256, K=16, the tile
-//     read MN-major from the same shared-memory bytes), O_h in TMEM;
-//   * FP8 tiles stay codes: the page scale multiplies the scores and P
-//     (so O accumulates code x scale x weight); l sums unscaled weights;
+//   * the 128 head rows are the M = 128 rows of every MMA.  Q is f16: its
+//     channels [0, 256) sit in TMEM (A operand of the TS-form MMA), channels
+//     [256, 576) in shared memory (K-major, 128-byte swizzle);
+//   * latents are consumed in 64-token chunks of nine 64-channel k-blocks.
+//     A converter warpgroup loads each k-block from global memory (the
+//     producer warp bulk-prefetches chunks into L2 a few chunks ahead),
+//     converts it to f16 x 2^-8 in registers (FP8 by integer bit placement,
+//     exact; dense by one multiply, exact above the f16 subnormal range) and
+//     stores it once, swizzled, into
+//     shared memory: the 5 k-blocks outside this CTA's value half go to a
+//     9-slot ring released as soon as S has read them, the 4 value k-blocks
+//     to a double-buffered set held until P.V has read them;
+//   * S = Q . C^T: M=128, N=64 tokens, K=576 (36 tcgen05.mma; N = 64 keeps
+//     the MMA above the per-instruction floor that makes N <= 32 slow),
+//     fp32 in TMEM, two S buffers.  The softmax warpgroup owns one TMEM lane
+//     (= one head) per thread, so the online softmax needs no cross-thread
+//     reduction; P (f16) is written back over S and is the TMEM A operand of
+//     O_h += P . C[:, h*256 : h*256+256] (M=128, N=256, K=64 in 4 MMAs, the
+//     value k-blocks read MN-major), O_h fp32 in TMEM;
+//   * FP8 latents stay codes: the page scale multiplies the scores and P (so
+//     O accumulates code x scale x weight); l sums unscaled weights;
 //   * the O accumulator is rescaled lazily (only when a row max grows by
 //     more than 2^8), in TMEM.
-// TMEM: O_h 256 columns + 3 x 16 S/P columns (512 allocated: one CTA per SM).
-// The two value halves of a (b, split) recompute S: TMEM cannot hold
-// 128 x 512 fp32 next to S.
+// TMEM: O_h 256 | S/P 2 x 64 | Q 128 columns (512 allocated: one CTA per SM).
+// The two value halves of a (b, split) each compute S: TMEM cannot hold a
+// 128 x 512 fp32 accumulator next to S.
 //
 // Reference: triton_mla_decode.py:155-186 (_mla_decode_cpu) per query row,
 // restated per head; rows without pages give 0.
-#include <cuda.h>
-#include <cudaTypedefs.h>
-
 #include <algorithm>
 #include <cstring>
 #include <mutex>
-#include <unordered_map>
 
 #include "mla_internal.cuh"
 
@@ -41,48 +45,57 @@ __device__ unsigned int g_mla_timeouts = 0;
 
 namespace {
 
-constexpr int kDqk = 576, kDv = 512, kHalf = kDv / 2, kRows = 128, kTile = 16;
-constexpr int kStages = 4, kSBuf = 3;
-constexpr int kKBlocks = kDqk / 64;                 // 128-byte swizzle atoms along the channels
+constexpr int kDqk = 576, kDv = 512, kHalf = kDv / 2, kRows = 128, kChunk = 64;
+constexpr int kKBlocks = kDqk / 64;                 // 64-channel k-blocks (128-byte swizzle atoms)
+constexpr int kVBlocks = kHalf / 64;                // k-blocks of one value half
+constexpr int kKOnly = kKBlocks - kVBlocks;         // k-blocks only S reads
+constexpr int kKSlots = 9;                          // ring slots for them (more than one chunk)
+constexpr int kPrefetchAhead = 4;                   // chunks prefetched into L2 ahead of the converters
+constexpr int kQTmemDims = 256;                     // Q channels [0, 256) live in TMEM (A operand)
+constexpr int kQTmemCols = kQTmemDims / 2;          // two f16 per 32-bit column
+constexpr int kQSmemKb0 = kQTmemDims / 64;          // first Q k-block kept in shared memory
+constexpr int kQSmemKbs = kKBlocks - kQSmemKb0;     // 5 blocks: channels [256, 576)
 constexpr int kKbQ = kRows * 128;                   // bytes of one Q k-block (128 rows x 128 B)
-constexpr int kKbTile = kTile * 128;                // bytes of one tile k-block (16 rows x 128 B)
-constexpr int kQBytes = kKBlocks * kKbQ;            // 147456
-constexpr int kTileBytes = kKBlocks * kKbTile;      // 18432
-constexpr int kRawOff = kTileBytes / 2;             // an FP8 tile lands in the upper half
-constexpr int kFp8Part = 192;                       // bytes per row of one FP8 TMA box (3 boxes per row)
+constexpr int kKb = kChunk * 128;                   // bytes of one f16 latent k-block (64 rows x 128 B)
 constexpr int kMaxItemPages = 512;
-constexpr int kThreads = 320;                       // softmax wg | converter wg | TMA warp | MMA warp
-constexpr int kConvWarp0 = 4, kTmaWarp = 8, kMmaWarp = 9;
-constexpr int kOCol = 0, kSCol = kHalf, kTmemCols = 512;
+constexpr int kThreads = 320;                       // softmax wg | converter wg | prefetch warp | MMA warp
+constexpr int kConvWarp0 = 4, kPrefWarp = 8, kMmaWarp = 9;
+constexpr int kSBuf = 2;
+constexpr int kOCol = 0, kSCol = kHalf, kQCol = kSCol + kSBuf * kChunk, kTmemCols = 512;
+static_assert(kQCol + kQTmemCols <= kTmemCols, "TMEM budget");
 constexpr long long kWaitCycles = 4000000000LL;     // ~2 s at boost clock, then give up
 constexpr float kLazyLog2 = 8.f;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 
 enum {
-  B_FULL = 0,                    // TMA -> converters (tx bytes)
-  B_CONV = B_FULL + kStages,     // converters -> MMA (f16 tile ready)
-  B_EMPTY = B_CONV + kStages,    // MMA commit -> TMA (tile no longer read)
-  B_SFULL = B_EMPTY + kStages,   // MMA commit -> softmax (S ready)
-  B_PFULL = B_SFULL + kSBuf,     // softmax -> MMA (P written, O rescaled)
-  B_PVDONE = B_PFULL + kSBuf,    // MMA commit -> softmax / MMA (PV done: O current, S/P buffer free)
-  B_DONE = B_PVDONE + kSBuf,     // MMA commit -> MMA (all MMAs retired)
-  B_CREAD,                       // converters: every FP8 code of the tile read (in-place conversion)
+  B_VCONV = 0,                    // value set: converters -> MMA (f16 k-blocks stored)
+  B_VEMPTY = B_VCONV + 2,         // value set: MMA commit after P.V -> converters
+  B_KCONV = B_VEMPTY + 2,         // ring slot: converters -> MMA
+  B_KEMPTY = B_KCONV + kKSlots,   // ring slot: MMA commit after S -> converters
+  B_SFULL = B_KEMPTY + kKSlots,   // MMA commit -> softmax (S ready)
+  B_PFULL = B_SFULL + kSBuf,      // softmax -> MMA (P written, O rescaled)
+  B_PVDONE = B_PFULL + kSBuf,     // MMA commit -> softmax / MMA (P.V done: O current, S/P buffer free)
+  B_DONE = B_PVDONE + kSBuf,      // MMA commit -> MMA (all MMAs retired)
+  B_QREADY,                       // softmax warps -> MMA: Q channels stored in TMEM
   B_COUNT
 };
 
 struct Smem {
-  static constexpr int q = 0;
-  static constexpr int tiles = kQBytes;
-  static constexpr int pid = tiles + kStages * kTileBytes;
-  static constexpr int pfmt = pid + kMaxItemPages * 4;
+  static constexpr int q = 0;                                       // Q k-blocks 4..8
+  static constexpr int vset = q + kQSmemKbs * kKbQ;                 // 2 x 4 value k-blocks
+  static constexpr int kring = vset + 2 * kVBlocks * kKb;           // 9 ring k-blocks
+  static constexpr int pid = kring + kKSlots * kKb;
+  static constexpr int pscale = pid + kMaxItemPages * 4;
+  static constexpr int pfmt = pscale + kMaxItemPages * 4;
   static constexpr int bars = pfmt + kMaxItemPages;
   static constexpr int tmem = bars + B_COUNT * 8;
   static constexpr int nvalid = tmem + 4;
   static constexpr int total = nvalid + 12;
 };
-static_assert(Smem::tiles % 1024 == 0 && kTileBytes % 1024 == 0, "swizzle atoms need 1024-byte alignment");
+static_assert(Smem::vset % 1024 == 0 && Smem::kring % 1024 == 0, "1024-byte alignment");
 static_assert(Smem::bars % 8 == 0, "mbarriers need 8-byte alignment");
+static_assert(Smem::total + 1024 <= 232448, "shared memory budget");
 
 // ----------------------------------------------------------------- PTX ---
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -93,9 +106,6 @@ __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
 }
 __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
 }
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   uint32_t ok;
@@ -114,12 +124,22 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
     if (clock64() - t0 > kWaitCycles) return false;
   return true;
 }
-__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-          dst),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
-      : "memory");
+// Bounded wait with sleep back-off between polls: for roles off the MMA issue path, so that
+// waiting warps leave issue slots to the warps sharing their scheduler.
+__device__ __forceinline__ bool mbar_wait_sleep(uint32_t bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  unsigned ns = 32;
+  while (!mbar_try_wait(bar, parity)) {
+    if (clock64() - t0 > kWaitCycles) return false;
+    __nanosleep(ns);
+    if (ns < 256) ns <<= 1;
+  }
+  return true;
+}
+// Bulk prefetch of [src, src + bytes) into L2 (bytes a multiple of 16, src 16-byte aligned).
+__device__ __forceinline__ void prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
@@ -152,35 +172,32 @@ __device__ __forceinline__ void mma_commit(uint32_t bar) {
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
-        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
+// Latent tiles are stored in shared memory as f16 holding value * 2^-8 (kTileScale):
+// * an e4m3 code s.eeee.mmm placed as the f16 bit pattern s.0eeee.mmm0000000 is
+//   exactly code * 2^-8 for every finite code, normals and subnormals alike (e4m3
+//   bias 7, f16 bias 15, both keep an implicit 1 above 0 and the same subnormal
+//   scaling), so FP8 k-blocks need only integer ops, no conversion instructions;
+// * dense rows are multiplied by 2^-8 on the way (exact above the f16 subnormal
+//   range, 2^-24 absolute resolution below it).
+// The 2^8 is restored in the score scale and in the final normalisation.
+constexpr float kTileScale = 1.f / 256.f;
+// codes in bytes 0 and 2 of t (bytes 1 and 3 zero) -> f16x2 of code * 2^-8
+__device__ __forceinline__ uint32_t e4m3_pair_bits(uint32_t t) {
+  return ((t & 0x007F007Fu) << 7) | ((t & 0x00800080u) << 8);
 }
-__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
-          taddr),
-      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
-      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
-      : "memory");
-}
-__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8]) {
-  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(r[0]),
-               "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
-               : "memory");
-}
-
-__device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint16_t h) {
-  uint32_t r;
-  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(r) : "h"(h));
-  return r;
+// four codes of w -> two f16x2 words (first code in the low half of the first word)
+__device__ __forceinline__ void e4m3x4_to_f16(uint32_t w, uint32_t& lo, uint32_t& hi) {
+  lo = e4m3_pair_bits(__byte_perm(w, 0u, 0x4140));
+  hi = e4m3_pair_bits(__byte_perm(w, 0u, 0x4342));
 }
 // two bf16 (low half = first element) -> two f16, exact inside the f16 range
-__device__ __forceinline__ uint32_t bf16x2_to_f16x2(uint32_t w) {
-  const __half2 h = __floats2half2_rn(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));
+__device__ __forceinline__ uint32_t bf16x2_to_f16x2(uint32_t w, float mul = 1.f) {
+  const __half2 h = __floats2half2_rn(__uint_as_float(w << 16) * mul, __uint_as_float(w & 0xFFFF0000u) * mul);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+// two f16 times 2^-8
+__device__ __forceinline__ uint32_t f16x2_tile_scale(uint32_t w) {
+  const __half2 h = __hmul2(*reinterpret_cast<const __half2*>(&w), __float2half2_rn(kTileScale));
   return *reinterpret_cast<const uint32_t*>(&h);
 }
 
@@ -194,9 +211,39 @@ __device__ __forceinline__ int mla_fmt(const MlaParams& p, int64_t pid) {
 // Byte offset of 16-byte chunk `c` (0..7) of row `r` inside a 128-byte-swizzled atom column.
 __device__ __forceinline__ uint32_t swz(int r, int c) { return static_cast<uint32_t>(r * 128 + ((c ^ (r & 7)) << 4)); }
 
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,"
+      "%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
+      "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
+      "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
+      "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+
+__device__ __forceinline__ uint4 to_f16x8(uint4 x, bool bf) {
+  return bf ? make_uint4(bf16x2_to_f16x2(x.x), bf16x2_to_f16x2(x.y), bf16x2_to_f16x2(x.z), bf16x2_to_f16x2(x.w)) : x;
+}
+
 // ---------------------------------------------------------------- kernel ---
-__global__ void __launch_bounds__(kThreads, 1)
-    mla_tc_kernel(const MlaParams p, const __grid_constant__ CUtensorMap dmap, const __grid_constant__ CUtensorMap fmap) {
+// k-block order of a chunk: the blocks outside this CTA's value half ascending (ring), then the value half.
+__device__ __forceinline__ int chunk_kb(int half, int i) {
+  if (i >= kKOnly) return half * kVBlocks + (i - kKOnly);
+  return i < half * kVBlocks ? i : i + kVBlocks;
+}
+
+__global__ void __launch_bounds__(kThreads, 1) mla_tc_kernel(const MlaParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t sbase = (raw + 1023u) & ~1023u;
@@ -209,17 +256,25 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int b = (blockIdx.x >> 1) / S;
 
   int32_t* s_pid = reinterpret_cast<int32_t*>(sm + Smem::pid);
+  float* s_scale = reinterpret_cast<float*>(sm + Smem::pscale);
   uint8_t* s_fmt = sm + Smem::pfmt;
   volatile uint32_t* s_tmem = reinterpret_cast<volatile uint32_t*>(sm + Smem::tmem);
   volatile int* s_nvalid = reinterpret_cast<volatile int*>(sm + Smem::nvalid);
-  const uint32_t q_s = sbase + Smem::q, tiles_s = sbase + Smem::tiles;
   auto bar = [&](int i) -> uint32_t { return sbase + Smem::bars + 8u * static_cast<uint32_t>(i); };
+  // byte offsets (from sbase) of the f16 k-block slots
+  auto vslot = [&](int set, int i) -> uint32_t { return Smem::vset + (set * kVBlocks + i) * kKb; };
+  auto kslot = [&](int slot) -> uint32_t { return Smem::kring + slot * kKb; };
+  const bool q_bf16 = p.q_dtype == IAK_DT_BF16;
+  const uint16_t* qrow0 = static_cast<const uint16_t*>(p.q) + b * p.q_sb;
 
   if (tid == 0) {
-    for (int s = 0; s < kStages; ++s) {
-      mbar_init(bar(B_FULL + s), 1);
-      mbar_init(bar(B_CONV + s), 128);
-      mbar_init(bar(B_EMPTY + s), 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(bar(B_VCONV + i), 128);
+      mbar_init(bar(B_VEMPTY + i), 1);
+    }
+    for (int i = 0; i < kKSlots; ++i) {
+      mbar_init(bar(B_KCONV + i), 128);
+      mbar_init(bar(B_KEMPTY + i), 1);
     }
     for (int k = 0; k < kSBuf; ++k) {
       mbar_init(bar(B_SFULL + k), 1);
@@ -227,7 +282,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(bar(B_PVDONE + k), 1);
     }
     mbar_init(bar(B_DONE), 1);
-    mbar_init(bar(B_CREAD), 128);
+    mbar_init(bar(B_QREADY), 128);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   }
@@ -237,8 +292,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
-  if (warp == kTmaWarp) {
-    // compact this item's slice of the page table: valid ids of dense / FP8 pages, in order
+  if (warp == kPrefWarp) {
+    // compact this item's slice of the page table (valid ids of dense / FP8 pages, in order) with page scales
     const int n_tab = p.pc ? min(max(p.pc[b], 0), p.W) : p.W;
     const int lo = split * p.pages_per_split, hi = min(n_tab, lo + p.pages_per_split);
     const int32_t* table = p.pt + static_cast<int64_t>(b) * p.pt_sb;
@@ -256,23 +311,23 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int r = cnt + __popc(m & ((1u << lane) - 1u));
         s_pid[r] = pid;
         s_fmt[r] = static_cast<uint8_t>(fmt);
+        s_scale[r] = fmt == IAK_MLA_FP8 ? p.fp8_scale[pid] : 1.f;
       }
       cnt += __popc(m);
     }
     if (lane == 0) *s_nvalid = cnt;
   }
-  if (warp < kTmaWarp) {
-    // Q rows (heads) as f16 in the K-major 128-byte-swizzled layout; rows >= H are zero
-    const bool bf = p.q_dtype == IAK_DT_BF16;
-    for (int u = tid; u < kRows * (kDqk / 8); u += 256) {
-      const int r = u / (kDqk / 8), c8 = u % (kDqk / 8);
+  if (warp >= kConvWarp0 && warp < kPrefWarp) {
+    // Q channels [256, 576) as f16 in the K-major 128-byte-swizzled layout; rows >= H are zero
+    const int ct = tid - kConvWarp0 * 32;
+    constexpr int kChunks = kQSmemKbs * 8;   // 16-byte chunks per row kept in shared memory
+#pragma unroll 8
+    for (int i = 0; i < kRows * kChunks / 128; ++i) {
+      const int u = ct + 128 * i, r = u / kChunks, c = u % kChunks;
       uint4 v = make_uint4(0u, 0u, 0u, 0u);
-      if (r < p.H) {
-        const uint4 x = *reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p.q) + b * p.q_sb + r * p.q_sh +
-                                                        c8 * 8);
-        v = bf ? make_uint4(bf16x2_to_f16x2(x.x), bf16x2_to_f16x2(x.y), bf16x2_to_f16x2(x.z), bf16x2_to_f16x2(x.w)) : x;
-      }
-      *reinterpret_cast<uint4*>(sm + Smem::q + (c8 >> 3) * kKbQ + swz(r, c8 & 7)) = v;
+      if (r < p.H)
+        v = to_f16x8(*reinterpret_cast<const uint4*>(qrow0 + r * p.q_sh + kQTmemDims + c * 8), q_bf16);
+      *reinterpret_cast<uint4*>(sm + Smem::q + (c >> 3) * kKbQ + swz(r, c & 7)) = v;
     }
     fence_proxy_async();
   }
@@ -281,112 +336,183 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *s_tmem;
   const int n_valid = *s_nvalid;
-  const int tpp = p.PS / kTile;
-  const int T = n_valid * tpp;
+  const int cpp = p.PS / kChunk;     // chunks per page
+  const int T = n_valid * cpp;
   bool timed_out = false;
+  // first latent row of chunk j in its pool
+  auto chunk_row0 = [&](int j) -> int64_t {
+    return static_cast<int64_t>(s_pid[j / cpp]) * p.PS + (j % cpp) * kChunk;
+  };
 
-  if (warp == kTmaWarp) {
-    // ---------------------------------------------------------------- TMA producer
+  if (warp == kPrefWarp) {
+    // ---------------------------------------------------------------- L2 prefetch, paced by the converters
     if (lane == 0) {
-      for (int j = 0; j < T && !timed_out; ++j) {
-        const int s = j % kStages;
-        if (j >= kStages && !mbar_wait(bar(B_EMPTY + s), ((j / kStages) - 1) & 1)) { timed_out = true; break; }
-        const int pg = j / tpp, sub = j % tpp;
-        const int pid = s_pid[pg];
-        const int y = pid * p.PS + sub * kTile;
-        const uint32_t dst = tiles_s + s * kTileBytes;
-        if (s_fmt[pg] == IAK_MLA_FP8) {
-          mbar_arrive_expect_tx(bar(B_FULL + s), kTile * kDqk);
-#pragma unroll
-          for (int part = 0; part < kDqk / kFp8Part; ++part)
-            tma_load_2d(dst + kRawOff + part * kTile * kFp8Part, &fmap, part * kFp8Part, y, bar(B_FULL + s));
-        } else {
-          mbar_arrive_expect_tx(bar(B_FULL + s), kTileBytes);
-#pragma unroll
-          for (int kb = 0; kb < kKBlocks; ++kb) tma_load_2d(dst + kb * kKbTile, &dmap, kb * 64, y, bar(B_FULL + s));
-        }
+      auto prefetch_chunk = [&](int j) {
+        const int64_t row0 = chunk_row0(j);
+        if (s_fmt[j / cpp] == IAK_MLA_FP8)
+          prefetch_l2(p.fp8 + row0 * kDqk, kChunk * kDqk);
+        else
+          prefetch_l2(static_cast<const uint16_t*>(p.dense) + row0 * kDqk, kChunk * kDqk * 2);
+      };
+      for (int j = 0; j < kPrefetchAhead && j < T; ++j) prefetch_chunk(j);
+      for (int j = 0; j + kPrefetchAhead < T; ++j) {
+        // chunk j's value set is stored: the converters have moved past it
+        if (!mbar_wait_sleep(bar(B_VCONV + (j & 1)), (j >> 1) & 1)) { timed_out = true; break; }
+        prefetch_chunk(j + kPrefetchAhead);
       }
     }
-  } else if (warp >= kConvWarp0 && warp < kTmaWarp) {
-    // ---------------------------------------------------------------- converters
+  } else if (warp >= kConvWarp0 && warp < kPrefWarp) {
+    // ---------------------------------------------------------------- converters: global -> f16 -> shared
     const int ct = tid - kConvWarp0 * 32;
     const bool dense_bf16 = p.dense_dtype == IAK_DT_BF16;
-    int n_fp8 = 0;   // FP8 tiles converted so far (phase of B_CREAD)
-    for (int j = 0; j < T && !timed_out; ++j) {
-      const int s = j % kStages;
-      if (!mbar_wait(bar(B_FULL + s), (j / kStages) & 1)) { timed_out = true; break; }
-      const int fmt = s_fmt[j / tpp];
-      uint8_t* tile = sm + Smem::tiles + s * kTileBytes;
-      if (fmt == IAK_MLA_FP8) {
-        // 1152 units of 8 codes (one 16-byte f16 chunk each); read all, then write (in place)
-        uint2 x[9];
+    // FP8: one 16-byte load = 16 codes of a row = two f16 chunks; 256 loads per k-block (2 per thread)
+    // dense: one 16-byte load = one f16 chunk; 512 loads per k-block (4 per thread)
+    auto load_fp8 = [&](const uint8_t* rows, int kb, uint4 (&x)[2]) {
 #pragma unroll
-        for (int i = 0; i < 9; ++i) {
-          const int u = ct + 128 * i, r = u / 72, c8 = u % 72;
-          const int e = c8 * 8;
-          x[i] = *reinterpret_cast<const uint2*>(tile + kRawOff + (e / kFp8Part) * (kTile * kFp8Part) +
-                                                 r * kFp8Part + e % kFp8Part);
-        }
-        // every converter has its codes in registers before any f16 chunk overwrites them
-        mbar_arrive(bar(B_CREAD));
-        if (!mbar_wait(bar(B_CREAD), n_fp8 & 1)) { timed_out = true; break; }
-        ++n_fp8;
+      for (int i = 0; i < 2; ++i) {
+        const int u = ct + 128 * i, r = u >> 2, q = u & 3;
+        x[i] = *reinterpret_cast<const uint4*>(rows + r * kDqk + kb * 64 + q * 16);
+      }
+    };
+    auto store_fp8 = [&](uint32_t off, const uint4 (&x)[2]) {
 #pragma unroll
-        for (int i = 0; i < 9; ++i) {
-          const int u = ct + 128 * i, r = u / 72, c8 = u % 72;
+      for (int i = 0; i < 2; ++i) {
+        const int u = ct + 128 * i, r = u >> 2, q = u & 3;
+        const uint32_t w[4] = {x[i].x, x[i].y, x[i].z, x[i].w};
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
           uint4 v;
-          v.x = e4m3x2_to_f16x2(static_cast<uint16_t>(x[i].x & 0xFFFFu));
-          v.y = e4m3x2_to_f16x2(static_cast<uint16_t>(x[i].x >> 16));
-          v.z = e4m3x2_to_f16x2(static_cast<uint16_t>(x[i].y & 0xFFFFu));
-          v.w = e4m3x2_to_f16x2(static_cast<uint16_t>(x[i].y >> 16));
-          *reinterpret_cast<uint4*>(tile + (c8 >> 3) * kKbTile + swz(r, c8 & 7)) = v;
-        }
-      } else if (dense_bf16) {
-#pragma unroll
-        for (int i = 0; i < 9; ++i) {
-          uint4* c = reinterpret_cast<uint4*>(tile + 16 * (ct + 128 * i));
-          uint4 v = *c;
-          v = make_uint4(bf16x2_to_f16x2(v.x), bf16x2_to_f16x2(v.y), bf16x2_to_f16x2(v.z), bf16x2_to_f16x2(v.w));
-          *c = v;
+          e4m3x4_to_f16(w[2 * h], v.x, v.y);
+          e4m3x4_to_f16(w[2 * h + 1], v.z, v.w);
+          *reinterpret_cast<uint4*>(sm + off + swz(r, 2 * q + h)) = v;
         }
       }
+    };
+    auto load_dense = [&](const uint16_t* rows, int kb, uint4 (&x)[4]) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int u = ct + 128 * i, r = u >> 3, c = u & 7;
+        x[i] = *reinterpret_cast<const uint4*>(rows + r * kDqk + kb * 64 + c * 8);
+      }
+    };
+    auto store_dense = [&](uint32_t off, const uint4 (&x)[4]) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int u = ct + 128 * i, r = u >> 3, c = u & 7;
+        const uint4 y = x[i];
+        *reinterpret_cast<uint4*>(sm + off + swz(r, c)) =
+            dense_bf16 ? make_uint4(bf16x2_to_f16x2(y.x, kTileScale), bf16x2_to_f16x2(y.y, kTileScale),
+                                    bf16x2_to_f16x2(y.z, kTileScale), bf16x2_to_f16x2(y.w, kTileScale))
+                       : make_uint4(f16x2_tile_scale(y.x), f16x2_tile_scale(y.y), f16x2_tile_scale(y.z),
+                                    f16x2_tile_scale(y.w));
+      }
+    };
+    // Per chunk: issue the global loads of every k-block first (FP8: all nine; dense: the five ring
+    // blocks, then the four value blocks), then wait for each destination slot and store.
+    int ring_c = 0;     // ring slot uses so far (5 per chunk)
+    for (int j = 0; j < T && !timed_out; ++j) {
+      const int vs = j & 1;
+      const int pg = j / cpp;
+      const bool fp8 = s_fmt[pg] == IAK_MLA_FP8;
+      const int64_t row0 = static_cast<int64_t>(s_pid[pg]) * p.PS + (j - pg * cpp) * kChunk;
+      auto ring_store = [&](int i, auto&& store) -> bool {
+        const int c = ring_c + i, ks = c % kKSlots;
+        if (c >= kKSlots && !mbar_wait_sleep(bar(B_KEMPTY + ks), ((c / kKSlots) - 1) & 1)) return false;
+        store(kslot(ks));
+        fence_proxy_async();
+        mbar_arrive(bar(B_KCONV + ks));
+        return true;
+      };
+      bool ok = true;
+      if (fp8) {
+        const uint8_t* rows = p.fp8 + row0 * kDqk;
+        uint4 x[kKBlocks][2];
+#pragma unroll
+        for (int i = 0; i < kKBlocks; ++i) load_fp8(rows, chunk_kb(half, i), x[i]);
+#pragma unroll
+        for (int i = 0; i < kKOnly; ++i)
+          if (ok) ok = ring_store(i, [&](uint32_t off) { store_fp8(off, x[i]); });
+        if (ok && j >= 2) ok = mbar_wait_sleep(bar(B_VEMPTY + vs), ((j >> 1) - 1) & 1);
+        if (ok) {
+#pragma unroll
+          for (int i = 0; i < kVBlocks; ++i) store_fp8(vslot(vs, i), x[kKOnly + i]);
+        }
+      } else {
+        const uint16_t* rows = static_cast<const uint16_t*>(p.dense) + row0 * kDqk;
+        {
+          uint4 x[kKOnly][4];
+#pragma unroll
+          for (int i = 0; i < kKOnly; ++i) load_dense(rows, chunk_kb(half, i), x[i]);
+#pragma unroll
+          for (int i = 0; i < kKOnly; ++i)
+            if (ok) ok = ring_store(i, [&](uint32_t off) { store_dense(off, x[i]); });
+        }
+        if (ok) {
+          uint4 x[kVBlocks][4];
+#pragma unroll
+          for (int i = 0; i < kVBlocks; ++i) load_dense(rows, chunk_kb(half, kKOnly + i), x[i]);
+          if (j >= 2) ok = mbar_wait_sleep(bar(B_VEMPTY + vs), ((j >> 1) - 1) & 1);
+          if (ok) {
+#pragma unroll
+            for (int i = 0; i < kVBlocks; ++i) store_dense(vslot(vs, i), x[i]);
+          }
+        }
+      }
+      if (!ok) { timed_out = true; break; }
       fence_proxy_async();
-      mbar_arrive(bar(B_CONV + s));
+      mbar_arrive(bar(B_VCONV + vs));
+      ring_c += kKOnly;
     }
   } else if (warp == kMmaWarp) {
     // ---------------------------------------------------------------- MMA issuer
     if (lane == 0) {
-      constexpr uint32_t kIdS = idesc_f16(kRows, kTile, 0, 0);   // S = Q . C^T
-      constexpr uint32_t kIdPV = idesc_f16(kRows, kHalf, 0, 1);  // O += P . C (C read MN-major)
-      auto issue_s = [&](int j) -> bool {
-        const int s = j % kStages, k = j % kSBuf;
-        if (!mbar_wait(bar(B_CONV + s), (j / kStages) & 1)) return false;
-        if (j >= kSBuf && !mbar_wait(bar(B_PVDONE + k), ((j / kSBuf) - 1) & 1)) return false;
-        tc_fence_after();
-        const uint32_t d = tmem + kSCol + k * kTile;
-        const uint32_t tile = tiles_s + s * kTileBytes;
-#pragma unroll 4
-        for (int ks = 0; ks < kDqk / 16; ++ks) {
-          const uint32_t off = static_cast<uint32_t>(ks & 3) << 5;   // 16 channels = 32 bytes inside the atom
-          const uint64_t a = sw128_desc(q_s + (ks >> 2) * kKbQ + off, 16, 1024);
-          const uint64_t bd = sw128_desc(tile + (ks >> 2) * kKbTile + off, 16, 1024);
-          mma_ss(d, a, bd, kIdS, ks > 0 ? 1u : 0u);
+      constexpr uint32_t kIdS = idesc_f16(kRows, kChunk, 0, 0);  // S = Q . C^T
+      constexpr uint32_t kIdPV = idesc_f16(kRows, kHalf, 0, 1);  // O += P . C (value blocks read MN-major)
+      const uint64_t q_desc0 = sw128_desc(sbase + Smem::q, 16, 1024);
+      // S MMAs over one k-block: A = Q block kb (TMEM for kb < 4, else shared), B = the latent block
+      auto s_block = [&](uint32_t d, int kb, uint32_t blk_off, bool first) {
+        const uint64_t bd = sw128_desc(sbase + blk_off, 16, 1024);
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          const uint32_t acc = (first && t == 0) ? 0u : 1u;
+          if (kb < kQSmemKb0)
+            mma_ts(d, tmem + kQCol + kb * 32 + t * 8, bd + (t * 2), kIdS, acc);
+          else
+            mma_ss(d, q_desc0 + (((kb - kQSmemKb0) * kKbQ + t * 32) >> 4), bd + (t * 2), kIdS, acc);
         }
+      };
+      if (!mbar_wait(bar(B_QREADY), 0)) timed_out = true;
+      auto issue_s = [&](int j) -> bool {
+        const int k = j & 1, vs = j & 1;
+        if (j >= kSBuf && !mbar_wait(bar(B_PVDONE + k), ((j >> 1) - 1) & 1)) return false;
+        const uint32_t d = tmem + kSCol + k * kChunk;
+        for (int i = 0; i < kKOnly; ++i) {
+          const int c = kKOnly * j + i, ks = c % kKSlots;
+          if (!mbar_wait(bar(B_KCONV + ks), (c / kKSlots) & 1)) return false;
+          tc_fence_after();
+          s_block(d, chunk_kb(half, i), kslot(ks), i == 0);
+          mma_commit(bar(B_KEMPTY + ks));
+        }
+        if (!mbar_wait(bar(B_VCONV + vs), (j >> 1) & 1)) return false;
+        tc_fence_after();
+        for (int i = 0; i < kVBlocks; ++i) s_block(d, chunk_kb(half, kKOnly + i), vslot(vs, i), false);
         mma_commit(bar(B_SFULL + k));
         return true;
       };
       auto issue_pv = [&](int j) -> bool {
-        const int s = j % kStages, k = j % kSBuf;
-        if (!mbar_wait(bar(B_PFULL + k), (j / kSBuf) & 1)) return false;
+        const int k = j & 1, vs = j & 1;
+        if (!mbar_wait(bar(B_PFULL + k), (j >> 1) & 1)) return false;
         tc_fence_after();
-        const uint32_t tile = tiles_s + s * kTileBytes;
-        const uint64_t bd = sw128_desc(tile + half * (kHalf / 64) * kKbTile, kKbTile, 1024);
-        mma_ts(tmem + kOCol, tmem + kSCol + k * kTile, bd, kIdPV, j > 0 ? 1u : 0u);
+        const uint64_t bd = sw128_desc(sbase + vslot(vs, 0), kKb, 1024);
+#pragma unroll
+        for (int t = 0; t < kChunk / 16; ++t)
+          mma_ts(tmem + kOCol, tmem + kSCol + k * kChunk + t * 8, bd + ((t * 2048) >> 4), kIdPV,
+                 (j > 0 || t > 0) ? 1u : 0u);
         mma_commit(bar(B_PVDONE + k));
-        mma_commit(bar(B_EMPTY + s));
+        mma_commit(bar(B_VEMPTY + vs));
         return true;
       };
-      if (T > 0 && !issue_s(0)) timed_out = true;
+      if (!timed_out && T > 0 && !issue_s(0)) timed_out = true;
       for (int j = 0; j < T && !timed_out; ++j) {
         if (j + 1 < T && !issue_s(j + 1)) { timed_out = true; break; }
         if (!issue_pv(j)) { timed_out = true; break; }
@@ -399,34 +525,57 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------------------------------------------------------- softmax (warps 0-3, one head row per thread)
     const int r = tid;                                   // TMEM lane = head row
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(warp * 32) << 16);
-    const float base_scale = p.sm_scale * kLog2e;
+    {
+      // Q channels [0, 256) of this row into TMEM columns kQCol.. (f16 pairs), the A operand of S
+      const uint16_t* qr = qrow0 + r * p.q_sh;
+#pragma unroll 1
+      for (int c = 0; c < kQTmemCols / 32; ++c) {
+        uint32_t v[32];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          uint4 x = make_uint4(0u, 0u, 0u, 0u);
+          if (r < p.H) x = to_f16x8(*reinterpret_cast<const uint4*>(qr + c * 64 + i * 8), q_bf16);
+          v[4 * i] = x.x; v[4 * i + 1] = x.y; v[4 * i + 2] = x.z; v[4 * i + 3] = x.w;
+        }
+        tmem_st32(lane_addr + kQCol + c * 32, v);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(bar(B_QREADY));
+    }
+    const float base_scale = p.sm_scale * kLog2e / kTileScale;
     float m_used = -INFINITY, l = 0.f;
     for (int j = 0; j < T && !timed_out; ++j) {
-      const int k = j % kSBuf;
+      const int k = j & 1;
       // warp-uniform outcome: the TMEM loads below are warp-collective
-      if (!__all_sync(0xffffffffu, mbar_wait(bar(B_SFULL + k), (j / kSBuf) & 1))) { timed_out = true; break; }
+      // one lane polls; the outcome is broadcast (warp-uniform: the TMEM loads below are warp-collective)
+      bool ok = true;
+      if (lane == 0) ok = mbar_wait_sleep(bar(B_SFULL + k), (j >> 1) & 1);
+      if (!__shfl_sync(0xffffffffu, ok, 0)) { timed_out = true; break; }
       tc_fence_after();
-      uint32_t sr[16];
-      tmem_ld16(lane_addr + kSCol + k * kTile, sr);
-      tmem_wait_ld();
-      const int pg = j / tpp;
-      // FP8 tiles hold codes: the page scale multiplies the scores (key side)
+      // FP8 latents hold codes: the page scale multiplies the scores (key side)
       // and P (value side); l stays in unscaled softmax weights
-      const float vs = s_fmt[pg] == IAK_MLA_FP8 ? p.fp8_scale[s_pid[pg]] : 1.f;
+      const float vs = s_scale[j / cpp];
       const float sc = base_scale * vs;
-      float x[16], tmax = -INFINITY;
+      float x[kChunk], tmax = -INFINITY;
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        x[i] = __uint_as_float(sr[i]) * sc;
-        tmax = fmaxf(tmax, x[i]);
+      for (int h2 = 0; h2 < 2; ++h2) {
+        uint32_t sr[32];
+        tmem_ld32(lane_addr + kSCol + k * kChunk + h2 * 32, sr);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          x[h2 * 32 + i] = __uint_as_float(sr[i]) * sc;
+          tmax = fmaxf(tmax, x[h2 * 32 + i]);
+        }
       }
       if (j == 0) {
         m_used = tmax;
       } else {
         const bool need = tmax > m_used + kLazyLog2;
         if (__any_sync(0xffffffffu, need)) {
-          // rescale O_h in TMEM: every earlier PV must have landed
-          if (!__all_sync(0xffffffffu, mbar_wait(bar(B_PVDONE + (j - 1) % kSBuf), ((j - 1) / kSBuf) & 1))) {
+          // rescale O_h in TMEM: every earlier P.V must have landed
+          if (!__all_sync(0xffffffffu, mbar_wait_sleep(bar(B_PVDONE + ((j - 1) & 1)), ((j - 1) >> 1) & 1))) {
             timed_out = true;
             break;
           }
@@ -437,28 +586,28 @@ __global__ void __launch_bounds__(kThreads, 1)
             m_used = tmax;
           }
 #pragma unroll 1
-          for (int c = 0; c < kHalf / 16; ++c) {
-            uint32_t o[16];
-            tmem_ld16(lane_addr + kOCol + c * 16, o);
+          for (int c = 0; c < kHalf / 32; ++c) {
+            uint32_t o[32];
+            tmem_ld32(lane_addr + kOCol + c * 32, o);
             tmem_wait_ld();
 #pragma unroll
-            for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * f);
-            tmem_st16(lane_addr + kOCol + c * 16, o);
+            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * f);
+            tmem_st32(lane_addr + kOCol + c * 32, o);
           }
           tmem_wait_st();
         }
       }
-      uint32_t pk[8];
+      uint32_t pk[kChunk / 2];
       float lsum = 0.f;
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
+      for (int i = 0; i < kChunk / 2; ++i) {
         const float p0 = exp2f(x[2 * i] - m_used), p1 = exp2f(x[2 * i + 1] - m_used);
         lsum += p0 + p1;
         const __half2 h = __floats2half2_rn(p0 * vs, p1 * vs);
         pk[i] = *reinterpret_cast<const uint32_t*>(&h);
       }
       l += lsum;
-      tmem_st8(lane_addr + kSCol + k * kTile, pk);
+      tmem_st32(lane_addr + kSCol + k * kChunk, pk);
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(bar(B_PFULL + k));
@@ -466,7 +615,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------------------------------------------------------- epilogue
     bool have = T > 0 && !timed_out;
     if (have) {
-      if (!__all_sync(0xffffffffu, mbar_wait(bar(B_PVDONE + (T - 1) % kSBuf), ((T - 1) / kSBuf) & 1))) {
+      if (!__all_sync(0xffffffffu, mbar_wait(bar(B_PVDONE + ((T - 1) & 1)), ((T - 1) >> 1) & 1))) {
         timed_out = true;
         have = false;
       }
@@ -474,7 +623,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     const bool row_ok = r < p.H;
     const int64_t row = static_cast<int64_t>(b) * p.H + r;
-    const float inv = l > 0.f ? 1.f / l : 0.f;
+    const float inv = l > 0.f ? 1.f / (l * kTileScale) : 0.f;   // O holds values * 2^-8
     const float m_nat = l > 0.f ? m_used * kLn2 : -INFINITY;
     float* acc_dst = nullptr;
     if (S > 1) {
@@ -492,26 +641,26 @@ __global__ void __launch_bounds__(kThreads, 1)
       acc_dst = p.ex_acc + row * p.Dv;
     }
 #pragma unroll 1
-    for (int c = 0; c < kHalf / 16; ++c) {
-      uint32_t o[16];
+    for (int c = 0; c < kHalf / 32; ++c) {
+      uint32_t o[32];
       if (have) {
-        tmem_ld16(lane_addr + kOCol + c * 16, o);
+        tmem_ld32(lane_addr + kOCol + c * 32, o);
         tmem_wait_ld();
       } else {
 #pragma unroll
-        for (int i = 0; i < 16; ++i) o[i] = 0u;
+        for (int i = 0; i < 32; ++i) o[i] = 0u;
       }
       if (!row_ok) continue;
-      const int d0 = half * kHalf + c * 16;
+      const int d0 = half * kHalf + c * 32;
       if (acc_dst) {
 #pragma unroll
-        for (int i = 0; i < 16; i += 4)
+        for (int i = 0; i < 32; i += 4)
           *reinterpret_cast<float4*>(acc_dst + d0 + i) =
-              make_float4(__uint_as_float(o[i]), __uint_as_float(o[i + 1]), __uint_as_float(o[i + 2]),
-                          __uint_as_float(o[i + 3]));
+              make_float4(__uint_as_float(o[i]) / kTileScale, __uint_as_float(o[i + 1]) / kTileScale,
+                          __uint_as_float(o[i + 2]) / kTileScale, __uint_as_float(o[i + 3]) / kTileScale);
       } else {
 #pragma unroll
-        for (int i = 0; i < 16; ++i)
+        for (int i = 0; i < 32; ++i)
           store_from_float(p.out, p.out_dtype, b * p.o_sb + r * p.o_sh + d0 + i, __uint_as_float(o[i]) * inv);
       }
     }
@@ -526,72 +675,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (timed_out) atomicAdd(&g_mla_timeouts, 1u);
 }
 
-// --------------------------------------------------------- tensor maps ---
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* q = nullptr;
-    cudaDriverEntryPointQueryResult res;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &q, cudaEnableDefault, &res) == cudaSuccess &&
-        res == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(q);
-  });
-  return fn;
-}
-
-// [rows, 576] latent rows: dense 16-bit (box 64 x 16, 128-byte swizzle) or FP8 bytes (box 192 x 16, no swizzle).
-int make_latent_map(CUtensorMap* m, const void* base, int kind, int64_t rows) {
-  auto fn = encode_fn();
-  if (!fn) return fail(IAK_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
-  const bool fp8 = kind == 2;
-  const CUtensorMapDataType dt =
-      fp8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : (kind == 1 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16);
-  const uint64_t eb = fp8 ? 1 : 2;
-  cuuint64_t dims[2] = {static_cast<cuuint64_t>(kDqk), static_cast<cuuint64_t>(rows)};
-  cuuint64_t strides[1] = {static_cast<cuuint64_t>(kDqk * eb)};
-  cuuint32_t box[2] = {fp8 ? static_cast<cuuint32_t>(kFp8Part) : 64u, static_cast<cuuint32_t>(kTile)};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = fn(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                  fp8 ? CU_TENSOR_MAP_SWIZZLE_NONE : CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return fail(IAK_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
-  return IAK_OK;
-}
-
-int cached_latent_map(CUtensorMap* out, const void* base, int kind, int64_t rows) {
-  struct Key {
-    const void* base; int kind; int64_t rows;
-    bool operator==(const Key& o) const { return base == o.base && kind == o.kind && rows == o.rows; }
-  };
-  struct Hash {
-    size_t operator()(const Key& k) const {
-      return std::hash<const void*>()(k.base) ^ (static_cast<size_t>(k.rows) * 2654435761u) ^ k.kind;
-    }
-  };
-  static std::mutex mu;
-  static std::unordered_map<Key, CUtensorMap, Hash> cache;
-  const Key key{base, kind, rows};
-  {
-    std::lock_guard<std::mutex> lock(mu);
-    auto it = cache.find(key);
-    if (it != cache.end()) {
-      *out = it->second;
-      return IAK_OK;
-    }
-  }
-  const int st = make_latent_map(out, base, kind, rows);
-  if (st) return st;
-  std::lock_guard<std::mutex> lock(mu);
-  if (cache.size() > 64) cache.clear();
-  cache.emplace(key, *out);
-  return IAK_OK;
-}
-
 }  // namespace
 
 bool mla_tc_eligible(const MlaParams& p) {
-  if (p.Dqk != kDqk || p.Dv != kDv || p.H > kRows || p.PS % kTile) return false;
+  if (p.Dqk != kDqk || p.Dv != kDv || p.H > kRows || p.PS % kChunk) return false;
   if (p.q_dtype != IAK_DT_BF16 && p.q_dtype != IAK_DT_F16) return false;
   if (reinterpret_cast<uintptr_t>(p.q) % 16 || p.q_sb % 8 || p.q_sh % 8) return false;
   if (p.dense && ((p.dense_dtype != IAK_DT_BF16 && p.dense_dtype != IAK_DT_F16) ||
@@ -630,19 +717,6 @@ void plan_mla_tc(MlaParams* p, int requested) {
 }
 
 int launch_mla_tc(const MlaParams& p, cudaStream_t s) {
-  CUtensorMap dmap, fmap;
-  std::memset(&dmap, 0, sizeof(dmap));
-  std::memset(&fmap, 0, sizeof(fmap));
-  const int64_t rows = p.num_pages * p.PS;
-  if (rows <= 0) return fail(IAK_ERR_INVALID_ARG, "empty latent pool");
-  if (p.dense) {
-    const int st = cached_latent_map(&dmap, p.dense, p.dense_dtype == IAK_DT_BF16 ? 1 : 0, rows);
-    if (st) return st;
-  }
-  if (p.fp8) {
-    const int st = cached_latent_map(&fmap, p.fp8, 2, rows);
-    if (st) return st;
-  }
   const int64_t items = static_cast<int64_t>(p.B) * p.num_splits * 2;
   if (items > 0x7FFFFFFF) return fail(IAK_ERR_UNSUPPORTED, "too many MLA work items");
   const size_t smem = Smem::total + 1024;
@@ -660,7 +734,7 @@ int launch_mla_tc(const MlaParams& p, cudaStream_t s) {
     }
   }
   kernel_timer_begin(s);
-  mla_tc_kernel<<<static_cast<unsigned>(items), kThreads, smem, s>>>(p, dmap, fmap);
+  mla_tc_kernel<<<static_cast<unsigned>(items), kThreads, smem, s>>>(p);
   err = cudaGetLastError();
   kernel_timer_end(s);
   return check_cuda(err, "mla_tc launch");

@@ -74,8 +74,8 @@ def test_tensor_kernel_fewer_heads(H):
     _close(run(case, "tensor"), case["oracle"](1.0 / np.sqrt(576)))
 
 
-def test_tensor_kernel_f16_pages_and_q_and_page_size_16():
-    case = make_mla_case(31, B=2, PS=16, NP=200, W=40, dense_dtype=torch.float16, q_dtype=torch.float16)
+def test_tensor_kernel_f16_pages_and_q_and_page_size_128():
+    case = make_mla_case(31, B=2, PS=128, NP=40, W=12, dense_dtype=torch.float16, q_dtype=torch.float16)
     _close(run(case, "tensor"), case["oracle"](1.0 / np.sqrt(576)))
 
 
@@ -129,6 +129,11 @@ def test_tensor_kernel_rejects_other_shapes():
     case = make_mla_case(91, B=1, H=8, Dqk=128, Dv=128, PS=16, NP=10, W=4)
     with pytest.raises(RuntimeError, match="tensor-core MLA"):
         run(case, "tensor")
+    case = make_mla_case(92, B=1, H=8, PS=32, NP=10, W=4)      # pages must hold whole 64-token chunks
+    with pytest.raises(RuntimeError, match="tensor-core MLA"):
+        run(case, "tensor")
+    # the automatic choice falls back to the CUDA-core kernel for such shapes
+    _close(run(case), case["oracle"](1.0 / np.sqrt(576)))
 
 
 # --------------------------------------------------------------- CUDA-core kernel
