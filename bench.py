@@ -328,7 +328,7 @@ def run_gpu(args):
     pool, table, counts, tags, q = build_gpu_workload(w, ids, fmt, device, 0 if seq_shard else rank)
     tag_map = make_tag_map({c: (f if f in w["mix"] else "SKIP") for f, c in FMT_CODE.items()})
     out = torch.empty(q.shape, dtype=torch.bfloat16, device=device)
-    decoder = SequenceShardedDecoder() if seq_shard else None
+    decoder = SequenceShardedDecoder(transport=args.exchange) if seq_shard else None
 
     def decode(q_, table_, counts_):
         if decoder is not None:
@@ -416,7 +416,8 @@ def run_gpu(args):
 
     # tensor-core path (forced above, so an ineligible shape fails loudly): query-table preparation,
     # the persistent decode kernel and the LSE merge
-    launches_per_step = 3 + (1 if seq_shard else 0)   # + merge of the gathered partial blocks
+    # + for sequence shards: the block merge (NCCL), or push + bounded wait + block merge (peer stores)
+    launches_per_step = 3 + ((3 if args.exchange == "p2p" else 1) if seq_shard else 0)
     if world > 1:
         t = torch.tensor([kernel_ms], device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -441,7 +442,10 @@ def run_gpu(args):
                        "selected_kv_bytes_per_step_per_gpu": nbytes,
                        "l2": f"inputs larger than L2 ({nbytes / 1e9:.2f} GB of selected KV per step)",
                        "parallelism": (f"sp{world} (each sequence's selected pages cut into {world} ranges; partial "
-                                       "(m, l, acc) blocks all-gathered over NCCL, LSE-merged on every rank)")
+                                       "(m, l, acc) blocks exchanged "
+                                       + ("by NVLink peer stores with epoch flags (CUDA IPC)" if args.exchange == "p2p"
+                                          else "with one NCCL all-gather")
+                                       + ", LSE-merged on every rank)")
                        if seq_shard else f"dp{world} (batch shards, no collective on the data path)"},
             "roofline": {"bound": "hbm", "achieved": round(kernel_gbs, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(kernel_gbs / peak, 4), "traffic": traffic,
@@ -466,6 +470,11 @@ def run_gpu(args):
                                    "sample": f"{units} of {w['B'] * w['Hkv']} (sequence, kv-head) units timed with the "
                                              "numpy oracle decode, extrapolated linearly to the full step"}
         print(json.dumps(rec), flush=True)
+    if decoder is not None:
+        if decoder._x is not None:
+            decoder._x.check()
+        dist.barrier()
+        decoder.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -771,6 +780,8 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--splits", type=int, default=0)
     ap.add_argument("--batch", type=int, default=0, help="override the workload's batch (profiling runs)")
+    ap.add_argument("--exchange", default="p2p", choices=["p2p", "nccl"],
+                    help="C5 on several GPUs: partial blocks over NVLink peer stores or one NCCL all-gather")
     ap.add_argument("--cpu-budget", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()

@@ -6,8 +6,10 @@
  * CUDA types (a CUDA stream is passed as `void*`, NULL = legacy default
  * stream).  Every entry point returns an iak_status; on failure
  * iak_last_error() returns a thread-local message.  Entry points never
- * allocate device memory and never synchronise the stream; they are
- * reentrant across devices (the current CUDA device is used).
+ * allocate device memory and never synchronise the stream (exceptions: the
+ * iak_ipc_* helpers, which exist to allocate and map exchange areas, and
+ * iak_kernel_timer_read); they are reentrant across devices (the current
+ * CUDA device is used).
  *
  * Reference interfaces replaced (manishklach/intent-attention-kernel,
  * paths inside src/intent_attention/):
@@ -239,6 +241,52 @@ int iak_merge_partials(const float* m, const float* l, const float* acc,
  * rows without pages anywhere become 0. */
 int iak_merge_partial_blocks(const float* blocks, int32_t num_parts, int64_t rows, int32_t head_dim,
                              void* out, int32_t out_dtype, int64_t out_row_stride, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Peer-memory exchange of partial blocks (multi-GPU split-KV over NVLink).
+ * No counterpart in the reference.  Replaces a collective all-gather of the
+ * blocks with stores straight into the peers' memory.
+ *
+ * Every rank owns an exchange area in its own device memory
+ * (iak_exchange_area_bytes): for each of two parities, a receive array of
+ * `world` partial blocks and `world` uint32 arrival flags.  The areas are
+ * allocated with iak_ipc_alloc and shared once through their 64-byte CUDA IPC
+ * handles (iak_ipc_open in every other rank), so each rank can write every
+ * peer's area.  Per step, with a host epoch counter starting at 1 and
+ * parity = epoch & 1:
+ *   1. decode with partial export into this rank's own slot
+ *      (iak_exchange_block_ptr(area, ..., parity, rank));
+ *   2. iak_exchange_push: copy that block into slot `rank` of every peer's
+ *      area, then raise those areas' flag[parity][rank] to epoch;
+ *   3. iak_exchange_merge: wait until every flag[parity][*] of this rank's
+ *      area equals epoch (bounded by timeout_us; on expiry *status becomes 1
+ *      and out is not written), then LSE-merge the world blocks into out.
+ * Two parities let a rank run one step ahead without overwriting blocks a
+ * slower peer is still merging.  All ranks must call the three steps every
+ * step, in the same order.
+ * ------------------------------------------------------------------------ */
+#define IAK_MAX_PEERS 8
+typedef struct iak_peer_exchange {
+  void* areas[IAK_MAX_PEERS];     /* rank r's exchange area as mapped in this process */
+  int32_t rank, world;
+  int64_t rows;                   /* batch * num_q_heads                            */
+  int32_t head_dim;               /* block = rows * (head_dim + 2) floats           */
+} iak_peer_exchange;
+
+int iak_exchange_area_bytes(int32_t world, int64_t rows, int32_t head_dim, size_t* bytes);
+/* Address of block `slot` of `parity` inside an exchange area. */
+float* iak_exchange_block_ptr(void* area, int32_t world, int64_t rows, int32_t head_dim, int32_t parity,
+                              int32_t slot);
+int iak_exchange_push(const iak_peer_exchange* x, uint32_t epoch, void* stream);
+int iak_exchange_merge(const iak_peer_exchange* x, uint32_t epoch, void* out, int32_t out_dtype,
+                       int64_t out_row_stride, uint32_t* status, uint32_t timeout_us, void* stream);
+
+/* CUDA IPC helpers (device memory of the current device; handle = 64 bytes).
+ * iak_ipc_alloc zero-fills the allocation. */
+int iak_ipc_alloc(size_t bytes, void** ptr, void* handle);
+int iak_ipc_open(const void* handle, void** ptr);
+int iak_ipc_close(void* ptr);
+int iak_ipc_free(void* ptr);
 
 /* Metadata packing on the device.  Logical page ids (one list shared by
  * every (b, h), the router's selected_page_ids order) are mapped to

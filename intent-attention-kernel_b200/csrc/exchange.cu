@@ -1,0 +1,207 @@
+// Peer-memory exchange of partial blocks for multi-GPU split-KV decode, and
+// the CUDA IPC helpers that map the ranks' exchange areas into each process.
+//
+// Area of one rank (device memory of its GPU), for world W and block size
+// BF = rows * (head_dim + 2) floats padded to BS (a multiple of 64 floats):
+//   float  blocks[2][W][BS]      receive arrays, one per parity
+//   uint32 flags[2][W]           arrival epoch of each sender, per parity
+//   uint32 push_count[2]         CTAs of this rank's push kernel that finished
+// A rank's push writes its block into slot `rank` of every peer's
+// blocks[parity] with plain stores over NVLink, then (after a system-scope
+// fence, from the last CTA to finish) raises flag[parity][rank] = epoch in
+// every area.  The merge waits, bounded in time, for all W flags of its own
+// area and then LSE-merges the W blocks.
+#include <algorithm>
+#include <cstring>
+
+#include "iak_internal.cuh"
+
+namespace iak {
+namespace {
+
+constexpr int kPushThreads = 256;
+
+__host__ __device__ inline int64_t block_stride(int64_t rows, int D) {
+  const int64_t bf = rows * (static_cast<int64_t>(D) + 2);
+  return (bf + 63) / 64 * 64;
+}
+__host__ __device__ inline size_t flags_offset(int world, int64_t rows, int D) {
+  return static_cast<size_t>(2) * world * block_stride(rows, D) * sizeof(float);
+}
+
+struct PushParams {
+  float* areas[IAK_MAX_PEERS];
+  int rank, world;
+  int64_t bs;        // block stride (floats)
+  int64_t n4;        // float4 per block copy
+  size_t flags_off;  // byte offset of flags in an area
+  int parity;
+  uint32_t epoch;
+};
+
+__device__ __forceinline__ uint32_t* area_flags(float* area, size_t off) {
+  return reinterpret_cast<uint32_t*>(reinterpret_cast<char*>(area) + off);
+}
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+__global__ void __launch_bounds__(kPushThreads) push_kernel(const PushParams p) {
+  float* own = p.areas[p.rank];
+  const float4* src = reinterpret_cast<const float4*>(own + (static_cast<int64_t>(p.parity) * p.world + p.rank) * p.bs);
+  for (int r = 0; r < p.world; ++r) {
+    if (r == p.rank) continue;
+    float4* dst = reinterpret_cast<float4*>(p.areas[r] + (static_cast<int64_t>(p.parity) * p.world + p.rank) * p.bs);
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < p.n4;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+      dst[i] = src[i];
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    uint32_t* count = area_flags(own, p.flags_off) + 2 * p.world + p.parity;
+    if (atomicAdd(count, 1u) == gridDim.x - 1) {
+      // every CTA's stores are fenced: publish the block to every rank
+      *count = 0u;
+      __threadfence_system();
+      for (int r = 0; r < p.world; ++r)
+        st_release_sys(area_flags(p.areas[r], p.flags_off) + p.parity * p.world + p.rank, p.epoch);
+    }
+  }
+}
+
+// One thread waits (bounded by timeout_ns of wall time) for every sender's flag.
+__global__ void wait_kernel(const uint32_t* flags, int world, uint32_t epoch, uint32_t* status, uint64_t timeout_ns) {
+  if (threadIdx.x != 0) return;
+  const uint64_t t0 = global_ns();
+  for (int r = 0; r < world; ++r) {
+    unsigned ns = 64;
+    while (ld_acquire_sys(flags + r) != epoch) {
+      if (global_ns() - t0 > timeout_ns) {
+        if (status) atomicExch(status, 1u);
+        return;
+      }
+      __nanosleep(ns);
+      if (ns < 1024) ns <<= 1;
+    }
+  }
+}
+
+int check_exchange(const iak_peer_exchange* x) {
+  if (!x) return fail(IAK_ERR_INVALID_ARG, "null exchange descriptor");
+  if (x->world < 1 || x->world > IAK_MAX_PEERS) return fail(IAK_ERR_INVALID_ARG, "world %d outside 1..%d", x->world, IAK_MAX_PEERS);
+  if (x->rank < 0 || x->rank >= x->world) return fail(IAK_ERR_INVALID_ARG, "rank %d outside world %d", x->rank, x->world);
+  if (x->rows < 0 || x->head_dim <= 0) return fail(IAK_ERR_INVALID_ARG, "bad block shape");
+  for (int r = 0; r < x->world; ++r)
+    if (!x->areas[r] || reinterpret_cast<uintptr_t>(x->areas[r]) % 256)
+      return fail(IAK_ERR_INVALID_ARG, "exchange area of rank %d is NULL or not 256-byte aligned", r);
+  return IAK_OK;
+}
+
+}  // namespace
+}  // namespace iak
+
+using namespace iak;
+
+extern "C" {
+
+int iak_exchange_area_bytes(int32_t world, int64_t rows, int32_t head_dim, size_t* bytes) {
+  if (!bytes) return fail(IAK_ERR_INVALID_ARG, "bytes is NULL");
+  if (world < 1 || world > IAK_MAX_PEERS || rows < 0 || head_dim <= 0) return fail(IAK_ERR_INVALID_ARG, "bad exchange shape");
+  *bytes = flags_offset(world, rows, head_dim) + 256;
+  return IAK_OK;
+}
+
+float* iak_exchange_block_ptr(void* area, int32_t world, int64_t rows, int32_t head_dim, int32_t parity, int32_t slot) {
+  if (!area || world < 1 || parity < 0 || parity > 1 || slot < 0 || slot >= world) return nullptr;
+  return static_cast<float*>(area) + (static_cast<int64_t>(parity) * world + slot) * block_stride(rows, head_dim);
+}
+
+int iak_exchange_push(const iak_peer_exchange* x, uint32_t epoch, void* stream) {
+  int st = check_exchange(x);
+  if (st) return st;
+  if (epoch == 0) return fail(IAK_ERR_INVALID_ARG, "epoch must be >= 1 (flags start at 0)");
+  PushParams p;
+  std::memset(&p, 0, sizeof(p));
+  for (int r = 0; r < x->world; ++r) p.areas[r] = static_cast<float*>(x->areas[r]);
+  p.rank = x->rank; p.world = x->world;
+  p.bs = block_stride(x->rows, x->head_dim);
+  p.n4 = (x->rows * (static_cast<int64_t>(x->head_dim) + 2) + 3) / 4;
+  p.flags_off = flags_offset(x->world, x->rows, x->head_dim);
+  p.parity = static_cast<int>(epoch & 1u);
+  p.epoch = epoch;
+  const int64_t want = (p.n4 + kPushThreads - 1) / kPushThreads;
+  const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(want, device_sm_count())));
+  push_kernel<<<grid, kPushThreads, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  return check_cuda(cudaGetLastError(), "exchange push launch");
+}
+
+int iak_exchange_merge(const iak_peer_exchange* x, uint32_t epoch, void* out, int32_t out_dtype, int64_t out_row_stride,
+                       uint32_t* status, uint32_t timeout_us, void* stream) {
+  int st = check_exchange(x);
+  if (st) return st;
+  if (epoch == 0) return fail(IAK_ERR_INVALID_ARG, "epoch must be >= 1");
+  if (!out) return fail(IAK_ERR_INVALID_ARG, "out is NULL");
+  if (out_dtype < 0 || out_dtype > 2) return fail(IAK_ERR_INVALID_ARG, "bad out dtype");
+  if (out_row_stride < x->head_dim) return fail(IAK_ERR_INVALID_ARG, "out_row_stride < head_dim");
+  if (x->rows == 0) return IAK_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int parity = static_cast<int>(epoch & 1u);
+  float* own = static_cast<float*>(x->areas[x->rank]);
+  const size_t foff = flags_offset(x->world, x->rows, x->head_dim);
+  const uint32_t* flags = reinterpret_cast<const uint32_t*>(reinterpret_cast<char*>(own) + foff) + parity * x->world;
+  wait_kernel<<<1, 32, 0, s>>>(flags, x->world, epoch, status, static_cast<uint64_t>(timeout_us) * 1000ull);
+  st = check_cuda(cudaGetLastError(), "exchange wait launch");
+  if (st) return st;
+  const int64_t bs = block_stride(x->rows, x->head_dim);
+  const float* blocks = own + static_cast<int64_t>(parity) * x->world * bs;
+  return launch_merge_strided(blocks, blocks + x->rows, blocks + 2 * x->rows, 1, bs, x->head_dim, bs, x->rows,
+                              x->world, x->head_dim, out, out_dtype, out_row_stride, nullptr, nullptr, nullptr,
+                              nullptr, s);
+}
+
+int iak_ipc_alloc(size_t bytes, void** ptr, void* handle) {
+  if (!ptr || !handle || bytes == 0) return fail(IAK_ERR_INVALID_ARG, "bad ipc alloc arguments");
+  *ptr = nullptr;
+  cudaError_t e = cudaMalloc(ptr, bytes);
+  if (e != cudaSuccess) return check_cuda(e, "ipc cudaMalloc");
+  e = cudaMemset(*ptr, 0, bytes);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(static_cast<cudaIpcMemHandle_t*>(handle), *ptr);
+  if (e != cudaSuccess) {
+    cudaFree(*ptr);
+    *ptr = nullptr;
+    return check_cuda(e, "ipc handle");
+  }
+  return IAK_OK;
+}
+
+int iak_ipc_open(const void* handle, void** ptr) {
+  if (!ptr || !handle) return fail(IAK_ERR_INVALID_ARG, "bad ipc open arguments");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  return check_cuda(cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle");
+}
+
+int iak_ipc_close(void* ptr) {
+  if (!ptr) return IAK_OK;
+  return check_cuda(cudaIpcCloseMemHandle(ptr), "cudaIpcCloseMemHandle");
+}
+
+int iak_ipc_free(void* ptr) {
+  if (!ptr) return IAK_OK;
+  return check_cuda(cudaFree(ptr), "ipc cudaFree");
+}
+
+}  // extern "C"

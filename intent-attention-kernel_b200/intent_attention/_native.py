@@ -92,6 +92,13 @@ class MlaArgs(ctypes.Structure):
 
 MLA_SKIP, MLA_DENSE, MLA_FP8 = 0, 1, 2
 
+MAX_PEERS = 8
+
+
+class PeerExchange(ctypes.Structure):
+    _fields_ = [("areas", c_void_p * MAX_PEERS), ("rank", c_i32), ("world", c_i32), ("rows", c_i64),
+                ("head_dim", c_i32)]
+
 
 # name -> (restype, argtypes); mirrors every declaration of the public header
 SIGNATURES = {
@@ -109,6 +116,15 @@ SIGNATURES = {
     "iak_merge_partial_blocks": (ctypes.c_int, [c_void_p, c_i32, c_i64, c_i32, c_void_p, c_i32, c_i64, c_void_p]),
     "iak_mla_workspace_size": (ctypes.c_int, [ctypes.POINTER(MlaArgs), ctypes.POINTER(ctypes.c_size_t)]),
     "iak_mla_decode": (ctypes.c_int, [ctypes.POINTER(MlaArgs), c_void_p, ctypes.c_size_t, c_void_p]),
+    "iak_exchange_area_bytes": (ctypes.c_int, [c_i32, c_i64, c_i32, ctypes.POINTER(ctypes.c_size_t)]),
+    "iak_exchange_block_ptr": (c_void_p, [c_void_p, c_i32, c_i64, c_i32, c_i32, c_i32]),
+    "iak_exchange_push": (ctypes.c_int, [ctypes.POINTER(PeerExchange), ctypes.c_uint32, c_void_p]),
+    "iak_exchange_merge": (ctypes.c_int, [ctypes.POINTER(PeerExchange), ctypes.c_uint32, c_void_p, c_i32, c_i64,
+                                          c_void_p, ctypes.c_uint32, c_void_p]),
+    "iak_ipc_alloc": (ctypes.c_int, [ctypes.c_size_t, ctypes.POINTER(c_void_p), c_void_p]),
+    "iak_ipc_open": (ctypes.c_int, [c_void_p, ctypes.POINTER(c_void_p)]),
+    "iak_ipc_close": (ctypes.c_int, [c_void_p]),
+    "iak_ipc_free": (ctypes.c_int, [c_void_p]),
     "iak_kernel_timer_enable": (ctypes.c_int, [c_i32]),
     "iak_kernel_timer_read": (ctypes.c_int, [ctypes.POINTER(ctypes.c_double), ctypes.POINTER(c_i32)]),
     "iak_kernel_timer_disable": (ctypes.c_int, []),

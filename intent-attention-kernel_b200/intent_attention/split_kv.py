@@ -14,7 +14,10 @@ Block layout (``IAK_PARTIAL_BLOCK_FLOATS`` in the C header):
 ``[m: rows][l: rows][acc: rows x D]`` with rows = B * Hq, row = b * Hq + h.
 
 The decode and merge run in libiak_b200.so; this module only cuts page
-lists, allocates blocks and drives the exchange.  ``shard_bounds``,
+lists, allocates blocks and drives the exchange: either one NCCL all-gather
+(``transport="nccl"``) or stores straight into the peers' exchange areas over
+NVLink with epoch flags and a bounded wait (``transport="p2p"``, CUDA IPC,
+``PeerExchange``).  ``shard_bounds``,
 ``block_views`` and ``shard_page_lists`` are plain index helpers that also
 run on CPU tensors.
 """
@@ -117,6 +120,101 @@ def merge_partial_blocks(blocks: torch.Tensor, rows: int, head_dim: int,
     return out
 
 
+class _DeviceArray:
+    """Minimal __cuda_array_interface__ wrapper to view raw device memory as a tensor."""
+
+    def __init__(self, ptr: int, n: int, device: torch.device):
+        self.__cuda_array_interface__ = {"shape": (n,), "typestr": "<f4", "data": (ptr, False), "version": 3}
+        self.device = device
+
+
+class PeerExchange:
+    """Exchange areas of all ranks mapped into this process over CUDA IPC, for
+    the NVLink peer-store exchange of partial blocks (``iak_exchange_*``).
+
+    Collective to construct (every rank of ``group``); afterwards
+    ``block(epoch)`` is this rank's slot to decode into, ``push(epoch)``
+    stores it into every peer and ``merge(epoch, out)`` waits (bounded) for
+    all peers and merges.  ``check()`` raises if any wait ran out."""
+
+    def __init__(self, rows: int, head_dim: int, device: torch.device, group=None, timeout_us: int = 2_000_000):
+        import ctypes
+        import torch.distributed as dist
+        self.dist, self.group = dist, group
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        if self.world > N.MAX_PEERS:
+            raise ValueError(f"peer exchange supports at most {N.MAX_PEERS} ranks")
+        self.rows, self.head_dim, self.device, self.timeout_us = rows, head_dim, device, timeout_us
+        L = N.lib()
+        nbytes = ctypes.c_size_t(0)
+        N.check(L.iak_exchange_area_bytes(self.world, rows, head_dim, ctypes.byref(nbytes)), "iak_exchange_area_bytes")
+        handle = (ctypes.c_uint8 * 64)()
+        own = ctypes.c_void_p(0)
+        with torch.cuda.device(device):
+            N.check(L.iak_ipc_alloc(nbytes.value, ctypes.byref(own), handle), "iak_ipc_alloc")
+        self._own = own.value
+        handles = [bytes(handle)]
+        if self.world > 1:
+            handles = [None] * self.world
+            dist.all_gather_object(handles, bytes(handle), group=group)
+        self._opened = []
+        x = N.PeerExchange()
+        with torch.cuda.device(device):
+            for r in range(self.world):
+                if r == self.rank:
+                    x.areas[r] = self._own
+                    continue
+                ptr = ctypes.c_void_p(0)
+                buf = (ctypes.c_uint8 * 64).from_buffer_copy(handles[r])
+                N.check(L.iak_ipc_open(buf, ctypes.byref(ptr)), "iak_ipc_open")
+                x.areas[r] = ptr.value
+                self._opened.append(ptr.value)
+        x.rank, x.world, x.rows, x.head_dim = self.rank, self.world, rows, head_dim
+        self.x = x
+        self.status = torch.zeros(1, dtype=torch.int32, device=device)
+        self.epoch = 0
+        self._views = {}
+
+    def block(self, epoch: int) -> torch.Tensor:
+        """This rank's slot for ``epoch`` as a flat fp32 tensor of rows*(D+2) floats."""
+        parity = epoch & 1
+        if parity not in self._views:
+            ptr = N.lib().iak_exchange_block_ptr(self._own, self.world, self.rows, self.head_dim, parity, self.rank)
+            n = block_floats(self.rows, self.head_dim)
+            self._views[parity] = torch.as_tensor(_DeviceArray(ptr, n, self.device), device=self.device)
+        return self._views[parity]
+
+    def push(self, epoch: int) -> None:
+        import ctypes
+        N.check(N.lib().iak_exchange_push(ctypes.byref(self.x), epoch, _stream(self.device)), "iak_exchange_push")
+
+    def merge(self, epoch: int, out: torch.Tensor) -> torch.Tensor:
+        import ctypes
+        o2 = out.view(self.rows, self.head_dim)
+        N.check(N.lib().iak_exchange_merge(ctypes.byref(self.x), epoch, o2.data_ptr(), _DT[out.dtype], o2.stride(0),
+                                           self.status.data_ptr(), self.timeout_us, _stream(self.device)),
+                "iak_exchange_merge")
+        return out
+
+    def check(self) -> None:
+        """Raise if a bounded wait for a peer ran out (synchronises the device)."""
+        if int(self.status.item()):
+            raise RuntimeError("peer exchange: a rank's partial block did not arrive within the timeout")
+
+    def close(self) -> None:
+        L = N.lib()
+        with torch.cuda.device(self.device):
+            torch.cuda.synchronize(self.device)
+            for ptr in self._opened:
+                L.iak_ipc_close(ptr)
+            self._opened = []
+            if self._own:
+                L.iak_ipc_free(self._own)
+                self._own = 0
+        self._views = {}
+
+
 class SequenceShardedDecoder:
     """Per-rank driver of the sharded decode: owns the send / receive blocks
     so that repeated steps allocate nothing.
@@ -126,13 +224,17 @@ class SequenceShardedDecoder:
     the partial blocks over ``group`` and returns the merged [B, Hq, D]
     output on every rank.  Every rank must call it with the same q shape."""
 
-    def __init__(self, group=None):
+    def __init__(self, group=None, transport: str = "nccl"):
         import torch.distributed as dist
+        if transport not in ("nccl", "p2p"):
+            raise ValueError("transport must be 'nccl' or 'p2p'")
         self.dist = dist
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.transport = transport
         self._send = None
         self._recv = None
+        self._x = None
 
     def _buffers(self, rows, D, device):
         n = block_floats(rows, D)
@@ -151,15 +253,35 @@ class SequenceShardedDecoder:
         self.dist.all_gather_into_tensor(recv, send, group=self.group)
         return recv
 
+    def peer_exchange(self, rows: int, head_dim: int, device) -> PeerExchange:
+        if self._x is None or self._x.rows != rows or self._x.head_dim != head_dim:
+            if self._x is not None:
+                self._x.close()
+            self._x = PeerExchange(rows, head_dim, device, self.group)
+        return self._x
+
+    def close(self) -> None:
+        if self._x is not None:
+            self._x.close()
+            self._x = None
+
     def decode(self, q, pool, local_table, local_counts, page_tags, tag_map, tag_default=N.FMT_SKIP,
                sm_scale=None, out=None, num_splits: int = 0, kernel: str = "auto"):
         B, Hq, D = q.shape
         rows = B * Hq
+        if out is None:
+            out = torch.empty(q.shape, dtype=q.dtype, device=q.device)
+        if self.transport == "p2p":
+            # decode into this rank's slot, store it into every peer over NVLink, bounded wait + merge
+            x = self.peer_exchange(rows, D, q.device)
+            x.epoch += 1
+            decode_partial_block(q, pool, local_table, local_counts, page_tags, tag_map, tag_default, sm_scale,
+                                 block=x.block(x.epoch), num_splits=num_splits, kernel=kernel)
+            x.push(x.epoch)
+            return x.merge(x.epoch, out)
         send, recv = self._buffers(rows, D, q.device)
         decode_partial_block(q, pool, local_table, local_counts, page_tags, tag_map, tag_default, sm_scale,
                              block=send, num_splits=num_splits, kernel=kernel)
         blocks = self.exchange(send, recv)
-        if out is None:
-            out = torch.empty(q.shape, dtype=q.dtype, device=q.device)
         merge_partial_blocks(blocks, rows, D, out=out)
         return out

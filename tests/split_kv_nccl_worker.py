@@ -28,11 +28,19 @@ def main():
     case = make_case(941, B=3, Hq=32, Ht=8, W=150, NP=1800, formats=("F16", "FP8", "INT8", "INT4"), device=dev)
     world = dist.get_world_size()
     lt, lc = shard_page_lists(case["table"], case["counts"], rank, world)
-    dec = SequenceShardedDecoder()
-    out = dec.decode(case["q"], case["pool"], lt, lc, case["tags"], tag_map_for(case["formats"]),
-                     out=torch.empty(case["q"].shape, dtype=torch.float32, device=dev))
-    torch.cuda.synchronize(dev)
-    ok = np.allclose(out.cpu().numpy(), run_oracle(case), atol=2e-3, rtol=1e-2)
+    ref = run_oracle(case)
+    ok = True
+    for transport in ("nccl", "p2p"):
+        dec = SequenceShardedDecoder(transport=transport)
+        for _ in range(3):      # both exchange parities and a reuse
+            out = dec.decode(case["q"], case["pool"], lt, lc, case["tags"], tag_map_for(case["formats"]),
+                             out=torch.empty(case["q"].shape, dtype=torch.float32, device=dev))
+        torch.cuda.synchronize(dev)
+        if transport == "p2p":
+            dec._x.check()
+        ok = ok and np.allclose(out.cpu().numpy(), ref, atol=2e-3, rtol=1e-2)
+        dist.barrier()
+        dec.close()
     np.save(os.path.join(os.environ["RESULT_DIR"], f"rank{rank}.npy"), np.array([0.0 if ok else 1.0]))
     dist.barrier()
     dist.destroy_process_group()

@@ -60,6 +60,8 @@ int main(void) {
   printf("iak_pack_args %zu\n", sizeof(iak_pack_args));
   printf("iak_quant_args %zu\n", sizeof(iak_quant_args));
   printf("iak_mla_args %zu\n", sizeof(iak_mla_args));
+  printf("iak_peer_exchange %zu\n", sizeof(iak_peer_exchange));
+  P(iak_peer_exchange, rank) P(iak_peer_exchange, rows) P(iak_peer_exchange, head_dim)
   P(iak_page_pools, num_pages) P(iak_page_pools, scale_mode)
   P(iak_decode_args, tag_map) P(iak_decode_args, sm_scale) P(iak_decode_args, partial_acc) P(iak_decode_args, num_splits) P(iak_decode_args, kernel)
   P(iak_pack_args, pad_value) P(iak_quant_args, scale_mode) P(iak_quant_args, num_pages)
@@ -78,7 +80,8 @@ int main(void) {
         out = subprocess.run([exe], capture_output=True, text=True).stdout
     got = dict(line.rsplit(" ", 1) for line in out.strip().splitlines())
     types = {"iak_page_pools": N.PagePools, "iak_decode_args": N.DecodeArgs, "iak_pack_args": N.PackArgs,
-             "iak_quant_args": N.QuantArgs, "iak_mla_args": N.MlaArgs}
+             "iak_quant_args": N.QuantArgs, "iak_mla_args": N.MlaArgs,
+             "iak_peer_exchange": N.PeerExchange}
     for k, v in got.items():
         if "." in k:
             t, f = k.split(".")

@@ -81,3 +81,45 @@ def test_nccl_two_ranks_match_oracle(tmp_path):
     subprocess.run(["timeout", "-k", "30", "300"] + cmd, check=True, env=env, cwd=os.path.dirname(HERE))
     for r in range(2):
         assert float(np.load(os.path.join(tmp_path, f"rank{r}.npy"))[0]) == 0.0
+
+
+# ------------------------------------------------------------------ peer-memory exchange
+def test_p2p_single_rank_decoder_is_plain_decode():
+    case = make_case(951, B=2, Hq=16, Ht=4, W=80, NP=500)
+    dec = SequenceShardedDecoder(transport="p2p")
+    for _ in range(3):       # both parities and a reuse
+        out = dec.decode(case["q"], case["pool"], case["table"], case["counts"], case["tags"],
+                         tag_map_for(case["formats"]), out=torch.empty(case["q"].shape, device="cuda"))
+    dec._x.check()
+    np.testing.assert_allclose(out.cpu().numpy(), run_oracle(case), atol=ATOL, rtol=RTOL)
+    dec.close()
+
+
+def test_p2p_merge_wait_times_out_with_status_when_a_peer_never_arrives():
+    # a two-rank descriptor whose "peer" area is this rank's own: rank 1's flag is never raised,
+    # so the bounded wait must give up, report the timeout in the status word and leave the
+    # context usable
+    import ctypes
+    from intent_attention import _native as N
+    L = N.lib()
+    rows, D = 8, 64
+    nbytes = ctypes.c_size_t(0)
+    N.check(L.iak_exchange_area_bytes(2, rows, D, ctypes.byref(nbytes)), "area")
+    area, handle = ctypes.c_void_p(0), (ctypes.c_uint8 * 64)()
+    N.check(L.iak_ipc_alloc(nbytes.value, ctypes.byref(area), handle), "alloc")
+    try:
+        x = N.PeerExchange()
+        x.areas[0] = x.areas[1] = area.value
+        x.rank, x.world, x.rows, x.head_dim = 0, 2, rows, D
+        status = torch.zeros(1, dtype=torch.int32, device="cuda")
+        out = torch.zeros((rows, D), device="cuda")
+        s = torch.cuda.current_stream().cuda_stream
+        N.check(L.iak_exchange_push(ctypes.byref(x), 1, s), "push")
+        N.check(L.iak_exchange_merge(ctypes.byref(x), 1, out.data_ptr(), N.DT_F32, D, status.data_ptr(), 200_000, s),
+                "merge")
+        torch.cuda.synchronize()
+        assert int(status.item()) == 1
+        # the context is still usable
+        assert float((torch.ones(4, device="cuda") * 2).sum().item()) == 8.0
+    finally:
+        L.iak_ipc_free(area.value)
