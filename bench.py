@@ -341,6 +341,9 @@ def run_gpu(args):
     def step():
         decode(q, table, counts)
 
+    # NCCL collectives stay outside graph capture; every other path is captured
+    use_graph = not args.no_graph and not (seq_shard and args.exchange == "nccl")
+
     step()
     torch.cuda.synchronize(device)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -368,13 +371,30 @@ def run_gpu(args):
             dist.barrier()
         torch.cuda.synchronize(device)
         with KernelTimer(args.steps) as ktimer:
-            ev0.record()
-            for _ in range(args.steps):
-                step()
-            ev1.record()
+            if use_graph:
+                # the K steps captured once as a CUDA graph (the library never allocates or
+                # synchronises while decoding); one warm-up replay, then the timed replay
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph):
+                    for _ in range(args.steps):
+                        step()
+                graph.replay()
+                torch.cuda.synchronize(device)
+                if world > 1:
+                    dist.barrier()
+                ev0.record()
+                graph.replay()
+                ev1.record()
+            else:
+                ev0.record()
+                for _ in range(args.steps):
+                    step()
+                ev1.record()
             torch.cuda.synchronize(device)
     t_ms = ev0.elapsed_time(ev1) / args.steps
     kernel_ms = ktimer.total_ms / max(1, ktimer.launches)
+    if use_graph:
+        del graph
     if world > 1:
         t = torch.tensor([t_ms], device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -441,6 +461,8 @@ def run_gpu(args):
                        "format_mix": w["mix"], "scale_mode": w["scale_mode"],
                        "selected_kv_bytes_per_step_per_gpu": nbytes,
                        "l2": f"inputs larger than L2 ({nbytes / 1e9:.2f} GB of selected KV per step)",
+                       "timing": ("one CUDA graph of all timed steps, replayed once after a warm-up replay"
+                                  if use_graph else "eager launches"),
                        "parallelism": (f"sp{world} (each sequence's selected pages cut into {world} ranges; partial "
                                        "(m, l, acc) blocks exchanged "
                                        + ("by NVLink peer stores with epoch flags (CUDA IPC)" if args.exchange == "p2p"
@@ -782,6 +804,7 @@ def main():
     ap.add_argument("--batch", type=int, default=0, help="override the workload's batch (profiling runs)")
     ap.add_argument("--exchange", default="p2p", choices=["p2p", "nccl"],
                     help="C5 on several GPUs: partial blocks over NVLink peer stores or one NCCL all-gather")
+    ap.add_argument("--no-graph", action="store_true", help="time eager launches instead of a captured CUDA graph")
     ap.add_argument("--cpu-budget", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()

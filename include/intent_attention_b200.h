@@ -211,7 +211,9 @@ int iak_mla_decode(const iak_mla_args* args, void* workspace, size_t workspace_b
  * preparation or merge launches), for the first max_launches calls.
  * iak_kernel_timer_read waits for the recorded events and returns the summed
  * kernel time and the number of timed launches; iak_kernel_timer_disable
- * releases the events.  Process-wide; do not enable during stream capture. */
+ * releases the events.  Process-wide.  Launches captured into a CUDA graph
+ * record graph event nodes, so each replay of the graph re-times them; enable
+ * the timer before the capture and read it after the replay to be timed. */
 int iak_kernel_timer_enable(int32_t max_launches);
 int iak_kernel_timer_read(double* total_ms, int32_t* launches);
 int iak_kernel_timer_disable(void);
@@ -248,22 +250,25 @@ int iak_merge_partial_blocks(const float* blocks, int32_t num_parts, int64_t row
  * blocks with stores straight into the peers' memory.
  *
  * Every rank owns an exchange area in its own device memory
- * (iak_exchange_area_bytes): for each of two parities, a receive array of
- * `world` partial blocks and `world` uint32 arrival flags.  The areas are
- * allocated with iak_ipc_alloc and shared once through their 64-byte CUDA IPC
- * handles (iak_ipc_open in every other rank), so each rank can write every
- * peer's area.  Per step, with a host epoch counter starting at 1 and
- * parity = epoch & 1:
- *   1. decode with partial export into this rank's own slot
- *      (iak_exchange_block_ptr(area, ..., parity, rank));
- *   2. iak_exchange_push: copy that block into slot `rank` of every peer's
- *      area, then raise those areas' flag[parity][rank] to epoch;
- *   3. iak_exchange_merge: wait until every flag[parity][*] of this rank's
- *      area equals epoch (bounded by timeout_us; on expiry *status becomes 1
- *      and out is not written), then LSE-merge the world blocks into out.
- * Two parities let a rank run one step ahead without overwriting blocks a
- * slower peer is still merging.  All ranks must call the three steps every
- * step, in the same order.
+ * (iak_exchange_area_bytes): a staging block, for each of two parities a
+ * receive array of `world` partial blocks and `world` uint32 arrival flags,
+ * and a device-side epoch counter.  The areas are allocated with
+ * iak_ipc_alloc and shared once through their 64-byte CUDA IPC handles
+ * (iak_ipc_open in every other rank), so each rank can write every peer's
+ * area.  Per step:
+ *   1. decode with partial export into this rank's staging block
+ *      (iak_exchange_staging_ptr; the block layout of IAK_PARTIAL_BLOCK_FLOATS);
+ *   2. iak_exchange_push: advance the epoch e -> e+1, copy the staging block
+ *      into slot `rank` of every rank's receive array of parity (e+1) & 1
+ *      over NVLink, then raise those areas' flag[parity][rank] to e+1;
+ *   3. iak_exchange_merge: wait until every flag of that parity in this
+ *      rank's area equals e+1 (bounded by timeout_us; on expiry *status
+ *      becomes 1 and the merge reads whatever arrived), then LSE-merge the
+ *      world blocks into out.
+ * The epoch lives in device memory, so the three steps can be captured once
+ * in a CUDA graph and replayed.  Two parities let a rank run one step ahead
+ * without overwriting blocks a slower peer is still merging.  All ranks must
+ * run the three steps every step, in the same order.
  * ------------------------------------------------------------------------ */
 #define IAK_MAX_PEERS 8
 typedef struct iak_peer_exchange {
@@ -274,12 +279,11 @@ typedef struct iak_peer_exchange {
 } iak_peer_exchange;
 
 int iak_exchange_area_bytes(int32_t world, int64_t rows, int32_t head_dim, size_t* bytes);
-/* Address of block `slot` of `parity` inside an exchange area. */
-float* iak_exchange_block_ptr(void* area, int32_t world, int64_t rows, int32_t head_dim, int32_t parity,
-                              int32_t slot);
-int iak_exchange_push(const iak_peer_exchange* x, uint32_t epoch, void* stream);
-int iak_exchange_merge(const iak_peer_exchange* x, uint32_t epoch, void* out, int32_t out_dtype,
-                       int64_t out_row_stride, uint32_t* status, uint32_t timeout_us, void* stream);
+/* Address of the staging block inside an exchange area. */
+float* iak_exchange_staging_ptr(void* area, int32_t world, int64_t rows, int32_t head_dim);
+int iak_exchange_push(const iak_peer_exchange* x, void* stream);
+int iak_exchange_merge(const iak_peer_exchange* x, void* out, int32_t out_dtype, int64_t out_row_stride,
+                       uint32_t* status, uint32_t timeout_us, void* stream);
 
 /* CUDA IPC helpers (device memory of the current device; handle = 64 bytes).
  * iak_ipc_alloc zero-fills the allocation. */

@@ -60,17 +60,26 @@ struct KernelTimer {
 };
 static KernelTimer g_timer;
 
+// During stream capture the records become event-record nodes of the graph
+// (cudaEventRecordExternal), so every replay of the graph times the kernel.
+static cudaError_t timer_record(cudaEvent_t e, cudaStream_t s) {
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(s, &cs) == cudaSuccess && cs == cudaStreamCaptureStatusActive)
+    return cudaEventRecordWithFlags(e, s, cudaEventRecordExternal);
+  return cudaEventRecord(e, s);
+}
+
 void kernel_timer_begin(cudaStream_t s) {
   std::lock_guard<std::mutex> lock(g_timer.mu);
   if (!g_timer.on || g_timer.used >= static_cast<int>(g_timer.start.size())) return;
-  if (cudaEventRecord(g_timer.start[g_timer.used], s) == cudaSuccess) g_timer.open = true;
+  if (timer_record(g_timer.start[g_timer.used], s) == cudaSuccess) g_timer.open = true;
 }
 
 void kernel_timer_end(cudaStream_t s) {
   std::lock_guard<std::mutex> lock(g_timer.mu);
   if (!g_timer.open) return;
   g_timer.open = false;
-  if (cudaEventRecord(g_timer.stop[g_timer.used], s) == cudaSuccess) ++g_timer.used;
+  if (timer_record(g_timer.stop[g_timer.used], s) == cudaSuccess) ++g_timer.used;
 }
 
 static void timer_release_locked() {

@@ -4,13 +4,16 @@
 // Area of one rank (device memory of its GPU), for world W and block size
 // BF = rows * (head_dim + 2) floats padded to BS (a multiple of 64 floats):
 //   float  blocks[2][W][BS]      receive arrays, one per parity
+//   float  staging[BS]           this rank's partial block (written by the decode)
 //   uint32 flags[2][W]           arrival epoch of each sender, per parity
 //   uint32 push_count[2]         CTAs of this rank's push kernel that finished
-// A rank's push writes its block into slot `rank` of every peer's
-// blocks[parity] with plain stores over NVLink, then (after a system-scope
-// fence, from the last CTA to finish) raises flag[parity][rank] = epoch in
-// every area.  The merge waits, bounded in time, for all W flags of its own
-// area and then LSE-merges the W blocks.
+//   uint32 epoch                 last epoch this rank pushed (device-side, so a
+//                                captured CUDA graph can replay the steps)
+// A push reads epoch e, copies the staging block into slot `rank` of every
+// rank's blocks[(e+1) & 1] with plain stores over NVLink, and its last CTA
+// (after a system-scope fence) raises flag[(e+1) & 1][rank] = e+1 in every
+// area and advances epoch.  The merge waits, bounded in time, for all W flags
+// of that parity in its own area and then LSE-merges the W blocks.
 #include <algorithm>
 #include <cstring>
 
@@ -25,18 +28,20 @@ __host__ __device__ inline int64_t block_stride(int64_t rows, int D) {
   const int64_t bf = rows * (static_cast<int64_t>(D) + 2);
   return (bf + 63) / 64 * 64;
 }
-__host__ __device__ inline size_t flags_offset(int world, int64_t rows, int D) {
+__host__ __device__ inline size_t staging_offset(int world, int64_t rows, int D) {
   return static_cast<size_t>(2) * world * block_stride(rows, D) * sizeof(float);
+}
+__host__ __device__ inline size_t flags_offset(int world, int64_t rows, int D) {
+  return staging_offset(world, rows, D) + block_stride(rows, D) * sizeof(float);
 }
 
 struct PushParams {
   float* areas[IAK_MAX_PEERS];
   int rank, world;
-  int64_t bs;        // block stride (floats)
-  int64_t n4;        // float4 per block copy
-  size_t flags_off;  // byte offset of flags in an area
-  int parity;
-  uint32_t epoch;
+  int64_t bs;          // block stride (floats)
+  int64_t n4;          // float4 per block copy
+  size_t staging_off;  // byte offsets inside an area
+  size_t flags_off;
 };
 
 __device__ __forceinline__ uint32_t* area_flags(float* area, size_t off) {
@@ -59,10 +64,13 @@ __device__ __forceinline__ uint64_t global_ns() {
 
 __global__ void __launch_bounds__(kPushThreads) push_kernel(const PushParams p) {
   float* own = p.areas[p.rank];
-  const float4* src = reinterpret_cast<const float4*>(own + (static_cast<int64_t>(p.parity) * p.world + p.rank) * p.bs);
+  uint32_t* own_flags = area_flags(own, p.flags_off);
+  // epoch word: read by every CTA before the last one advances it
+  const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(own_flags + 2 * p.world + 2) + 1u;
+  const int parity = static_cast<int>(epoch & 1u);
+  const float4* src = reinterpret_cast<const float4*>(reinterpret_cast<const char*>(own) + p.staging_off);
   for (int r = 0; r < p.world; ++r) {
-    if (r == p.rank) continue;
-    float4* dst = reinterpret_cast<float4*>(p.areas[r] + (static_cast<int64_t>(p.parity) * p.world + p.rank) * p.bs);
+    float4* dst = reinterpret_cast<float4*>(p.areas[r] + (static_cast<int64_t>(parity) * p.world + p.rank) * p.bs);
     for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < p.n4;
          i += static_cast<int64_t>(gridDim.x) * blockDim.x)
       dst[i] = src[i];
@@ -70,24 +78,28 @@ __global__ void __launch_bounds__(kPushThreads) push_kernel(const PushParams p) 
   __threadfence_system();
   __syncthreads();
   if (threadIdx.x == 0) {
-    uint32_t* count = area_flags(own, p.flags_off) + 2 * p.world + p.parity;
+    uint32_t* count = own_flags + 2 * p.world + parity;
     if (atomicAdd(count, 1u) == gridDim.x - 1) {
-      // every CTA's stores are fenced: publish the block to every rank
+      // every CTA's stores are fenced: publish the block to every rank, then advance the epoch
       *count = 0u;
       __threadfence_system();
       for (int r = 0; r < p.world; ++r)
-        st_release_sys(area_flags(p.areas[r], p.flags_off) + p.parity * p.world + p.rank, p.epoch);
+        st_release_sys(area_flags(p.areas[r], p.flags_off) + parity * p.world + p.rank, epoch);
+      own_flags[2 * p.world + 2] = epoch;
     }
   }
 }
 
-// One thread waits (bounded by timeout_ns of wall time) for every sender's flag.
-__global__ void wait_kernel(const uint32_t* flags, int world, uint32_t epoch, uint32_t* status, uint64_t timeout_ns) {
+// One thread waits (bounded by timeout_ns of wall time) for every sender's flag of the
+// current epoch (the one this rank's push just published).
+__global__ void wait_kernel(const uint32_t* flags, int world, uint32_t* status, uint64_t timeout_ns) {
   if (threadIdx.x != 0) return;
+  const uint32_t epoch = *reinterpret_cast<const volatile uint32_t*>(flags + 2 * world + 2);
+  const uint32_t* f = flags + (epoch & 1u) * world;
   const uint64_t t0 = global_ns();
   for (int r = 0; r < world; ++r) {
     unsigned ns = 64;
-    while (ld_acquire_sys(flags + r) != epoch) {
+    while (ld_acquire_sys(f + r) != epoch) {
       if (global_ns() - t0 > timeout_ns) {
         if (status) atomicExch(status, 1u);
         return;
@@ -95,6 +107,51 @@ __global__ void wait_kernel(const uint32_t* flags, int world, uint32_t epoch, ui
       __nanosleep(ns);
       if (ns < 1024) ns <<= 1;
     }
+  }
+}
+
+// LSE merge of the W blocks of the current parity into out (one CTA per row).
+__global__ void exchange_merge_kernel(const float* area, const uint32_t* flags, int world, int64_t rows, int D,
+                                      int64_t bs, void* out, int out_dtype, int64_t out_row_stride) {
+  extern __shared__ float w_s[];
+  __shared__ float stat[2];
+  const uint32_t epoch = *reinterpret_cast<const volatile uint32_t*>(flags + 2 * world + 2);
+  const float* blocks = area + static_cast<int64_t>(epoch & 1u) * world * bs;
+  for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
+    if (threadIdx.x < 32) {
+      float M = -INFINITY;
+      for (int s = threadIdx.x; s < world; s += 32) {
+        const float* b = blocks + s * bs;
+        if (b[rows + r] > 0.f) M = fmaxf(M, b[r]);
+      }
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+      float L = 0.f;
+      for (int s = threadIdx.x; s < world; s += 32) {
+        const float* b = blocks + s * bs;
+        const float ls = b[rows + r];
+        const float w = (ls > 0.f && M != -INFINITY) ? expf(b[r] - M) : 0.f;
+        w_s[s] = w;
+        L += ls * w;
+      }
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
+      if (threadIdx.x == 0) {
+        stat[0] = M;
+        stat[1] = L;
+      }
+    }
+    __syncthreads();
+    const float L = stat[1];
+    for (int d = threadIdx.x; d < D; d += blockDim.x) {
+      float A = 0.f;
+      for (int s = 0; s < world; ++s) {
+        const float w = w_s[s];
+        if (w != 0.f) A = fmaf(blocks[s * bs + 2 * rows + r * D + d], w, A);
+      }
+      store_from_float(out, out_dtype, r * out_row_stride + d, L > 0.f ? A / L : 0.f);
+    }
+    __syncthreads();
   }
 }
 
@@ -123,52 +180,48 @@ int iak_exchange_area_bytes(int32_t world, int64_t rows, int32_t head_dim, size_
   return IAK_OK;
 }
 
-float* iak_exchange_block_ptr(void* area, int32_t world, int64_t rows, int32_t head_dim, int32_t parity, int32_t slot) {
-  if (!area || world < 1 || parity < 0 || parity > 1 || slot < 0 || slot >= world) return nullptr;
-  return static_cast<float*>(area) + (static_cast<int64_t>(parity) * world + slot) * block_stride(rows, head_dim);
+float* iak_exchange_staging_ptr(void* area, int32_t world, int64_t rows, int32_t head_dim) {
+  if (!area || world < 1 || world > IAK_MAX_PEERS || rows < 0 || head_dim <= 0) return nullptr;
+  return reinterpret_cast<float*>(static_cast<char*>(area) + staging_offset(world, rows, head_dim));
 }
 
-int iak_exchange_push(const iak_peer_exchange* x, uint32_t epoch, void* stream) {
+int iak_exchange_push(const iak_peer_exchange* x, void* stream) {
   int st = check_exchange(x);
   if (st) return st;
-  if (epoch == 0) return fail(IAK_ERR_INVALID_ARG, "epoch must be >= 1 (flags start at 0)");
   PushParams p;
   std::memset(&p, 0, sizeof(p));
   for (int r = 0; r < x->world; ++r) p.areas[r] = static_cast<float*>(x->areas[r]);
   p.rank = x->rank; p.world = x->world;
   p.bs = block_stride(x->rows, x->head_dim);
   p.n4 = (x->rows * (static_cast<int64_t>(x->head_dim) + 2) + 3) / 4;
+  p.staging_off = staging_offset(x->world, x->rows, x->head_dim);
   p.flags_off = flags_offset(x->world, x->rows, x->head_dim);
-  p.parity = static_cast<int>(epoch & 1u);
-  p.epoch = epoch;
   const int64_t want = (p.n4 + kPushThreads - 1) / kPushThreads;
   const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(want, device_sm_count())));
   push_kernel<<<grid, kPushThreads, 0, static_cast<cudaStream_t>(stream)>>>(p);
   return check_cuda(cudaGetLastError(), "exchange push launch");
 }
 
-int iak_exchange_merge(const iak_peer_exchange* x, uint32_t epoch, void* out, int32_t out_dtype, int64_t out_row_stride,
+int iak_exchange_merge(const iak_peer_exchange* x, void* out, int32_t out_dtype, int64_t out_row_stride,
                        uint32_t* status, uint32_t timeout_us, void* stream) {
   int st = check_exchange(x);
   if (st) return st;
-  if (epoch == 0) return fail(IAK_ERR_INVALID_ARG, "epoch must be >= 1");
   if (!out) return fail(IAK_ERR_INVALID_ARG, "out is NULL");
   if (out_dtype < 0 || out_dtype > 2) return fail(IAK_ERR_INVALID_ARG, "bad out dtype");
   if (out_row_stride < x->head_dim) return fail(IAK_ERR_INVALID_ARG, "out_row_stride < head_dim");
   if (x->rows == 0) return IAK_OK;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const int parity = static_cast<int>(epoch & 1u);
-  float* own = static_cast<float*>(x->areas[x->rank]);
-  const size_t foff = flags_offset(x->world, x->rows, x->head_dim);
-  const uint32_t* flags = reinterpret_cast<const uint32_t*>(reinterpret_cast<char*>(own) + foff) + parity * x->world;
-  wait_kernel<<<1, 32, 0, s>>>(flags, x->world, epoch, status, static_cast<uint64_t>(timeout_us) * 1000ull);
+  const float* own = static_cast<const float*>(x->areas[x->rank]);
+  const uint32_t* flags = reinterpret_cast<const uint32_t*>(reinterpret_cast<const char*>(own) +
+                                                           flags_offset(x->world, x->rows, x->head_dim));
+  wait_kernel<<<1, 32, 0, s>>>(flags, x->world, status, static_cast<uint64_t>(timeout_us) * 1000ull);
   st = check_cuda(cudaGetLastError(), "exchange wait launch");
   if (st) return st;
-  const int64_t bs = block_stride(x->rows, x->head_dim);
-  const float* blocks = own + static_cast<int64_t>(parity) * x->world * bs;
-  return launch_merge_strided(blocks, blocks + x->rows, blocks + 2 * x->rows, 1, bs, x->head_dim, bs, x->rows,
-                              x->world, x->head_dim, out, out_dtype, out_row_stride, nullptr, nullptr, nullptr,
-                              nullptr, s);
+  const int threads = x->head_dim >= 128 ? 128 : (x->head_dim >= 64 ? 64 : 32);
+  const int64_t blocks = std::min<int64_t>(x->rows, 65535LL * 8);
+  exchange_merge_kernel<<<static_cast<unsigned>(blocks), threads, x->world * sizeof(float), s>>>(
+      own, flags, x->world, x->rows, x->head_dim, block_stride(x->rows, x->head_dim), out, out_dtype, out_row_stride);
+  return check_cuda(cudaGetLastError(), "exchange merge launch");
 }
 
 int iak_ipc_alloc(size_t bytes, void** ptr, void* handle) {

@@ -117,10 +117,10 @@ SIGNATURES = {
     "iak_mla_workspace_size": (ctypes.c_int, [ctypes.POINTER(MlaArgs), ctypes.POINTER(ctypes.c_size_t)]),
     "iak_mla_decode": (ctypes.c_int, [ctypes.POINTER(MlaArgs), c_void_p, ctypes.c_size_t, c_void_p]),
     "iak_exchange_area_bytes": (ctypes.c_int, [c_i32, c_i64, c_i32, ctypes.POINTER(ctypes.c_size_t)]),
-    "iak_exchange_block_ptr": (c_void_p, [c_void_p, c_i32, c_i64, c_i32, c_i32, c_i32]),
-    "iak_exchange_push": (ctypes.c_int, [ctypes.POINTER(PeerExchange), ctypes.c_uint32, c_void_p]),
-    "iak_exchange_merge": (ctypes.c_int, [ctypes.POINTER(PeerExchange), ctypes.c_uint32, c_void_p, c_i32, c_i64,
-                                          c_void_p, ctypes.c_uint32, c_void_p]),
+    "iak_exchange_staging_ptr": (c_void_p, [c_void_p, c_i32, c_i64, c_i32]),
+    "iak_exchange_push": (ctypes.c_int, [ctypes.POINTER(PeerExchange), c_void_p]),
+    "iak_exchange_merge": (ctypes.c_int, [ctypes.POINTER(PeerExchange), c_void_p, c_i32, c_i64, c_void_p,
+                                          ctypes.c_uint32, c_void_p]),
     "iak_ipc_alloc": (ctypes.c_int, [ctypes.c_size_t, ctypes.POINTER(c_void_p), c_void_p]),
     "iak_ipc_open": (ctypes.c_int, [c_void_p, ctypes.POINTER(c_void_p)]),
     "iak_ipc_close": (ctypes.c_int, [c_void_p]),

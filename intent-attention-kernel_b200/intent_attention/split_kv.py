@@ -132,10 +132,12 @@ class PeerExchange:
     """Exchange areas of all ranks mapped into this process over CUDA IPC, for
     the NVLink peer-store exchange of partial blocks (``iak_exchange_*``).
 
-    Collective to construct (every rank of ``group``); afterwards
-    ``block(epoch)`` is this rank's slot to decode into, ``push(epoch)``
-    stores it into every peer and ``merge(epoch, out)`` waits (bounded) for
-    all peers and merges.  ``check()`` raises if any wait ran out."""
+    Collective to construct (every rank of ``group``); afterwards a step is
+    decode into ``staging`` (this rank's partial block), ``push()`` (stores it
+    into every rank's area over NVLink and raises this rank's flags) and
+    ``merge(out)`` (bounded wait for every rank, then the LSE merge).  The
+    epoch counter lives in device memory, so a step can be captured in a CUDA
+    graph and replayed.  ``check()`` raises if any wait ran out."""
 
     def __init__(self, rows: int, head_dim: int, device: torch.device, group=None, timeout_us: int = 2_000_000):
         import ctypes
@@ -173,26 +175,17 @@ class PeerExchange:
         x.rank, x.world, x.rows, x.head_dim = self.rank, self.world, rows, head_dim
         self.x = x
         self.status = torch.zeros(1, dtype=torch.int32, device=device)
-        self.epoch = 0
-        self._views = {}
+        ptr = L.iak_exchange_staging_ptr(self._own, self.world, rows, head_dim)
+        self.staging = torch.as_tensor(_DeviceArray(ptr, block_floats(rows, head_dim), device), device=device)
 
-    def block(self, epoch: int) -> torch.Tensor:
-        """This rank's slot for ``epoch`` as a flat fp32 tensor of rows*(D+2) floats."""
-        parity = epoch & 1
-        if parity not in self._views:
-            ptr = N.lib().iak_exchange_block_ptr(self._own, self.world, self.rows, self.head_dim, parity, self.rank)
-            n = block_floats(self.rows, self.head_dim)
-            self._views[parity] = torch.as_tensor(_DeviceArray(ptr, n, self.device), device=self.device)
-        return self._views[parity]
-
-    def push(self, epoch: int) -> None:
+    def push(self) -> None:
         import ctypes
-        N.check(N.lib().iak_exchange_push(ctypes.byref(self.x), epoch, _stream(self.device)), "iak_exchange_push")
+        N.check(N.lib().iak_exchange_push(ctypes.byref(self.x), _stream(self.device)), "iak_exchange_push")
 
-    def merge(self, epoch: int, out: torch.Tensor) -> torch.Tensor:
+    def merge(self, out: torch.Tensor) -> torch.Tensor:
         import ctypes
         o2 = out.view(self.rows, self.head_dim)
-        N.check(N.lib().iak_exchange_merge(ctypes.byref(self.x), epoch, o2.data_ptr(), _DT[out.dtype], o2.stride(0),
+        N.check(N.lib().iak_exchange_merge(ctypes.byref(self.x), o2.data_ptr(), _DT[out.dtype], o2.stride(0),
                                            self.status.data_ptr(), self.timeout_us, _stream(self.device)),
                 "iak_exchange_merge")
         return out
@@ -212,7 +205,7 @@ class PeerExchange:
             if self._own:
                 L.iak_ipc_free(self._own)
                 self._own = 0
-        self._views = {}
+        self.staging = None
 
 
 class SequenceShardedDecoder:
@@ -274,11 +267,10 @@ class SequenceShardedDecoder:
         if self.transport == "p2p":
             # decode into this rank's slot, store it into every peer over NVLink, bounded wait + merge
             x = self.peer_exchange(rows, D, q.device)
-            x.epoch += 1
             decode_partial_block(q, pool, local_table, local_counts, page_tags, tag_map, tag_default, sm_scale,
-                                 block=x.block(x.epoch), num_splits=num_splits, kernel=kernel)
-            x.push(x.epoch)
-            return x.merge(x.epoch, out)
+                                 block=x.staging, num_splits=num_splits, kernel=kernel)
+            x.push()
+            return x.merge(out)
         send, recv = self._buffers(rows, D, q.device)
         decode_partial_block(q, pool, local_table, local_counts, page_tags, tag_map, tag_default, sm_scale,
                              block=send, num_splits=num_splits, kernel=kernel)

@@ -114,8 +114,8 @@ def test_p2p_merge_wait_times_out_with_status_when_a_peer_never_arrives():
         status = torch.zeros(1, dtype=torch.int32, device="cuda")
         out = torch.zeros((rows, D), device="cuda")
         s = torch.cuda.current_stream().cuda_stream
-        N.check(L.iak_exchange_push(ctypes.byref(x), 1, s), "push")
-        N.check(L.iak_exchange_merge(ctypes.byref(x), 1, out.data_ptr(), N.DT_F32, D, status.data_ptr(), 200_000, s),
+        N.check(L.iak_exchange_push(ctypes.byref(x), s), "push")
+        N.check(L.iak_exchange_merge(ctypes.byref(x), out.data_ptr(), N.DT_F32, D, status.data_ptr(), 200_000, s),
                 "merge")
         torch.cuda.synchronize()
         assert int(status.item()) == 1
