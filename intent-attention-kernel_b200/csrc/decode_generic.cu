@@ -272,6 +272,95 @@ __global__ void merge_kernel(const float* __restrict__ m, const float* __restric
   }
 }
 
+// Vectorised LSE merge (same contract as merge_kernel) for D % 4 == 0 and
+// 16-byte aligned acc rows: the 8 warps of a CTA take every 8th split slot,
+// lanes take float4 groups of channels, and the warps' sums meet in shared memory.
+constexpr int kMergeWarps = 8;
+template <int C>   // float4 groups per lane: D <= 128 * C
+__global__ void __launch_bounds__(kMergeWarps * 32) merge_vec_kernel(
+    const float* __restrict__ m, const float* __restrict__ l, const float* __restrict__ acc, int64_t ms_r,
+    int64_t ms_s, int64_t as_r, int64_t as_s, int64_t rows, int S, int D, void* out, int out_dtype,
+    int64_t out_row_stride, int Hq, int64_t o_sb, int64_t o_sh, float* ex_m, float* ex_l, float* ex_acc) {
+  extern __shared__ float sm_f[];
+  float* w_s = sm_f;                       // [S]
+  float* red = sm_f + ((S + 3) & ~3);      // [kMergeWarps][D]
+  __shared__ float stat[2];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
+    const float* mr = m + r * ms_r;
+    const float* lr = l + r * ms_r;
+    if (warp == 0) {
+      float M = -INFINITY;
+      for (int s = lane; s < S; s += 32)
+        if (lr[s * ms_s] > 0.f) M = fmaxf(M, mr[s * ms_s]);
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+      float L = 0.f;
+      for (int s = lane; s < S; s += 32) {
+        const float ls = lr[s * ms_s];
+        const float w = (ls > 0.f && M != -INFINITY) ? expf(mr[s * ms_s] - M) : 0.f;
+        w_s[s] = w;
+        L += ls * w;
+      }
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
+      if (lane == 0) {
+        stat[0] = M;
+        stat[1] = L;
+      }
+    }
+    __syncthreads();
+    float4 a[C];
+#pragma unroll
+    for (int c = 0; c < C; ++c) a[c] = make_float4(0.f, 0.f, 0.f, 0.f);
+    const float* ar = acc + r * as_r;
+#pragma unroll 4
+    for (int s = warp; s < S; s += kMergeWarps) {
+      const float w = w_s[s];
+      if (w == 0.f) continue;
+      const float4* src = reinterpret_cast<const float4*>(ar + s * as_s);
+#pragma unroll
+      for (int c = 0; c < C; ++c) {
+        const int g = lane + 32 * c;
+        if (4 * g < D) {
+          const float4 v = src[g];
+          a[c].x = fmaf(v.x, w, a[c].x); a[c].y = fmaf(v.y, w, a[c].y);
+          a[c].z = fmaf(v.z, w, a[c].z); a[c].w = fmaf(v.w, w, a[c].w);
+        }
+      }
+    }
+#pragma unroll
+    for (int c = 0; c < C; ++c) {
+      const int g = lane + 32 * c;
+      if (4 * g < D) reinterpret_cast<float4*>(red + warp * D)[g] = a[c];
+    }
+    __syncthreads();
+    const float M = stat[0], L = stat[1];
+    for (int d = threadIdx.x; d < D; d += blockDim.x) {
+      float A = 0.f;
+#pragma unroll
+      for (int w = 0; w < kMergeWarps; ++w) A += red[w * D + d];
+      if (ex_l) {
+        ex_acc[r * D + d] = A;
+      } else {
+        int64_t off;
+        if (Hq > 0) {
+          const int64_t bb = r / Hq, hq = r % Hq;
+          off = bb * o_sb + hq * o_sh + d;
+        } else {
+          off = r * out_row_stride + d;
+        }
+        store_from_float(out, out_dtype, off, L > 0.f ? A / L : 0.f);
+      }
+    }
+    if (ex_l && threadIdx.x == 0) {
+      ex_m[r] = M;
+      ex_l[r] = L;
+    }
+    __syncthreads();
+  }
+}
+
 }  // namespace
 
 int launch_decode_generic(const DecodeParams& p, cudaStream_t s) {
@@ -302,8 +391,29 @@ int launch_merge_strided(const float* m, const float* l, const float* acc, int64
                          cudaStream_t s) {
   if (rows == 0) return IAK_OK;
   if (splits > 12288) return fail(IAK_ERR_UNSUPPORTED, "too many splits to merge (%d)", splits);
-  const int threads = D >= 128 ? 128 : (D >= 64 ? 64 : 32);
   const int64_t blocks = std::min<int64_t>(rows, 65535LL * 8);
+  const bool vec = D % 4 == 0 && D <= 1024 && as_r % 4 == 0 && as_s % 4 == 0 &&
+                   reinterpret_cast<uintptr_t>(acc) % 16 == 0;
+  if (vec) {
+    const size_t vsmem = (static_cast<size_t>((splits + 3) & ~3) + static_cast<size_t>(kMergeWarps) * D) * sizeof(float);
+    const int Hq = rowmap ? rowmap->Hq : 0;
+    const int64_t o_sb = rowmap ? rowmap->o_sb : 0, o_sh = rowmap ? rowmap->o_sh : 0;
+    auto go = [&](auto kern) -> int {
+      if (vsmem > 48 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(vsmem));
+        if (e != cudaSuccess) return check_cuda(e, "merge smem attribute");
+      }
+      kern<<<static_cast<unsigned>(blocks), kMergeWarps * 32, vsmem, s>>>(m, l, acc, ms_r, ms_s, as_r, as_s, rows,
+                                                                          splits, D, out, out_dtype, out_row_stride,
+                                                                          Hq, o_sb, o_sh, ex_m, ex_l, ex_acc);
+      return check_cuda(cudaGetLastError(), "merge launch");
+    };
+    if (D <= 128) return go(merge_vec_kernel<1>);
+    if (D <= 256) return go(merge_vec_kernel<2>);
+    if (D <= 512) return go(merge_vec_kernel<4>);
+    return go(merge_vec_kernel<8>);
+  }
+  const int threads = D >= 128 ? 128 : (D >= 64 ? 64 : 32);
   const size_t smem = static_cast<size_t>(splits) * sizeof(float);
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
