@@ -292,6 +292,75 @@ int iak_ipc_open(const void* handle, void** ptr);
 int iak_ipc_close(void* ptr);
 int iak_ipc_free(void* ptr);
 
+/* ------------------------------------------------------------------------
+ * Device router: block routing + page lists for a batch of sequences.
+ *
+ * Replaces, per sequence, block_router.py:101-266 BlockRouter.route_layout()
+ * (with intent_quant.py:77-131 IntentQuantizer.assign_block_precision() as
+ * the precision policy), :283-296 selected_page_ids() and the precision map
+ * of :383-421 routing_to_kernel_metadata(), followed by the page-table
+ * packing of iak_pack_metadata.  Per sequence: ALWAYS / GLOBAL / RECENT
+ * blocks are selected; scored ATTEND blocks are ranked by score (descending,
+ * ties in layout order) and the first top_k_blocks (Python slice semantics,
+ * so a negative value drops the last |k|) are selected unless the quantiser
+ * assigns them SKIP; SKIP-policy blocks with a score >= score_threshold are
+ * selected (with precision SKIP).  Page ids t / page_size of the selected
+ * blocks are listed in routed order (pinned blocks in layout order, then the
+ * top-k in score order, then the selected SKIP-policy blocks in layout
+ * order), each page once, at its first covering block, which also gives its
+ * precision.  Scores are doubles so that threshold tests compare exactly as
+ * Python floats do; NaN stands for "no score".
+ *
+ * Each sequence's layout is checked on the device with the conditions of
+ * block_metadata.py:41-70 BlockLayout.validate (start >= 0, end > start,
+ * end <= seq_lens[b] when seq_lens is given, sorted and non-overlapping,
+ * ATTEND blocks scored) plus policy < 5; a sequence that fails gets
+ * num_selected[b] = -1, page_counts 0 and a padded row, where the reference
+ * raises ValueError.  memory_pressure outside [0, 1] is IAK_ERR_INVALID_ARG,
+ * as IntentQuantizer.__init__ (intent_quant.py:67-70) raises.
+ * ------------------------------------------------------------------------ */
+enum { IAK_POLICY_ALWAYS = 0, IAK_POLICY_ATTEND = 1, IAK_POLICY_SKIP = 2, IAK_POLICY_RECENT = 3,
+       IAK_POLICY_GLOBAL = 4 };
+enum { IAK_PREC_FP16 = 0, IAK_PREC_FP8 = 1, IAK_PREC_INT8 = 2, IAK_PREC_INT4 = 3, IAK_PREC_INT4_RESIDUAL = 4,
+       IAK_PREC_SKIP = 5 };
+#define IAK_ROUTE_MAX_BLOCKS 8192
+
+typedef struct iak_route_args {
+  /* layouts: block arrays [batch, layout_stride] (layout_stride 0 = one layout for the batch) */
+  int32_t num_blocks;             /* blocks per layout row, <= IAK_ROUTE_MAX_BLOCKS          */
+  const int32_t* block_counts;    /* [batch] blocks of sequence b (<= num_blocks) or NULL     */
+  const int32_t* block_start;     /* token ranges [start, end)                                */
+  const int32_t* block_end;
+  const uint8_t* block_policy;    /* IAK_POLICY_*                                             */
+  int64_t layout_stride;
+  const double* scores;           /* [batch, score_stride] (0 = shared), NaN = no score       */
+  int64_t score_stride;
+  const int32_t* seq_lens;        /* [batch] total tokens for the end bound, or NULL          */
+  int32_t batch, num_table_heads, page_size;
+  /* RouterConfig (block_router.py:39-47) and IntentQuantizer (intent_quant.py:59-74) */
+  int32_t top_k_blocks;
+  int32_t preserve_recent, preserve_global;
+  double score_threshold, memory_pressure;
+  double high_score_threshold, medium_score_threshold;   /* 0.75 / 0.40 in the reference */
+  /* outputs, as iak_pack_metadata writes them: page_table [batch, Ht, table_width]
+   * holding bases[b*Ht + h] + logical page id (bases NULL = 0), pad_value
+   * padded; page_counts [batch, Ht] = min(n, table_width); num_selected
+   * [batch] = n before truncation or -1 (or NULL); page_prec [batch,
+   * table_width] IAK_PREC_* of each listed page, IAK_PREC_SKIP padded (or
+   * NULL); when page_tags is set, prec_to_tag[prec] is also stored at
+   * page_tags[physical id] for every head (ids outside [0, num_tag_pages)
+   * are dropped) */
+  const int32_t* bases;
+  int32_t table_width, pad_value;
+  int32_t* page_table;
+  int32_t* page_counts;
+  int32_t* num_selected;
+  uint8_t* page_prec;
+  uint8_t* page_tags; int64_t num_tag_pages;
+  uint8_t prec_to_tag[6];
+} iak_route_args;
+int iak_route_pages(const iak_route_args* args, void* stream);
+
 /* Metadata packing on the device.  Logical page ids (one list shared by
  * every (b, h), the router's selected_page_ids order) are mapped to
  * physical ids base[b*Ht + h] + logical, written -1 padded into

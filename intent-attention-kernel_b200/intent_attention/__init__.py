@@ -43,6 +43,7 @@ from .triton_adaptive_format_attention import (
     make_adaptive_page_tables,
 )
 from .paged import PagePool, merge_partials, pack_metadata, paged_decode
+from .device_router import LayoutBatch, RoutedPages, encode_layouts, route_layouts, route_pages
 from .split_kv import (
     SequenceShardedDecoder,
     decode_partial_block,
@@ -63,5 +64,6 @@ __all__ = [
     "AdaptiveFormatKernelConfig", "AdaptivePageFormat", "adaptive_format_decode_attention_triton",
     "make_adaptive_page_tables",
     "PagePool", "merge_partials", "pack_metadata", "paged_decode",
+    "LayoutBatch", "RoutedPages", "encode_layouts", "route_layouts", "route_pages",
     "SequenceShardedDecoder", "decode_partial_block", "merge_partial_blocks", "shard_bounds", "shard_page_lists",
 ]

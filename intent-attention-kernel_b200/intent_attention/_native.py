@@ -92,6 +92,28 @@ class MlaArgs(ctypes.Structure):
 
 MLA_SKIP, MLA_DENSE, MLA_FP8 = 0, 1, 2
 
+POLICY_ALWAYS, POLICY_ATTEND, POLICY_SKIP, POLICY_RECENT, POLICY_GLOBAL = range(5)
+PREC_FP16, PREC_FP8, PREC_INT8, PREC_INT4, PREC_INT4_RESIDUAL, PREC_SKIP = range(6)
+ROUTE_MAX_BLOCKS = 8192
+
+
+class RouteArgs(ctypes.Structure):
+    _fields_ = [
+        ("num_blocks", c_i32), ("block_counts", c_void_p),
+        ("block_start", c_void_p), ("block_end", c_void_p), ("block_policy", c_void_p),
+        ("layout_stride", c_i64),
+        ("scores", c_void_p), ("score_stride", c_i64),
+        ("seq_lens", c_void_p),
+        ("batch", c_i32), ("num_table_heads", c_i32), ("page_size", c_i32),
+        ("top_k_blocks", c_i32), ("preserve_recent", c_i32), ("preserve_global", c_i32),
+        ("score_threshold", ctypes.c_double), ("memory_pressure", ctypes.c_double),
+        ("high_score_threshold", ctypes.c_double), ("medium_score_threshold", ctypes.c_double),
+        ("bases", c_void_p), ("table_width", c_i32), ("pad_value", c_i32),
+        ("page_table", c_void_p), ("page_counts", c_void_p), ("num_selected", c_void_p),
+        ("page_prec", c_void_p),
+        ("page_tags", c_void_p), ("num_tag_pages", c_i64), ("prec_to_tag", ctypes.c_uint8 * 6),
+    ]
+
 MAX_PEERS = 8
 
 
@@ -111,6 +133,7 @@ SIGNATURES = {
     "iak_merge_partials": (ctypes.c_int, [c_void_p, c_void_p, c_void_p, c_i64, c_i32, c_i32, c_void_p, c_i32,
                                           c_i64, c_void_p]),
     "iak_pack_metadata": (ctypes.c_int, [ctypes.POINTER(PackArgs), c_void_p]),
+    "iak_route_pages": (ctypes.c_int, [ctypes.POINTER(RouteArgs), c_void_p]),
     "iak_quantize_pages": (ctypes.c_int, [ctypes.POINTER(QuantArgs), c_void_p]),
     "iak_decode_noalloc": (ctypes.c_int, [ctypes.POINTER(PagePools), ctypes.POINTER(DecodeArgs), c_void_p]),
     "iak_merge_partial_blocks": (ctypes.c_int, [c_void_p, c_i32, c_i64, c_i32, c_void_p, c_i32, c_i64, c_void_p]),

@@ -48,28 +48,20 @@ def test_version_and_error_query():
     assert b"merge" in L.iak_last_error()
 
 
+_STRUCTS = {"iak_page_pools": N.PagePools, "iak_decode_args": N.DecodeArgs, "iak_pack_args": N.PackArgs,
+            "iak_quant_args": N.QuantArgs, "iak_mla_args": N.MlaArgs, "iak_peer_exchange": N.PeerExchange,
+            "iak_route_args": N.RouteArgs}
+
+
 def test_struct_layout_matches_header():
-    prog = r"""
-#include <stdio.h>
-#include <stddef.h>
-#include "intent_attention_b200.h"
-#define P(T, f) printf(#T "." #f " %zu\n", offsetof(T, f));
-int main(void) {
-  printf("iak_page_pools %zu\n", sizeof(iak_page_pools));
-  printf("iak_decode_args %zu\n", sizeof(iak_decode_args));
-  printf("iak_pack_args %zu\n", sizeof(iak_pack_args));
-  printf("iak_quant_args %zu\n", sizeof(iak_quant_args));
-  printf("iak_mla_args %zu\n", sizeof(iak_mla_args));
-  printf("iak_peer_exchange %zu\n", sizeof(iak_peer_exchange));
-  P(iak_peer_exchange, rank) P(iak_peer_exchange, rows) P(iak_peer_exchange, head_dim)
-  P(iak_page_pools, num_pages) P(iak_page_pools, scale_mode)
-  P(iak_decode_args, tag_map) P(iak_decode_args, sm_scale) P(iak_decode_args, partial_acc) P(iak_decode_args, num_splits) P(iak_decode_args, kernel)
-  P(iak_pack_args, pad_value) P(iak_quant_args, scale_mode) P(iak_quant_args, num_pages)
-  P(iak_mla_args, dense_pages) P(iak_mla_args, num_pages) P(iak_mla_args, page_table) P(iak_mla_args, tag_map)
-  P(iak_mla_args, sm_scale) P(iak_mla_args, partial_acc) P(iak_mla_args, kernel)
-  return 0;
-}
-"""
+    """sizeof and every field offset of each ctypes mirror equal the C compiler's."""
+    lines = []
+    for cname, ct in _STRUCTS.items():
+        lines.append(f'  printf("{cname} %zu\\n", sizeof({cname}));')
+        for f, _ in ct._fields_:
+            lines.append(f'  printf("{cname}.{f} %zu\\n", offsetof({cname}, {f}));')
+    prog = ("#include <stdio.h>\n#include <stddef.h>\n#include \"intent_attention_b200.h\"\n"
+            "int main(void) {\n" + "\n".join(lines) + "\n  return 0;\n}\n")
     with tempfile.TemporaryDirectory() as d:
         c = os.path.join(d, "t.c")
         exe = os.path.join(d, "t")
@@ -79,12 +71,42 @@ int main(void) {
             pytest.skip("gcc unavailable: " + r.stderr[:200])
         out = subprocess.run([exe], capture_output=True, text=True).stdout
     got = dict(line.rsplit(" ", 1) for line in out.strip().splitlines())
-    types = {"iak_page_pools": N.PagePools, "iak_decode_args": N.DecodeArgs, "iak_pack_args": N.PackArgs,
-             "iak_quant_args": N.QuantArgs, "iak_mla_args": N.MlaArgs,
-             "iak_peer_exchange": N.PeerExchange}
+    assert len(got) == sum(1 + len(ct._fields_) for ct in _STRUCTS.values())
     for k, v in got.items():
         if "." in k:
             t, f = k.split(".")
-            assert getattr(types[t], f).offset == int(v), k
+            assert getattr(_STRUCTS[t], f).offset == int(v), k
         else:
-            assert ctypes.sizeof(types[k]) == int(v), k
+            assert ctypes.sizeof(_STRUCTS[k]) == int(v), k
+
+
+def test_route_args_rejected_on_the_host():
+    """iak_route_pages validates its scalars before any device call
+    (memory_pressure outside [0, 1] is a ValueError in IntentQuantizer)."""
+    L = N.lib()
+    a = N.RouteArgs()
+    a.batch, a.num_table_heads, a.page_size, a.num_blocks = 1, 1, 16, 4
+    a.memory_pressure = 1.5
+    assert L.iak_route_pages(ctypes.byref(a), None) == N.IAK_ERR_INVALID_ARG
+    assert b"memory_pressure" in L.iak_last_error()
+    a.memory_pressure = float("nan")
+    assert L.iak_route_pages(ctypes.byref(a), None) == N.IAK_ERR_INVALID_ARG
+    a.memory_pressure = 0.5
+    a.page_size = 0
+    assert L.iak_route_pages(ctypes.byref(a), None) == N.IAK_ERR_INVALID_ARG
+    a.page_size = 16
+    a.num_blocks = N.ROUTE_MAX_BLOCKS + 1
+    assert L.iak_route_pages(ctypes.byref(a), None) == N.IAK_ERR_UNSUPPORTED
+    a.num_blocks = 4
+    a.layout_stride = 2
+    assert L.iak_route_pages(ctypes.byref(a), None) == N.IAK_ERR_INVALID_ARG
+    a.layout_stride = 0
+    a.page_tags = 1
+    a.prec_to_tag[3] = 16
+    assert L.iak_route_pages(ctypes.byref(a), None) == N.IAK_ERR_INVALID_ARG
+    a.page_tags = None
+    # batch 0 is a no-op; missing outputs are an argument error
+    a.batch = 0
+    assert L.iak_route_pages(ctypes.byref(a), None) == N.IAK_OK
+    a.batch = 2
+    assert L.iak_route_pages(ctypes.byref(a), None) == N.IAK_ERR_INVALID_ARG
