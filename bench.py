@@ -1,6 +1,6 @@
 """Benchmark: fused selected-quant paged decode on B200 (sm_100a).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload c2|c3|c4|c5|c1] [--impl b200|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload c2|c3|c4|c5|c1|route] [--impl b200|reference]
 
 One "step" is one decode step of the workload's whole batch (all sequences,
 all heads) over its router-selected pages.  ``value`` is the selected-KV HBM
@@ -793,12 +793,185 @@ def run_gpu_mla(args):
         dist.destroy_process_group()
 
 
+# --------------------------------------------------------------------------- #
+#  Device router (iak_route_pages) on the C2 layout
+# --------------------------------------------------------------------------- #
+
+ROUTE_METRIC = "device router: sequences routed (block routing + page list + precision map + table rows) per s"
+
+
+def route_workload(batch: int = 0):
+    """C2's semantic layout (system prompt, 64-token ATTEND blocks, recent
+    tail) for every sequence of the batch, each with its own seeded scores."""
+    from intent_attention import BlockLayout, BlockPolicy, RouterConfig, SemanticBlock
+    w = workload("c2")
+    if batch:
+        w["B"] = batch
+    PS, T = w["PS"], w["T"]
+    rng = np.random.default_rng(w["seed"] + 77)
+    bt = w["attend_block_pages"] * PS
+    mid_start, mid_end = w["head_tokens"], T - w["tail_tokens"]
+    layouts = []
+    for _ in range(w["B"]):
+        blocks = [SemanticBlock("system", 0, w["head_tokens"], BlockPolicy.ALWAYS)]
+        for i in range((mid_end - mid_start) // bt):
+            blocks.append(SemanticBlock(f"doc{i}", mid_start + i * bt, mid_start + (i + 1) * bt, BlockPolicy.ATTEND,
+                                        score=float(rng.random())))
+        blocks.append(SemanticBlock("recent", mid_end, T, BlockPolicy.RECENT))
+        layouts.append(BlockLayout(blocks))
+    fixed = (w["head_tokens"] + w["tail_tokens"]) // PS
+    cfg = RouterConfig(top_k_blocks=(w["select_pages"] - fixed) // w["attend_block_pages"], memory_pressure=0.0)
+    return w, layouts, cfg
+
+
+def cpu_route(w, layouts, cfg, budget_s: float):
+    """Host routing per sequence (route_layout + selected_page_ids + the
+    precision map of routing_to_kernel_metadata + table rows): seconds per
+    sequence over a bounded sample."""
+    from intent_attention import BlockRouter, routing_to_kernel_metadata
+    router = BlockRouter(cfg)
+    PS, T, Hkv, NLP = w["PS"], w["T"], w["Hkv"], w["T"] // w["PS"]
+    t0 = time.perf_counter()
+    done = 0
+    while done < len(layouts) and (time.perf_counter() - t0 < budget_s or done == 0):
+        routed = router.route_layout(layouts[done], T)
+        meta = routing_to_kernel_metadata(routed, PS)
+        ids = np.asarray(meta["selected_page_ids"], dtype=np.int32)
+        rows = (np.arange(Hkv, dtype=np.int32)[:, None] + done * Hkv) * NLP + ids[None, :]
+        _ = rows, [meta["block_precision_by_page"][str(p)] for p in ids[:4]]
+        done += 1
+    return (time.perf_counter() - t0) / done, done
+
+
+def run_route(args):
+    import torch
+    from intent_attention import KVPrecision, encode_layouts, route_pages
+    from intent_attention.device_router import RoutedPages
+    w, layouts, cfg = route_workload(args.batch)
+    if args.impl == "reference":
+        vals, n = [], 0
+        for i in range(args.warmup + args.steps):
+            sec, n = cpu_route(w, layouts, cfg, args.cpu_budget / max(1, args.steps + args.warmup))
+            if i >= args.warmup:
+                vals.append(sec)
+        v = 1.0 / statistics.median(vals)
+        print(json.dumps({"impl": "reference", "metric": ROUTE_METRIC, "value": round(v, 2), "unit": "seq/s",
+                          "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+                          "ms_per_step": round(w["B"] / v * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+                          "vs_baseline": None, "dtype": "float64 scores", "data": "synthetic",
+                          "config": {"workload": "C2 layout routing", "batch": w["B"]},
+                          "cpu_baseline": {"value": round(v, 2), "unit": "seq/s", "cores": 1, "kind": "port",
+                                           "sample": f"{n} sequences per step through the host BlockRouter"},
+                          "e2e": {"value": round(v, 2), "unit": "seq/s", "h2d_bytes_per_step": 0,
+                                  "d2h_bytes_per_step": 0}}), flush=True)
+        return
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    B, Hkv, PS, T = w["B"], w["Hkv"], w["PS"], w["T"]
+    NLP, W = T // PS, T // PS
+    batch = encode_layouts(layouts, device)
+    nb = batch.num_blocks
+    bases = (torch.arange(B * Hkv, dtype=torch.int32, device=device) * NLP).view(B, Hkv)
+    tags = torch.zeros(B * Hkv * NLP, dtype=torch.uint8, device=device)
+    prec_to_tag = {KVPrecision.FP16: 1, KVPrecision.FP8: 2, KVPrecision.INT8: 3, KVPrecision.INT4: 4,
+                   KVPrecision.INT4_RESIDUAL: 5, KVPrecision.SKIP: 0}
+    out = RoutedPages(torch.empty((B, Hkv, W), dtype=torch.int32, device=device),
+                      torch.empty((B, Hkv), dtype=torch.int32, device=device),
+                      torch.empty(B, dtype=torch.int32, device=device),
+                      torch.empty((B, W), dtype=torch.uint8, device=device))
+
+    def step(lb=batch):
+        route_pages(lb, cfg, PS, W, table_heads=Hkv, bases=bases, page_tags=tags, prec_to_tag=prec_to_tag, out=out)
+
+    step()
+    torch.cuda.synchronize()
+    n_sel = out.num_selected.cpu()
+    assert (n_sel == w["select_pages"]).all(), n_sel
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(0) as clocks:
+        t_probe = time.perf_counter()
+        while len(clocks.rows) < 3 and time.perf_counter() - t_probe < 3.0:
+            for _ in range(50):
+                step()
+            torch.cuda.synchronize()
+        for _ in range(args.warmup):
+            step()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for _ in range(args.steps):
+                step()
+        graph.replay()
+        torch.cuda.synchronize()
+        ev0.record()
+        graph.replay()
+        ev1.record()
+        torch.cuda.synchronize()
+    t_ms = ev0.elapsed_time(ev1) / args.steps
+    del graph
+    # end to end: per-sequence scores from pinned host memory, counts and
+    # selected totals back to the host
+    scores_host = batch.scores.cpu().pin_memory()
+    counts_host = torch.empty((B, Hkv), dtype=torch.int32).pin_memory()
+    nsel_host = torch.empty(B, dtype=torch.int32).pin_memory()
+    scores_dev = torch.empty_like(batch.scores)
+    from intent_attention import LayoutBatch
+    lb_e2e = LayoutBatch(batch.start, batch.end, batch.policy, scores_dev, batch.counts)
+
+    def e2e_step():
+        scores_dev.copy_(scores_host, non_blocking=True)
+        step(lb_e2e)
+        counts_host.copy_(out.page_counts, non_blocking=True)
+        nsel_host.copy_(out.num_selected, non_blocking=True)
+
+    for _ in range(args.warmup):
+        e2e_step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / args.steps
+    # algorithmic bytes per launch: layout + scores read, table rows / counts /
+    # precisions / tags written
+    n = w["select_pages"]
+    nbytes = B * (nb * (4 + 4 + 1 + 8) + Hkv * W * 4 + Hkv * 4 + 4 + W + Hkv * n)
+    peak, peak_kind = measured_hbm_peak()
+    gbs = nbytes / (t_ms * 1e-3) / 1e9
+    rec = {"metric": ROUTE_METRIC, "value": round(B / (t_ms * 1e-3), 1), "unit": "seq/s", "n_gpus": 1,
+           "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t_ms, 5),
+           "us_per_step": round(t_ms * 1e3, 2), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+           "dtype": "float64 scores, int32 pages", "data": "synthetic (seeded per-sequence block scores)",
+           "config": {"workload": "C2 layout routing (iak_route_pages)", "batch": B, "blocks_per_seq": nb,
+                      "kv_heads": Hkv, "page_size": PS, "table_width": W, "pages_listed_per_seq": n,
+                      "top_k_blocks": cfg.top_k_blocks,
+                      "l2": "inputs smaller than L2 (a per-step router reads its layout from L2 in practice)",
+                      "timing": "one CUDA graph of all timed launches, replayed once after a warm-up replay"},
+           "roofline": {"bound": "hbm", "achieved": round(gbs, 2), "peak": peak, "unit": "GB/s",
+                        "frac": round(gbs / peak, 5), "traffic": None, "kernel": "route_kernel",
+                        "kernel_us": round(t_ms * 1e3, 2),
+                        "note": f"peak = {peak_kind} HBM copy bandwidth; latency-bound (one CTA per sequence, "
+                                "bitonic sort + 4 CTA scans), not bandwidth-bound"},
+           "e2e": {"value": round(B / (e2e_ms * 1e-3), 1), "unit": "seq/s", "ms_per_step": round(e2e_ms, 5),
+                   "h2d_bytes_per_step": scores_host.numel() * 8,
+                   "d2h_bytes_per_step": counts_host.numel() * 4 + nsel_host.numel() * 4,
+                   "api": "intent_attention.route_pages with pinned host scores in, counts out"},
+           "gpu_launches": args.steps, "clocks": clocks.summary()}
+    if not args.no_cpu_baseline:
+        sec, done = cpu_route(w, layouts, cfg, args.cpu_budget)
+        rec["cpu_baseline"] = {"value": round(1.0 / sec, 2), "unit": "seq/s", "cores": 1, "kind": "port",
+                               "sample": f"{done} sequences through the host BlockRouter (route_layout + "
+                                         "routing_to_kernel_metadata + table rows)"}
+    print(json.dumps(rec), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--workload", default="c2", choices=["c1", "c2", "c3", "c4", "c5"])
+    ap.add_argument("--workload", default="c2", choices=["c1", "c2", "c3", "c4", "c5", "route"])
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--splits", type=int, default=0)
     ap.add_argument("--batch", type=int, default=0, help="override the workload's batch (profiling runs)")
@@ -810,7 +983,9 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.impl == "reference":
+    if args.workload == "route":
+        run_route(args)
+    elif args.impl == "reference":
         run_reference(args)
     elif args.workload == "c4":
         run_gpu_mla(args)

@@ -398,6 +398,65 @@ typedef struct iak_quant_args {
 } iak_quant_args;
 int iak_quantize_pages(const iak_quant_args* args, void* stream);
 
+/* ------------------------------------------------------------------------
+ * KV append with quantise-on-write, and page format transitions.
+ *
+ * iak_append_tokens replaces, on the device and for a whole batch, the
+ * page writes of kv_memory_manager.py:225-256 KVMemoryManager.write_page
+ * (quantise a page on write into its storage format; the device precedent is
+ * triton_kernel.py:186-279 _quant_kernel) for tokens produced while decoding.
+ * num_new new K/V rows of every (sequence b, table head h) go to logical
+ * token positions positions[b] .. positions[b]+num_new-1, i.e. to physical
+ * page bases[b*Ht+h] + pos / page_size, row pos % page_size.  Each touched
+ * page is re-quantised in the format its tag names (tag_map as in
+ * iak_decode_args) from the rows staged for it, with the arithmetic of
+ * iak_quantize_pages, so a page always holds exactly what quantising its
+ * dense rows (zeros past the last appended row) gives.  The stage keeps the
+ * rows of each (b, h)'s open page between calls: a page that begins inside
+ * the appended range is restaged from zero; the rows of a page opened by
+ * an earlier call are taken from the stage.  Pages outside [0, num_pages)
+ * are not written and are counted in *dropped (when given).
+ * new_lengths[b] = positions[b] + num_new when given (may alias nothing
+ * read by the call).
+ * ------------------------------------------------------------------------ */
+typedef struct iak_append_args {
+  const void* k_new; const void* v_new;  /* [batch, Ht, num_new, head_dim] contiguous      */
+  int32_t new_dtype;                     /* IAK_DT_*                                       */
+  int32_t batch, num_table_heads, num_new;
+  const int32_t* positions;              /* [batch] index of the first appended token      */
+  int32_t* new_lengths;                  /* [batch] or NULL                                */
+  const int32_t* bases;                  /* [batch*Ht] physical id of logical page 0, NULL = 0 */
+  const void* page_tags; int32_t tag_bytes;              /* 1 (uint8) or 4 (int32)       */
+  uint8_t tag_map[16]; uint8_t tag_default;
+  float* k_stage; float* v_stage;        /* [batch*Ht, page_size, head_dim] fp32           */
+  int32_t* dropped;                      /* device counter or NULL                         */
+} iak_append_args;
+int iak_append_tokens(const iak_page_pools* pools, const iak_append_args* args, void* stream);
+
+/* Page format transitions (demotion / promotion): replaces
+ * kv_memory_manager.py:258-274 KVMemoryManager.set_page_format as used by
+ * demote_cold_pages / promote_hot_pages / _prefetch_warmup (:329-362).  Each
+ * listed page is read in its current format (its tag through tag_map;
+ * dequantised as the decode kernels read it: code x scale in fp32) and
+ * re-quantised into new_formats[i] with the arithmetic of
+ * iak_quantize_pages; then fmt_to_tag[new format] is stored as its tag.
+ * A page already in its target format is left untouched (set_page_format
+ * returns early); SKIP / SPARSE pages read as zeros; converting to SKIP /
+ * SPARSE only retags.  page_ids must be distinct; ids outside
+ * [0, num_pages) are ignored; a page whose target pool (or scales) is absent
+ * is left untouched and counted in *rejected (when given).
+ * page_size * head_dim <= IAK_CONVERT_MAX_ELEMS. */
+#define IAK_CONVERT_MAX_ELEMS 16384
+typedef struct iak_convert_args {
+  const int32_t* page_ids; int32_t num_ids;
+  const uint8_t* new_formats;            /* [num_ids] IAK_FMT_*                            */
+  void* page_tags; int32_t tag_bytes;    /* read for the current format, then rewritten    */
+  uint8_t tag_map[16]; uint8_t tag_default;
+  uint8_t fmt_to_tag[8];                 /* tag written for each IAK_FMT_* target          */
+  int32_t* rejected;                     /* device counter or NULL                         */
+} iak_convert_args;
+int iak_convert_pages(const iak_page_pools* pools, const iak_convert_args* args, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -42,7 +42,7 @@ from .triton_adaptive_format_attention import (
     adaptive_format_decode_attention_triton,
     make_adaptive_page_tables,
 )
-from .paged import PagePool, merge_partials, pack_metadata, paged_decode
+from .paged import KVStage, PagePool, append_tokens, convert_pages, merge_partials, pack_metadata, paged_decode
 from .device_router import LayoutBatch, RoutedPages, encode_layouts, route_layouts, route_pages
 from .split_kv import (
     SequenceShardedDecoder,
@@ -63,7 +63,7 @@ __all__ = [
     "make_page_tables_from_selected_pages", "make_precision_tensor",
     "AdaptiveFormatKernelConfig", "AdaptivePageFormat", "adaptive_format_decode_attention_triton",
     "make_adaptive_page_tables",
-    "PagePool", "merge_partials", "pack_metadata", "paged_decode",
+    "PagePool", "merge_partials", "pack_metadata", "paged_decode", "KVStage", "append_tokens", "convert_pages",
     "LayoutBatch", "RoutedPages", "encode_layouts", "route_layouts", "route_pages",
     "SequenceShardedDecoder", "decode_partial_block", "merge_partial_blocks", "shard_bounds", "shard_page_lists",
 ]

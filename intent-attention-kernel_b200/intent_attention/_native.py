@@ -92,6 +92,27 @@ class MlaArgs(ctypes.Structure):
 
 MLA_SKIP, MLA_DENSE, MLA_FP8 = 0, 1, 2
 
+CONVERT_MAX_ELEMS = 16384
+
+
+class AppendArgs(ctypes.Structure):
+    _fields_ = [
+        ("k_new", c_void_p), ("v_new", c_void_p), ("new_dtype", c_i32),
+        ("batch", c_i32), ("num_table_heads", c_i32), ("num_new", c_i32),
+        ("positions", c_void_p), ("new_lengths", c_void_p), ("bases", c_void_p),
+        ("page_tags", c_void_p), ("tag_bytes", c_i32), ("tag_map", ctypes.c_uint8 * 16),
+        ("tag_default", ctypes.c_uint8),
+        ("k_stage", c_void_p), ("v_stage", c_void_p), ("dropped", c_void_p),
+    ]
+
+
+class ConvertArgs(ctypes.Structure):
+    _fields_ = [
+        ("page_ids", c_void_p), ("num_ids", c_i32), ("new_formats", c_void_p),
+        ("page_tags", c_void_p), ("tag_bytes", c_i32), ("tag_map", ctypes.c_uint8 * 16),
+        ("tag_default", ctypes.c_uint8), ("fmt_to_tag", ctypes.c_uint8 * 8), ("rejected", c_void_p),
+    ]
+
 POLICY_ALWAYS, POLICY_ATTEND, POLICY_SKIP, POLICY_RECENT, POLICY_GLOBAL = range(5)
 PREC_FP16, PREC_FP8, PREC_INT8, PREC_INT4, PREC_INT4_RESIDUAL, PREC_SKIP = range(6)
 ROUTE_MAX_BLOCKS = 8192
@@ -134,6 +155,8 @@ SIGNATURES = {
                                           c_i64, c_void_p]),
     "iak_pack_metadata": (ctypes.c_int, [ctypes.POINTER(PackArgs), c_void_p]),
     "iak_route_pages": (ctypes.c_int, [ctypes.POINTER(RouteArgs), c_void_p]),
+    "iak_append_tokens": (ctypes.c_int, [ctypes.POINTER(PagePools), ctypes.POINTER(AppendArgs), c_void_p]),
+    "iak_convert_pages": (ctypes.c_int, [ctypes.POINTER(PagePools), ctypes.POINTER(ConvertArgs), c_void_p]),
     "iak_quantize_pages": (ctypes.c_int, [ctypes.POINTER(QuantArgs), c_void_p]),
     "iak_decode_noalloc": (ctypes.c_int, [ctypes.POINTER(PagePools), ctypes.POINTER(DecodeArgs), c_void_p]),
     "iak_merge_partial_blocks": (ctypes.c_int, [c_void_p, c_i32, c_i64, c_i32, c_void_p, c_i32, c_i64, c_void_p]),

@@ -351,3 +351,104 @@ def pack_metadata(logical_ids: torch.Tensor, batch: int, table_heads: int, width
     a.page_table, a.page_counts, a.pad_value = page_table.data_ptr(), page_counts.data_ptr(), pad_value
     N.check(N.lib().iak_pack_metadata(ctypes.byref(a), _stream(dev)), "iak_pack_metadata")
     return page_table, page_counts
+
+
+# --------------------------------------------------------------------------- #
+#  KV append (quantise-on-write) and page format transitions
+# --------------------------------------------------------------------------- #
+
+@dataclass
+class KVStage:
+    """fp32 rows of every (sequence, table head)'s open page, [units, PS, D]
+    per plane, kept between ``append_tokens`` calls."""
+
+    k: torch.Tensor
+    v: torch.Tensor
+
+    @classmethod
+    def allocate(cls, units: int, pool: PagePool, device=None) -> "KVStage":
+        dev = torch.device(device) if device is not None else pool.tensors()[0].device
+        shape = (units, pool.page_size, pool.head_dim)
+        return cls(torch.zeros(shape, dtype=torch.float32, device=dev),
+                   torch.zeros(shape, dtype=torch.float32, device=dev))
+
+
+def _tags_args(page_tags: torch.Tensor):
+    _require_cuda(page_tags, "page_tags")
+    if page_tags.dtype not in (torch.uint8, torch.int32) or not page_tags.is_contiguous():
+        raise ValueError("page_tags must be a contiguous uint8 or int32 tensor")
+    return page_tags.data_ptr(), page_tags.element_size()
+
+
+def append_tokens(pool: PagePool, k_new: torch.Tensor, v_new: torch.Tensor, positions: torch.Tensor,
+                  page_tags: torch.Tensor, tag_map: Sequence[int], stage: KVStage,
+                  bases: Optional[torch.Tensor] = None, new_lengths: Optional[torch.Tensor] = None,
+                  dropped: Optional[torch.Tensor] = None, tag_default: int = N.FMT_SKIP) -> None:
+    """Append ``k_new``/``v_new`` [B, Ht, n, D] at token ``positions[b]`` of
+    every (b, h) and re-quantise each touched page in the format its tag names.
+
+    Physical page of token t = ``bases[b, h]`` + t // page_size.  A page
+    always ends up holding what ``PagePool.quantize_`` gives for its dense
+    rows (zeros past the last appended row).  Never synchronises.
+    """
+    _require_cuda(k_new, "k_new")
+    if k_new.shape != v_new.shape or k_new.dim() != 4 or k_new.shape[-1] != pool.head_dim:
+        raise ValueError(f"k_new / v_new must both be [B, Ht, n, {pool.head_dim}]")
+    if k_new.dtype != v_new.dtype or k_new.dtype not in _DT:
+        raise ValueError("k_new / v_new must share a float32 / float16 / bfloat16 dtype")
+    B, Ht, n, _ = k_new.shape
+    dev = k_new.device
+    k_new, v_new = k_new.contiguous(), v_new.contiguous()
+    positions = positions.to(device=dev, dtype=torch.int32).contiguous()
+    if positions.numel() != B:
+        raise ValueError("positions must hold one entry per sequence")
+    for t in (stage.k, stage.v):
+        if t.dtype != torch.float32 or tuple(t.shape) != (B * Ht, pool.page_size, pool.head_dim) \
+                or not t.is_contiguous():
+            raise ValueError(f"stage planes must be contiguous float32 [{B * Ht}, {pool.page_size}, {pool.head_dim}]")
+    keep = [k_new, v_new, positions]
+    a = N.AppendArgs()
+    a.k_new, a.v_new, a.new_dtype = k_new.data_ptr(), v_new.data_ptr(), _DT[k_new.dtype]
+    a.batch, a.num_table_heads, a.num_new = B, Ht, n
+    a.positions = positions.data_ptr()
+    if new_lengths is not None:
+        if new_lengths.dtype != torch.int32 or new_lengths.numel() != B or new_lengths.data_ptr() == positions.data_ptr():
+            raise ValueError("new_lengths must be a separate int32 tensor of B entries")
+        a.new_lengths = new_lengths.data_ptr()
+    if bases is not None:
+        bases = bases.to(device=dev, dtype=torch.int32).contiguous()
+        keep.append(bases)
+        a.bases = bases.data_ptr()
+    a.page_tags, a.tag_bytes = _tags_args(page_tags)
+    for i, f in enumerate(tag_map):
+        a.tag_map[i] = f
+    a.tag_default = tag_default
+    a.k_stage, a.v_stage = stage.k.data_ptr(), stage.v.data_ptr()
+    if dropped is not None:
+        a.dropped = dropped.data_ptr()
+    s = pool.struct()
+    N.check(N.lib().iak_append_tokens(ctypes.byref(s), ctypes.byref(a), _stream(dev)), "iak_append_tokens")
+
+
+def convert_pages(pool: PagePool, page_ids: torch.Tensor, new_formats, page_tags: torch.Tensor,
+                  tag_map: Sequence[int], fmt_to_tag: Mapping[str, int], tag_default: int = N.FMT_SKIP,
+                  rejected: Optional[torch.Tensor] = None) -> None:
+    """Demote / promote pool pages: read each page in its current format,
+    re-quantise it into ``new_formats`` (names or IAK_FMT codes) and store
+    ``fmt_to_tag[format name]`` as its tag.  Never synchronises."""
+    dev = page_ids.device
+    _require_cuda(page_ids, "page_ids")
+    ids = page_ids.to(torch.int32).contiguous()
+    fm = _format_tensor(new_formats, ids.numel(), dev)
+    a = N.ConvertArgs()
+    a.page_ids, a.num_ids, a.new_formats = ids.data_ptr(), ids.numel(), fm.data_ptr()
+    a.page_tags, a.tag_bytes = _tags_args(page_tags)
+    for i, f in enumerate(tag_map):
+        a.tag_map[i] = f
+    a.tag_default = tag_default
+    for name, tag in fmt_to_tag.items():
+        a.fmt_to_tag[FORMAT_CODES[name.upper()]] = int(tag)
+    if rejected is not None:
+        a.rejected = rejected.data_ptr()
+    s = pool.struct()
+    N.check(N.lib().iak_convert_pages(ctypes.byref(s), ctypes.byref(a), _stream(dev)), "iak_convert_pages")
