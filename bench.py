@@ -1,6 +1,6 @@
 """Benchmark: fused selected-quant paged decode on B200 (sm_100a).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload c2|c3|c4|c5|c1|route] [--impl b200|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload c2|c3|c4|c5|c1|route|append] [--impl b200|reference]
 
 One "step" is one decode step of the workload's whole batch (all sequences,
 all heads) over its router-selected pages.  ``value`` is the selected-KV HBM
@@ -966,12 +966,166 @@ def run_route(args):
     print(json.dumps(rec), flush=True)
 
 
+# --------------------------------------------------------------------------- #
+#  KV append with quantise-on-write (iak_append_tokens) at the C2 shape
+# --------------------------------------------------------------------------- #
+
+APPEND_METRIC = "KV append: (sequence, kv-head) rows appended with their open page re-quantised, per s"
+
+
+def append_page_bytes(fmt_code: int, PS: int, D: int) -> int:
+    """Algorithmic bytes of one (unit, plane) append: new bf16 row in, the
+    fp32 row into the stage, the staged page read back, the page's codes and
+    scale written."""
+    codes = {1: 2 * D, 2: D, 3: D}[fmt_code] * PS
+    scales = 0 if fmt_code == 1 else 4
+    return 2 * D + 4 * D + 4 * PS * D + codes + scales
+
+
+def cpu_append(w, fmt_units, budget_s):
+    """The oracle's page quantiser over sampled units (one page per plane per
+    unit): seconds per full step."""
+    import sys as _s
+    _s.path.insert(0, ROOT)
+    from oracle import quant as oq
+    g = np.random.default_rng(5)
+    PS, D = w["PS"], w["D"]
+    names = {1: "FP16", 2: "FP8", 3: "INT8"}
+    t0 = time.perf_counter()
+    done = 0
+    while done < len(fmt_units) and (time.perf_counter() - t0 < budget_s or done == 0):
+        page = g.standard_normal((1, PS, D)).astype(np.float32)
+        for _ in range(2):
+            oq.quantize_pages(page, names[int(fmt_units[done])], w["scale_mode"])
+        done += 1
+    return (time.perf_counter() - t0) / done * len(fmt_units), done
+
+
+def run_append(args):
+    import torch
+    from intent_attention import KVStage, PagePool, append_tokens
+    from intent_attention.paged import make_tag_map
+    w = workload("c2")
+    if args.batch:
+        w["B"] = args.batch
+    B, Hkv, D, PS = w["B"], w["Hkv"], w["D"], w["PS"]
+    units = B * Hkv
+    rng = np.random.default_rng(w["seed"] + 5)
+    mix = w["mix"]
+    fmt_units = rng.choice([FMT_CODE[k] for k in mix], size=units, p=list(mix.values())).astype(np.uint8)
+    if args.impl == "reference":
+        vals, n = [], 0
+        for i in range(args.warmup + args.steps):
+            sec, n = cpu_append(w, fmt_units, args.cpu_budget / max(1, args.steps + args.warmup))
+            if i >= args.warmup:
+                vals.append(sec)
+        v = units / statistics.median(vals)
+        print(json.dumps({"impl": "reference", "metric": APPEND_METRIC, "value": round(v, 1), "unit": "rows/s",
+                          "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+                          "ms_per_step": round(units / v * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+                          "vs_baseline": None, "dtype": "fp32 -> fp16/fp8/int8 pages", "data": "synthetic",
+                          "config": {"workload": "C2 decode-step KV append", "units": units},
+                          "cpu_baseline": {"value": round(v, 1), "unit": "rows/s", "cores": 1, "kind": "port",
+                                           "sample": f"{n} units per step through the oracle page quantiser"},
+                          "e2e": {"value": round(v, 1), "unit": "rows/s", "h2d_bytes_per_step": 0,
+                                  "d2h_bytes_per_step": 0}}), flush=True)
+        return
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    K = args.steps
+    pages_per_unit = (40 + K) // PS + 1
+    pool = PagePool.allocate(units * pages_per_unit, PS, D, sorted(mix), w["scale_mode"], device, zero=True)
+    tags = torch.from_numpy(np.repeat(fmt_units, pages_per_unit)).to(device)
+    bases = (torch.arange(units, dtype=torch.int32, device=device) * pages_per_unit).view(B, Hkv)
+    stage = KVStage.allocate(units, pool)
+    tag_map = make_tag_map({c: f for f, c in FMT_CODE.items() if f in mix})
+    g = torch.Generator(device=device).manual_seed(w["seed"])
+    k_rows = torch.randn((K, B, Hkv, 1, D), generator=g, device=device).to(torch.bfloat16)
+    v_rows = torch.randn((K, B, Hkv, 1, D), generator=g, device=device).to(torch.bfloat16)
+    # step i appends token 40 + i of every sequence: it lands mid-page, so
+    # every step re-quantises a partly filled open page
+    positions = [torch.full((B,), 40 + i, dtype=torch.int32, device=device) for i in range(K)]
+
+    def step(i):
+        append_tokens(pool, k_rows[i], v_rows[i], positions[i], tags, tag_map, stage, bases=bases)
+
+    for i in range(K):
+        step(i)
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(0) as clocks:
+        t_probe = time.perf_counter()
+        while len(clocks.rows) < 3 and time.perf_counter() - t_probe < 3.0:
+            for i in range(K):
+                step(i)
+            torch.cuda.synchronize()
+        for i in range(min(args.warmup, K)):
+            step(i)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for i in range(K):
+                step(i)
+        graph.replay()
+        torch.cuda.synchronize()
+        ev0.record()
+        graph.replay()
+        ev1.record()
+        torch.cuda.synchronize()
+    t_ms = ev0.elapsed_time(ev1) / K
+    del graph
+    # end to end: the new rows from pinned host memory each step
+    k_host = k_rows[0].cpu().pin_memory()
+    v_host = v_rows[0].cpu().pin_memory()
+    k_dev, v_dev = torch.empty_like(k_rows[0]), torch.empty_like(v_rows[0])
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for i in range(args.warmup):
+        k_dev.copy_(k_host, non_blocking=True)
+        v_dev.copy_(v_host, non_blocking=True)
+        append_tokens(pool, k_dev, v_dev, positions[i % K], tags, tag_map, stage, bases=bases)
+    torch.cuda.synchronize()
+    e0.record()
+    for i in range(K):
+        k_dev.copy_(k_host, non_blocking=True)
+        v_dev.copy_(v_host, non_blocking=True)
+        append_tokens(pool, k_dev, v_dev, positions[i], tags, tag_map, stage, bases=bases)
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / K
+    nbytes = 2 * sum(append_page_bytes(int(f), PS, D) for f in fmt_units)
+    peak, peak_kind = measured_hbm_peak()
+    gbs = nbytes / (t_ms * 1e-3) / 1e9
+    rec = {"metric": APPEND_METRIC, "value": round(units / (t_ms * 1e-3), 1), "unit": "rows/s", "n_gpus": 1,
+           "steps": K, "warmup": args.warmup, "ms_per_step": round(t_ms, 5), "us_per_step": round(t_ms * 1e3, 2),
+           "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+           "dtype": "bf16 rows -> fp16/fp8/int8 pages (fp32 stage)", "data": "synthetic (seeded N(0,1) rows)",
+           "config": {"workload": "C2 decode-step KV append (iak_append_tokens)", "batch": B, "kv_heads": Hkv,
+                      "head_dim": D, "page_size": PS, "rows_per_step": units, "format_mix": mix,
+                      "scale_mode": w["scale_mode"],
+                      "l2": "inputs smaller than L2 (the open pages of a decode step stay L2-resident)",
+                      "timing": "one CUDA graph of all timed launches, replayed once after a warm-up replay"},
+           "roofline": {"bound": "hbm", "achieved": round(gbs, 2), "peak": peak, "unit": "GB/s",
+                        "frac": round(gbs / peak, 5), "traffic": None, "kernel": "append_kernel",
+                        "kernel_us": round(t_ms * 1e3, 2),
+                        "note": f"peak = {peak_kind} HBM copy bandwidth; {nbytes} algorithmic bytes per launch "
+                                "(new rows, stage row write, staged page re-read, page codes + scales); one CTA "
+                                "per (unit, plane): latency-bound at this size"},
+           "e2e": {"value": round(units / (e2e_ms * 1e-3), 1), "unit": "rows/s", "ms_per_step": round(e2e_ms, 5),
+                   "h2d_bytes_per_step": 2 * k_host.numel() * k_host.element_size(), "d2h_bytes_per_step": 0,
+                   "api": "intent_attention.append_tokens with pinned host K/V rows in"},
+           "gpu_launches": K, "clocks": clocks.summary()}
+    if not args.no_cpu_baseline:
+        sec, done = cpu_append(w, fmt_units, args.cpu_budget)
+        rec["cpu_baseline"] = {"value": round(units / sec, 1), "unit": "rows/s", "cores": 1, "kind": "port",
+                               "sample": f"{done} of {units} units through the oracle page quantiser, extrapolated"}
+    print(json.dumps(rec), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--workload", default="c2", choices=["c1", "c2", "c3", "c4", "c5", "route"])
+    ap.add_argument("--workload", default="c2", choices=["c1", "c2", "c3", "c4", "c5", "route", "append"])
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--splits", type=int, default=0)
     ap.add_argument("--batch", type=int, default=0, help="override the workload's batch (profiling runs)")
@@ -985,6 +1139,8 @@ def main():
         args.warmup = 3
     if args.workload == "route":
         run_route(args)
+    elif args.workload == "append":
+        run_append(args)
     elif args.impl == "reference":
         run_reference(args)
     elif args.workload == "c4":

@@ -5,10 +5,11 @@
 // (routing_to_kernel_metadata), written straight into packed page-table rows.
 //
 // One CTA per sequence.  The per-block state lives in shared memory sized for
-// the longest layout of the launch: sort keys (ordered score bits + block
-// index, bitonic-sorted so that rank r is the r-th scored ATTEND block in
-// descending score, ties in layout order), routed positions, precisions and a
-// scan scratch array.  Routed positions come from three CTA-wide exclusive
+// the longest layout of the launch: sort keys (ordered score bits; rank r is
+// the r-th scored ATTEND block in descending score, ties in layout order, found
+// by counting for layouts of up to 1024 blocks and by a bitonic sort of
+// (key, index) pairs above that), routed positions, precisions and a scan
+// scratch array.  Routed positions come from three CTA-wide exclusive
 // scans (pinned blocks in layout order, the selected top-k in rank order,
 // selected SKIP-policy blocks in layout order); a fourth scan over the
 // per-block counts of first-occurrence pages gives every block its output
@@ -183,22 +184,41 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(const iak_route_ar
   if (scored) atomicAdd(&n_scored, scored);
   __syncthreads();
   const int nA = n_scored;
-  for (int size = 2; size <= n2; size <<= 1) {
-    for (int stride = size >> 1; stride > 0; stride >>= 1) {
-      for (int i = tid; i < n2; i += kRouteThreads) {
-        const int j = i ^ stride;
-        if (j > i) {
-          const bool up = (i & size) == 0;
-          const uint64_t ka = key[i], kb = key[j];
-          const int ia = kidx[i], ib = kidx[j];
-          const bool greater = ka > kb || (ka == kb && ia > ib);
-          if (greater == up) {
-            key[i] = kb; key[j] = ka;
-            kidx[i] = ib; kidx[j] = ia;
+  if (n <= kRouteThreads) {
+    // rank by counting: every scored block counts the keys before it (the
+    // reads are shared-memory broadcasts, no barrier per step); ranks are a
+    // permutation of [0, nA) because ties are broken by block index
+    if (tid < n) {
+      const uint64_t ki = key[tid];
+      if (ki != kNoKey) {
+        int r = 0;
+        for (int j = 0; j < n; ++j) {
+          const uint64_t kj = key[j];
+          r += (kj < ki) || (kj == ki && j < tid);
+        }
+        kidx[r] = tid;
+      }
+    }
+    __syncthreads();
+  } else {
+    // bitonic sort of (key, index) pairs
+    for (int size = 2; size <= n2; size <<= 1) {
+      for (int stride = size >> 1; stride > 0; stride >>= 1) {
+        for (int i = tid; i < n2; i += kRouteThreads) {
+          const int j = i ^ stride;
+          if (j > i) {
+            const bool up = (i & size) == 0;
+            const uint64_t ka = key[i], kb = key[j];
+            const int ia = kidx[i], ib = kidx[j];
+            const bool greater = ka > kb || (ka == kb && ia > ib);
+            if (greater == up) {
+              key[i] = kb; key[j] = ka;
+              kidx[i] = ib; kidx[j] = ia;
+            }
           }
         }
+        __syncthreads();
       }
-      __syncthreads();
     }
   }
   // top_k = scored_attends[:k] with Python slice bounds
@@ -235,7 +255,8 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(const iak_route_ar
 
   // ---- first-occurrence page counts and output offsets ------------------------
   // Page pg of selected block i is listed by i when no selected block that
-  // also covers pg comes earlier in routed order.
+  // also covers pg comes earlier in routed order.  Interior pages always are,
+  // so the pages a block lists form one run [first, first + cnt).
   auto owns = [&](int i, int pg) -> bool {
     const int me = pos[i];
     for (int j = i - 1; j >= 0 && (bend[j] - 1) / PS >= pg; --j)
@@ -244,40 +265,45 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(const iak_route_ar
       if (pos[j] >= 0 && pos[j] < me) return false;
     return true;
   };
+  int2* run = reinterpret_cast<int2*>(key);   // [nsel] (first listed page, block) by routed position
   for (int i = tid; i < n; i += kRouteThreads) {
     const int me = pos[i];
     if (me < 0) continue;
     const int ps = bstart[i] / PS, pe = (bend[i] - 1) / PS;
-    int cnt = pe - ps + 1;
-    if (!owns(i, ps)) --cnt;
+    const bool skip_first = !owns(i, ps);
+    int cnt = pe - ps + 1 - (skip_first ? 1 : 0);
     if (pe != ps && !owns(i, pe)) --cnt;
     work[me] = cnt;   // positions are a permutation of [0, nsel)
+    run[me] = make_int2(ps + (skip_first ? 1 : 0), i);
   }
   __syncthreads();
   const int total = cta_exclusive_scan(work, nsel, warp_sums);
-
-  // ---- emit ----------------------------------------------------------------
-  for (int i = tid; i < n; i += kRouteThreads) {
-    const int me = pos[i];
-    if (me < 0) continue;
-    const int ps = bstart[i] / PS, pe = (bend[i] - 1) / PS;
-    const int pr = prec[i];
-    int o = work[me];
-    for (int pg = ps; pg <= pe && o < W; ++pg) {
-      if ((pg == ps || pg == pe) && !owns(i, pg)) continue;
-      if (prow) prow[o] = static_cast<uint8_t>(pr);
-      for (int h = 0; h < Ht; ++h) {
-        const int32_t phys = (p.bases ? p.bases[static_cast<int64_t>(b) * Ht + h] : 0) + pg;
-        table[static_cast<int64_t>(h) * W + o] = phys;
-        if (p.page_tags && phys >= 0 && phys < p.num_tag_pages) p.page_tags[phys] = p.prec_to_tag[pr];
-      }
-      ++o;
-    }
-  }
   const int listed = min(total, W);
-  for (int o = listed + tid; o < W; o += kRouteThreads) {
-    if (prow) prow[o] = IAK_PREC_SKIP;
-    for (int h = 0; h < Ht; ++h) table[static_cast<int64_t>(h) * W + o] = p.pad_value;
+
+  // ---- emit: every slot in parallel, all heads per slot --------------------------
+  // slot o belongs to the last routed position r with work[r] <= o (positions
+  // that list no page share their successor's offset)
+  const int32_t* hbase = p.bases ? p.bases + static_cast<int64_t>(b) * Ht : nullptr;
+  for (int o = tid; o < W; o += kRouteThreads) {
+    if (o >= listed) {
+      for (int h = 0; h < Ht; ++h) table[static_cast<int64_t>(h) * W + o] = p.pad_value;
+      if (prow) prow[o] = IAK_PREC_SKIP;
+      continue;
+    }
+    int lo = 0, hi = nsel - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (work[mid] <= o) lo = mid; else hi = mid - 1;
+    }
+    const int2 r = run[lo];
+    const int pg = r.x + (o - work[lo]);
+    const int pr = prec[r.y];
+    if (prow) prow[o] = static_cast<uint8_t>(pr);
+    for (int h = 0; h < Ht; ++h) {
+      const int32_t phys = (hbase ? hbase[h] : 0) + pg;
+      table[static_cast<int64_t>(h) * W + o] = phys;
+      if (p.page_tags && phys >= 0 && phys < p.num_tag_pages) p.page_tags[phys] = p.prec_to_tag[pr];
+    }
   }
   for (int h = tid; h < Ht; h += kRouteThreads) counts[h] = listed;
   if (tid == 0 && p.num_selected) p.num_selected[b] = total;
