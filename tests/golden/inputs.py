@@ -64,3 +64,19 @@ def many_attend_layout(seed: int, n_blocks: int = 24, block_tokens: int = 64,
     cur += 96
     blocks.append(("recent", cur, cur + tail, "RECENT", None))
     return blocks
+
+
+# Layouts with block boundaries inside pages (prefill parity cases).
+PREFILL_PARTIAL_LAYOUT = [
+    ("sys", 0, 13, "ALWAYS", None),
+    ("tool", 13, 50, "SKIP", None),
+    ("doc", 50, 77, "ATTEND", 0.9),
+    ("doc_low", 77, 85, "ATTEND", 0.2),
+    ("recent", 85, 100, "RECENT", None),
+]
+# The first 32 tokens are skipped: causal queries 0..31 see no key.
+PREFILL_GAP_LAYOUT = [
+    ("skipped", 0, 32, "SKIP", None),
+    ("doc", 32, 80, "ATTEND", 0.7),
+    ("recent", 80, 96, "RECENT", None),
+]

@@ -313,6 +313,24 @@ def gen_router():
     print("wrote router_golden.json", len(cases), "cases")
 
 
+def gen_prefill():
+    """reference.py:82-130 semantic_block_attention (the exact-token CPU path)
+    with causal masks on the original token positions (reference.py:16-45)."""
+    from intent_attention.reference import semantic_block_attention
+    out = {}
+    cases = [("e2e_causal", gi.E2E_LAYOUT, (1, 2, 448, 64), 448, True),
+             ("e2e_chunk", gi.E2E_LAYOUT, (2, 2, 16, 64), 448, False),
+             ("partial_causal", gi.PREFILL_PARTIAL_LAYOUT, (2, 3, 100, 32), 100, True),
+             ("gap_causal", gi.PREFILL_GAP_LAYOUT, (1, 2, 96, 32), 96, True)]
+    for i, (name, spec, qshape, T_kv, causal) in enumerate(cases):
+        B, H, M, D = qshape
+        q = gi.normal(600 + 3 * i, qshape)
+        k = gi.normal(601 + 3 * i, (B, H, T_kv, D))
+        v = gi.normal(602 + 3 * i, (B, H, T_kv, D))
+        out[name] = semantic_block_attention(T(q), T(k), T(v), layout_of(spec), causal=causal).numpy()
+    save("prefill_golden.npz", **out)
+
+
 if __name__ == "__main__":
     torch.manual_seed(0)
     gen_quant()
@@ -321,3 +339,4 @@ if __name__ == "__main__":
     gen_triton_interp()
     gen_mla()
     gen_router()
+    gen_prefill()
