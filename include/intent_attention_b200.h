@@ -457,6 +457,39 @@ typedef struct iak_convert_args {
 } iak_convert_args;
 int iak_convert_pages(const iak_page_pools* pools, const iak_convert_args* args, void* stream);
 
+/* ------------------------------------------------------------------------
+ * Multi-query (prefill / chunked prefill) attention over selected pages.
+ *
+ * Replaces triton_kernel.py:74-181 _fwd_kernel and :285-410
+ * _fwd_kernel_quant as driven by :668-760 semantic_block_attention_triton,
+ * with the exact-token semantics of reference.py:82-130
+ * semantic_block_attention (causal masks on ORIGINAL token positions,
+ * reference.py:16-45) that the reference's GPU path lacks: per-page row
+ * masks select the rows of partially selected pages, and a key at token
+ * position (page - bases[b*Ht+h]) * page_size + row is visible to query m iff
+ * it is <= q_positions[b, m] (causal) .  Query rows that see no key are
+ * written as 0 (the reference's softmax gives NaN there).
+ * q [B, Hq, M, D], out [B, Hq, M, D]; G = Hq / Ht query heads share a
+ * page-table row.  page_size <= 64 when row_masks is given.
+ * ------------------------------------------------------------------------ */
+typedef struct iak_prefill_args {
+  const void* q; int32_t q_dtype; int64_t q_stride_b, q_stride_h, q_stride_m;
+  void* out; int32_t out_dtype; int64_t out_stride_b, out_stride_h, out_stride_m;
+  int32_t batch, num_q_heads, num_table_heads, num_queries;
+  const int32_t* q_positions;   /* [B, M] (row stride qp_stride_b) or NULL = m */
+  int64_t qp_stride_b;
+  int32_t causal;
+  const int32_t* page_table; int64_t pt_stride_b, pt_stride_h; int32_t table_width;
+  const int32_t* page_counts; int64_t pc_stride_b;    /* [B, Ht] or NULL = W     */
+  const int32_t* bases;         /* [B*Ht] or NULL = 0                             */
+  const uint64_t* row_masks;    /* [B, W] (row stride rm_stride_b): bit r = row r selected; NULL = all */
+  int64_t rm_stride_b;
+  const void* page_tags; int32_t tag_bytes; uint8_t tag_map[16]; uint8_t tag_default;
+  float sm_scale;
+  int32_t kernel;               /* IAK_KERNEL_AUTO / GENERIC / TENSOR             */
+} iak_prefill_args;
+int iak_prefill(const iak_page_pools* pools, const iak_prefill_args* args, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -95,6 +95,21 @@ MLA_SKIP, MLA_DENSE, MLA_FP8 = 0, 1, 2
 CONVERT_MAX_ELEMS = 16384
 
 
+class PrefillArgs(ctypes.Structure):
+    _fields_ = [
+        ("q", c_void_p), ("q_dtype", c_i32), ("q_stride_b", c_i64), ("q_stride_h", c_i64), ("q_stride_m", c_i64),
+        ("out", c_void_p), ("out_dtype", c_i32), ("out_stride_b", c_i64), ("out_stride_h", c_i64),
+        ("out_stride_m", c_i64),
+        ("batch", c_i32), ("num_q_heads", c_i32), ("num_table_heads", c_i32), ("num_queries", c_i32),
+        ("q_positions", c_void_p), ("qp_stride_b", c_i64), ("causal", c_i32),
+        ("page_table", c_void_p), ("pt_stride_b", c_i64), ("pt_stride_h", c_i64), ("table_width", c_i32),
+        ("page_counts", c_void_p), ("pc_stride_b", c_i64),
+        ("bases", c_void_p), ("row_masks", c_void_p), ("rm_stride_b", c_i64),
+        ("page_tags", c_void_p), ("tag_bytes", c_i32), ("tag_map", ctypes.c_uint8 * 16), ("tag_default", ctypes.c_uint8),
+        ("sm_scale", ctypes.c_float), ("kernel", c_i32),
+    ]
+
+
 class AppendArgs(ctypes.Structure):
     _fields_ = [
         ("k_new", c_void_p), ("v_new", c_void_p), ("new_dtype", c_i32),
@@ -157,6 +172,7 @@ SIGNATURES = {
     "iak_route_pages": (ctypes.c_int, [ctypes.POINTER(RouteArgs), c_void_p]),
     "iak_append_tokens": (ctypes.c_int, [ctypes.POINTER(PagePools), ctypes.POINTER(AppendArgs), c_void_p]),
     "iak_convert_pages": (ctypes.c_int, [ctypes.POINTER(PagePools), ctypes.POINTER(ConvertArgs), c_void_p]),
+    "iak_prefill": (ctypes.c_int, [ctypes.POINTER(PagePools), ctypes.POINTER(PrefillArgs), c_void_p]),
     "iak_quantize_pages": (ctypes.c_int, [ctypes.POINTER(QuantArgs), c_void_p]),
     "iak_decode_noalloc": (ctypes.c_int, [ctypes.POINTER(PagePools), ctypes.POINTER(DecodeArgs), c_void_p]),
     "iak_merge_partial_blocks": (ctypes.c_int, [c_void_p, c_i32, c_i64, c_i32, c_void_p, c_i32, c_i64, c_void_p]),

@@ -452,3 +452,79 @@ def convert_pages(pool: PagePool, page_ids: torch.Tensor, new_formats, page_tags
         a.rejected = rejected.data_ptr()
     s = pool.struct()
     N.check(N.lib().iak_convert_pages(ctypes.byref(s), ctypes.byref(a), _stream(dev)), "iak_convert_pages")
+
+
+# --------------------------------------------------------------------------- #
+#  Multi-query (prefill) attention over selected pages
+# --------------------------------------------------------------------------- #
+
+def paged_prefill(q: torch.Tensor, pool: PagePool, page_table: torch.Tensor, page_counts: Optional[torch.Tensor],
+                  page_tags: torch.Tensor, tag_map: Sequence[int], q_positions: Optional[torch.Tensor] = None,
+                  causal: bool = True, bases: Optional[torch.Tensor] = None,
+                  row_masks: Optional[torch.Tensor] = None, sm_scale: Optional[float] = None,
+                  out: Optional[torch.Tensor] = None, out_dtype: Optional[torch.dtype] = None,
+                  tag_default: int = N.FMT_SKIP, kernel: str = "auto") -> torch.Tensor:
+    """Attention of ``q`` [B, Hq, M, D] over the selected pages -> [B, Hq, M, D].
+
+    Unit (b, h) attends to the rows of ``page_table[b, h, :page_counts[b, h]]``
+    that ``row_masks[b, slot]`` (uint64 bit masks, None = every row) selects;
+    a row of page ``pid`` sits at token position ``(pid - bases[b, h]) *
+    page_size + row``.  With ``causal`` a key is visible to query m iff its
+    position <= ``q_positions[b, m]`` (default m).  Rows that see no key are 0.
+    """
+    _require_cuda(q, "q")
+    if q.dim() != 4:
+        raise ValueError("q must be [B, Hq, M, D]")
+    B, Hq, M, D = q.shape
+    if D != pool.head_dim:
+        raise ValueError(f"q head_dim {D} does not match the pool head_dim {pool.head_dim}")
+    if q.dtype not in _DT:
+        raise ValueError("q must be float32 / float16 / bfloat16")
+    if page_table.dim() != 3 or page_table.shape[0] != B or page_table.dtype != torch.int32:
+        raise ValueError(f"page_table must be int32 [B, Ht, W] with B={B}")
+    Ht, W = page_table.shape[1], page_table.shape[2]
+    dev = q.device
+    keep = []
+    if out is None:
+        out = torch.empty((B, Hq, M, D), dtype=out_dtype or q.dtype, device=dev)
+    a = N.PrefillArgs()
+    a.q, a.q_dtype = q.data_ptr(), _DT[q.dtype]
+    a.q_stride_b, a.q_stride_h, a.q_stride_m = q.stride(0), q.stride(1), q.stride(2)
+    if q.stride(3) != 1 or out.stride(3) != 1:
+        raise ValueError("q and out need a unit stride along head_dim")
+    a.out, a.out_dtype = out.data_ptr(), _DT[out.dtype]
+    a.out_stride_b, a.out_stride_h, a.out_stride_m = out.stride(0), out.stride(1), out.stride(2)
+    a.batch, a.num_q_heads, a.num_table_heads, a.num_queries = B, Hq, Ht, M
+    if q_positions is not None:
+        q_positions = q_positions.to(device=dev, dtype=torch.int32).contiguous()
+        if tuple(q_positions.shape) != (B, M):
+            raise ValueError("q_positions must be [B, M]")
+        keep.append(q_positions)
+        a.q_positions, a.qp_stride_b = q_positions.data_ptr(), M
+    a.causal = 1 if causal else 0
+    a.page_table, a.pt_stride_b, a.pt_stride_h = page_table.data_ptr(), page_table.stride(0), page_table.stride(1)
+    if page_table.stride(2) != 1:
+        raise ValueError("page_table rows must be contiguous")
+    a.table_width = W
+    if page_counts is not None:
+        if page_counts.dtype != torch.int32 or page_counts.dim() != 2 or page_counts.stride(1) != 1:
+            raise ValueError("page_counts must be int32 [B, Ht] with contiguous rows")
+        a.page_counts, a.pc_stride_b = page_counts.data_ptr(), page_counts.stride(0)
+    if bases is not None:
+        bases = bases.to(device=dev, dtype=torch.int32).contiguous()
+        keep.append(bases)
+        a.bases = bases.data_ptr()
+    if row_masks is not None:
+        if row_masks.dtype not in (torch.int64, torch.uint64) or tuple(row_masks.shape) != (B, W) \
+                or row_masks.stride(1) != 1:
+            raise ValueError("row_masks must be 64-bit [B, W] with contiguous rows")
+        a.row_masks, a.rm_stride_b = row_masks.data_ptr(), row_masks.stride(0)
+    a.page_tags, a.tag_bytes = _tags_args(page_tags)
+    for i, f in enumerate(tag_map):
+        a.tag_map[i] = f
+    a.tag_default = tag_default
+    a.sm_scale = float(1.0 / math.sqrt(D) if sm_scale is None else sm_scale)
+    a.kernel = N.KERNELS[kernel]
+    s = pool.struct()
+    N.check(N.lib().iak_prefill(ctypes.byref(s), ctypes.byref(a), _stream(dev)), "iak_prefill")
+    return out

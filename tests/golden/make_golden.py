@@ -321,7 +321,8 @@ def gen_prefill():
     cases = [("e2e_causal", gi.E2E_LAYOUT, (1, 2, 448, 64), 448, True),
              ("e2e_chunk", gi.E2E_LAYOUT, (2, 2, 16, 64), 448, False),
              ("partial_causal", gi.PREFILL_PARTIAL_LAYOUT, (2, 3, 100, 32), 100, True),
-             ("gap_causal", gi.PREFILL_GAP_LAYOUT, (1, 2, 96, 32), 96, True)]
+             ("gap_causal", gi.PREFILL_GAP_LAYOUT, (1, 2, 96, 32), 96, True),
+             ("partial_causal_d128", gi.PREFILL_PARTIAL_LAYOUT, (1, 2, 100, 128), 100, True)]
     for i, (name, spec, qshape, T_kv, causal) in enumerate(cases):
         B, H, M, D = qshape
         q = gi.normal(600 + 3 * i, qshape)

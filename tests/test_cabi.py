@@ -50,7 +50,8 @@ def test_version_and_error_query():
 
 _STRUCTS = {"iak_page_pools": N.PagePools, "iak_decode_args": N.DecodeArgs, "iak_pack_args": N.PackArgs,
             "iak_quant_args": N.QuantArgs, "iak_mla_args": N.MlaArgs, "iak_peer_exchange": N.PeerExchange,
-            "iak_route_args": N.RouteArgs, "iak_append_args": N.AppendArgs, "iak_convert_args": N.ConvertArgs}
+            "iak_route_args": N.RouteArgs, "iak_append_args": N.AppendArgs, "iak_convert_args": N.ConvertArgs,
+            "iak_prefill_args": N.PrefillArgs}
 
 
 def test_struct_layout_matches_header():

@@ -9,7 +9,8 @@ from oracle import prefill as op
 CASES = [("e2e_causal", gi.E2E_LAYOUT, (1, 2, 448, 64), 448, True),
          ("e2e_chunk", gi.E2E_LAYOUT, (2, 2, 16, 64), 448, False),
          ("partial_causal", gi.PREFILL_PARTIAL_LAYOUT, (2, 3, 100, 32), 100, True),
-         ("gap_causal", gi.PREFILL_GAP_LAYOUT, (1, 2, 96, 32), 96, True)]
+         ("gap_causal", gi.PREFILL_GAP_LAYOUT, (1, 2, 96, 32), 96, True),
+         ("partial_causal_d128", gi.PREFILL_PARTIAL_LAYOUT, (1, 2, 100, 128), 100, True)]
 
 
 def _inputs(i, qshape, T_kv):
