@@ -466,9 +466,10 @@ int iak_convert_pages(const iak_page_pools* pools, const iak_convert_args* args,
  * semantic_block_attention (causal masks on ORIGINAL token positions,
  * reference.py:16-45) that the reference's GPU path lacks: per-page row
  * masks select the rows of partially selected pages, and a key at token
- * position (page - bases[b*Ht+h]) * page_size + row is visible to query m iff
- * it is <= q_positions[b, m] (causal) .  Query rows that see no key are
- * written as 0 (the reference's softmax gives NaN there).
+ * position (page - bases[b*Ht+h]) * page_size + row (or page_positions[b, h,
+ * slot] + row) is visible to query m iff it is <= q_positions[b, m] (causal).
+ * Query rows that see no key are written as 0 (the reference's softmax gives
+ * NaN there).
  * q [B, Hq, M, D], out [B, Hq, M, D]; G = Hq / Ht query heads share a
  * page-table row.  page_size <= 64 when row_masks is given.
  * ------------------------------------------------------------------------ */
@@ -482,6 +483,9 @@ typedef struct iak_prefill_args {
   const int32_t* page_table; int64_t pt_stride_b, pt_stride_h; int32_t table_width;
   const int32_t* page_counts; int64_t pc_stride_b;    /* [B, Ht] or NULL = W     */
   const int32_t* bases;         /* [B*Ht] or NULL = 0                             */
+  const int32_t* page_positions;/* [B, Ht, W] token position of row 0 of each slot's page (overrides
+                                   (page - base) * page_size), or NULL                            */
+  int64_t pp_stride_b, pp_stride_h;
   const uint64_t* row_masks;    /* [B, W] (row stride rm_stride_b): bit r = row r selected; NULL = all */
   int64_t rm_stride_b;
   const void* page_tags; int32_t tag_bytes; uint8_t tag_map[16]; uint8_t tag_default;

@@ -43,7 +43,7 @@ __global__ void __launch_bounds__(kGenericWarps * 32) prefill_generic_kernel(con
     const int fmt = prefill_fmt(p, pid);
     if (!qpage::writable(p.k, fmt) || !qpage::writable(p.v, fmt)) continue;
     const uint64_t mask = prefill_mask(p, b, o);
-    const int64_t pos0 = (pid - base) * PS;
+    const int64_t pos0 = prefill_pos0(p, b, h, o, pid, base);
     for (int r = 0; r < PS; ++r) {
       if (!((mask >> r) & 1ull)) continue;
       if (p.causal && pos0 + r > qpos) continue;
@@ -125,6 +125,7 @@ extern "C" int iak_prefill(const iak_page_pools* pools, const iak_prefill_args* 
   p.pt = a->page_table; p.pt_sb = a->pt_stride_b; p.pt_sh = a->pt_stride_h; p.W = a->table_width;
   p.pc = a->page_counts; p.pc_sb = a->pc_stride_b;
   p.bases = a->bases; p.masks = a->row_masks; p.rm_sb = a->rm_stride_b;
+  p.ppos = a->page_positions; p.pp_sb = a->pp_stride_b; p.pp_sh = a->pp_stride_h;
   p.tags = a->page_tags; p.tag_bytes = a->tag_bytes;
   for (int i = 0; i < 16; ++i) p.tag_map[i] = a->tag_map[i];
   p.tag_default = a->tag_default;

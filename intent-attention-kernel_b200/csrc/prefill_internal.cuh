@@ -16,6 +16,7 @@ struct PrefillParams {
   const int32_t* pt; int64_t pt_sb, pt_sh; int W;
   const int32_t* pc; int64_t pc_sb;
   const int32_t* bases;
+  const int32_t* ppos; int64_t pp_sb, pp_sh;
   const uint64_t* masks; int64_t rm_sb;
   const void* tags; int tag_bytes; uint8_t tag_map[16]; uint8_t tag_default;
   float sm_scale;
@@ -37,6 +38,13 @@ __device__ __forceinline__ int prefill_count(const PrefillParams& p, int b, int 
 __device__ __forceinline__ uint64_t prefill_mask(const PrefillParams& p, int b, int o) {
   const uint64_t all = p.k.PS >= 64 ? ~0ull : ((1ull << p.k.PS) - 1ull);
   return p.masks ? (p.masks[static_cast<int64_t>(b) * p.rm_sb + o] & all) : all;
+}
+
+// Token position of row 0 of slot o's page pid in unit (b, h).
+__device__ __forceinline__ int64_t prefill_pos0(const PrefillParams& p, int b, int h, int o, int64_t pid,
+                                                int64_t base) {
+  return p.ppos ? static_cast<int64_t>(p.ppos[static_cast<int64_t>(b) * p.pp_sb + static_cast<int64_t>(h) * p.pp_sh + o])
+                : (pid - base) * p.k.PS;
 }
 
 bool prefill_tc_eligible(const PrefillParams& p);

@@ -65,7 +65,8 @@ struct Smem {
   static constexpr int kv = q + 2 * kKbQ;                       // stages x (K tile, V tile)
   static constexpr int pid = kv + kStages * 2 * kTile;          // compacted slots: page id
   static constexpr int mask = pid + kMaxSlots * 4;              //   row mask
-  static constexpr int fmt = mask + kMaxSlots * 8;              //   format
+  static constexpr int pos0 = mask + kMaxSlots * 8;             //   token position of row 0
+  static constexpr int fmt = pos0 + kMaxSlots * 4;              //   format
   static constexpr int bars = fmt + kMaxSlots;
   static constexpr int tmem = bars + B_COUNT * 8;
   static constexpr int nvalid = tmem + 4;
@@ -173,6 +174,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const PrefillPa
   int32_t* s_pid = reinterpret_cast<int32_t*>(sm + Smem::pid);
   uint64_t* s_mask = reinterpret_cast<uint64_t*>(sm + Smem::mask);
   uint8_t* s_fmt = sm + Smem::fmt;
+  int32_t* s_pos0 = reinterpret_cast<int32_t*>(sm + Smem::pos0);
   volatile uint32_t* s_tmem = reinterpret_cast<volatile uint32_t*>(sm + Smem::tmem);
   volatile int* s_nvalid = reinterpret_cast<volatile int*>(sm + Smem::nvalid);
   int* s_qmax = reinterpret_cast<int*>(sm + Smem::qmax);
@@ -246,14 +248,17 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const PrefillPa
       int64_t pid = -1;
       int fmt = IAK_FMT_SKIP;
       uint64_t mask = 0;
+      int64_t pos0 = 0;
       if (o < count) {
         pid = row[o];
         if (pid >= 0 && pid < p.k.num_pages) {
           fmt = prefill_fmt(p, pid);
           if (qpage::writable(p.k, fmt) && qpage::writable(p.v, fmt)) {
             mask = prefill_mask(p, b, o);
-            ok = mask != 0;
-            if (ok && p.causal) ok = (pid - base) * PS + (__ffsll(static_cast<long long>(mask)) - 1) <= qmax;
+            pos0 = prefill_pos0(p, b, h, o, pid, base);
+            // positions outside int32 cannot be compared with a query position: such slots are dropped
+            ok = mask != 0 && pos0 >= -(1LL << 30) && pos0 < (1LL << 30);
+            if (ok && p.causal) ok = pos0 + (__ffsll(static_cast<long long>(mask)) - 1) <= qmax;
           }
         }
       }
@@ -263,6 +268,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const PrefillPa
         if (r < kMaxSlots) {
           s_pid[r] = static_cast<int32_t>(pid);
           s_mask[r] = mask;
+          s_pos0[r] = static_cast<int32_t>(pos0);
           s_fmt[r] = static_cast<uint8_t>(fmt);
         }
       }
@@ -383,8 +389,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const PrefillPa
         int64_t lim = -1;                       // last visible row offset within the page
         if (si < n_valid) {
           mask = s_mask[si];
-          lim = p.causal ? static_cast<int64_t>(qpos) - (static_cast<int64_t>(s_pid[si]) - base) * PS
-                         : static_cast<int64_t>(PS);
+          lim = p.causal ? static_cast<int64_t>(qpos) - s_pos0[si] : static_cast<int64_t>(PS);
         }
 #pragma unroll
         for (int r = 0; r < PS; ++r) {

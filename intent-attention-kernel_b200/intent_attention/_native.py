@@ -104,7 +104,8 @@ class PrefillArgs(ctypes.Structure):
         ("q_positions", c_void_p), ("qp_stride_b", c_i64), ("causal", c_i32),
         ("page_table", c_void_p), ("pt_stride_b", c_i64), ("pt_stride_h", c_i64), ("table_width", c_i32),
         ("page_counts", c_void_p), ("pc_stride_b", c_i64),
-        ("bases", c_void_p), ("row_masks", c_void_p), ("rm_stride_b", c_i64),
+        ("bases", c_void_p), ("page_positions", c_void_p), ("pp_stride_b", c_i64), ("pp_stride_h", c_i64),
+        ("row_masks", c_void_p), ("rm_stride_b", c_i64),
         ("page_tags", c_void_p), ("tag_bytes", c_i32), ("tag_map", ctypes.c_uint8 * 16), ("tag_default", ctypes.c_uint8),
         ("sm_scale", ctypes.c_float), ("kernel", c_i32),
     ]

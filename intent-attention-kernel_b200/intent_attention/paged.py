@@ -463,14 +463,17 @@ def paged_prefill(q: torch.Tensor, pool: PagePool, page_table: torch.Tensor, pag
                   causal: bool = True, bases: Optional[torch.Tensor] = None,
                   row_masks: Optional[torch.Tensor] = None, sm_scale: Optional[float] = None,
                   out: Optional[torch.Tensor] = None, out_dtype: Optional[torch.dtype] = None,
-                  tag_default: int = N.FMT_SKIP, kernel: str = "auto") -> torch.Tensor:
+                  tag_default: int = N.FMT_SKIP, kernel: str = "auto",
+                  page_positions: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Attention of ``q`` [B, Hq, M, D] over the selected pages -> [B, Hq, M, D].
 
     Unit (b, h) attends to the rows of ``page_table[b, h, :page_counts[b, h]]``
     that ``row_masks[b, slot]`` (uint64 bit masks, None = every row) selects;
     a row of page ``pid`` sits at token position ``(pid - bases[b, h]) *
     page_size + row``.  With ``causal`` a key is visible to query m iff its
-    position <= ``q_positions[b, m]`` (default m).  Rows that see no key are 0.
+    position <= ``q_positions[b, m]`` (default m).  ``page_positions`` [B, Ht, W]
+    (int32) gives the position of row 0 of each slot's page directly instead.
+    Rows that see no key are 0.
     """
     _require_cuda(q, "q")
     if q.dim() != 4:
@@ -514,6 +517,12 @@ def paged_prefill(q: torch.Tensor, pool: PagePool, page_table: torch.Tensor, pag
         bases = bases.to(device=dev, dtype=torch.int32).contiguous()
         keep.append(bases)
         a.bases = bases.data_ptr()
+    if page_positions is not None:
+        page_positions = page_positions.to(device=dev, dtype=torch.int32).contiguous()
+        if tuple(page_positions.shape) != (B, Ht, W):
+            raise ValueError("page_positions must be [B, Ht, W]")
+        keep.append(page_positions)
+        a.page_positions, a.pp_stride_b, a.pp_stride_h = page_positions.data_ptr(), Ht * W, W
     if row_masks is not None:
         if row_masks.dtype not in (torch.int64, torch.uint64) or tuple(row_masks.shape) != (B, W) \
                 or row_masks.stride(1) != 1:

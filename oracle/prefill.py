@@ -58,7 +58,7 @@ def semantic_block_attention(q: np.ndarray, k: np.ndarray, v: np.ndarray, spec: 
 
 
 def unit_tokens(page_table, counts, bases, row_masks, tags, tag_map, default_fmt, pools, scales, scale_mode,
-                b: int, h: int, page_size: int, head_dim: int):
+                b: int, h: int, page_size: int, head_dim: int, page_positions=None):
     """Selected keys / values / positions of one (sequence, table head) unit."""
     Ht = page_table.shape[1]
     row = np.asarray(page_table[b, h]).astype(np.int64)
@@ -81,7 +81,8 @@ def unit_tokens(page_table, counts, bases, row_masks, tags, tag_map, default_fmt
         vp = _dequant_page_set(fmt, np.array([pid]), "v", pools, scales, scale_mode, head_dim)[0]
         ks.append(kp[rows])
         vs.append(vp[rows])
-        pos.extend((pid - base) * page_size + r for r in rows)
+        pos0 = (pid - base) * page_size if page_positions is None else int(page_positions[b, h, o])
+        pos.extend(pos0 + r for r in rows)
     if not ks:
         return np.zeros((0, head_dim)), np.zeros((0, head_dim)), np.zeros(0, np.int64)
     return (np.concatenate(ks).astype(np.float64), np.concatenate(vs).astype(np.float64),
@@ -92,9 +93,11 @@ def paged_prefill(q: np.ndarray, page_table: np.ndarray, counts: Optional[np.nda
                   tag_map: Mapping[int, str], pools: Mapping, scales: Optional[Mapping] = None,
                   scale_mode: str = "page", bases: Optional[np.ndarray] = None,
                   row_masks: Optional[np.ndarray] = None, q_positions: Optional[np.ndarray] = None,
-                  causal: bool = True, sm_scale: Optional[float] = None, default_fmt: str = "SKIP") -> np.ndarray:
+                  causal: bool = True, sm_scale: Optional[float] = None, default_fmt: str = "SKIP",
+                  page_positions: Optional[np.ndarray] = None) -> np.ndarray:
     """q [B, Hq, M, D]; page_table [B, Ht, W]; row_masks [B, W] uint64 (bit r = row r) or None;
-    q_positions [B, M] or None (= m).  Returns [B, Hq, M, D] float64; rows that see no key are 0."""
+    q_positions [B, M] or None (= m); page_positions [B, Ht, W] (position of row 0 of each
+    slot) or None.  Returns [B, Hq, M, D] float64; rows that see no key are 0."""
     q = np.asarray(q, np.float64)
     B, Hq, M, D = q.shape
     Ht = page_table.shape[1]
@@ -106,7 +109,7 @@ def paged_prefill(q: np.ndarray, page_table: np.ndarray, counts: Optional[np.nda
         qpos = np.arange(M) if q_positions is None else np.asarray(q_positions[b], np.int64)
         for h in range(Ht):
             K, V, pos = unit_tokens(page_table, counts, bases, row_masks, tags, tag_map, default_fmt, pools,
-                                    scales or {}, scale_mode, b, h, page_size, D)
+                                    scales or {}, scale_mode, b, h, page_size, D, page_positions)
             if pos.size == 0:
                 continue
             for g in range(G):
@@ -145,3 +148,36 @@ def layout_pages(spec: Sequence[Tuple], page_size: int, threshold: Optional[floa
                 pages.append(pg)
             masks[pg] |= 1 << (t - pg * page_size)
     return np.asarray(pages, np.int64), np.asarray([masks[p] for p in pages], np.uint64)
+
+
+def semantic_paged_attention(query: np.ndarray, key_cache: np.ndarray, value_cache: np.ndarray,
+                             block_table: np.ndarray, spec: Sequence[Tuple], block_size: int,
+                             causal: bool) -> np.ndarray:
+    """Per-head attention of query [T, H, D] over the selected cache blocks
+    ([NB, H, D, BS] caches) with the block selection of ``vllm_bridge.py:37-58``
+    and the compacted-index causal mask of ``dense_attention(causal=True)``
+    (``reference.py:27-40``): query i sees the first i + 1 concatenated keys.
+    The reference itself contracts over the head axis (a defect); this is the
+    per-head attention its docstring describes."""
+    num_logical = len(block_table)
+    phys = {}
+    for _name, start, end, policy, score in spec:
+        if policy == "SKIP" or (policy == "ATTEND" and score is not None and score < 0.5):
+            continue
+        for logical in range(start // block_size, min((end + block_size - 1) // block_size, num_logical)):
+            phys.setdefault(int(block_table[logical]), None)
+    T, H, D = query.shape
+    if not phys:
+        return np.zeros((T, H, D))
+    ids = list(phys)
+    K = np.concatenate([np.asarray(key_cache[p], np.float64).transpose(2, 0, 1) for p in ids])    # [N, H, D]
+    V = np.concatenate([np.asarray(value_cache[p], np.float64).transpose(2, 0, 1) for p in ids])
+    out = np.zeros((T, H, D))
+    for h in range(H):
+        s = np.asarray(query[:, h], np.float64) @ K[:, h].T / np.sqrt(D)        # [T, N]
+        if causal:
+            s = np.where(np.arange(K.shape[0])[None, :] > np.arange(T)[:, None], -np.inf, s)
+        m = s.max(axis=1, keepdims=True)
+        e = np.exp(s - m)
+        out[:, h] = (e / e.sum(axis=1, keepdims=True)) @ V[:, h]
+    return out
