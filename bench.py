@@ -1,6 +1,6 @@
 """Benchmark: fused selected-quant paged decode on B200 (sm_100a).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload c2|c3|c4|c5|c1|route|append] [--impl b200|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload c2|c3|c4|c5|c1|route|append|prefill] [--impl b200|reference]
 
 One "step" is one decode step of the workload's whole batch (all sequences,
 all heads) over its router-selected pages.  ``value`` is the selected-KV HBM
@@ -967,6 +967,162 @@ def run_route(args):
 
 
 # --------------------------------------------------------------------------- #
+#  Chunked prefill over router-selected pages (iak_prefill, tcgen05 kernel)
+# --------------------------------------------------------------------------- #
+
+PREFILL_METRIC = "chunked-prefill attention over router-selected pages: useful TFLOP/s (causal, exact tokens)"
+PREFILL = dict(name="Llama-3-8B-shape GQA chunked prefill over router-selected pages", B=2, M=2048)
+
+
+def prefill_workload(args):
+    """C2's model shape and router layout; per sequence the last M tokens of
+    the 32k context are the query chunk (positions T - M .. T - 1), attending
+    causally to the router-selected pages (1024 of 2048, C2 format mix)."""
+    w = workload("c2")
+    w["B"] = args.batch or PREFILL["B"]
+    w["M"] = PREFILL["M"]
+    ids, fmt = select_pages(w)
+    PS, T, M, D = w["PS"], w["T"], w["M"], w["D"]
+    pos = np.sort((ids.astype(np.int64)[:, None] * PS + np.arange(PS)[None, :]).reshape(-1))
+    qpos = T - M + np.arange(M)
+    pairs = int(np.searchsorted(pos, qpos, side="right").sum())        # visible (query, key) pairs per q head
+    flops = 4 * D * pairs * w["Hq"] * w["B"]
+    return w, ids, fmt, qpos, pairs, flops
+
+
+def cpu_prefill(w, ids, fmt, qpos, budget_s, rows=8):
+    """The numpy oracle over a few query rows of one (sequence, kv head) unit,
+    extrapolated to the step: seconds per step."""
+    import sys as _s
+    _s.path.insert(0, ROOT)
+    from oracle import prefill as op
+    g = np.random.default_rng(3)
+    PS, D, n = w["PS"], w["D"], ids.size
+    pools = {"k_f16": g.standard_normal((n, PS, D)).astype(np.float32),
+             "v_f16": g.standard_normal((n, PS, D)).astype(np.float32)}
+    table = np.arange(n, dtype=np.int32).reshape(1, 1, n)
+    ppos = (ids.astype(np.int64) * PS).reshape(1, 1, n)
+    tags = np.ones(n, np.uint8)
+    t0 = time.perf_counter()
+    done = 0
+    while done == 0 or (time.perf_counter() - t0 < budget_s and done < 64):
+        sel = qpos[-rows:] if done % 2 else qpos[:rows]
+        q = g.standard_normal((1, 1, rows, D)).astype(np.float32)
+        op.paged_prefill(q, table, None, tags, {1: "F16"}, pools, bases=None, q_positions=sel[None],
+                         causal=True, page_positions=ppos)
+        done += 1
+    per_row = (time.perf_counter() - t0) / (done * rows)
+    return per_row * w["M"] * w["Hq"] * w["B"], done * rows
+
+
+def run_prefill(args):
+    import torch
+    from intent_attention import PagePool
+    from intent_attention._native import KernelTimer
+    from intent_attention.paged import make_tag_map, paged_prefill
+    w, ids, fmt, qpos, pairs, flops = prefill_workload(args)
+    if args.impl == "reference":
+        vals, rows = [], 0
+        for i in range(args.warmup + args.steps):
+            sec, rows = cpu_prefill(w, ids, fmt, qpos, args.cpu_budget / max(1, args.steps + args.warmup))
+            if i >= args.warmup:
+                vals.append(sec)
+        sec = statistics.median(vals)
+        v = flops / sec / 1e12
+        print(json.dumps({"impl": "reference", "metric": PREFILL_METRIC, "value": round(v, 6), "unit": "TFLOP/s",
+                          "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(sec * 1e3, 1),
+                          "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp64 (numpy)",
+                          "data": "synthetic", "config": {"workload": PREFILL["name"], "batch": w["B"]},
+                          "cpu_baseline": {"value": round(v, 6), "unit": "TFLOP/s", "cores": 1, "kind": "port",
+                                           "sample": f"{rows} query rows of one (sequence, kv head) unit through the "
+                                                     "numpy oracle, extrapolated"},
+                          "e2e": {"value": round(v, 6), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                                  "d2h_bytes_per_step": 0}}), flush=True)
+        return
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    B, Hq, Hkv, D, PS, T, M = w["B"], w["Hq"], w["Hkv"], w["D"], w["PS"], w["T"], w["M"]
+    pool, table, counts, tags, _ = build_gpu_workload(w, ids, fmt, device, 0)
+    tag_map = make_tag_map({c: (f if f in w["mix"] else "SKIP") for f, c in FMT_CODE.items()})
+    NLP = T // PS
+    bases = (torch.arange(B * Hkv, dtype=torch.int32, device=device) * NLP).view(B, Hkv)
+    g = torch.Generator(device=device).manual_seed(w["seed"] + 9)
+    q = torch.randn((B, Hq, M, D), generator=g, device=device).to(torch.bfloat16)
+    qp = torch.from_numpy(np.tile(qpos.astype(np.int32), (B, 1))).to(device)
+    out = torch.empty((B, Hq, M, D), dtype=torch.bfloat16, device=device)
+
+    def step(q_=q):
+        paged_prefill(q_, pool, table, counts, tags, tag_map, q_positions=qp, causal=True, bases=bases, out=out,
+                      kernel="tensor")
+
+    step()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(0) as clocks:
+        t_probe = time.perf_counter()
+        while len(clocks.rows) < 3 and time.perf_counter() - t_probe < 3.0:
+            for _ in range(5):
+                step()
+            torch.cuda.synchronize()
+        for _ in range(args.warmup):
+            step()
+        torch.cuda.synchronize()
+        with KernelTimer(args.steps) as ktimer:
+            ev0.record()
+            for _ in range(args.steps):
+                step()
+            ev1.record()
+            torch.cuda.synchronize()
+    t_ms = ev0.elapsed_time(ev1) / args.steps
+    kernel_ms = ktimer.total_ms / max(1, ktimer.launches)
+    q_host = q.cpu().pin_memory()
+    out_host = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+    q_dev = torch.empty_like(q)
+
+    def e2e_step():
+        q_dev.copy_(q_host, non_blocking=True)
+        step(q_dev)
+        out_host.copy_(out, non_blocking=True)
+
+    for _ in range(args.warmup):
+        e2e_step()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / args.steps
+    peak, peak_kind = measured_tensor_peak()
+    tf = flops / (kernel_ms * 1e-3) / 1e12
+    rec = {"metric": PREFILL_METRIC, "value": round(flops / (t_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
+           "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(t_ms, 4),
+           "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+           "dtype": "bf16 q, fp16/fp8/int8 pages -> f16 tcgen05 MMA, fp32 accumulate",
+           "data": "synthetic (seeded N(0,1) K/V, bf16 Q)",
+           "config": {"workload": PREFILL["name"], "batch": B, "query_tokens": M, "q_heads": Hq, "kv_heads": Hkv,
+                      "head_dim": D, "ctx": T, "page_size": PS, "selected_pages_per_seq_head": int(ids.size),
+                      "format_mix": w["mix"], "visible_pairs_per_q_head": pairs, "useful_flops_per_step": flops,
+                      "l2": "selected KV (2.1 GB) larger than L2",
+                      "timing": "eager launches, CUDA events around the timed steps"},
+           "roofline": {"bound": "tensor", "achieved": round(tf, 1), "peak": peak, "unit": "TFLOP/s",
+                        "frac": round(tf / peak, 4), "traffic": None, "kernel": "prefill_tc_kernel<16>",
+                        "kernel_ms": round(kernel_ms, 4),
+                        "note": f"peak = {peak_kind} dense bf16 cuBLAS burst; achieved = useful FLOPs (4 x head_dim "
+                                "per visible (query, key) pair per q head) / the kernel's CUDA-event time"},
+           "e2e": {"value": round(flops / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s", "ms_per_step": round(e2e_ms, 4),
+                   "h2d_bytes_per_step": q_host.numel() * 2, "d2h_bytes_per_step": out_host.numel() * 2,
+                   "api": "intent_attention.paged_prefill with pinned host q in, output out"},
+           "gpu_launches": args.steps, "clocks": clocks.summary()}
+    if not args.no_cpu_baseline:
+        sec, rows = cpu_prefill(w, ids, fmt, qpos, args.cpu_budget)
+        rec["cpu_baseline"] = {"value": round(flops / sec / 1e12, 6), "unit": "TFLOP/s", "cores": 1, "kind": "port",
+                               "sample": f"{rows} query rows of one unit through the numpy oracle, extrapolated"}
+    print(json.dumps(rec), flush=True)
+
+
+# --------------------------------------------------------------------------- #
 #  KV append with quantise-on-write (iak_append_tokens) at the C2 shape
 # --------------------------------------------------------------------------- #
 
@@ -1125,7 +1281,7 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--workload", default="c2", choices=["c1", "c2", "c3", "c4", "c5", "route", "append"])
+    ap.add_argument("--workload", default="c2", choices=["c1", "c2", "c3", "c4", "c5", "route", "append", "prefill"])
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--splits", type=int, default=0)
     ap.add_argument("--batch", type=int, default=0, help="override the workload's batch (profiling runs)")
@@ -1141,6 +1297,8 @@ def main():
         run_route(args)
     elif args.workload == "append":
         run_append(args)
+    elif args.workload == "prefill":
+        run_prefill(args)
     elif args.impl == "reference":
         run_reference(args)
     elif args.workload == "c4":

@@ -108,15 +108,6 @@ static_assert(Smem::total + 1024 <= 232448, "shared memory budget");
 //   range, 2^-24 absolute resolution below it).
 // The 2^8 is restored in the score scale and in the final normalisation.
 constexpr float kTileScale = 1.f / 256.f;
-// codes in bytes 0 and 2 of t (bytes 1 and 3 zero) -> f16x2 of code * 2^-8
-__device__ __forceinline__ uint32_t e4m3_pair_bits(uint32_t t) {
-  return ((t & 0x007F007Fu) << 7) | ((t & 0x00800080u) << 8);
-}
-// four codes of w -> two f16x2 words (first code in the low half of the first word)
-__device__ __forceinline__ void e4m3x4_to_f16(uint32_t w, uint32_t& lo, uint32_t& hi) {
-  lo = e4m3_pair_bits(__byte_perm(w, 0u, 0x4140));
-  hi = e4m3_pair_bits(__byte_perm(w, 0u, 0x4342));
-}
 // two bf16 (low half = first element) -> two f16, exact inside the f16 range
 __device__ __forceinline__ uint32_t bf16x2_to_f16x2(uint32_t w, float mul = 1.f) {
   const __half2 h = __floats2half2_rn(__uint_as_float(w << 16) * mul, __uint_as_float(w & 0xFFFF0000u) * mul);

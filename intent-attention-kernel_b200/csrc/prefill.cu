@@ -132,6 +132,11 @@ extern "C" int iak_prefill(const iak_page_pools* pools, const iak_prefill_args* 
   p.sm_scale = a->sm_scale;
   p.q_vec = (a->q_dtype != IAK_DT_F32 && reinterpret_cast<uintptr_t>(a->q) % 16 == 0 && a->q_stride_b % 8 == 0 &&
              a->q_stride_h % 8 == 0 && a->q_stride_m % 8 == 0) ? 1 : 0;
+  {
+    const int64_t esz = a->out_dtype == IAK_DT_F32 ? 4 : 2, per16 = 16 / esz;
+    p.o_vec = (reinterpret_cast<uintptr_t>(a->out) % 16 == 0 && a->out_stride_b % per16 == 0 &&
+               a->out_stride_h % per16 == 0 && a->out_stride_m % per16 == 0) ? 1 : 0;
+  }
   const cudaStream_t s = static_cast<cudaStream_t>(stream);
   const bool tc_ok = prefill_tc_eligible(p);
   if (a->kernel == IAK_KERNEL_TENSOR && !tc_ok)

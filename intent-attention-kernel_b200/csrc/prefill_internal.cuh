@@ -21,6 +21,7 @@ struct PrefillParams {
   const void* tags; int tag_bytes; uint8_t tag_map[16]; uint8_t tag_default;
   float sm_scale;
   int q_vec;     // q rows are 16-byte aligned f16 / bf16 (vector loads)
+  int o_vec;     // output rows are 16-byte aligned (vector stores)
 };
 
 __device__ __forceinline__ int prefill_fmt(const PrefillParams& p, int64_t pid) {

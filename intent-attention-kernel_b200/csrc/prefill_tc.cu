@@ -4,22 +4,25 @@
 // One CTA = one work item (sequence b, page-table head h, tile of 128 query
 // rows).  Rows are (query m, head g of the group) pairs, m-major, so a tile
 // holds 128 / G consecutive queries of the G query heads sharing the table.
-//   * the planner warp compacts the unit's table into shared memory: slots
-//     with a page in a supported format, a non-empty row mask and (causal) a
-//     first selected row not after the tile's last query position; the
-//     compacted slots form 64-token chunks (64 / PS slots each);
-//   * a converter warpgroup dequantises each chunk's K and V rows (code x
-//     scale, fp32) to f16 into shared memory, 128-byte swizzled, rows the slot
-//     mask does not select written as zero, over a 3-stage ring;
-//   * S = Q . K^T (M = 128, N = 64, K = 128: 8 tcgen05.mma, Q f16 in shared
-//     memory) lands in TMEM; the softmax warpgroup owns one TMEM lane (= one
-//     query row) per thread: it applies the row masks and the causal
+//   * the producer warp first compacts the unit's table into shared memory
+//     (slots with a page in a supported format, a non-empty row mask and,
+//     causal, a first selected row not after the tile's last query position;
+//     64-token chunks of 64 / PS slots), then bulk-copies each chunk's raw K
+//     and V page bytes (cp.async.bulk, mbarrier transaction counts) into a
+//     2-stage staging ring, running ahead of the converters;
+//   * a converter warpgroup dequantises the staged rows (code x scale, fp32;
+//     scales read ahead of the wait) to f16 tiles, 128-byte swizzled, rows the
+//     slot mask does not select written as zero, over a 3-stage ring;
+//   * S = Q . K^T (M = 128, N = 64, K = 128: 8 tcgen05.mma, Q f16 in TMEM as
+//     the A operand) lands in TMEM; the softmax warpgroup owns one TMEM lane
+//     (= one query row) per thread: it applies the row masks and the causal
 //     comparison of each key's token position with the row's query position,
 //     runs the online softmax in the exp2 domain with lazy O rescaling, and
 //     writes P (f16) back over S;
 //   * O += P . V (M = 128, N = 128, K = 64: 4 tcgen05.mma, P the TMEM A
 //     operand, V read MN-major) accumulates in TMEM (fp32).
-// TMEM: O 128 | S/P 2 x 64 columns.  Rows that see no key are written as 0.
+// TMEM: O 128 | S/P 2 x 64 | Q 64 columns (512 allocated, one CTA per SM).
+// Rows that see no key are written as 0.
 //
 // Reference semantics: reference.py:82-130 semantic_block_attention with the
 // causal mask on original token positions of reference.py:16-45.
@@ -37,43 +40,52 @@ namespace {
 using namespace tc;
 
 constexpr int kD = 128, kRows = 128, kChunk = 64;
-constexpr int kStages = 3;
-constexpr int kMaxSlots = 4096;
-constexpr int kThreads = 320;                 // softmax wg | converter wg | planner warp | MMA warp
-constexpr int kConvWarp0 = 4, kPlanWarp = 8, kMmaWarp = 9;
+constexpr int kTileStages = 3, kRawStages = 3;
+constexpr int kMaxSlots = 1024;
+constexpr int kThreads = 320;                 // softmax wg | converter wg | producer warp | MMA warp
+constexpr int kConvWarp0 = 4, kProdWarp = 8, kMmaWarp = 9;
 constexpr int kKb = kChunk * 128;             // 64 token rows x 64 channels of f16 (one swizzle-atom column)
-constexpr int kKbQ = kRows * 128;             // 128 query rows x 64 channels
 constexpr int kTile = 2 * kKb;                // 64 tokens x 128 channels
+constexpr int kRawPlane = kChunk * kD * 2;    // staged bytes of one plane of a chunk (room for f16 rows)
+constexpr int kRawStage = 2 * kRawPlane;      // K plane, then V plane
 constexpr int kSBuf = 2;
-constexpr int kOCol = 0, kSCol = kD, kTmemCols = 256;
+constexpr int kOCol = 0, kSCol = kD, kQCol = kSCol + kSBuf * kChunk, kTmemCols = 512;
+static_assert(kQCol + kD / 2 <= kTmemCols, "TMEM budget");
 constexpr float kLazyLog2 = 8.f;
 constexpr float kLog2e = 1.4426950408889634f;
 
 enum {
-  B_KFULL = 0,                     // converters -> MMA: K tile of a stage stored
-  B_VFULL = B_KFULL + kStages,     // converters -> MMA: V tile of a stage stored
-  B_EMPTY = B_VFULL + kStages,     // MMA commit after P.V -> converters: stage free
-  B_SFULL = B_EMPTY + kStages,     // MMA commit -> softmax: S ready
-  B_PFULL = B_SFULL + kSBuf,       // softmax -> MMA: P written
-  B_PVDONE = B_PFULL + kSBuf,      // MMA commit -> softmax / MMA: P.V retired
-  B_DONE = B_PVDONE + kSBuf,       // MMA commit: every MMA retired
+  B_KFULL = 0,                         // converters -> MMA: K tile of a stage stored
+  B_VFULL = B_KFULL + kTileStages,     // converters -> MMA: V tile of a stage stored
+  B_EMPTY = B_VFULL + kTileStages,     // MMA commit after P.V -> converters: tile stage free
+  B_RFULL = B_EMPTY + kTileStages,     // producer expect_tx + bulk copies -> converters: raw stage staged
+  B_REMPTY = B_RFULL + kRawStages,     // converters -> producer: raw stage read
+  B_SFULL = B_REMPTY + kRawStages,     // MMA commit -> softmax: S ready
+  B_PFULL = B_SFULL + kSBuf,           // softmax -> MMA: P written
+  B_PVDONE = B_PFULL + kSBuf,          // MMA commit -> softmax / MMA: P.V retired
+  B_DONE = B_PVDONE + kSBuf,           // MMA commit: every MMA retired
+  B_QREADY,                            // softmax warps -> MMA: Q rows stored in TMEM
   B_COUNT
 };
 
 struct Smem {
-  static constexpr int q = 0;                                   // 2 Q k-blocks
-  static constexpr int kv = q + 2 * kKbQ;                       // stages x (K tile, V tile)
-  static constexpr int pid = kv + kStages * 2 * kTile;          // compacted slots: page id
-  static constexpr int mask = pid + kMaxSlots * 4;              //   row mask
-  static constexpr int pos0 = mask + kMaxSlots * 8;             //   token position of row 0
-  static constexpr int fmt = pos0 + kMaxSlots * 4;              //   format
-  static constexpr int bars = fmt + kMaxSlots;
+  static constexpr int tiles = 0;                                // tile stages x (K tile, V tile)
+  static constexpr int raw = tiles + kTileStages * 2 * kTile;    // raw staging ring
+  static constexpr int pid = raw + kRawStages * kRawStage;       // compacted slots: page id
+  static constexpr int mask = pid + kMaxSlots * 4;               //   row mask
+  static constexpr int pos0 = mask + kMaxSlots * 8;              //   token position of row 0
+  static constexpr int fmt = pos0 + kMaxSlots * 4;               //   format
+  static constexpr int cfull = fmt + kMaxSlots;                  // per chunk: every key visible to every row
+  static constexpr int scales = cfull + kMaxSlots;               // raw stages x slots x {k, v, k res, v res} x 4
+  static constexpr int fac = scales + kRawStages * 8 * 4 * 4 * 4; // tile stages x slots x {score, value} factor
+  static constexpr int bars = fac + kTileStages * 8 * 2 * 4;
   static constexpr int tmem = bars + B_COUNT * 8;
   static constexpr int nvalid = tmem + 4;
   static constexpr int qmax = nvalid + 4;
-  static constexpr int total = qmax + 8;
+  static constexpr int qmin = qmax + 4;
+  static constexpr int total = qmin + 4;
 };
-static_assert(Smem::kv % 1024 == 0 && Smem::pid % 1024 == 0, "1024-byte alignment");
+static_assert(Smem::raw % 1024 == 0 && Smem::pid % 1024 == 0, "1024-byte alignment");
 static_assert(Smem::mask % 8 == 0 && Smem::bars % 8 == 0, "8-byte alignment");
 static_assert(Smem::total + 1024 <= 232448, "shared memory budget");
 
@@ -81,68 +93,94 @@ __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
   const __half2 h = __floats2half2_rn(a, b);
   return *reinterpret_cast<const uint32_t*>(&h);
 }
+// 2^x with the hardware approximation (flush-to-zero; 2^-inf = 0)
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 
-// Channels [32g, 32g + 32) of row r of pool page pid, dequantised (code x
-// scale in fp32) and packed as 16 f16 pairs in channel order.
-__device__ __forceinline__ void load_group(const qpage::PlanePools& q, int fmt, int64_t pid, int r, int g,
-                                           uint32_t (&h)[16]) {
-  const int64_t row = pid * q.PS + r;
-  if (fmt == IAK_FMT_F16) {
-    const uint4* src = reinterpret_cast<const uint4*>(q.f16 + row * kD + g * 32);
+// Bytes of one plane of one page of format fmt as staged (row r of a slot's
+// region at r * row_bytes; INT4_RESIDUAL's residual rows follow the base rows).
+__device__ __forceinline__ uint32_t staged_plane_bytes(int fmt, int PS) {
+  return fmt == IAK_FMT_F16 ? PS * 256u : (fmt == IAK_FMT_INT4 ? PS * 64u : PS * 128u);
+}
+
+// Page-scaled FP8 / INT8 / INT4 rows are widened to f16 without their scale, exactly:
+// FP8 by bit placement (code * 2^-8), INT8 and the INT4 nibbles through the
+// f16 magic number 1024 (0x6400) + the offset-binary code, then one half2
+// subtraction.  The page scale (x 256 for FP8) is applied to the scores and to
+// P by the softmax.
+__device__ __forceinline__ uint32_t hsub_bits(uint32_t a, uint32_t b) {
+  const __half2 r = __hsub2(*reinterpret_cast<const __half2*>(&a), *reinterpret_cast<const __half2*>(&b));
+  return *reinterpret_cast<const uint32_t*>(&r);
+}
+// 16 consecutive channels [ch0, ch0 + 16) of an FP8 / INT8 row from one 16-byte chunk w, as 8 f16
+// pairs: widened exactly (fold: the page scale goes to the softmax) or times their scales in fp32.
+__device__ __forceinline__ void cvt8(uint4 w4, int fmt, bool fold, int ch0, float s_all, const float* chs,
+                                     uint32_t (&h)[8]) {
+  const uint32_t w[4] = {w4.x, w4.y, w4.z, w4.w};
+  if (fold) {
+    if (fmt == IAK_FMT_FP8) {
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const uint4 x = src[i];
-      h[4 * i] = x.x; h[4 * i + 1] = x.y; h[4 * i + 2] = x.z; h[4 * i + 3] = x.w;
-    }
-    return;
-  }
-  const float* sp = q.scale + pid * q.ns;
-  const float* rsp = q.res_scale ? q.res_scale + pid * q.ns : nullptr;
-  const bool per_ch = q.mode == IAK_SCALE_CHANNEL;
-  const float s_all = per_ch ? 0.f : sp[q.mode == IAK_SCALE_GROUP32 ? g : 0];
-  auto sc = [&](int c) { return per_ch ? sp[g * 32 + c] : s_all; };
-  if (fmt == IAK_FMT_FP8 || fmt == IAK_FMT_INT8) {
-    const uint4* src = reinterpret_cast<const uint4*>((fmt == IAK_FMT_FP8 ? q.fp8 : reinterpret_cast<const uint8_t*>(q.i8)) +
-                                                      row * kD + g * 32);
-    const uint4 a = src[0], b = src[1];
-    const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+      for (int i = 0; i < 4; ++i) e4m3x4_to_f16(w[i], h[2 * i], h[2 * i + 1]);
+    } else {
+      constexpr uint32_t kBias = 0x64806480u;    // half2(1152, 1152) = 1024 + 128
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-#pragma unroll
-      for (int k = 0; k < 2; ++k) {
-        const int c = 4 * i + 2 * k;
-        const uint32_t pair = (w[i] >> (16 * k)) & 0xFFFFu;
-        float x0, x1;
-        if (fmt == IAK_FMT_FP8) {
-          const __half2_raw hr = __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(pair), __NV_E4M3);
-          const float2 f = __half22float2(__half2(hr));
-          x0 = f.x; x1 = f.y;
-        } else {
-          x0 = static_cast<float>(static_cast<int8_t>(pair & 0xFFu));
-          x1 = static_cast<float>(static_cast<int8_t>(pair >> 8));
-        }
-        h[c / 2] = pack_h2(x0 * sc(c), x1 * sc(c + 1));
+      for (int i = 0; i < 4; ++i) {
+        const uint32_t x = w[i] ^ 0x80808080u;  // offset binary
+        h[2 * i] = hsub_bits(__byte_perm(x, 0x64646464u, 0x4140), kBias);
+        h[2 * i + 1] = hsub_bits(__byte_perm(x, 0x64646464u, 0x4342), kBias);
       }
     }
     return;
   }
-  // packed INT4 (+ residual): word j of the group holds channels 4j + {0, 2, 16, 18, 1, 3, 17, 19}
-  // in nibbles 0..7, offset-binary; nibbles (n, n + 4) are the channel pair (d, d + 1)
-  const uint4 bw = *reinterpret_cast<const uint4*>(q.i4 + row * (kD / 2) + g * 16);
-  const uint32_t base[4] = {bw.x, bw.y, bw.z, bw.w};
-  uint32_t res[4] = {0u, 0u, 0u, 0u};
-  const bool resid = fmt == IAK_FMT_INT4R;
-  if (resid) {
-    const uint4 rw = *reinterpret_cast<const uint4*>(q.i4r + row * (kD / 2) + g * 16);
-    res[0] = rw.x; res[1] = rw.y; res[2] = rw.z; res[3] = rw.w;
+  auto sc = [&](int c) { return chs ? chs[ch0 + c] : s_all; };
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const int c = 4 * i + 2 * k;
+      const uint32_t pair = (w[i] >> (16 * k)) & 0xFFFFu;
+      float x0, x1;
+      if (fmt == IAK_FMT_FP8) {
+        const __half2_raw hr = __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(pair), __NV_E4M3);
+        const float2 f = __half22float2(__half2(hr));
+        x0 = f.x; x1 = f.y;
+      } else {
+        x0 = static_cast<float>(static_cast<int8_t>(pair & 0xFFu));
+        x1 = static_cast<float>(static_cast<int8_t>(pair >> 8));
+      }
+      h[c / 2] = pack_h2(x0 * sc(c), x1 * sc(c + 1));
+    }
   }
-  const float rs_all = (resid && !per_ch) ? rsp[q.mode == IAK_SCALE_GROUP32 ? g : 0] : 0.f;
-  auto rsc = [&](int c) { return per_ch ? rsp[g * 32 + c] : rs_all; };
+}
+
+// The 32 channels [32g, 32g + 32) of a packed INT4 row from one 16-byte chunk (4 words), plus the
+// residual chunk for INT4_RESIDUAL, as 16 f16 pairs in channel order.  Word j holds channels
+// 4j + {0, 2, 16, 18, 1, 3, 17, 19} in nibbles 0..7; nibbles (n, n + 4) are a channel pair.
+__device__ __forceinline__ void cvt4(uint4 b4, uint4 r4, bool resid, bool fold, int g, float s_all, float rs_all,
+                                     const float* chs, const float* rchs, uint32_t (&h)[16]) {
+  const uint32_t base[4] = {b4.x, b4.y, b4.z, b4.w};
+  if (fold) {
+    constexpr uint32_t kBias4 = 0x64086408u;     // half2(1032, 1032) = 1024 + 8
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int n = 0; n < 4; ++n) {
+        const int c = 4 * j + (n & 1) * 2 + (n >> 1) * 16;
+        h[c / 2] = hsub_bits(((base[j] >> (4 * n)) & 0x000F000Fu) | 0x64006400u, kBias4);
+      }
+    return;
+  }
+  const uint32_t res[4] = {r4.x, r4.y, r4.z, r4.w};
+  auto sc = [&](int c) { return chs ? chs[g * 32 + c] : s_all; };
+  auto rsc = [&](int c) { return rchs ? rchs[g * 32 + c] : rs_all; };
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
 #pragma unroll
     for (int n = 0; n < 4; ++n) {
-      const int c = 4 * j + (n & 1) * 2 + (n >> 1) * 16;      // first channel of the pair
+      const int c = 4 * j + (n & 1) * 2 + (n >> 1) * 16;
       const int c0 = static_cast<int>((base[j] >> (4 * n)) & 0xFu) - 8;
       const int c1 = static_cast<int>((base[j] >> (4 * n + 16)) & 0xFu) - 8;
       float x0 = static_cast<float>(c0) * sc(c), x1 = static_cast<float>(c1) * sc(c + 1);
@@ -160,10 +198,11 @@ __device__ __forceinline__ void load_group(const qpage::PlanePools& q, int fmt, 
 template <int PS>
 __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const PrefillParams p, int tiles) {
   constexpr int kSlotsPerChunk = kChunk / PS;
+  constexpr int kSlotRaw = PS * 256;            // staged bytes reserved per slot and plane
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  const uint32_t raw = smem_u32(smem_raw);
-  const uint32_t sbase = (raw + 1023u) & ~1023u;
-  uint8_t* sm = smem_raw + (sbase - raw);
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  const uint32_t sbase = (raw_addr + 1023u) & ~1023u;
+  uint8_t* sm = smem_raw + (sbase - raw_addr);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
   const int tile = blockIdx.x % tiles;
@@ -173,19 +212,34 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const PrefillPa
 
   int32_t* s_pid = reinterpret_cast<int32_t*>(sm + Smem::pid);
   uint64_t* s_mask = reinterpret_cast<uint64_t*>(sm + Smem::mask);
-  uint8_t* s_fmt = sm + Smem::fmt;
   int32_t* s_pos0 = reinterpret_cast<int32_t*>(sm + Smem::pos0);
+  uint8_t* s_fmt = sm + Smem::fmt;
   volatile uint32_t* s_tmem = reinterpret_cast<volatile uint32_t*>(sm + Smem::tmem);
   volatile int* s_nvalid = reinterpret_cast<volatile int*>(sm + Smem::nvalid);
   int* s_qmax = reinterpret_cast<int*>(sm + Smem::qmax);
+  int* s_qmin = reinterpret_cast<int*>(sm + Smem::qmin);
+  uint8_t* s_cfull = sm + Smem::cfull;
+  float* s_scales = reinterpret_cast<float*>(sm + Smem::scales);
+  float* s_fac = reinterpret_cast<float*>(sm + Smem::fac);     // [tile stage][slot][score, value]
+  // staged page / group scales: [raw stage][slot in chunk][k, v, k residual, v residual][group]
+  auto scale_at = [&](int rs, int sl, int kind, int g) -> float* {
+    return s_scales + (((rs * 8 + sl) * 4 + kind) * 4 + g);
+  };
   auto bar = [&](int i) -> uint32_t { return sbase + Smem::bars + 8u * static_cast<uint32_t>(i); };
-  auto tile_off = [&](int st, int plane) -> uint32_t { return Smem::kv + (st * 2 + plane) * kTile; };
+  auto tile_off = [&](int st, int plane) -> uint32_t { return Smem::tiles + (st * 2 + plane) * kTile; };
+  auto raw_off = [&](int rs, int plane, int slot) -> uint32_t {
+    return Smem::raw + rs * kRawStage + plane * kRawPlane + slot * kSlotRaw;
+  };
 
   if (tid == 0) {
-    for (int i = 0; i < kStages; ++i) {
+    for (int i = 0; i < kTileStages; ++i) {
       mbar_init(bar(B_KFULL + i), 128);
       mbar_init(bar(B_VFULL + i), 128);
       mbar_init(bar(B_EMPTY + i), 1);
+    }
+    for (int i = 0; i < kRawStages; ++i) {
+      mbar_init(bar(B_RFULL + i), 1);
+      mbar_init(bar(B_REMPTY + i), 128);
     }
     for (int k = 0; k < kSBuf; ++k) {
       mbar_init(bar(B_SFULL + k), 1);
@@ -193,7 +247,9 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const PrefillPa
       mbar_init(bar(B_PVDONE + k), 1);
     }
     mbar_init(bar(B_DONE), 1);
+    mbar_init(bar(B_QREADY), 128);
     *s_qmax = -1;
+    *s_qmin = 0x7FFFFFFF;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   }
@@ -203,41 +259,56 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const PrefillPa
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
+  tc_fence_before();
   __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *s_tmem;
 
-  // ---- this thread's query row (softmax warps): position, and Q into shared memory
+  // ---- this thread's query row (softmax warps): position, and Q into TMEM
   const int R = tile * kRows + tid;
   const int qm = R / p.G, qg = R % p.G;
   const bool row_ok = warp < 4 && qm < p.M;
   const int hq = h * p.G + qg;
+  const uint32_t lane_addr = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
   int qpos = -1;
   if (warp < 4) {
     if (row_ok) {
       qpos = p.qpos ? p.qpos[static_cast<int64_t>(b) * p.qp_sb + qm] : qm;
-      if (p.causal) atomicMax(s_qmax, qpos);
+      if (p.causal) {
+        atomicMax(s_qmax, qpos);
+        atomicMin(s_qmin, qpos);
+      }
     }
     const int64_t qoff = b * p.q_sb + static_cast<int64_t>(hq) * p.q_sh + static_cast<int64_t>(qm) * p.q_sm;
-#pragma unroll 4
-    for (int c = 0; c < 16; ++c) {
-      uint4 v = make_uint4(0u, 0u, 0u, 0u);
-      if (row_ok) {
-        if (p.q_vec && p.q_dtype == IAK_DT_F16) {
-          v = *reinterpret_cast<const uint4*>(static_cast<const __half*>(p.q) + qoff + c * 8);
-        } else {
-          float f[8];
+#pragma unroll 1
+    for (int half = 0; half < 2; ++half) {
+      uint32_t v[32];
 #pragma unroll
-          for (int i = 0; i < 8; ++i) f[i] = load_as_float(p.q, p.q_dtype, qoff + c * 8 + i);
-          v = make_uint4(pack_h2(f[0], f[1]), pack_h2(f[2], f[3]), pack_h2(f[4], f[5]), pack_h2(f[6], f[7]));
+      for (int c = 0; c < 8; ++c) {
+        uint4 x = make_uint4(0u, 0u, 0u, 0u);
+        const int ch = half * 64 + c * 8;
+        if (row_ok) {
+          if (p.q_vec && p.q_dtype == IAK_DT_F16) {
+            x = *reinterpret_cast<const uint4*>(static_cast<const __half*>(p.q) + qoff + ch);
+          } else {
+            float f[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) f[i] = load_as_float(p.q, p.q_dtype, qoff + ch + i);
+            x = make_uint4(pack_h2(f[0], f[1]), pack_h2(f[2], f[3]), pack_h2(f[4], f[5]), pack_h2(f[6], f[7]));
+          }
         }
+        v[4 * c] = x.x; v[4 * c + 1] = x.y; v[4 * c + 2] = x.z; v[4 * c + 3] = x.w;
       }
-      *reinterpret_cast<uint4*>(sm + Smem::q + (c >> 3) * kKbQ + swz(tid, c & 7)) = v;
+      tmem_st32(lane_addr + kQCol + half * 32, v);
     }
-    fence_proxy_async();
+    tmem_wait_st();
+    tc_fence_before();
+    mbar_arrive(bar(B_QREADY));
   }
   __syncthreads();
 
-  // ---- planner: compact the unit's table
-  if (warp == kPlanWarp) {
+  // ---- producer warp: compact the unit's table
+  if (warp == kProdWarp) {
     const int count = prefill_count(p, b, h);
     const int32_t* row = p.pt + static_cast<int64_t>(b) * p.pt_sb + static_cast<int64_t>(h) * p.pt_sh;
     const int qmax = *s_qmax;
@@ -274,41 +345,170 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const PrefillPa
       }
       cnt += __popc(bal);
     }
-    if (lane == 0) *s_nvalid = min(cnt, kMaxSlots);
+    const int nv = min(cnt, kMaxSlots);
+    if (lane == 0) *s_nvalid = nv;
+    __syncwarp();
+    // chunks whose every key every row sees: all slots present, full row masks, and
+    // (causal) the chunk's last key position not after the tile's first query position
+    const uint64_t all = PS >= 64 ? ~0ull : ((1ull << PS) - 1ull);
+    const int qmin = *s_qmin;
+    for (int c = lane; c * kSlotsPerChunk < nv; c += 32) {
+      bool full = true;
+      for (int sl = 0; sl < kSlotsPerChunk; ++sl) {
+        const int si = c * kSlotsPerChunk + sl;
+        full = full && si < nv && s_mask[si] == all && (!p.causal || s_pos0[si] + PS - 1 <= qmin);
+      }
+      s_cfull[c] = full ? 1 : 0;
+    }
   }
-  tc_fence_before();
   __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *s_tmem;
   const int n_valid = *s_nvalid;
   const int T = (n_valid + kSlotsPerChunk - 1) / kSlotsPerChunk;
   bool timed_out = false;
 
-  if (warp >= kConvWarp0 && warp < kPlanWarp) {
-    // ---------------------------------------------------------------- converters: pools -> f16 tiles
+  if (warp == kProdWarp) {
+    // ---------------------------------------------------------------- producer: scales + bulk copies
+    const int mode = p.k.mode, ns = p.k.ns;
+    const int ngrp = mode == IAK_SCALE_GROUP32 ? 4 : 1;   // channel-mode scales are read by the converters
+    for (int j = 0; j < T; ++j) {
+      const int rs = j % kRawStages;
+      bool ok = true;
+      if (lane == 0 && j >= kRawStages) ok = mbar_wait_sleep(bar(B_REMPTY + rs), ((j / kRawStages) - 1) & 1);
+      if (!__shfl_sync(0xffffffffu, ok, 0)) { timed_out = true; break; }
+      // page / group scales of the chunk's slots into shared memory, one (slot, kind, group) per lane
+      if (mode != IAK_SCALE_CHANNEL) {
+        for (int it = lane; it < kSlotsPerChunk * 4 * ngrp; it += 32) {
+          const int sl = it / (4 * ngrp), kind = (it / ngrp) % 4, g = it % ngrp;
+          const int si = j * kSlotsPerChunk + sl;
+          float v = 0.f;
+          if (si < n_valid) {
+            const int fmt = s_fmt[si];
+            const float* arr = kind == 0 ? p.k.scale : (kind == 1 ? p.v.scale : (kind == 2 ? p.k.res_scale : p.v.res_scale));
+            const bool need = fmt != IAK_FMT_F16 && (kind < 2 || fmt == IAK_FMT_INT4R);
+            if (need && arr) v = arr[static_cast<int64_t>(s_pid[si]) * ns + g];
+          }
+          *scale_at(rs, sl, kind, g) = v;
+        }
+      }
+      __syncwarp();
+      if (lane == 0) {
+        uint32_t total = 0;
+        for (int sl = 0; sl < kSlotsPerChunk; ++sl) {
+          const int si = j * kSlotsPerChunk + sl;
+          if (si < n_valid) total += 2 * staged_plane_bytes(s_fmt[si], PS);
+        }
+        mbar_arrive_expect_tx(bar(B_RFULL + rs), total);
+        for (int sl = 0; sl < kSlotsPerChunk; ++sl) {
+          const int si = j * kSlotsPerChunk + sl;
+          if (si >= n_valid) break;
+          const int fmt = s_fmt[si];
+          const int64_t pid = s_pid[si];
+          for (int plane = 0; plane < 2; ++plane) {
+            // pool base of this page's format and plane (selected pointer by pointer: a reference to
+            // one of the two by-value parameter structs would be copied to local memory)
+            const uint8_t* src;
+            uint32_t bytes;
+            if (fmt == IAK_FMT_F16) {
+              src = reinterpret_cast<const uint8_t*>(plane ? p.v.f16 : p.k.f16) + pid * PS * kD * 2;
+              bytes = PS * 256;
+            } else if (fmt == IAK_FMT_FP8) {
+              src = (plane ? p.v.fp8 : p.k.fp8) + pid * PS * kD;
+              bytes = PS * 128;
+            } else if (fmt == IAK_FMT_INT8) {
+              src = reinterpret_cast<const uint8_t*>(plane ? p.v.i8 : p.k.i8) + pid * PS * kD;
+              bytes = PS * 128;
+            } else {
+              src = (plane ? p.v.i4 : p.k.i4) + pid * PS * (kD / 2);
+              bytes = PS * 64;
+            }
+            const uint32_t dst = sbase + raw_off(rs, plane, sl);
+            bulk_load(dst, src, bytes, bar(B_RFULL + rs));
+            if (fmt == IAK_FMT_INT4R)
+              bulk_load(dst + PS * 64, (plane ? p.v.i4r : p.k.i4r) + pid * PS * (kD / 2), PS * 64, bar(B_RFULL + rs));
+          }
+        }
+      }
+      __syncwarp();
+    }
+  } else if (warp >= kConvWarp0 && warp < kProdWarp) {
+    // ---------------------------------------------------------------- converters: staged pages -> f16 tiles
     const int ct = tid - kConvWarp0 * 32;
+    const int mode = p.k.mode, ns = p.k.ns;
     for (int j = 0; j < T && !timed_out; ++j) {
-      const int st = j % kStages, use = j / kStages;
-      if (j >= kStages && !mbar_wait_sleep(bar(B_EMPTY + st), (use - 1) & 1)) { timed_out = true; break; }
+      const int st = j % kTileStages, rs = j % kRawStages;
+      if (!mbar_wait_sleep(bar(B_RFULL + rs), (j / kRawStages) & 1)) { timed_out = true; break; }
+      if (j >= kTileStages && !mbar_wait_sleep(bar(B_EMPTY + st), ((j / kTileStages) - 1) & 1)) {
+        timed_out = true;
+        break;
+      }
+      // per-slot score / probability factors of this chunk: pages whose codes are widened
+      // without their scale (page scale mode) hand the scale to the softmax
+      if (ct < 2 * kSlotsPerChunk) {
+        const int sl = ct >> 1, pl = ct & 1, s2 = j * kSlotsPerChunk + sl;
+        float f = 1.f;
+        if (s2 < n_valid && mode == IAK_SCALE_PAGE) {
+          const int f2 = s_fmt[s2];
+          if (f2 == IAK_FMT_FP8 || f2 == IAK_FMT_INT8 || f2 == IAK_FMT_INT4)
+            f = *scale_at(rs, sl, pl, 0) * (f2 == IAK_FMT_FP8 ? 256.f : 1.f);
+        }
+        s_fac[(st * 8 + sl) * 2 + pl] = f;
+      }
 #pragma unroll 1
       for (int plane = 0; plane < 2; ++plane) {
-        const qpage::PlanePools pl = plane ? p.v : p.k;
         const uint32_t toff = tile_off(st, plane);
-#pragma unroll
+        const float* scale_rows = plane ? p.v.scale : p.k.scale;
+        const float* rscale_rows = plane ? p.v.res_scale : p.k.res_scale;
+#pragma unroll 1
         for (int i = 0; i < 2; ++i) {
-          const int u = ct + 128 * i;              // 256 units: 64 token rows x 4 groups of 32 channels
-          const int trow = u >> 2, g = u & 3;
-          const int si = j * kSlotsPerChunk + trow / PS, r = trow % PS;
+          // unit i of this thread: (token row, 32-channel group); a warp covers 8 rows of one slot,
+          // so the format is warp-uniform
+          const int u = ct + 128 * i;
+          const int trow = u >> 2, g = u & 3, slot = trow / PS, r = trow % PS;
+          const int si = j * kSlotsPerChunk + slot;
+          const bool live = si < n_valid && ((s_mask[si] >> r) & 1ull);
+          const int f = live ? s_fmt[si] : IAK_FMT_SKIP;
+          const uint8_t* rawp = sm + raw_off(rs, plane, slot);
           uint32_t hv[16];
-          if (si < n_valid && ((s_mask[si] >> r) & 1ull)) {
-            load_group(pl, s_fmt[si], s_pid[si], r, g, hv);
-          } else {
+          if (f == IAK_FMT_F16 || f == IAK_FMT_SKIP) {
 #pragma unroll
-            for (int k = 0; k < 16; ++k) hv[k] = 0u;
+            for (int k = 0; k < 4; ++k) {
+              uint4 v = make_uint4(0u, 0u, 0u, 0u);
+              if (f == IAK_FMT_F16) v = *reinterpret_cast<const uint4*>(rawp + r * 256 + g * 64 + k * 16);
+              hv[4 * k] = v.x; hv[4 * k + 1] = v.y; hv[4 * k + 2] = v.z; hv[4 * k + 3] = v.w;
+            }
+          } else {
+            const int64_t pid = s_pid[si];
+            const bool ch = mode == IAK_SCALE_CHANNEL;
+            const int grp = mode == IAK_SCALE_GROUP32 ? g : 0;
+            if (f == IAK_FMT_FP8 || f == IAK_FMT_INT8) {
+              const bool fold = mode == IAK_SCALE_PAGE;
+              const float s_all = (fold || ch) ? 0.f : *scale_at(rs, slot, plane, grp);
+              const float* chs = ch ? scale_rows + pid * ns : nullptr;
+              const uint4 w0 = *reinterpret_cast<const uint4*>(rawp + r * 128 + g * 32);
+              const uint4 w1 = *reinterpret_cast<const uint4*>(rawp + r * 128 + g * 32 + 16);
+              uint32_t h0[8], h1[8];
+              cvt8(w0, f, fold, g * 32, s_all, chs, h0);
+              cvt8(w1, f, fold, g * 32 + 16, s_all, chs, h1);
+#pragma unroll
+              for (int k = 0; k < 8; ++k) {
+                hv[k] = h0[k];
+                hv[8 + k] = h1[k];
+              }
+            } else {
+              const bool resid = f == IAK_FMT_INT4R;
+              const bool fold = mode == IAK_SCALE_PAGE && !resid;
+              const float s_all = (fold || ch) ? 0.f : *scale_at(rs, slot, plane, grp);
+              const float rs_all = (resid && !ch) ? *scale_at(rs, slot, 2 + plane, grp) : 0.f;
+              const uint4 b4 = *reinterpret_cast<const uint4*>(rawp + r * 64 + g * 16);
+              const uint4 r4 = resid ? *reinterpret_cast<const uint4*>(rawp + PS * 64 + r * 64 + g * 16)
+                                     : make_uint4(0u, 0u, 0u, 0u);
+              cvt4(b4, r4, resid, fold, g, s_all, rs_all, ch ? scale_rows + pid * ns : nullptr,
+                   (ch && resid) ? rscale_rows + pid * ns : nullptr, hv);
+            }
           }
 #pragma unroll
           for (int qd = 0; qd < 4; ++qd) {
-            const int c = g * 4 + qd;               // 16-byte chunk index of the row (0..15)
+            const int c = g * 4 + qd;            // 16-byte chunk index of the row (0..15)
             *reinterpret_cast<uint4*>(sm + toff + (c >> 3) * kKb + swz(trow, c & 7)) =
                 make_uint4(hv[4 * qd], hv[4 * qd + 1], hv[4 * qd + 2], hv[4 * qd + 3]);
           }
@@ -316,17 +516,17 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const PrefillPa
         fence_proxy_async();
         mbar_arrive(bar((plane ? B_VFULL : B_KFULL) + st));
       }
+      mbar_arrive(bar(B_REMPTY + rs));
     }
   } else if (warp == kMmaWarp) {
     // ---------------------------------------------------------------- MMA issuer
     if (lane == 0) {
       constexpr uint32_t kIdS = idesc_f16(kRows, kChunk, 0, 0);  // S = Q . K^T
       constexpr uint32_t kIdPV = idesc_f16(kRows, kD, 0, 1);     // O += P . V (V read MN-major)
-      const uint64_t q_desc = sw128_desc(sbase + Smem::q, 16, 1024);
       auto issue_s = [&](int j) -> bool {
-        const int k = j & 1, st = j % kStages;
+        const int k = j & 1, st = j % kTileStages;
         if (j >= kSBuf && !mbar_wait(bar(B_PVDONE + k), ((j >> 1) - 1) & 1)) return false;
-        if (!mbar_wait(bar(B_KFULL + st), (j / kStages) & 1)) return false;
+        if (!mbar_wait(bar(B_KFULL + st), (j / kTileStages) & 1)) return false;
         tc_fence_after();
         const uint32_t d = tmem + kSCol + k * kChunk;
 #pragma unroll
@@ -334,15 +534,15 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const PrefillPa
           const uint64_t bd = sw128_desc(sbase + tile_off(st, 0) + kb * kKb, 16, 1024);
 #pragma unroll
           for (int t = 0; t < 4; ++t)
-            mma_ss(d, q_desc + ((kb * kKbQ + t * 32) >> 4), bd + (t * 2), kIdS, (kb | t) ? 1u : 0u);
+            mma_ts(d, tmem + kQCol + kb * 32 + t * 8, bd + (t * 2), kIdS, (kb | t) ? 1u : 0u);
         }
         mma_commit(bar(B_SFULL + k));
         return true;
       };
       auto issue_pv = [&](int j) -> bool {
-        const int k = j & 1, st = j % kStages;
+        const int k = j & 1, st = j % kTileStages;
         if (!mbar_wait(bar(B_PFULL + k), (j >> 1) & 1)) return false;
-        if (!mbar_wait(bar(B_VFULL + st), (j / kStages) & 1)) return false;
+        if (!mbar_wait(bar(B_VFULL + st), (j / kTileStages) & 1)) return false;
         tc_fence_after();
         const uint64_t bd = sw128_desc(sbase + tile_off(st, 1), kKb, 1024);
 #pragma unroll
@@ -353,7 +553,9 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const PrefillPa
         mma_commit(bar(B_EMPTY + st));
         return true;
       };
-      if (T > 0 && !issue_s(0)) timed_out = true;
+      if (!mbar_wait(bar(B_QREADY), 0)) timed_out = true;
+      tc_fence_after();
+      if (!timed_out && T > 0 && !issue_s(0)) timed_out = true;
       for (int j = 0; j < T && !timed_out; ++j) {
         if (j + 1 < T && !issue_s(j + 1)) { timed_out = true; break; }
         if (!issue_pv(j)) { timed_out = true; break; }
@@ -363,42 +565,57 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const PrefillPa
     }
   } else if (warp < 4) {
     // ---------------------------------------------------------------- softmax (one query row per thread)
-    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(warp * 32) << 16);
     const float scale = p.sm_scale * kLog2e;
     float m_used = -INFINITY, l = 0.f;
     for (int j = 0; j < T && !timed_out; ++j) {
       const int k = j & 1;
       bool ok = true;
-      if (lane == 0) ok = mbar_wait_sleep(bar(B_SFULL + k), (j >> 1) & 1);
+      const int st = j % kTileStages;
+      // S ready; the K tile barrier (already complete) orders the converters' factor writes
+      if (lane == 0)
+        ok = mbar_wait_sleep(bar(B_SFULL + k), (j >> 1) & 1) && mbar_wait(bar(B_KFULL + st), (j / kTileStages) & 1);
       if (!__shfl_sync(0xffffffffu, ok, 0)) { timed_out = true; break; }
       tc_fence_after();
-      float x[kChunk];
-      float tmax = -INFINITY;
+      // a chunk is handled in two halves of 32 columns (S is read from TMEM twice) to keep the
+      // unrolled code small; the visibility bits, score and value factors of the half's slots
+      // come from shared memory
+      const bool cfull = s_cfull[j] != 0;
+      constexpr int kSPH = PS <= 32 ? 32 / PS : 1;    // slots per half chunk
+      auto half_slots = [&](int hh, uint64_t (&vis)[kSPH], float (&kf)[kSPH], float (&vf)[kSPH]) {
 #pragma unroll
-      for (int h2 = 0; h2 < 2; ++h2) {
+        for (int q = 0; q < kSPH; ++q) {
+          const int sl = PS <= 32 ? hh * kSPH + q : 0;
+          const int si = j * kSlotsPerChunk + sl;
+          vis[q] = cfull ? ~0ull : 0ull;
+          if (!cfull && si < n_valid) {
+            const int64_t lim = p.causal ? static_cast<int64_t>(qpos) - s_pos0[si] : PS - 1;   // last visible row
+            const uint64_t upto = lim < 0 ? 0ull : (lim >= PS - 1 ? ~0ull : ((2ull << lim) - 1ull));
+            vis[q] = s_mask[si] & upto;
+          }
+          if (PS == 64) vis[q] >>= hh * 32;    // this half's 32 rows of the one slot
+          kf[q] = s_fac[(st * 8 + sl) * 2];
+          vf[q] = s_fac[(st * 8 + sl) * 2 + 1];
+        }
+      };
+      float tmax_raw = -INFINITY;               // max over visible columns of score x factor (factors > 0)
+#pragma unroll 1
+      for (int hh = 0; hh < 2; ++hh) {
         uint32_t sr[32];
-        tmem_ld32(lane_addr + kSCol + k * kChunk + h2 * 32, sr);
+        tmem_ld32(lane_addr + kSCol + k * kChunk + hh * 32, sr);
+        uint64_t vis[kSPH];
+        float kf[kSPH], vf[kSPH];
+        half_slots(hh, vis, kf, vf);
         tmem_wait_ld();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) x[h2 * 32 + i] = __uint_as_float(sr[i]) * scale;
-      }
+        for (int q = 0; q < kSPH; ++q) {
+          float m = -INFINITY;
 #pragma unroll
-      for (int sl = 0; sl < kSlotsPerChunk; ++sl) {
-        const int si = j * kSlotsPerChunk + sl;
-        uint64_t mask = 0;
-        int64_t lim = -1;                       // last visible row offset within the page
-        if (si < n_valid) {
-          mask = s_mask[si];
-          lim = p.causal ? static_cast<int64_t>(qpos) - s_pos0[si] : static_cast<int64_t>(PS);
-        }
-#pragma unroll
-        for (int r = 0; r < PS; ++r) {
-          const bool vis = ((mask >> r) & 1ull) && r <= lim;
-          const int c = sl * PS + r;
-          x[c] = vis ? x[c] : -INFINITY;
-          tmax = fmaxf(tmax, x[c]);
+          for (int r = 0; r < (PS <= 32 ? PS : 32); ++r)
+            if ((vis[q] >> r) & 1ull) m = fmaxf(m, __uint_as_float(sr[q * PS + r]));
+          tmax_raw = fmaxf(tmax_raw, m * kf[q]);
         }
       }
+      const float tmax = tmax_raw == -INFINITY ? -INFINITY : tmax_raw * scale;
       if (j == 0) {
         m_used = tmax;
       } else {
@@ -427,17 +644,31 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const PrefillPa
           tmem_wait_st();
         }
       }
-      uint32_t pk[kChunk / 2];
       float lsum = 0.f;
+      const float neg_m = -m_used;
+      // l sums the softmax weights; P (f16, packed over the first 32 columns of the S buffer)
+      // carries them times the value factor of their slot
+#pragma unroll 1
+      for (int hh = 0; hh < 2; ++hh) {
+        uint32_t sr[32];
+        tmem_ld32(lane_addr + kSCol + k * kChunk + hh * 32, sr);
+        uint64_t vis[kSPH];
+        float kf[kSPH], vf[kSPH];
+        half_slots(hh, vis, kf, vf);
+        tmem_wait_ld();
+        uint32_t pk[16];
 #pragma unroll
-      for (int i = 0; i < kChunk / 2; ++i) {
-        const float p0 = x[2 * i] != -INFINITY ? exp2f(x[2 * i] - m_used) : 0.f;
-        const float p1 = x[2 * i + 1] != -INFINITY ? exp2f(x[2 * i + 1] - m_used) : 0.f;
-        lsum += p0 + p1;
-        pk[i] = pack_h2(p0, p1);
+        for (int i = 0; i < 16; ++i) {
+          const int q = PS <= 32 ? (2 * i) / PS : 0, r = PS <= 32 ? (2 * i) % PS : 2 * i;
+          const float a = scale * kf[q];
+          const float p0 = ((vis[q] >> r) & 1ull) ? ex2(fmaf(__uint_as_float(sr[2 * i]), a, neg_m)) : 0.f;
+          const float p1 = ((vis[q] >> (r + 1)) & 1ull) ? ex2(fmaf(__uint_as_float(sr[2 * i + 1]), a, neg_m)) : 0.f;
+          lsum += p0 + p1;
+          pk[i] = pack_h2(p0 * vf[q], p1 * vf[q]);
+        }
+        tmem_st16(lane_addr + kSCol + k * kChunk + hh * 16, pk);
       }
       l += lsum;
-      tmem_st32(lane_addr + kSCol + k * kChunk, pk);
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(bar(B_PFULL + k));
@@ -453,6 +684,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const PrefillPa
     }
     const float inv = l > 0.f ? 1.f / l : 0.f;
     const int64_t obase = b * p.o_sb + static_cast<int64_t>(hq) * p.o_sh + static_cast<int64_t>(qm) * p.o_sm;
+    const bool ovec = p.o_vec;
 #pragma unroll 1
     for (int c = 0; c < kD / 32; ++c) {
       uint32_t o[32];
@@ -464,8 +696,35 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const PrefillPa
         for (int i = 0; i < 32; ++i) o[i] = 0u;
       }
       if (!row_ok) continue;
+      const int64_t e0 = obase + c * 32;
+      if (ovec && p.out_dtype == IAK_DT_F32) {
+        float4* dst = reinterpret_cast<float4*>(static_cast<float*>(p.out) + e0);
 #pragma unroll
-      for (int i = 0; i < 32; ++i) store_from_float(p.out, p.out_dtype, obase + c * 32 + i, __uint_as_float(o[i]) * inv);
+        for (int i = 0; i < 8; ++i)
+          dst[i] = make_float4(__uint_as_float(o[4 * i]) * inv, __uint_as_float(o[4 * i + 1]) * inv,
+                               __uint_as_float(o[4 * i + 2]) * inv, __uint_as_float(o[4 * i + 3]) * inv);
+      } else if (ovec) {
+        uint4* dst = reinterpret_cast<uint4*>(static_cast<uint16_t*>(p.out) + e0);
+        const bool bf = p.out_dtype == IAK_DT_BF16;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          uint32_t w[4];
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const float a0 = __uint_as_float(o[8 * i + 2 * k]) * inv, a1 = __uint_as_float(o[8 * i + 2 * k + 1]) * inv;
+            if (bf) {
+              const __nv_bfloat162 hb = __floats2bfloat162_rn(a0, a1);
+              w[k] = *reinterpret_cast<const uint32_t*>(&hb);
+            } else {
+              w[k] = pack_h2(a0, a1);
+            }
+          }
+          dst[i] = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) store_from_float(p.out, p.out_dtype, e0 + i, __uint_as_float(o[i]) * inv);
+      }
     }
   }
 
