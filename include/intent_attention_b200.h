@@ -358,6 +358,10 @@ typedef struct iak_route_args {
   uint8_t* page_prec;
   uint8_t* page_tags; int64_t num_tag_pages;
   uint8_t prec_to_tag[6];
+  /* row_masks [batch, table_width] (or NULL; page_size <= 64): bit r of a
+   * listed page = token page * page_size + r lies in a selected block (the
+   * exact-token bounds iak_prefill takes); 0 padded */
+  uint64_t* row_masks;
 } iak_route_args;
 int iak_route_pages(const iak_route_args* args, void* stream);
 

@@ -154,7 +154,10 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(const iak_route_ar
   int32_t* table = p.page_table + static_cast<int64_t>(b) * Ht * W;
   int32_t* counts = p.page_counts + static_cast<int64_t>(b) * Ht;
   uint8_t* prow = p.page_prec ? p.page_prec + static_cast<int64_t>(b) * W : nullptr;
+  uint64_t* mrow = p.row_masks ? p.row_masks + static_cast<int64_t>(b) * W : nullptr;
   if (bad) {
+    if (mrow)
+      for (int o = tid; o < W; o += kRouteThreads) mrow[o] = 0ull;
     for (int o = tid; o < Ht * W; o += kRouteThreads) table[o] = p.pad_value;
     if (prow)
       for (int o = tid; o < W; o += kRouteThreads) prow[o] = IAK_PREC_SKIP;
@@ -288,6 +291,7 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(const iak_route_ar
     if (o >= listed) {
       for (int h = 0; h < Ht; ++h) table[static_cast<int64_t>(h) * W + o] = p.pad_value;
       if (prow) prow[o] = IAK_PREC_SKIP;
+      if (mrow) mrow[o] = 0ull;
       continue;
     }
     int lo = 0, hi = nsel - 1;
@@ -299,6 +303,23 @@ __global__ void __launch_bounds__(kRouteThreads) route_kernel(const iak_route_ar
     const int pg = r.x + (o - work[lo]);
     const int pr = prec[r.y];
     if (prow) prow[o] = static_cast<uint8_t>(pr);
+    if (mrow) {
+      // rows of the page covered by any selected block: the owner and its neighbours sharing the page
+      const int i = r.y;
+      const int64_t lo = static_cast<int64_t>(pg) * PS, hi = lo + PS;
+      auto cover = [&](int blk) -> uint64_t {
+        const int64_t s0 = max(static_cast<int64_t>(bstart[blk]), lo), e0 = min(static_cast<int64_t>(bend[blk]), hi);
+        if (e0 <= s0) return 0ull;
+        const int rows = static_cast<int>(e0 - s0);
+        return (rows >= 64 ? ~0ull : ((1ull << rows) - 1ull)) << (s0 - lo);
+      };
+      uint64_t m = cover(i);
+      for (int jb = i - 1; jb >= 0 && (bend[jb] - 1) / PS >= pg; --jb)
+        if (pos[jb] >= 0) m |= cover(jb);
+      for (int jb = i + 1; jb < n && bstart[jb] / PS <= pg; ++jb)
+        if (pos[jb] >= 0) m |= cover(jb);
+      mrow[o] = m;
+    }
     for (int h = 0; h < Ht; ++h) {
       const int32_t phys = (hbase ? hbase[h] : 0) + pg;
       table[static_cast<int64_t>(h) * W + o] = phys;
@@ -336,6 +357,7 @@ extern "C" int iak_route_pages(const iak_route_args* a, void* stream) {
     return fail(IAK_ERR_INVALID_ARG, "null route output");
   if (a->num_blocks > 0 && (!a->block_start || !a->block_end || !a->block_policy || !a->scores))
     return fail(IAK_ERR_INVALID_ARG, "null route input");
+  if (a->row_masks && a->page_size > 64) return fail(IAK_ERR_UNSUPPORTED, "row masks need page_size <= 64");
   if (static_cast<int64_t>(a->num_table_heads) * a->table_width > 0x7FFFFFFFLL)
     return fail(IAK_ERR_UNSUPPORTED, "page table row too large");
   int slots = 1;

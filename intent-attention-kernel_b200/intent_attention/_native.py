@@ -149,6 +149,7 @@ class RouteArgs(ctypes.Structure):
         ("page_table", c_void_p), ("page_counts", c_void_p), ("num_selected", c_void_p),
         ("page_prec", c_void_p),
         ("page_tags", c_void_p), ("num_tag_pages", c_i64), ("prec_to_tag", ctypes.c_uint8 * 6),
+        ("row_masks", c_void_p),
     ]
 
 MAX_PEERS = 8

@@ -78,6 +78,7 @@ class RoutedPages:
     page_counts: torch.Tensor    # [B, Ht] int32, min(n, W)
     num_selected: torch.Tensor   # [B] int32, n before truncation, -1 for an invalid layout
     page_prec: torch.Tensor      # [B, W] uint8 precision code per listed page (PREC_SKIP padding)
+    row_masks: Optional[torch.Tensor] = None   # [B, W] int64 bit masks of the selected rows (0 padding)
 
 
 def encode_layouts(layouts: Sequence[BlockLayout], device, scores: Optional[Sequence[Sequence[float]]] = None,
@@ -112,14 +113,17 @@ def route_pages(layouts: LayoutBatch, config: RouterConfig, page_size: int, tabl
                 bases: Optional[torch.Tensor] = None, seq_lens: Optional[torch.Tensor] = None,
                 page_tags: Optional[torch.Tensor] = None,
                 prec_to_tag: Optional[Mapping[KVPrecision, int]] = None, pad_value: int = -1,
-                out: Optional[RoutedPages] = None) -> RoutedPages:
+                out: Optional[RoutedPages] = None, row_masks: bool = False) -> RoutedPages:
     """Route every sequence of ``layouts`` and write its page-table rows on the device.
 
     ``config`` and ``quantizer`` mean what they mean for ``BlockRouter``
     (``quantizer=None`` builds the router's default from ``config``).
     Physical page id = ``bases[b, h]`` + logical page id.  With ``page_tags``
     (uint8, one per physical page) and ``prec_to_tag`` (precision -> decode
-    tag), every listed page's tag is written too.  Never synchronises.
+    tag), every listed page's tag is written too.  ``row_masks`` also returns,
+    per listed page, the bit mask of its rows inside selected blocks (the
+    exact-token bounds ``paged_prefill`` takes; page_size <= 64).  Never
+    synchronises.
     """
     dev = layouts.scores.device
     _require_cuda(layouts.scores, "layouts.scores")
@@ -142,6 +146,8 @@ def route_pages(layouts: LayoutBatch, config: RouterConfig, page_size: int, tabl
                           torch.empty((B, table_heads), dtype=torch.int32, device=dev),
                           torch.empty(B, dtype=torch.int32, device=dev),
                           torch.empty((B, table_width), dtype=torch.uint8, device=dev))
+    if row_masks and out.row_masks is None:
+        out.row_masks = torch.empty((B, table_width), dtype=torch.int64, device=dev)
     a = N.RouteArgs()
     a.num_blocks = nb
     keep = []   # temporaries must outlive the launch's argument capture
@@ -180,6 +186,10 @@ def route_pages(layouts: LayoutBatch, config: RouterConfig, page_size: int, tabl
         a.page_tags, a.num_tag_pages = page_tags.data_ptr(), page_tags.numel()
         for prec, code in PRECISION_CODES.items():
             a.prec_to_tag[code] = int(prec_to_tag.get(prec, 0))
+    if out.row_masks is not None:
+        if out.row_masks.dtype != torch.int64 or tuple(out.row_masks.shape) != (B, table_width):
+            raise ValueError("row_masks must be int64 [B, table_width]")
+        a.row_masks = out.row_masks.data_ptr()
     N.check(N.lib().iak_route_pages(ctypes.byref(a), _stream(dev)), "iak_route_pages")
     return out
 

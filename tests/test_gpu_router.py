@@ -6,6 +6,8 @@ Page ids, counts, precisions and tags are integer outputs: bit-exact.
 """
 
 import math
+
+import numpy as np
 import random
 
 import pytest
@@ -267,3 +269,61 @@ def test_route_then_decode_matches_host_packed_table():
     torch.cuda.synchronize()
     assert torch.isfinite(o_dev).all()
     assert torch.equal(o_dev, o_host)
+
+
+def test_row_masks_match_selected_block_rows():
+    rng = random.Random(31)
+    for trial in range(8):
+        ps = rng.choice([8, 16, 64])
+        layout, total = _random_layout(rng, 60, ps)
+        router = BlockRouter(RouterConfig(top_k_blocks=rng.randrange(0, 20), memory_pressure=rng.random()))
+        out = route_layouts(router, [layout], [total], ps, 512, "cuda", row_masks=True)
+        routed = router.route_layout(layout, total)
+        sel = router.selected_blocks(routed)
+        ids = router.selected_page_ids(routed, ps)
+        expect = []
+        for pg in ids:
+            m = 0
+            for blk in sel:
+                for t in range(max(blk.start, pg * ps), min(blk.end, (pg + 1) * ps)):
+                    m |= 1 << (t - pg * ps)
+            expect.append(m)
+        got = out.row_masks[0, :len(ids)].cpu().numpy().view(np.uint64).tolist()
+        assert got == expect, trial
+        assert (out.row_masks[0, len(ids):] == 0).all()
+
+
+def test_route_then_prefill_attends_exactly_the_selected_tokens():
+    """Router pages + row masks drive the tensor-core prefill; the result is the
+    exact-token attention over the router's selected blocks."""
+    from intent_attention import PagePool
+    from intent_attention.paged import make_tag_map, paged_prefill
+    from oracle import prefill as op
+    rng = random.Random(41)
+    ps, D, B, H = 16, 128, 2, 2
+    layout, total = _random_layout(rng, 40, ps)
+    total += 7
+    n_log = (total + ps - 1) // ps
+    g = np.random.default_rng(5)
+    k = g.standard_normal((B, H, n_log * ps, D)).astype(np.float32)
+    v = g.standard_normal((B, H, n_log * ps, D)).astype(np.float32)
+    pool = PagePool.allocate(B * H * n_log, ps, D, ["F16"], "page", "cuda")
+    pool.quantize_(torch.from_numpy(k.reshape(-1, ps, D)).cuda(), torch.from_numpy(v.reshape(-1, ps, D)).cuda(),
+                   ["F16"] * (B * H * n_log))
+    bases = (torch.arange(B * H, dtype=torch.int32) * n_log).view(B, H).cuda()
+    router = BlockRouter(RouterConfig(top_k_blocks=6, memory_pressure=0.2))
+    out = route_layouts(router, [layout] * B, [total] * B, ps, n_log, "cuda", table_heads=H, bases=bases,
+                        row_masks=True)
+    M = total
+    q = g.standard_normal((B, H, M, D)).astype(np.float32)
+    tags = torch.ones(B * H * n_log, dtype=torch.uint8, device="cuda")
+    got = paged_prefill(torch.from_numpy(q).cuda(), pool, out.page_table, out.page_counts, tags,
+                        make_tag_map({1: "F16"}), causal=True, bases=bases, row_masks=out.row_masks,
+                        kernel="tensor")
+    routed = router.route_layout(layout, total)
+    spec = [(b.name, b.start, b.end, "ALWAYS", None) for b in router.selected_blocks(routed)]
+    spec.sort(key=lambda s: s[1])
+    kk = torch.from_numpy(k).half().float().numpy()[:, :, :total]
+    vv = torch.from_numpy(v).half().float().numpy()[:, :, :total]
+    ref = np.nan_to_num(op.semantic_block_attention(q, kk, vv, spec, True), nan=0.0)
+    np.testing.assert_allclose(got.cpu().numpy(), ref, atol=2e-3, rtol=1e-2)
