@@ -111,3 +111,39 @@ def test_route_args_rejected_on_the_host():
     assert L.iak_route_pages(ctypes.byref(a), None) == N.IAK_OK
     a.batch = 2
     assert L.iak_route_pages(ctypes.byref(a), None) == N.IAK_ERR_INVALID_ARG
+
+
+def test_prefill_and_kv_write_args_rejected_on_the_host():
+    """iak_prefill / iak_append_tokens / iak_convert_pages validate their
+    scalars and pointers before any device call."""
+    L = N.lib()
+    pools = N.PagePools()
+    pools.num_pages, pools.page_size, pools.head_dim, pools.scale_mode = 4, 16, 128, 0
+    a = N.PrefillArgs()
+    a.batch, a.num_q_heads, a.num_table_heads, a.num_queries, a.table_width = 1, 4, 3, 8, 4
+    assert L.iak_prefill(ctypes.byref(pools), ctypes.byref(a), None) == N.IAK_ERR_INVALID_ARG   # 4 % 3 != 0
+    assert b"multiple" in L.iak_last_error()
+    a.num_table_heads = 2
+    assert L.iak_prefill(ctypes.byref(pools), ctypes.byref(a), None) == N.IAK_ERR_INVALID_ARG   # null q / out
+    a.num_queries = 0
+    assert L.iak_prefill(ctypes.byref(pools), ctypes.byref(a), None) == N.IAK_OK               # nothing to do
+    a.num_queries = 8
+    a.q, a.out, a.page_table, a.page_tags, a.tag_bytes = 16, 16, 16, 16, 2
+    assert L.iak_prefill(ctypes.byref(pools), ctypes.byref(a), None) == N.IAK_ERR_INVALID_ARG   # tag_bytes
+    a.tag_bytes = 1
+    pools.page_size, a.row_masks = 128, 16
+    assert L.iak_prefill(ctypes.byref(pools), ctypes.byref(a), None) == N.IAK_ERR_UNSUPPORTED   # masks, PS > 64
+    pools.page_size, pools.head_dim = 16, 40
+    assert L.iak_prefill(ctypes.byref(pools), ctypes.byref(a), None) == N.IAK_ERR_UNSUPPORTED   # head_dim
+    pools.head_dim = 128
+    ap = N.AppendArgs()
+    ap.batch, ap.num_table_heads, ap.num_new = 2, 1, 1
+    assert L.iak_append_tokens(ctypes.byref(pools), ctypes.byref(ap), None) == N.IAK_ERR_INVALID_ARG
+    ap.num_new = 0
+    assert L.iak_append_tokens(ctypes.byref(pools), ctypes.byref(ap), None) == N.IAK_OK
+    cv = N.ConvertArgs()
+    cv.num_ids = 3
+    assert L.iak_convert_pages(ctypes.byref(pools), ctypes.byref(cv), None) == N.IAK_ERR_INVALID_ARG
+    pools.page_size = 256
+    cv.page_ids, cv.new_formats, cv.page_tags, cv.tag_bytes = 16, 16, 16, 1
+    assert L.iak_convert_pages(ctypes.byref(pools), ctypes.byref(cv), None) == N.IAK_ERR_UNSUPPORTED   # PS*D too big
