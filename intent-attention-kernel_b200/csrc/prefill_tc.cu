@@ -370,24 +370,38 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const PrefillPa
     // ---------------------------------------------------------------- producer: scales + bulk copies
     const int mode = p.k.mode, ns = p.k.ns;
     const int ngrp = mode == IAK_SCALE_GROUP32 ? 4 : 1;   // channel-mode scales are read by the converters
+    // (slot, kind, group) items of a chunk's page / group scales: at most 8 x 4 x 4 = 128, 4 per lane
+    constexpr int kScaleItemsPerLane = 4;
+    const int n_items = mode == IAK_SCALE_CHANNEL ? 0 : kSlotsPerChunk * 4 * ngrp;
     for (int j = 0; j < T; ++j) {
       const int rs = j % kRawStages;
-      bool ok = true;
-      if (lane == 0 && j >= kRawStages) ok = mbar_wait_sleep(bar(B_REMPTY + rs), ((j / kRawStages) - 1) & 1);
-      if (!__shfl_sync(0xffffffffu, ok, 0)) { timed_out = true; break; }
-      // page / group scales of the chunk's slots into shared memory, one (slot, kind, group) per lane
-      if (mode != IAK_SCALE_CHANNEL) {
-        for (int it = lane; it < kSlotsPerChunk * 4 * ngrp; it += 32) {
+      // the chunk's scales are loaded before the wait for a free stage, so their latency
+      // overlaps it; they are stored once the stage is free
+      float sv[kScaleItemsPerLane];
+#pragma unroll
+      for (int q = 0; q < kScaleItemsPerLane; ++q) {
+        const int it = lane + 32 * q;
+        sv[q] = 0.f;
+        if (it < n_items) {
           const int sl = it / (4 * ngrp), kind = (it / ngrp) % 4, g = it % ngrp;
           const int si = j * kSlotsPerChunk + sl;
-          float v = 0.f;
           if (si < n_valid) {
             const int fmt = s_fmt[si];
             const float* arr = kind == 0 ? p.k.scale : (kind == 1 ? p.v.scale : (kind == 2 ? p.k.res_scale : p.v.res_scale));
             const bool need = fmt != IAK_FMT_F16 && (kind < 2 || fmt == IAK_FMT_INT4R);
-            if (need && arr) v = arr[static_cast<int64_t>(s_pid[si]) * ns + g];
+            if (need && arr) sv[q] = arr[static_cast<int64_t>(s_pid[si]) * ns + g];
           }
-          *scale_at(rs, sl, kind, g) = v;
+        }
+      }
+      bool ok = true;
+      if (lane == 0 && j >= kRawStages) ok = mbar_wait_sleep(bar(B_REMPTY + rs), ((j / kRawStages) - 1) & 1);
+      if (!__shfl_sync(0xffffffffu, ok, 0)) { timed_out = true; break; }
+#pragma unroll
+      for (int q = 0; q < kScaleItemsPerLane; ++q) {
+        const int it = lane + 32 * q;
+        if (it < n_items) {
+          const int sl = it / (4 * ngrp), kind = (it / ngrp) % 4, g = it % ngrp;
+          *scale_at(rs, sl, kind, g) = sv[q];
         }
       }
       __syncwarp();
