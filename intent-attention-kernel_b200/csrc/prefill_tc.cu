@@ -482,14 +482,23 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const PrefillPa
           const bool live = si < n_valid && ((s_mask[si] >> r) & 1ull);
           const int f = live ? s_fmt[si] : IAK_FMT_SKIP;
           const uint8_t* rawp = sm + raw_off(rs, plane, slot);
-          uint32_t hv[16];
+          auto put = [&](int c, uint32_t x0, uint32_t x1, uint32_t x2, uint32_t x3) {
+            // 16-byte chunk c (0..15) of the tile row, 128-byte swizzled
+            *reinterpret_cast<uint4*>(sm + toff + (c >> 3) * kKb + swz(trow, c & 7)) = make_uint4(x0, x1, x2, x3);
+          };
+          // Staged rows are 256 (F16) or 128 (8-bit) bytes apart, so a warp's eight rows share banks:
+          // each row reads its chunks in an order rotated by the row index, which spreads one load
+          // instruction of the warp over distinct banks.  All loads precede the stores.
           if (f == IAK_FMT_F16 || f == IAK_FMT_SKIP) {
+            uint4 v[4];
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
-              uint4 v = make_uint4(0u, 0u, 0u, 0u);
-              if (f == IAK_FMT_F16) v = *reinterpret_cast<const uint4*>(rawp + r * 256 + g * 64 + k * 16);
-              hv[4 * k] = v.x; hv[4 * k + 1] = v.y; hv[4 * k + 2] = v.z; hv[4 * k + 3] = v.w;
+              const int kk = (k + r) & 3;
+              v[k] = f == IAK_FMT_F16 ? *reinterpret_cast<const uint4*>(rawp + r * 256 + g * 64 + kk * 16)
+                                      : make_uint4(0u, 0u, 0u, 0u);
             }
+#pragma unroll
+            for (int k = 0; k < 4; ++k) put(g * 4 + ((k + r) & 3), v[k].x, v[k].y, v[k].z, v[k].w);
           } else {
             const int64_t pid = s_pid[si];
             const bool ch = mode == IAK_SCALE_CHANNEL;
@@ -498,16 +507,16 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const PrefillPa
               const bool fold = mode == IAK_SCALE_PAGE;
               const float s_all = (fold || ch) ? 0.f : *scale_at(rs, slot, plane, grp);
               const float* chs = ch ? scale_rows + pid * ns : nullptr;
-              const uint4 w0 = *reinterpret_cast<const uint4*>(rawp + r * 128 + g * 32);
-              const uint4 w1 = *reinterpret_cast<const uint4*>(rawp + r * 128 + g * 32 + 16);
+              const int k0 = r & 1;
+              const uint4 w0 = *reinterpret_cast<const uint4*>(rawp + r * 128 + g * 32 + k0 * 16);
+              const uint4 w1 = *reinterpret_cast<const uint4*>(rawp + r * 128 + g * 32 + (k0 ^ 1) * 16);
               uint32_t h0[8], h1[8];
-              cvt8(w0, f, fold, g * 32, s_all, chs, h0);
-              cvt8(w1, f, fold, g * 32 + 16, s_all, chs, h1);
-#pragma unroll
-              for (int k = 0; k < 8; ++k) {
-                hv[k] = h0[k];
-                hv[8 + k] = h1[k];
-              }
+              cvt8(w0, f, fold, g * 32 + k0 * 16, s_all, chs, h0);
+              cvt8(w1, f, fold, g * 32 + (k0 ^ 1) * 16, s_all, chs, h1);
+              put(g * 4 + 2 * k0, h0[0], h0[1], h0[2], h0[3]);
+              put(g * 4 + 2 * k0 + 1, h0[4], h0[5], h0[6], h0[7]);
+              put(g * 4 + 2 * (k0 ^ 1), h1[0], h1[1], h1[2], h1[3]);
+              put(g * 4 + 2 * (k0 ^ 1) + 1, h1[4], h1[5], h1[6], h1[7]);
             } else {
               const bool resid = f == IAK_FMT_INT4R;
               const bool fold = mode == IAK_SCALE_PAGE && !resid;
@@ -516,15 +525,12 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const PrefillPa
               const uint4 b4 = *reinterpret_cast<const uint4*>(rawp + r * 64 + g * 16);
               const uint4 r4 = resid ? *reinterpret_cast<const uint4*>(rawp + PS * 64 + r * 64 + g * 16)
                                      : make_uint4(0u, 0u, 0u, 0u);
+              uint32_t hv[16];
               cvt4(b4, r4, resid, fold, g, s_all, rs_all, ch ? scale_rows + pid * ns : nullptr,
                    (ch && resid) ? rscale_rows + pid * ns : nullptr, hv);
-            }
-          }
 #pragma unroll
-          for (int qd = 0; qd < 4; ++qd) {
-            const int c = g * 4 + qd;            // 16-byte chunk index of the row (0..15)
-            *reinterpret_cast<uint4*>(sm + toff + (c >> 3) * kKb + swz(trow, c & 7)) =
-                make_uint4(hv[4 * qd], hv[4 * qd + 1], hv[4 * qd + 2], hv[4 * qd + 3]);
+              for (int qd = 0; qd < 4; ++qd) put(g * 4 + qd, hv[4 * qd], hv[4 * qd + 1], hv[4 * qd + 2], hv[4 * qd + 3]);
+            }
           }
         }
         fence_proxy_async();
