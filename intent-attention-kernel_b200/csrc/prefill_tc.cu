@@ -1,27 +1,34 @@
 // Tensor-core (tcgen05 / TMEM) multi-query attention over selected pages, for
 // head_dim 128 and page sizes 8..64 (any page format of the pools).
 //
-// One CTA = one work item (sequence b, page-table head h, tile of 128 query
-// rows).  Rows are (query m, head g of the group) pairs, m-major, so a tile
-// holds 128 / G consecutive queries of the G query heads sharing the table.
+// One CTA = one work item (sequence b, page-table head h, two tiles of 128
+// query rows that share every converted K / V chunk).  Rows are (query m,
+// head g of the group) pairs, m-major, so a tile holds 128 / G consecutive
+// queries of the G query heads sharing the table.
 //   * the producer warp first compacts the unit's table into shared memory
 //     (slots with a page in a supported format, a non-empty row mask and,
-//     causal, a first selected row not after the tile's last query position;
-//     64-token chunks of 64 / PS slots), then bulk-copies each chunk's raw K
-//     and V page bytes (cp.async.bulk, mbarrier transaction counts) into a
-//     2-stage staging ring, running ahead of the converters;
-//   * a converter warpgroup dequantises the staged rows (code x scale, fp32;
-//     scales read ahead of the wait) to f16 tiles, 128-byte swizzled, rows the
-//     slot mask does not select written as zero, over a 3-stage ring;
-//   * S = Q . K^T (M = 128, N = 64, K = 128: 8 tcgen05.mma, Q f16 in TMEM as
-//     the A operand) lands in TMEM; the softmax warpgroup owns one TMEM lane
-//     (= one query row) per thread: it applies the row masks and the causal
-//     comparison of each key's token position with the row's query position,
-//     runs the online softmax in the exp2 domain with lazy O rescaling, and
-//     writes P (f16) back over S;
-//   * O += P . V (M = 128, N = 128, K = 64: 4 tcgen05.mma, P the TMEM A
-//     operand, V read MN-major) accumulates in TMEM (fp32).
-// TMEM: O 128 | S/P 2 x 64 | Q 64 columns (512 allocated, one CTA per SM).
+//     causal, a first selected row not after the CTA's last query position;
+//     64-token chunks of 64 / PS slots) and flags the chunks every row sees
+//     whole; then, per chunk, it stages the pages' scales in shared memory and
+//     bulk-copies their raw K and V bytes (cp.async.bulk, mbarrier transaction
+//     counts) into a 3-stage ring, running ahead of the converters;
+//   * a converter warpgroup (one 32-channel row segment per thread, unit and
+//     plane) widens the staged rows to f16 tiles, 128-byte swizzled, rows the
+//     slot mask does not select written as zero, over a 3-stage ring: F16 rows
+//     are copied, page-scaled FP8 / INT8 / INT4 codes are widened exactly (the
+//     page scale goes to the softmax), group / channel scales and
+//     INT4_RESIDUAL are applied in fp32;
+//   * per chunk and query tile, S = Q . K^T (M = 128, N = 64, K = 128: 8
+//     tcgen05.mma, Q f16 in TMEM as the A operand) lands in TMEM; each tile's
+//     softmax warpgroup owns one TMEM lane (= one query row) per thread: it
+//     applies the row masks and the causal comparison of each key's token
+//     position with the row's query position (skipped for chunks seen whole),
+//     multiplies in the slots' score factors, runs the online softmax in the
+//     exp2 domain with lazy O rescaling over two half chunks, and writes P
+//     (f16, times the slots' value factors) back over S;
+//   * O += P . V (M = 128, N = 128, K = 64: 4 tcgen05.mma per tile, P the
+//     TMEM A operand, V read MN-major) accumulates in TMEM (fp32).
+// TMEM: O 2 x 128 | S/P 2 x 64 | Q 2 x 64 columns (512 allocated, one CTA per SM).
 // Rows that see no key are written as 0.
 //
 // Reference semantics: reference.py:82-130 semantic_block_attention with the
@@ -40,17 +47,18 @@ namespace {
 using namespace tc;
 
 constexpr int kD = 128, kRows = 128, kChunk = 64;
+constexpr int kQTiles = 2;                    // 128-row query tiles per CTA, sharing every converted K/V chunk
 constexpr int kTileStages = 3, kRawStages = 3;
 constexpr int kMaxSlots = 1024;
-constexpr int kThreads = 320;                 // softmax wg | converter wg | producer warp | MMA warp
-constexpr int kConvWarp0 = 4, kProdWarp = 8, kMmaWarp = 9;
+constexpr int kThreads = 448;                 // 2 softmax wgs | converter wg | producer warp | MMA warp
+constexpr int kSoftWarps = 4 * kQTiles, kConvWarp0 = 8, kProdWarp = 12, kMmaWarp = 13;
 constexpr int kKb = kChunk * 128;             // 64 token rows x 64 channels of f16 (one swizzle-atom column)
 constexpr int kTile = 2 * kKb;                // 64 tokens x 128 channels
 constexpr int kRawPlane = kChunk * kD * 2;    // staged bytes of one plane of a chunk (room for f16 rows)
 constexpr int kRawStage = 2 * kRawPlane;      // K plane, then V plane
-constexpr int kSBuf = 2;
-constexpr int kOCol = 0, kSCol = kD, kQCol = kSCol + kSBuf * kChunk, kTmemCols = 512;
-static_assert(kQCol + kD / 2 <= kTmemCols, "TMEM budget");
+// TMEM columns: O of each tile | S / P of each tile | Q of each tile (f16 pairs)
+constexpr int kOCol = 0, kSCol = kQTiles * kD, kQCol = kSCol + kQTiles * kChunk, kTmemCols = 512;
+static_assert(kQCol + kQTiles * kD / 2 <= kTmemCols, "TMEM budget");
 constexpr float kLazyLog2 = 8.f;
 constexpr float kLog2e = 1.4426950408889634f;
 
@@ -60,10 +68,10 @@ enum {
   B_EMPTY = B_VFULL + kTileStages,     // MMA commit after P.V -> converters: tile stage free
   B_RFULL = B_EMPTY + kTileStages,     // producer expect_tx + bulk copies -> converters: raw stage staged
   B_REMPTY = B_RFULL + kRawStages,     // converters -> producer: raw stage read
-  B_SFULL = B_REMPTY + kRawStages,     // MMA commit -> softmax: S ready
-  B_PFULL = B_SFULL + kSBuf,           // softmax -> MMA: P written
-  B_PVDONE = B_PFULL + kSBuf,          // MMA commit -> softmax / MMA: P.V retired
-  B_DONE = B_PVDONE + kSBuf,           // MMA commit: every MMA retired
+  B_SFULL = B_REMPTY + kRawStages,     // MMA commit -> softmax of a tile: S ready
+  B_PFULL = B_SFULL + kQTiles,         // softmax of a tile -> MMA: P written
+  B_PVDONE = B_PFULL + kQTiles,        // MMA commit -> softmax / MMA: a tile's P.V retired
+  B_DONE = B_PVDONE + kQTiles,         // MMA commit: every MMA retired
   B_QREADY,                            // softmax warps -> MMA: Q rows stored in TMEM
   B_COUNT
 };
@@ -241,13 +249,13 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const PrefillPa
       mbar_init(bar(B_RFULL + i), 1);
       mbar_init(bar(B_REMPTY + i), 128);
     }
-    for (int k = 0; k < kSBuf; ++k) {
+    for (int k = 0; k < kQTiles; ++k) {
       mbar_init(bar(B_SFULL + k), 1);
       mbar_init(bar(B_PFULL + k), 128);
       mbar_init(bar(B_PVDONE + k), 1);
     }
     mbar_init(bar(B_DONE), 1);
-    mbar_init(bar(B_QREADY), 128);
+    mbar_init(bar(B_QREADY), 32 * kSoftWarps);
     *s_qmax = -1;
     *s_qmin = 0x7FFFFFFF;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -264,14 +272,16 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const PrefillPa
   tc_fence_after();
   const uint32_t tmem = *s_tmem;
 
-  // ---- this thread's query row (softmax warps): position, and Q into TMEM
-  const int R = tile * kRows + tid;
+  // ---- this thread's query row (softmax warps): position, and Q into TMEM.  Query tile qt = warp / 4
+  // of the CTA owns TMEM lane (warp % 4) * 32 + lane of its own O, S and Q columns.
+  const int R = tile * (kQTiles * kRows) + tid;
   const int qm = R / p.G, qg = R % p.G;
-  const bool row_ok = warp < 4 && qm < p.M;
+  const bool row_ok = warp < kSoftWarps && qm < p.M;
   const int hq = h * p.G + qg;
+  const int qt = warp >> 2;
   const uint32_t lane_addr = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
   int qpos = -1;
-  if (warp < 4) {
+  if (warp < kSoftWarps) {
     if (row_ok) {
       qpos = p.qpos ? p.qpos[static_cast<int64_t>(b) * p.qp_sb + qm] : qm;
       if (p.causal) {
@@ -299,7 +309,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const PrefillPa
         }
         v[4 * c] = x.x; v[4 * c + 1] = x.y; v[4 * c + 2] = x.z; v[4 * c + 3] = x.w;
       }
-      tmem_st32(lane_addr + kQCol + half * 32, v);
+      tmem_st32(lane_addr + kQCol + qt * (kD / 2) + half * 32, v);
     }
     tmem_wait_st();
     tc_fence_before();
@@ -543,57 +553,59 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const PrefillPa
     if (lane == 0) {
       constexpr uint32_t kIdS = idesc_f16(kRows, kChunk, 0, 0);  // S = Q . K^T
       constexpr uint32_t kIdPV = idesc_f16(kRows, kD, 0, 1);     // O += P . V (V read MN-major)
-      auto issue_s = [&](int j) -> bool {
-        const int k = j & 1, st = j % kTileStages;
-        if (j >= kSBuf && !mbar_wait(bar(B_PVDONE + k), ((j >> 1) - 1) & 1)) return false;
-        if (!mbar_wait(bar(B_KFULL + st), (j / kTileStages) & 1)) return false;
+      // per chunk: S of both tiles, then P.V of both (a tile's S buffer is reused once its
+      // previous P.V has retired; the other tile's MMAs keep the pipe busy meanwhile)
+      auto issue_s = [&](int j, int t2) -> bool {
+        const int st = j % kTileStages;
+        if (j >= 1 && !mbar_wait(bar(B_PVDONE + t2), (j - 1) & 1)) return false;
         tc_fence_after();
-        const uint32_t d = tmem + kSCol + k * kChunk;
+        const uint32_t d = tmem + kSCol + t2 * kChunk;
 #pragma unroll
         for (int kb = 0; kb < 2; ++kb) {
           const uint64_t bd = sw128_desc(sbase + tile_off(st, 0) + kb * kKb, 16, 1024);
 #pragma unroll
           for (int t = 0; t < 4; ++t)
-            mma_ts(d, tmem + kQCol + kb * 32 + t * 8, bd + (t * 2), kIdS, (kb | t) ? 1u : 0u);
+            mma_ts(d, tmem + kQCol + t2 * (kD / 2) + kb * 32 + t * 8, bd + (t * 2), kIdS, (kb | t) ? 1u : 0u);
         }
-        mma_commit(bar(B_SFULL + k));
+        mma_commit(bar(B_SFULL + t2));
         return true;
       };
-      auto issue_pv = [&](int j) -> bool {
-        const int k = j & 1, st = j % kTileStages;
-        if (!mbar_wait(bar(B_PFULL + k), (j >> 1) & 1)) return false;
-        if (!mbar_wait(bar(B_VFULL + st), (j / kTileStages) & 1)) return false;
+      auto issue_pv = [&](int j, int t2) -> bool {
+        const int st = j % kTileStages;
+        if (!mbar_wait(bar(B_PFULL + t2), j & 1)) return false;
         tc_fence_after();
         const uint64_t bd = sw128_desc(sbase + tile_off(st, 1), kKb, 1024);
 #pragma unroll
         for (int t = 0; t < kChunk / 16; ++t)
-          mma_ts(tmem + kOCol, tmem + kSCol + k * kChunk + t * 8, bd + ((t * 2048) >> 4), kIdPV,
+          mma_ts(tmem + kOCol + t2 * kD, tmem + kSCol + t2 * kChunk + t * 8, bd + ((t * 2048) >> 4), kIdPV,
                  (j > 0 || t > 0) ? 1u : 0u);
-        mma_commit(bar(B_PVDONE + k));
-        mma_commit(bar(B_EMPTY + st));
+        mma_commit(bar(B_PVDONE + t2));
         return true;
       };
       if (!mbar_wait(bar(B_QREADY), 0)) timed_out = true;
       tc_fence_after();
-      if (!timed_out && T > 0 && !issue_s(0)) timed_out = true;
       for (int j = 0; j < T && !timed_out; ++j) {
-        if (j + 1 < T && !issue_s(j + 1)) { timed_out = true; break; }
-        if (!issue_pv(j)) { timed_out = true; break; }
+        const int st = j % kTileStages;
+        if (!mbar_wait(bar(B_KFULL + st), (j / kTileStages) & 1)) { timed_out = true; break; }
+        if (!issue_s(j, 0) || !issue_s(j, 1)) { timed_out = true; break; }
+        if (!mbar_wait(bar(B_VFULL + st), (j / kTileStages) & 1)) { timed_out = true; break; }
+        if (!issue_pv(j, 0) || !issue_pv(j, 1)) { timed_out = true; break; }
+        mma_commit(bar(B_EMPTY + st));
       }
       mma_commit(bar(B_DONE));
       if (!mbar_wait(bar(B_DONE), 0)) timed_out = true;
     }
-  } else if (warp < 4) {
+  } else if (warp < kSoftWarps) {
     // ---------------------------------------------------------------- softmax (one query row per thread)
     const float scale = p.sm_scale * kLog2e;
     float m_used = -INFINITY, l = 0.f;
+    const uint32_t s_col = kSCol + qt * kChunk, o_col = kOCol + qt * kD;
     for (int j = 0; j < T && !timed_out; ++j) {
-      const int k = j & 1;
       bool ok = true;
       const int st = j % kTileStages;
       // S ready; the K tile barrier (already complete) orders the converters' factor writes
       if (lane == 0)
-        ok = mbar_wait_sleep(bar(B_SFULL + k), (j >> 1) & 1) && mbar_wait(bar(B_KFULL + st), (j / kTileStages) & 1);
+        ok = mbar_wait_sleep(bar(B_SFULL + qt), j & 1) && mbar_wait(bar(B_KFULL + st), (j / kTileStages) & 1);
       if (!__shfl_sync(0xffffffffu, ok, 0)) { timed_out = true; break; }
       tc_fence_after();
       // a chunk is handled in two halves of 32 columns (S is read from TMEM twice) to keep the
@@ -621,7 +633,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const PrefillPa
 #pragma unroll 1
       for (int hh = 0; hh < 2; ++hh) {
         uint32_t sr[32];
-        tmem_ld32(lane_addr + kSCol + k * kChunk + hh * 32, sr);
+        tmem_ld32(lane_addr + s_col + hh * 32, sr);
         uint64_t vis[kSPH];
         float kf[kSPH], vf[kSPH];
         half_slots(hh, vis, kf, vf);
@@ -642,7 +654,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const PrefillPa
         const bool need = tmax > m_used + kLazyLog2;
         if (__any_sync(0xffffffffu, need)) {
           // rescale O in TMEM: every earlier P.V must have landed
-          if (!__all_sync(0xffffffffu, mbar_wait_sleep(bar(B_PVDONE + ((j - 1) & 1)), ((j - 1) >> 1) & 1))) {
+          if (!__all_sync(0xffffffffu, mbar_wait_sleep(bar(B_PVDONE + qt), (j - 1) & 1))) {
             timed_out = true;
             break;
           }
@@ -655,11 +667,11 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const PrefillPa
 #pragma unroll 1
           for (int c = 0; c < kD / 32; ++c) {
             uint32_t o[32];
-            tmem_ld32(lane_addr + kOCol + c * 32, o);
+            tmem_ld32(lane_addr + o_col + c * 32, o);
             tmem_wait_ld();
 #pragma unroll
             for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * f);
-            tmem_st32(lane_addr + kOCol + c * 32, o);
+            tmem_st32(lane_addr + o_col + c * 32, o);
           }
           tmem_wait_st();
         }
@@ -671,7 +683,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const PrefillPa
 #pragma unroll 1
       for (int hh = 0; hh < 2; ++hh) {
         uint32_t sr[32];
-        tmem_ld32(lane_addr + kSCol + k * kChunk + hh * 32, sr);
+        tmem_ld32(lane_addr + s_col + hh * 32, sr);
         uint64_t vis[kSPH];
         float kf[kSPH], vf[kSPH];
         half_slots(hh, vis, kf, vf);
@@ -686,17 +698,17 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const PrefillPa
           lsum += p0 + p1;
           pk[i] = pack_h2(p0 * vf[q], p1 * vf[q]);
         }
-        tmem_st16(lane_addr + kSCol + k * kChunk + hh * 16, pk);
+        tmem_st16(lane_addr + s_col + hh * 16, pk);
       }
       l += lsum;
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(bar(B_PFULL + k));
+      mbar_arrive(bar(B_PFULL + qt));
     }
     // ---------------------------------------------------------------- epilogue
     bool have = T > 0 && !timed_out;
     if (have) {
-      if (!__all_sync(0xffffffffu, mbar_wait(bar(B_PVDONE + ((T - 1) & 1)), ((T - 1) >> 1) & 1))) {
+      if (!__all_sync(0xffffffffu, mbar_wait(bar(B_PVDONE + qt), (T - 1) & 1))) {
         timed_out = true;
         have = false;
       }
@@ -709,7 +721,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const PrefillPa
     for (int c = 0; c < kD / 32; ++c) {
       uint32_t o[32];
       if (have) {
-        tmem_ld32(lane_addr + kOCol + c * 32, o);
+        tmem_ld32(lane_addr + o_col + c * 32, o);
         tmem_wait_ld();
       } else {
 #pragma unroll
@@ -759,7 +771,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const PrefillPa
 
 template <int PS>
 int launch_ps(const PrefillParams& p, cudaStream_t s) {
-  const int64_t tiles = (static_cast<int64_t>(p.G) * p.M + kRows - 1) / kRows;
+  const int64_t tiles = (static_cast<int64_t>(p.G) * p.M + kQTiles * kRows - 1) / (kQTiles * kRows);
   const int64_t items = static_cast<int64_t>(p.B) * p.Ht * tiles;
   if (items > 0x7FFFFFFF) return fail(IAK_ERR_UNSUPPORTED, "too many prefill work items");
   const size_t smem = Smem::total + 1024;
