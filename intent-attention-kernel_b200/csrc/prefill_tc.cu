@@ -12,8 +12,8 @@
 //     whole; then, per chunk, it stages the pages' scales in shared memory and
 //     bulk-copies their raw K and V bytes (cp.async.bulk, mbarrier transaction
 //     counts) into a 3-stage ring, running ahead of the converters;
-//   * a converter warpgroup (one 32-channel row segment per thread, unit and
-//     plane) widens the staged rows to f16 tiles, 128-byte swizzled, rows the
+//   * two converter warpgroups (one 32-channel row segment per thread and
+//     plane) widen the staged rows to f16 tiles, 128-byte swizzled, rows the
 //     slot mask does not select written as zero, over a 3-stage ring: F16 rows
 //     are copied, page-scaled FP8 / INT8 / INT4 codes are widened exactly (the
 //     page scale goes to the softmax), group / channel scales and
@@ -50,8 +50,8 @@ constexpr int kD = 128, kRows = 128, kChunk = 64;
 constexpr int kQTiles = 2;                    // 128-row query tiles per CTA, sharing every converted K/V chunk
 constexpr int kTileStages = 3, kRawStages = 3;
 constexpr int kMaxSlots = 1024;
-constexpr int kThreads = 448;                 // 2 softmax wgs | converter wg | producer warp | MMA warp
-constexpr int kSoftWarps = 4 * kQTiles, kConvWarp0 = 8, kProdWarp = 12, kMmaWarp = 13;
+constexpr int kThreads = 576;                 // 2 softmax wgs | 2 converter wgs | producer warp | MMA warp
+constexpr int kSoftWarps = 4 * kQTiles, kConvWarp0 = 8, kConvThreads = 256, kProdWarp = 16, kMmaWarp = 17;
 constexpr int kKb = kChunk * 128;             // 64 token rows x 64 channels of f16 (one swizzle-atom column)
 constexpr int kTile = 2 * kKb;                // 64 tokens x 128 channels
 constexpr int kRawPlane = kChunk * kD * 2;    // staged bytes of one plane of a chunk (room for f16 rows)
@@ -241,13 +241,13 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const PrefillPa
 
   if (tid == 0) {
     for (int i = 0; i < kTileStages; ++i) {
-      mbar_init(bar(B_KFULL + i), 128);
-      mbar_init(bar(B_VFULL + i), 128);
+      mbar_init(bar(B_KFULL + i), kConvThreads);
+      mbar_init(bar(B_VFULL + i), kConvThreads);
       mbar_init(bar(B_EMPTY + i), 1);
     }
     for (int i = 0; i < kRawStages; ++i) {
       mbar_init(bar(B_RFULL + i), 1);
-      mbar_init(bar(B_REMPTY + i), 128);
+      mbar_init(bar(B_REMPTY + i), kConvThreads);
     }
     for (int k = 0; k < kQTiles; ++k) {
       mbar_init(bar(B_SFULL + k), 1);
@@ -482,11 +482,10 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const PrefillPa
         const uint32_t toff = tile_off(st, plane);
         const float* scale_rows = plane ? p.v.scale : p.k.scale;
         const float* rscale_rows = plane ? p.v.res_scale : p.k.res_scale;
-#pragma unroll 1
-        for (int i = 0; i < 2; ++i) {
-          // unit i of this thread: (token row, 32-channel group); a warp covers 8 rows of one slot,
+        {
+          // this thread's unit: (token row, 32-channel group); a warp covers 8 rows of one slot,
           // so the format is warp-uniform
-          const int u = ct + 128 * i;
+          const int u = ct;
           const int trow = u >> 2, g = u & 3, slot = trow / PS, r = trow % PS;
           const int si = j * kSlotsPerChunk + slot;
           const bool live = si < n_valid && ((s_mask[si] >> r) & 1ull);
