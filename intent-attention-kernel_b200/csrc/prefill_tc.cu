@@ -583,12 +583,22 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const PrefillPa
       };
       if (!mbar_wait(bar(B_QREADY), 0)) timed_out = true;
       tc_fence_after();
+      // staggered: P.V of tile 0 and its next S, then the same for tile 1, so one tile's softmax
+      // overlaps the other tile's MMAs
+      if (!timed_out && T > 0) {
+        if (!mbar_wait(bar(B_KFULL + 0), 0) || !issue_s(0, 0) || !issue_s(0, 1)) timed_out = true;
+      }
       for (int j = 0; j < T && !timed_out; ++j) {
-        const int st = j % kTileStages;
-        if (!mbar_wait(bar(B_KFULL + st), (j / kTileStages) & 1)) { timed_out = true; break; }
-        if (!issue_s(j, 0) || !issue_s(j, 1)) { timed_out = true; break; }
+        const int st = j % kTileStages, st1 = (j + 1) % kTileStages;
         if (!mbar_wait(bar(B_VFULL + st), (j / kTileStages) & 1)) { timed_out = true; break; }
-        if (!issue_pv(j, 0) || !issue_pv(j, 1)) { timed_out = true; break; }
+        const bool more = j + 1 < T;
+        if (more && !mbar_wait(bar(B_KFULL + st1), ((j + 1) / kTileStages) & 1)) { timed_out = true; break; }
+        bool ok = true;
+#pragma unroll 1
+        for (int t2 = 0; t2 < kQTiles && ok; ++t2) {
+          ok = issue_pv(j, t2) && (!more || issue_s(j + 1, t2));
+        }
+        if (!ok) { timed_out = true; break; }
         mma_commit(bar(B_EMPTY + st));
       }
       mma_commit(bar(B_DONE));
@@ -637,13 +647,23 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const PrefillPa
         float kf[kSPH], vf[kSPH];
         half_slots(hh, vis, kf, vf);
         tmem_wait_ld();
+        if (cfull) {                            // every column visible: no per-column test
 #pragma unroll
-        for (int q = 0; q < kSPH; ++q) {
-          float m = -INFINITY;
+          for (int q = 0; q < kSPH; ++q) {
+            float m = -INFINITY;
 #pragma unroll
-          for (int r = 0; r < (PS <= 32 ? PS : 32); ++r)
-            if ((vis[q] >> r) & 1ull) m = fmaxf(m, __uint_as_float(sr[q * PS + r]));
-          tmax_raw = fmaxf(tmax_raw, m * kf[q]);
+            for (int r = 0; r < (PS <= 32 ? PS : 32); ++r) m = fmaxf(m, __uint_as_float(sr[q * PS + r]));
+            tmax_raw = fmaxf(tmax_raw, m * kf[q]);
+          }
+        } else {
+#pragma unroll
+          for (int q = 0; q < kSPH; ++q) {
+            float m = -INFINITY;
+#pragma unroll
+            for (int r = 0; r < (PS <= 32 ? PS : 32); ++r)
+              if ((vis[q] >> r) & 1ull) m = fmaxf(m, __uint_as_float(sr[q * PS + r]));
+            tmax_raw = fmaxf(tmax_raw, m * kf[q]);
+          }
         }
       }
       const float tmax = tmax_raw == -INFINITY ? -INFINITY : tmax_raw * scale;
@@ -688,14 +708,26 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const PrefillPa
         half_slots(hh, vis, kf, vf);
         tmem_wait_ld();
         uint32_t pk[16];
+        if (cfull) {                            // m_used is finite once a chunk is seen whole
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int q = PS <= 32 ? (2 * i) / PS : 0, r = PS <= 32 ? (2 * i) % PS : 2 * i;
-          const float a = scale * kf[q];
-          const float p0 = ((vis[q] >> r) & 1ull) ? ex2(fmaf(__uint_as_float(sr[2 * i]), a, neg_m)) : 0.f;
-          const float p1 = ((vis[q] >> (r + 1)) & 1ull) ? ex2(fmaf(__uint_as_float(sr[2 * i + 1]), a, neg_m)) : 0.f;
-          lsum += p0 + p1;
-          pk[i] = pack_h2(p0 * vf[q], p1 * vf[q]);
+          for (int i = 0; i < 16; ++i) {
+            const int q = PS <= 32 ? (2 * i) / PS : 0;
+            const float a = scale * kf[q];
+            const float p0 = ex2(fmaf(__uint_as_float(sr[2 * i]), a, neg_m));
+            const float p1 = ex2(fmaf(__uint_as_float(sr[2 * i + 1]), a, neg_m));
+            lsum += p0 + p1;
+            pk[i] = pack_h2(p0 * vf[q], p1 * vf[q]);
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int q = PS <= 32 ? (2 * i) / PS : 0, r = PS <= 32 ? (2 * i) % PS : 2 * i;
+            const float a = scale * kf[q];
+            const float p0 = ((vis[q] >> r) & 1ull) ? ex2(fmaf(__uint_as_float(sr[2 * i]), a, neg_m)) : 0.f;
+            const float p1 = ((vis[q] >> (r + 1)) & 1ull) ? ex2(fmaf(__uint_as_float(sr[2 * i + 1]), a, neg_m)) : 0.f;
+            lsum += p0 + p1;
+            pk[i] = pack_h2(p0 * vf[q], p1 * vf[q]);
+          }
         }
         tmem_st16(lane_addr + s_col + hh * 16, pk);
       }
