@@ -141,7 +141,7 @@ extern "C" int iak_prefill(const iak_page_pools* pools, const iak_prefill_args* 
   const bool tc_ok = prefill_tc_eligible(p);
   if (a->kernel == IAK_KERNEL_TENSOR && !tc_ok)
     return fail(IAK_ERR_UNSUPPORTED, "the tensor-core prefill needs head_dim 128, page_size in {8,16,32,64}, "
-                                     "table_width <= 4096 and f16 / bf16 / f32 queries");
+                                     "table_width <= 1024, 16-byte aligned pools and a positive sm_scale");
   if (a->kernel != IAK_KERNEL_GENERIC && tc_ok) return launch_prefill_tc(p, s);
   const dim3 grid(static_cast<unsigned>((p.M + kGenericWarps - 1) / kGenericWarps), static_cast<unsigned>(p.Hq),
                   static_cast<unsigned>(p.B));

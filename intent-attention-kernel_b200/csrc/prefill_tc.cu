@@ -33,6 +33,7 @@
 //
 // Reference semantics: reference.py:82-130 semantic_block_attention with the
 // causal mask on original token positions of reference.py:16-45.
+#include <cmath>
 #include <mutex>
 
 #include "prefill_internal.cuh"
@@ -379,7 +380,8 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const PrefillPa
   if (warp == kProdWarp) {
     // ---------------------------------------------------------------- producer: scales + bulk copies
     const int mode = p.k.mode, ns = p.k.ns;
-    const int ngrp = mode == IAK_SCALE_GROUP32 ? 4 : 1;   // channel-mode scales are read by the converters
+    const int lg = mode == IAK_SCALE_GROUP32 ? 2 : 0;     // log2 of the groups per row (channel-mode scales
+    const int ngrp = 1 << lg;                              // are read by the converters)
     // (slot, kind, group) items of a chunk's page / group scales: at most 8 x 4 x 4 = 128, 4 per lane
     constexpr int kScaleItemsPerLane = 4;
     const int n_items = mode == IAK_SCALE_CHANNEL ? 0 : kSlotsPerChunk * 4 * ngrp;
@@ -393,7 +395,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const PrefillPa
         const int it = lane + 32 * q;
         sv[q] = 0.f;
         if (it < n_items) {
-          const int sl = it / (4 * ngrp), kind = (it / ngrp) % 4, g = it % ngrp;
+          const int sl = it >> (2 + lg), kind = (it >> lg) & 3, g = it & (ngrp - 1);
           const int si = j * kSlotsPerChunk + sl;
           if (si < n_valid) {
             const int fmt = s_fmt[si];
@@ -410,46 +412,49 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const PrefillPa
       for (int q = 0; q < kScaleItemsPerLane; ++q) {
         const int it = lane + 32 * q;
         if (it < n_items) {
-          const int sl = it / (4 * ngrp), kind = (it / ngrp) % 4, g = it % ngrp;
+          const int sl = it >> (2 + lg), kind = (it >> lg) & 3, g = it & (ngrp - 1);
           *scale_at(rs, sl, kind, g) = sv[q];
         }
       }
       __syncwarp();
-      if (lane == 0) {
-        uint32_t total = 0;
-        for (int sl = 0; sl < kSlotsPerChunk; ++sl) {
-          const int si = j * kSlotsPerChunk + sl;
-          if (si < n_valid) total += 2 * staged_plane_bytes(s_fmt[si], PS);
-        }
-        mbar_arrive_expect_tx(bar(B_RFULL + rs), total);
-        for (int sl = 0; sl < kSlotsPerChunk; ++sl) {
-          const int si = j * kSlotsPerChunk + sl;
-          if (si >= n_valid) break;
-          const int fmt = s_fmt[si];
-          const int64_t pid = s_pid[si];
-          for (int plane = 0; plane < 2; ++plane) {
-            // pool base of this page's format and plane (selected pointer by pointer: a reference to
-            // one of the two by-value parameter structs would be copied to local memory)
-            const uint8_t* src;
-            uint32_t bytes;
-            if (fmt == IAK_FMT_F16) {
-              src = reinterpret_cast<const uint8_t*>(plane ? p.v.f16 : p.k.f16) + pid * PS * kD * 2;
-              bytes = PS * 256;
-            } else if (fmt == IAK_FMT_FP8) {
-              src = (plane ? p.v.fp8 : p.k.fp8) + pid * PS * kD;
-              bytes = PS * 128;
-            } else if (fmt == IAK_FMT_INT8) {
-              src = reinterpret_cast<const uint8_t*>(plane ? p.v.i8 : p.k.i8) + pid * PS * kD;
-              bytes = PS * 128;
-            } else {
-              src = (plane ? p.v.i4 : p.k.i4) + pid * PS * (kD / 2);
-              bytes = PS * 64;
-            }
-            const uint32_t dst = sbase + raw_off(rs, plane, sl);
-            bulk_load(dst, src, bytes, bar(B_RFULL + rs));
-            if (fmt == IAK_FMT_INT4R)
-              bulk_load(dst + PS * 64, (plane ? p.v.i4r : p.k.i4r) + pid * PS * (kD / 2), PS * 64, bar(B_RFULL + rs));
+      // one lane per (slot, plane) of the chunk: lane 0 posts the byte count, then every lane
+      // issues its page's bulk copy (and the residual rows of an INT4_RESIDUAL page); issued
+      // from one lane, the copies of a chunk took most of the producer's time
+      {
+        const int sl = lane >> 1, plane = lane & 1;
+        const int si = j * kSlotsPerChunk + sl;
+        const bool mine = sl < kSlotsPerChunk && si < n_valid;
+        int fmt = 0;
+        int64_t pid = 0;
+        uint32_t bytes = 0;
+        const uint8_t* src = nullptr;
+        if (mine) {
+          fmt = s_fmt[si];
+          pid = s_pid[si];
+          // pool base of this page's format and plane (selected pointer by pointer: a reference
+          // to one of the two by-value parameter structs would be copied to local memory)
+          if (fmt == IAK_FMT_F16) {
+            src = reinterpret_cast<const uint8_t*>(plane ? p.v.f16 : p.k.f16) + pid * PS * kD * 2;
+            bytes = PS * 256;
+          } else if (fmt == IAK_FMT_FP8) {
+            src = (plane ? p.v.fp8 : p.k.fp8) + pid * PS * kD;
+            bytes = PS * 128;
+          } else if (fmt == IAK_FMT_INT8) {
+            src = reinterpret_cast<const uint8_t*>(plane ? p.v.i8 : p.k.i8) + pid * PS * kD;
+            bytes = PS * 128;
+          } else {
+            src = (plane ? p.v.i4 : p.k.i4) + pid * PS * (kD / 2);
+            bytes = PS * 64;
           }
+        }
+        const uint32_t total = __reduce_add_sync(0xffffffffu, mine ? staged_plane_bytes(fmt, PS) : 0u);
+        if (lane == 0) mbar_arrive_expect_tx(bar(B_RFULL + rs), total);
+        __syncwarp();
+        if (mine) {
+          const uint32_t dst = sbase + raw_off(rs, plane, sl);
+          bulk_load(dst, src, bytes, bar(B_RFULL + rs));
+          if (fmt == IAK_FMT_INT4R)
+            bulk_load(dst + PS * 64, (plane ? p.v.i4r : p.k.i4r) + pid * PS * (kD / 2), PS * 64, bar(B_RFULL + rs));
         }
       }
       __syncwarp();
@@ -836,6 +841,8 @@ bool prefill_tc_eligible(const PrefillParams& p) {
   const int PS = p.k.PS;
   if (PS != 8 && PS != 16 && PS != 32 && PS != 64) return false;
   if (p.W > kMaxSlots) return false;
+  // the softmax takes each slot's max score times a positive factor and scale
+  if (!(p.sm_scale > 0.f) || !std::isfinite(p.sm_scale)) return false;
   for (const qpage::PlanePools* pl : {&p.k, &p.v})
     if (!aligned16(pl->f16) || !aligned16(pl->fp8) || !aligned16(pl->i8) || !aligned16(pl->i4) || !aligned16(pl->i4r))
       return false;
