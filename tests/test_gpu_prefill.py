@@ -163,3 +163,22 @@ def test_reference_golden_through_pages(golden, i):
     ref = np.nan_to_num(golden("prefill_golden.npz")[name], nan=0.0)
     # K / V pass through f16 pages: 2e-3 covers the rounding
     np.testing.assert_allclose(got.float().cpu().numpy(), ref, atol=ATOL, rtol=RTOL)
+
+
+def test_non_positive_scale_runs_on_the_cuda_core_kernel():
+    """The tensor-core softmax takes each slot's max score times a positive scale:
+    kernel="tensor" refuses another scale, "auto" runs the CUDA-core kernel."""
+    from intent_attention.paged import paged_prefill
+    c = _case(71, M=40)
+    rm = torch.from_numpy(c["masks"].view(np.int64)).cuda()
+    args = (c["q"], c["pool"], torch.from_numpy(c["table"]).cuda(), torch.from_numpy(c["counts"]).cuda(),
+            torch.from_numpy(c["tags"]).cuda(), tag_map_for(c["formats"]))
+    kw = dict(q_positions=torch.from_numpy(c["qpos"]).cuda(), causal=True, bases=torch.from_numpy(c["bases"]).cuda(),
+              row_masks=rm, sm_scale=-0.05)
+    with pytest.raises(Exception):
+        paged_prefill(*args, kernel="tensor", **kw)
+    got = paged_prefill(*args, kernel="auto", **kw)
+    pools, sc = oracle_pools(c["pool"])
+    ref = op.paged_prefill(c["np_q"], c["table"], c["counts"], c["tags"], ORACLE_FMT, pools, sc, c["scale_mode"],
+                           bases=c["bases"], row_masks=c["masks"], q_positions=c["qpos"], causal=True, sm_scale=-0.05)
+    _close(got, ref)
