@@ -500,19 +500,22 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const PrefillPa
             // 16-byte chunk c (0..15) of the tile row, 128-byte swizzled
             *reinterpret_cast<uint4*>(sm + toff + (c >> 3) * kKb + swz(trow, c & 7)) = make_uint4(x0, x1, x2, x3);
           };
-          // Staged rows are 256 (F16) or 128 (8-bit) bytes apart, so a warp's eight rows share banks:
-          // each row reads its chunks in an order rotated by the row index, which spreads one load
-          // instruction of the warp over distinct banks.  All loads precede the stores.
+          // Staged rows are 256 (F16) or 128 (8-bit) bytes apart, so a warp's eight rows share banks.
+          // A 16-byte access of the warp runs in phases of 8 lanes (two rows x four groups): each
+          // thread visits its chunks in an order (chunk k ^ (g >> 1) ^ 2 (r & 1) for F16, pair
+          // (r & 1) ^ (g >> 1) first for 8-bit rows) under which the 8 lanes of a phase hit 8
+          // distinct bank groups both in the staged rows and in the 128-byte-swizzled tile.  All
+          // loads precede the stores.
           if (f == IAK_FMT_F16 || f == IAK_FMT_SKIP) {
             uint4 v[4];
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
-              const int kk = (k + r) & 3;
+              const int kk = k ^ (g >> 1) ^ ((r & 1) << 1);
               v[k] = f == IAK_FMT_F16 ? *reinterpret_cast<const uint4*>(rawp + r * 256 + g * 64 + kk * 16)
                                       : make_uint4(0u, 0u, 0u, 0u);
             }
 #pragma unroll
-            for (int k = 0; k < 4; ++k) put(g * 4 + ((k + r) & 3), v[k].x, v[k].y, v[k].z, v[k].w);
+            for (int k = 0; k < 4; ++k) put(g * 4 + (k ^ (g >> 1) ^ ((r & 1) << 1)), v[k].x, v[k].y, v[k].z, v[k].w);
           } else {
             const int64_t pid = s_pid[si];
             const bool ch = mode == IAK_SCALE_CHANNEL;
@@ -521,7 +524,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const PrefillPa
               const bool fold = mode == IAK_SCALE_PAGE;
               const float s_all = (fold || ch) ? 0.f : *scale_at(rs, slot, plane, grp);
               const float* chs = ch ? scale_rows + pid * ns : nullptr;
-              const int k0 = r & 1;
+              const int k0 = (r & 1) ^ (g >> 1);
               const uint4 w0 = *reinterpret_cast<const uint4*>(rawp + r * 128 + g * 32 + k0 * 16);
               const uint4 w1 = *reinterpret_cast<const uint4*>(rawp + r * 128 + g * 32 + (k0 ^ 1) * 16);
               uint32_t h0[8], h1[8];
