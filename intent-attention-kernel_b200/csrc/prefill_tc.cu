@@ -108,6 +108,37 @@ __device__ __forceinline__ float ex2(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
+// max of three (one instruction)
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+// packed pairs of fp32 (one instruction each, round to nearest)
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n .reg .b64 ra, rb, rc, rd;\n mov.b64 ra, {%2, %3};\n mov.b64 rb, {%4, %5};\n mov.b64 rc, {%6, %7};\n"
+      " fma.rn.f32x2 rd, ra, rb, rc;\n mov.b64 {%0, %1}, rd;\n}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n .reg .b64 ra, rb, rd;\n mov.b64 ra, {%2, %3};\n mov.b64 rb, {%4, %5};\n add.rn.f32x2 rd, ra, rb;\n"
+      " mov.b64 {%0, %1}, rd;\n}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+__device__ __forceinline__ float2 fmul2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n .reg .b64 ra, rb, rd;\n mov.b64 ra, {%2, %3};\n mov.b64 rb, {%4, %5};\n mul.rn.f32x2 rd, ra, rb;\n"
+      " mov.b64 {%0, %1}, rd;\n}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
 
 // Bytes of one plane of one page of format fmt as staged (row r of a slot's
 // region at r * row_bytes; INT4_RESIDUAL's residual rows follow the base rows).
@@ -625,121 +656,108 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const PrefillPa
         ok = mbar_wait_sleep(bar(B_SFULL + qt), j & 1) && mbar_wait(bar(B_KFULL + st), (j / kTileStages) & 1);
       if (!__shfl_sync(0xffffffffu, ok, 0)) { timed_out = true; break; }
       tc_fence_after();
-      // a chunk is handled in two halves of 32 columns (S is read from TMEM twice) to keep the
-      // unrolled code small; the visibility bits, score and value factors of the half's slots
-      // come from shared memory
-      const bool cfull = s_cfull[j] != 0;
-      constexpr int kSPH = PS <= 32 ? 32 / PS : 1;    // slots per half chunk
-      auto half_slots = [&](int hh, uint64_t (&vis)[kSPH], float (&kf)[kSPH], float (&vf)[kSPH]) {
+      // the chunk's S in one read; masked columns become -inf
+      uint32_t r0[32], r1[32];
+      tmem_ld32(lane_addr + s_col, r0);
+      tmem_ld32(lane_addr + s_col + 32, r1);
+      tmem_wait_ld();
+      // score factor of a slot (clamped above 0 so that -inf scores stay -inf) and value factor
+      auto factors = [&](int sl) -> float2 {
+        const float2 f = *reinterpret_cast<const float2*>(s_fac + (st * 8 + sl) * 2);
+        return make_float2(fmaxf(f.x, 1e-30f), f.y);
+      };
+      if (s_cfull[j] == 0) {
+        // columns this row does not see (row masks, causal positions, padding slots)
+        uint64_t vis = 0;
 #pragma unroll
-        for (int q = 0; q < kSPH; ++q) {
-          const int sl = PS <= 32 ? hh * kSPH + q : 0;
-          const int si = j * kSlotsPerChunk + sl;
-          vis[q] = cfull ? ~0ull : 0ull;
-          if (!cfull && si < n_valid) {
+        for (int q = 0; q < kSlotsPerChunk; ++q) {
+          const int si = j * kSlotsPerChunk + q;
+          if (si < n_valid) {
             const int64_t lim = p.causal ? static_cast<int64_t>(qpos) - s_pos0[si] : PS - 1;   // last visible row
             const uint64_t upto = lim < 0 ? 0ull : (lim >= PS - 1 ? ~0ull : ((2ull << lim) - 1ull));
-            vis[q] = s_mask[si] & upto;
+            uint64_t v = s_mask[si] & upto;
+            if (PS < 64) v = (v & ((1ull << (PS & 63)) - 1ull)) << (q * PS);
+            vis |= v;
           }
-          if (PS == 64) vis[q] >>= hh * 32;    // this half's 32 rows of the one slot
-          kf[q] = s_fac[(st * 8 + sl) * 2];
-          vf[q] = s_fac[(st * 8 + sl) * 2 + 1];
         }
-      };
-      float tmax_raw = -INFINITY;               // max over visible columns of score x factor (factors > 0)
-#pragma unroll 1
-      for (int hh = 0; hh < 2; ++hh) {
-        uint32_t sr[32];
-        tmem_ld32(lane_addr + s_col + hh * 32, sr);
-        uint64_t vis[kSPH];
-        float kf[kSPH], vf[kSPH];
-        half_slots(hh, vis, kf, vf);
-        tmem_wait_ld();
-        if (cfull) {                            // every column visible: no per-column test
+        const uint32_t vlo = static_cast<uint32_t>(vis), vhi = static_cast<uint32_t>(vis >> 32);
 #pragma unroll
-          for (int q = 0; q < kSPH; ++q) {
-            float m = -INFINITY;
-#pragma unroll
-            for (int r = 0; r < (PS <= 32 ? PS : 32); ++r) m = fmaxf(m, __uint_as_float(sr[q * PS + r]));
-            tmax_raw = fmaxf(tmax_raw, m * kf[q]);
-          }
-        } else {
-#pragma unroll
-          for (int q = 0; q < kSPH; ++q) {
-            float m = -INFINITY;
-#pragma unroll
-            for (int r = 0; r < (PS <= 32 ? PS : 32); ++r)
-              if ((vis[q] >> r) & 1ull) m = fmaxf(m, __uint_as_float(sr[q * PS + r]));
-            tmax_raw = fmaxf(tmax_raw, m * kf[q]);
-          }
+        for (int c = 0; c < 32; ++c) {
+          if (!((vlo >> c) & 1u)) r0[c] = 0xFF800000u;
+          if (!((vhi >> c) & 1u)) r1[c] = 0xFF800000u;
         }
       }
+      auto X = [&](int c) -> float { return __uint_as_float(c < 32 ? r0[c & 31] : r1[c & 31]); };
+      float tmax_raw = -INFINITY;               // max over visible columns of score x factor (factors > 0)
+#pragma unroll
+      for (int q = 0; q < kSlotsPerChunk; ++q) {
+        float ma = -INFINITY, mb = -INFINITY;
+#pragma unroll
+        for (int r = 0; r < PS; r += 4) {
+          ma = fmax3(ma, X(q * PS + r), X(q * PS + r + 1));
+          mb = fmax3(mb, X(q * PS + r + 2), X(q * PS + r + 3));
+        }
+        tmax_raw = fmaxf(tmax_raw, fmaxf(ma, mb) * factors(q).x);
+      }
       const float tmax = tmax_raw == -INFINITY ? -INFINITY : tmax_raw * scale;
+      // lazy rescaling: the running max moves only when it grows by more than 2^kLazyLog2; O is
+      // rescaled after P is written (the scores are no longer live then)
+      float f = 1.f;
+      bool rescale = false;
       if (j == 0) {
         m_used = tmax;
       } else {
         const bool need = tmax > m_used + kLazyLog2;
-        if (__any_sync(0xffffffffu, need)) {
-          // rescale O in TMEM: every earlier P.V must have landed
-          if (!__all_sync(0xffffffffu, mbar_wait_sleep(bar(B_PVDONE + qt), (j - 1) & 1))) {
-            timed_out = true;
-            break;
-          }
-          tc_fence_after();
-          const float f = need ? exp2f(m_used - tmax) : 1.f;
-          if (need) {
-            l *= f;
-            m_used = tmax;
-          }
-#pragma unroll 1
-          for (int c = 0; c < kD / 32; ++c) {
-            uint32_t o[32];
-            tmem_ld32(lane_addr + o_col + c * 32, o);
-            tmem_wait_ld();
-#pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * f);
-            tmem_st32(lane_addr + o_col + c * 32, o);
-          }
-          tmem_wait_st();
+        rescale = __any_sync(0xffffffffu, need);
+        if (need) {
+          f = exp2f(m_used - tmax);
+          l *= f;
+          m_used = tmax;
         }
       }
-      float lsum = 0.f;
-      const float neg_m = -m_used;
       // l sums the softmax weights; P (f16, packed over the first 32 columns of the S buffer)
-      // carries them times the value factor of their slot
-#pragma unroll 1
-      for (int hh = 0; hh < 2; ++hh) {
-        uint32_t sr[32];
-        tmem_ld32(lane_addr + s_col + hh * 32, sr);
-        uint64_t vis[kSPH];
-        float kf[kSPH], vf[kSPH];
-        half_slots(hh, vis, kf, vf);
-        tmem_wait_ld();
-        uint32_t pk[16];
-        if (cfull) {                            // m_used is finite once a chunk is seen whole
+      // carries them times the value factor of their slot.  A row with no visible column so far
+      // (m_used = -inf) has only -inf scores here: its weights are 0.
+      const float neg_m = m_used == -INFINITY ? 0.f : -m_used;
+      float2 ls = make_float2(0.f, 0.f);
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int q = PS <= 32 ? (2 * i) / PS : 0;
-            const float a = scale * kf[q];
-            const float p0 = ex2(fmaf(__uint_as_float(sr[2 * i]), a, neg_m));
-            const float p1 = ex2(fmaf(__uint_as_float(sr[2 * i + 1]), a, neg_m));
-            lsum += p0 + p1;
-            pk[i] = pack_h2(p0 * vf[q], p1 * vf[q]);
-          }
-        } else {
+      for (int g2 = 0; g2 < kChunk / 16; ++g2) {
+        uint32_t pk[8];
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int q = PS <= 32 ? (2 * i) / PS : 0, r = PS <= 32 ? (2 * i) % PS : 2 * i;
-            const float a = scale * kf[q];
-            const float p0 = ((vis[q] >> r) & 1ull) ? ex2(fmaf(__uint_as_float(sr[2 * i]), a, neg_m)) : 0.f;
-            const float p1 = ((vis[q] >> (r + 1)) & 1ull) ? ex2(fmaf(__uint_as_float(sr[2 * i + 1]), a, neg_m)) : 0.f;
-            lsum += p0 + p1;
-            pk[i] = pack_h2(p0 * vf[q], p1 * vf[q]);
+        for (int h = 0; h < 2; ++h) {
+          const int g = 2 * g2 + h;             // 8 columns of one slot
+          const float2 fv = factors((8 * g) / PS);
+          const float a = scale * fv.x;
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 t = ffma2(make_float2(X(8 * g + 2 * e), X(8 * g + 2 * e + 1)), make_float2(a, a),
+                                   make_float2(neg_m, neg_m));
+            const float2 pr = make_float2(ex2(t.x), ex2(t.y));
+            ls = fadd2(ls, pr);
+            const float2 pv = fmul2(pr, make_float2(fv.y, fv.y));
+            pk[4 * h + e] = pack_h2(pv.x, pv.y);
           }
         }
-        tmem_st16(lane_addr + s_col + hh * 16, pk);
+        tmem_st8(lane_addr + s_col + g2 * 8, pk);
       }
-      l += lsum;
+      l += ls.x + ls.y;
+      if (rescale) {
+        // rescale O in TMEM: every earlier P.V must have landed
+        if (!__all_sync(0xffffffffu, mbar_wait_sleep(bar(B_PVDONE + qt), (j - 1) & 1))) {
+          timed_out = true;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll 1
+        for (int c = 0; c < kD / 32; ++c) {
+          uint32_t o[32];
+          tmem_ld32(lane_addr + o_col + c * 32, o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * f);
+          tmem_st32(lane_addr + o_col + c * 32, o);
+        }
+      }
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(bar(B_PFULL + qt));
