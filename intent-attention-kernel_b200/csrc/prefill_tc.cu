@@ -653,7 +653,7 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const PrefillPa
       const int st = j % kTileStages;
       // S ready; the K tile barrier (already complete) orders the converters' factor writes
       if (lane == 0)
-        ok = mbar_wait_sleep(bar(B_SFULL + qt), j & 1) && mbar_wait(bar(B_KFULL + st), (j / kTileStages) & 1);
+        ok = mbar_wait(bar(B_SFULL + qt), j & 1) && mbar_wait(bar(B_KFULL + st), (j / kTileStages) & 1);
       if (!__shfl_sync(0xffffffffu, ok, 0)) { timed_out = true; break; }
       tc_fence_after();
       // the chunk's S in one read; masked columns become -inf
