@@ -588,60 +588,70 @@ __global__ void __launch_bounds__(kThreads, 1) prefill_tc_kernel(const PrefillPa
     }
   } else if (warp == kMmaWarp) {
     // ---------------------------------------------------------------- MMA issuer
-    if (lane == 0) {
+    // The whole warp runs the loop and polls every barrier; one elected lane issues the MMAs and
+    // their commits, so the operands stay warp-uniform (a lane issuing alone was ~1.5x slower per
+    // MMA).  The tcgen05 fence follows only the hand-offs of TMEM contents.
+    {
+      auto wait = [&](int b, uint32_t parity) -> bool { return __all_sync(0xffffffffu, mbar_wait(bar(b), parity)); };
       constexpr uint32_t kIdS = idesc_f16(kRows, kChunk, 0, 0);  // S = Q . K^T
       constexpr uint32_t kIdPV = idesc_f16(kRows, kD, 0, 1);     // O += P . V (V read MN-major)
-      // per chunk: S of both tiles, then P.V of both (a tile's S buffer is reused once its
-      // previous P.V has retired; the other tile's MMAs keep the pipe busy meanwhile)
+      // per chunk: P.V of tile 0 and its next S, then the same for tile 1 (a tile's S columns are
+      // reused once its P.V, which reads P over them, has retired), so one tile's softmax overlaps
+      // the other tile's MMAs
       auto issue_s = [&](int j, int t2) -> bool {
         const int st = j % kTileStages;
-        if (j >= 1 && !mbar_wait(bar(B_PVDONE + t2), (j - 1) & 1)) return false;
+        if (j >= 1 && !wait(B_PVDONE + t2, (j - 1) & 1)) return false;
         tc_fence_after();
         const uint32_t d = tmem + kSCol + t2 * kChunk;
+        if (elect_one()) {
 #pragma unroll
-        for (int kb = 0; kb < 2; ++kb) {
-          const uint64_t bd = sw128_desc(sbase + tile_off(st, 0) + kb * kKb, 16, 1024);
+          for (int kb = 0; kb < 2; ++kb) {
+            const uint64_t bd = sw128_desc(sbase + tile_off(st, 0) + kb * kKb, 16, 1024);
 #pragma unroll
-          for (int t = 0; t < 4; ++t)
-            mma_ts(d, tmem + kQCol + t2 * (kD / 2) + kb * 32 + t * 8, bd + (t * 2), kIdS, (kb | t) ? 1u : 0u);
+            for (int t = 0; t < 4; ++t)
+              mma_ts(d, tmem + kQCol + t2 * (kD / 2) + kb * 32 + t * 8, bd + (t * 2), kIdS, (kb | t) ? 1u : 0u);
+          }
+          mma_commit(bar(B_SFULL + t2));
         }
-        mma_commit(bar(B_SFULL + t2));
+        __syncwarp();
         return true;
       };
       auto issue_pv = [&](int j, int t2) -> bool {
         const int st = j % kTileStages;
-        if (!mbar_wait(bar(B_PFULL + t2), j & 1)) return false;
+        if (!wait(B_PFULL + t2, j & 1)) return false;
         tc_fence_after();
         const uint64_t bd = sw128_desc(sbase + tile_off(st, 1), kKb, 1024);
+        if (elect_one()) {
 #pragma unroll
-        for (int t = 0; t < kChunk / 16; ++t)
-          mma_ts(tmem + kOCol + t2 * kD, tmem + kSCol + t2 * kChunk + t * 8, bd + ((t * 2048) >> 4), kIdPV,
-                 (j > 0 || t > 0) ? 1u : 0u);
-        mma_commit(bar(B_PVDONE + t2));
+          for (int t = 0; t < kChunk / 16; ++t)
+            mma_ts(tmem + kOCol + t2 * kD, tmem + kSCol + t2 * kChunk + t * 8, bd + ((t * 2048) >> 4), kIdPV,
+                   (j > 0 || t > 0) ? 1u : 0u);
+          mma_commit(bar(B_PVDONE + t2));
+        }
+        __syncwarp();
         return true;
       };
-      if (!mbar_wait(bar(B_QREADY), 0)) timed_out = true;
+      if (!wait(B_QREADY, 0)) timed_out = true;
       tc_fence_after();
-      // staggered: P.V of tile 0 and its next S, then the same for tile 1, so one tile's softmax
-      // overlaps the other tile's MMAs
       if (!timed_out && T > 0) {
-        if (!mbar_wait(bar(B_KFULL + 0), 0) || !issue_s(0, 0) || !issue_s(0, 1)) timed_out = true;
+        if (!wait(B_KFULL + 0, 0) || !issue_s(0, 0) || !issue_s(0, 1)) timed_out = true;
       }
       for (int j = 0; j < T && !timed_out; ++j) {
         const int st = j % kTileStages, st1 = (j + 1) % kTileStages;
-        if (!mbar_wait(bar(B_VFULL + st), (j / kTileStages) & 1)) { timed_out = true; break; }
+        if (!wait(B_VFULL + st, (j / kTileStages) & 1)) { timed_out = true; break; }
         const bool more = j + 1 < T;
-        if (more && !mbar_wait(bar(B_KFULL + st1), ((j + 1) / kTileStages) & 1)) { timed_out = true; break; }
+        if (more && !wait(B_KFULL + st1, ((j + 1) / kTileStages) & 1)) { timed_out = true; break; }
         bool ok = true;
 #pragma unroll 1
-        for (int t2 = 0; t2 < kQTiles && ok; ++t2) {
-          ok = issue_pv(j, t2) && (!more || issue_s(j + 1, t2));
-        }
+        for (int t2 = 0; t2 < kQTiles && ok; ++t2) ok = issue_pv(j, t2) && (!more || issue_s(j + 1, t2));
         if (!ok) { timed_out = true; break; }
-        mma_commit(bar(B_EMPTY + st));
+        if (elect_one()) mma_commit(bar(B_EMPTY + st));
+        __syncwarp();
       }
-      mma_commit(bar(B_DONE));
-      if (!mbar_wait(bar(B_DONE), 0)) timed_out = true;
+      if (elect_one()) mma_commit(bar(B_DONE));
+      __syncwarp();
+      if (!wait(B_DONE, 0)) timed_out = true;
+      if (lane != 0) timed_out = false;           // counted once
     }
   } else if (warp < kSoftWarps) {
     // ---------------------------------------------------------------- softmax (one query row per thread)
