@@ -184,7 +184,7 @@ int prepare_mla(const iak_mla_args* a, MlaParams* p) {
   const bool tc_ok = mla_tc_eligible(*p);
   if (a->kernel == IAK_KERNEL_TENSOR && !tc_ok)
     return fail(IAK_ERR_UNSUPPORTED, "tensor-core MLA needs d_qk=576, d_v=512, heads<=128, page_size%%64==0, "
-                "bf16/f16 q, dense pages bf16/f16 (got d_qk=%d d_v=%d H=%d PS=%d)", p->Dqk, p->Dv, p->H, p->PS);
+                "bf16/f16 q, dense pages bf16/f16, a positive sm_scale (got d_qk=%d d_v=%d H=%d PS=%d)", p->Dqk, p->Dv, p->H, p->PS);
   p->tensor = tc_ok && a->kernel != IAK_KERNEL_GENERIC && work;
   int splits = a->num_splits;
   const int W = a->table_width;

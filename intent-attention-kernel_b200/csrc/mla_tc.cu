@@ -33,6 +33,7 @@
 //
 // Reference: triton_mla_decode.py:155-186 (_mla_decode_cpu) per query row,
 // restated per head; rows without pages give 0.
+#include <cmath>
 #include <algorithm>
 #include <cstring>
 #include <mutex>
@@ -444,7 +445,7 @@ __global__ void __launch_bounds__(kThreads, 1) mla_tc_kernel(const MlaParams p) 
       // warp-uniform outcome: the TMEM loads below are warp-collective
       // one lane polls; the outcome is broadcast (warp-uniform: the TMEM loads below are warp-collective)
       bool ok = true;
-      if (lane == 0) ok = mbar_wait_sleep(bar(B_SFULL + k), (j >> 1) & 1);
+      if (lane == 0) ok = mbar_wait(bar(B_SFULL + k), (j >> 1) & 1);
       if (!__shfl_sync(0xffffffffu, ok, 0)) { timed_out = true; break; }
       tc_fence_after();
       // FP8 latents hold codes: the page scale multiplies the scores (key side)
@@ -452,16 +453,20 @@ __global__ void __launch_bounds__(kThreads, 1) mla_tc_kernel(const MlaParams p) 
       const float vs = s_scale[j / cpp];
       const float sc = base_scale * vs;
       float x[kChunk], tmax = -INFINITY;
-#pragma unroll
-      for (int h2 = 0; h2 < 2; ++h2) {
-        uint32_t sr[32];
-        tmem_ld32(lane_addr + kSCol + k * kChunk + h2 * 32, sr);
+      {
+        uint32_t sr[2][32];
+        tmem_ld32(lane_addr + kSCol + k * kChunk, sr[0]);
+        tmem_ld32(lane_addr + kSCol + k * kChunk + 32, sr[1]);
         tmem_wait_ld();
+        float ma = -INFINITY, mb = -INFINITY;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          x[h2 * 32 + i] = __uint_as_float(sr[i]) * sc;
-          tmax = fmaxf(tmax, x[h2 * 32 + i]);
+        for (int i = 0; i < kChunk; ++i) {
+          x[i] = __uint_as_float(sr[i >> 5][i & 31]);
+          if (i & 1) mb = fmaxf(mb, x[i]);
+          else ma = fmaxf(ma, x[i]);
         }
+        // sc > 0: the max of the scaled scores is the scaled max
+        tmax = fmaxf(ma, mb) * sc;
       }
       if (j == 0) {
         m_used = tmax;
@@ -492,15 +497,16 @@ __global__ void __launch_bounds__(kThreads, 1) mla_tc_kernel(const MlaParams p) 
         }
       }
       uint32_t pk[kChunk / 2];
-      float lsum = 0.f;
+      float ls[2] = {0.f, 0.f};
+      const float neg_m = -m_used;
 #pragma unroll
       for (int i = 0; i < kChunk / 2; ++i) {
-        const float p0 = exp2f(x[2 * i] - m_used), p1 = exp2f(x[2 * i + 1] - m_used);
-        lsum += p0 + p1;
+        const float p0 = ex2(fmaf(x[2 * i], sc, neg_m)), p1 = ex2(fmaf(x[2 * i + 1], sc, neg_m));
+        ls[i & 1] += p0 + p1;
         const __half2 h = __floats2half2_rn(p0 * vs, p1 * vs);
         pk[i] = *reinterpret_cast<const uint32_t*>(&h);
       }
-      l += lsum;
+      l += ls[0] + ls[1];
       tmem_st32(lane_addr + kSCol + k * kChunk, pk);
       tmem_wait_st();
       tc_fence_before();
@@ -581,6 +587,8 @@ bool mla_tc_eligible(const MlaParams& p) {
   if (p.fp8 && reinterpret_cast<uintptr_t>(p.fp8) % 16) return false;
   if (p.num_pages * static_cast<int64_t>(p.PS) >= (1LL << 31)) return false;
   if (p.ex_acc && reinterpret_cast<uintptr_t>(p.ex_acc) % 16) return false;
+  // the softmax takes the max of the raw scores times a positive scale
+  if (!(p.sm_scale > 0.f) || !std::isfinite(p.sm_scale)) return false;
   return true;
 }
 

@@ -102,12 +102,6 @@ __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
   const __half2 h = __floats2half2_rn(a, b);
   return *reinterpret_cast<const uint32_t*>(&h);
 }
-// 2^x with the hardware approximation (flush-to-zero; 2^-inf = 0)
-__device__ __forceinline__ float ex2(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
 // max of three (one instruction)
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
   float d;
