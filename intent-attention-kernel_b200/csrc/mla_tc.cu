@@ -360,10 +360,13 @@ __global__ void __launch_bounds__(kThreads, 1) mla_tc_kernel(const MlaParams p) 
     }
   } else if (warp == kMmaWarp) {
     // ---------------------------------------------------------------- MMA issuer
-    if (lane == 0) {
+    // The whole warp runs the loop and polls every barrier; one elected lane issues the MMAs and
+    // their commits, so the operands stay warp-uniform.
+    {
       constexpr uint32_t kIdS = idesc_f16(kRows, kChunk, 0, 0);  // S = Q . C^T
       constexpr uint32_t kIdPV = idesc_f16(kRows, kHalf, 0, 1);  // O += P . C (value blocks read MN-major)
       const uint64_t q_desc0 = sw128_desc(sbase + Smem::q, 16, 1024);
+      auto wait = [&](int b, uint32_t parity) -> bool { return __all_sync(0xffffffffu, mbar_wait(bar(b), parity)); };
       // S MMAs over one k-block: A = Q block kb (TMEM for kb < 4, else shared), B = the latent block
       auto s_block = [&](uint32_t d, int kb, uint32_t blk_off, bool first) {
         const uint64_t bd = sw128_desc(sbase + blk_off, 16, 1024);
@@ -376,35 +379,44 @@ __global__ void __launch_bounds__(kThreads, 1) mla_tc_kernel(const MlaParams p) 
             mma_ss(d, q_desc0 + (((kb - kQSmemKb0) * kKbQ + t * 32) >> 4), bd + (t * 2), kIdS, acc);
         }
       };
-      if (!mbar_wait(bar(B_QREADY), 0)) timed_out = true;
+      if (!wait(B_QREADY, 0)) timed_out = true;
       auto issue_s = [&](int j) -> bool {
         const int k = j & 1, vs = j & 1;
-        if (j >= kSBuf && !mbar_wait(bar(B_PVDONE + k), ((j >> 1) - 1) & 1)) return false;
+        if (j >= kSBuf && !wait(B_PVDONE + k, ((j >> 1) - 1) & 1)) return false;
         const uint32_t d = tmem + kSCol + k * kChunk;
         for (int i = 0; i < kKOnly; ++i) {
           const int c = kKOnly * j + i, ks = c % kKSlots;
-          if (!mbar_wait(bar(B_KCONV + ks), (c / kKSlots) & 1)) return false;
+          if (!wait(B_KCONV + ks, (c / kKSlots) & 1)) return false;
           tc_fence_after();
-          s_block(d, chunk_kb(half, i), kslot(ks), i == 0);
-          mma_commit(bar(B_KEMPTY + ks));
+          if (elect_one()) {
+            s_block(d, chunk_kb(half, i), kslot(ks), i == 0);
+            mma_commit(bar(B_KEMPTY + ks));
+          }
+          __syncwarp();
         }
-        if (!mbar_wait(bar(B_VCONV + vs), (j >> 1) & 1)) return false;
+        if (!wait(B_VCONV + vs, (j >> 1) & 1)) return false;
         tc_fence_after();
-        for (int i = 0; i < kVBlocks; ++i) s_block(d, chunk_kb(half, kKOnly + i), vslot(vs, i), false);
-        mma_commit(bar(B_SFULL + k));
+        if (elect_one()) {
+          for (int i = 0; i < kVBlocks; ++i) s_block(d, chunk_kb(half, kKOnly + i), vslot(vs, i), false);
+          mma_commit(bar(B_SFULL + k));
+        }
+        __syncwarp();
         return true;
       };
       auto issue_pv = [&](int j) -> bool {
         const int k = j & 1, vs = j & 1;
-        if (!mbar_wait(bar(B_PFULL + k), (j >> 1) & 1)) return false;
+        if (!wait(B_PFULL + k, (j >> 1) & 1)) return false;
         tc_fence_after();
         const uint64_t bd = sw128_desc(sbase + vslot(vs, 0), kKb, 1024);
+        if (elect_one()) {
 #pragma unroll
-        for (int t = 0; t < kChunk / 16; ++t)
-          mma_ts(tmem + kOCol, tmem + kSCol + k * kChunk + t * 8, bd + ((t * 2048) >> 4), kIdPV,
-                 (j > 0 || t > 0) ? 1u : 0u);
-        mma_commit(bar(B_PVDONE + k));
-        mma_commit(bar(B_VEMPTY + vs));
+          for (int t = 0; t < kChunk / 16; ++t)
+            mma_ts(tmem + kOCol, tmem + kSCol + k * kChunk + t * 8, bd + ((t * 2048) >> 4), kIdPV,
+                   (j > 0 || t > 0) ? 1u : 0u);
+          mma_commit(bar(B_PVDONE + k));
+          mma_commit(bar(B_VEMPTY + vs));
+        }
+        __syncwarp();
         return true;
       };
       if (!timed_out && T > 0 && !issue_s(0)) timed_out = true;
@@ -413,8 +425,10 @@ __global__ void __launch_bounds__(kThreads, 1) mla_tc_kernel(const MlaParams p) 
         if (!issue_pv(j)) { timed_out = true; break; }
       }
       // every MMA issued above has retired once this commit lands
-      mma_commit(bar(B_DONE));
-      if (!mbar_wait(bar(B_DONE), 0)) timed_out = true;
+      if (elect_one()) mma_commit(bar(B_DONE));
+      __syncwarp();
+      if (!wait(B_DONE, 0)) timed_out = true;
+      if (lane != 0) timed_out = false;           // counted once
     }
   } else {
     // ---------------------------------------------------------------- softmax (warps 0-3, one head row per thread)
