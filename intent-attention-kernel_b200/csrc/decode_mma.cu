@@ -364,77 +364,81 @@ __device__ __forceinline__ void k_frag_f16(uint32_t tile_u32, int lane, int kk, 
 // |error| <= s2/2 ~ absmax/32258) for the integer MMA of INT8 / INT4 pages,
 // plus the per-32-channel sums of the terms that undo the INT4 +8 offset.
 template <int D>
-__global__ void __launch_bounds__(128) decode_prep_kernel(const DecodeParams p, char* __restrict__ qtab) {
+__global__ void __launch_bounds__(256) decode_prep_kernel(const DecodeParams p, char* __restrict__ qtab) {
   constexpr int KT = D / 16;
+  constexpr int E = D / 32;            // channels per lane: d = E * lane + e
+  constexpr int GL = 32 / E;           // lanes of one 32-channel block
   __shared__ float qs[8 * D];
   __shared__ int8_t i1s[8 * D], i2s[8 * D];
   __shared__ float qsc[128];
   const int unit = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int b = unit / p.Ht, hk = unit % p.Ht;
-  for (int idx = tid; idx < 8 * D; idx += 128) {
-    const int g = idx / D, d = idx % D;
-    const int64_t off = static_cast<int64_t>(b) * p.q_sb + static_cast<int64_t>(hk * p.G + g) * p.q_sh + d;
-    qs[idx] = g < p.G ? load_as_float(p.q, p.q_dtype, off) : 0.f;
-  }
-  for (int i = tid; i < 128; i += 128) qsc[i] = 0.f;
-  __syncthreads();
-  if (tid < 64) {
-    const int g = tid >> 3, sub = tid & 7;
-    const float* qr = qs + g * D;
+  if (tid < 128) qsc[tid] = 0.f;
+  {
+    // warp g quantises query head g of the group (zeros past G): q = s1 * i1 + s2 * i2
+    const int g = warp;
+    const int64_t off = static_cast<int64_t>(b) * p.q_sb + static_cast<int64_t>(hk * p.G + g) * p.q_sh + E * lane;
+    float q[E];
+#pragma unroll
+    for (int e = 0; e < E; ++e) q[e] = g < p.G ? load_as_float(p.q, p.q_dtype, off + e) : 0.f;
     float am = 0.f;
-    for (int d = sub; d < D; d += 8) am = fmaxf(am, fabsf(qr[d]));
-    for (int off = 1; off < 8; off <<= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, off));
+#pragma unroll
+    for (int e = 0; e < E; ++e) am = fmaxf(am, fabsf(q[e]));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
     const float s1 = am > 0.f ? am / 127.f : 1.f;
-    float am2 = 0.f;
-    for (int d = sub; d < D; d += 8) {
-      const float t = fminf(fmaxf(rintf(qr[d] / s1), -127.f), 127.f);
-      am2 = fmaxf(am2, fabsf(qr[d] - t * s1));
+    float t1[E], am2 = 0.f;
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+      t1[e] = fminf(fmaxf(rintf(q[e] / s1), -127.f), 127.f);
+      am2 = fmaxf(am2, fabsf(q[e] - t1[e] * s1));
     }
-    for (int off = 1; off < 8; off <<= 1) am2 = fmaxf(am2, __shfl_xor_sync(0xffffffffu, am2, off));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) am2 = fmaxf(am2, __shfl_xor_sync(0xffffffffu, am2, o));
     const float s2 = am2 > 0.f ? am2 / 127.f : 1.f;
-    int sum1[4] = {0, 0, 0, 0}, sum2[4] = {0, 0, 0, 0};
+    int sum1 = 0, sum2 = 0;
 #pragma unroll
-    for (int j = 0; j < D / 32; ++j)
+    for (int e = 0; e < E; ++e) {
+      const float t2 = fminf(fmaxf(rintf((q[e] - t1[e] * s1) / s2), -127.f), 127.f);
+      const int d = E * lane + e;
+      qs[g * D + d] = q[e];
+      i1s[g * D + d] = static_cast<int8_t>(t1[e]);
+      i2s[g * D + d] = static_cast<int8_t>(t2);
+      sum1 += static_cast<int>(t1[e]);
+      sum2 += static_cast<int>(t2);
+    }
+    // sums of the terms over each 32-channel block (they undo the INT4 +8 offset)
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const int d = 32 * j + sub + 8 * k;
-        const float t1 = fminf(fmaxf(rintf(qr[d] / s1), -127.f), 127.f);
-        const float t2 = fminf(fmaxf(rintf((qr[d] - t1 * s1) / s2), -127.f), 127.f);
-        i1s[g * D + d] = static_cast<int8_t>(t1);
-        i2s[g * D + d] = static_cast<int8_t>(t2);
-        sum1[j] += static_cast<int>(t1);
-        sum2[j] += static_cast<int>(t2);
-      }
-#pragma unroll
-    for (int j = 0; j < 4; ++j)
-      for (int off = 1; off < 8; off <<= 1) {
-        sum1[j] += __shfl_xor_sync(0xffffffffu, sum1[j], off);
-        sum2[j] += __shfl_xor_sync(0xffffffffu, sum2[j], off);
-      }
-    if (sub == 0) {
+    for (int o = 1; o < GL; o <<= 1) {
+      sum1 += __shfl_xor_sync(0xffffffffu, sum1, o);
+      sum2 += __shfl_xor_sync(0xffffffffu, sum2, o);
+    }
+    __syncthreads();                   // qsc zeroed
+    if (lane == 0) {
       qsc[g] = s1;
       qsc[8 + g] = s2;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        qsc[16 + j * 8 + g] = static_cast<float>(sum1[j]);
-        qsc[48 + j * 8 + g] = static_cast<float>(sum2[j]);
-      }
+    }
+    if (lane % GL == 0) {
+      const int j = lane / GL;
+      qsc[16 + j * 8 + g] = static_cast<float>(sum1);
+      qsc[48 + j * 8 + g] = static_cast<float>(sum2);
     }
   }
   __syncthreads();
   char* out = qtab + static_cast<int64_t>(unit) * kQTab;
+  const int r = lane >> 2, c = lane & 3;
   if (warp == 0) {
-    const int r = lane >> 2, c = lane & 3;
     const float* qr = qs + r * D;
     uint4* qfrag = reinterpret_cast<uint4*>(out + kQFrag);
-    uint4* qi8 = reinterpret_cast<uint4*>(out + kQI8);
-    uint4* qi4 = reinterpret_cast<uint4*>(out + kQI4);
 #pragma unroll
     for (int kk = 0; kk < KT; ++kk) {
       const int b0 = 16 * kk + 2 * c, b1 = 16 * kk + 4 * c;
       qfrag[kk * 32 + lane] = make_uint4(pack_f16x2(qr[b0], qr[b0 + 1]), pack_f16x2(qr[b0 + 8], qr[b0 + 9]),
                                          pack_f16x2(qr[b1], qr[b1 + 1]), pack_f16x2(qr[b1 + 2], qr[b1 + 3]));
     }
+  } else if (warp == 1) {
+    uint4* qi8 = reinterpret_cast<uint4*>(out + kQI8);
+    uint4* qi4 = reinterpret_cast<uint4*>(out + kQI4);
     auto pack4 = [&](const int8_t* t, int d0, int d1, int d2, int d3) {
       return static_cast<uint32_t>(static_cast<uint8_t>(t[d0])) |
              (static_cast<uint32_t>(static_cast<uint8_t>(t[d1])) << 8) |
@@ -1030,7 +1034,7 @@ static int launch_persistent(const DecodeParams& p, const TmaMaps& maps, int n_i
     }
   }
   const int ctas = std::max(1, std::min(n_items, per_sm * device_sm_count()));
-  decode_prep_kernel<D><<<p.B * p.Ht, 128, 0, s>>>(p, p.ws_qtab);
+  decode_prep_kernel<D><<<p.B * p.Ht, 256, 0, s>>>(p, p.ws_qtab);
   err = cudaGetLastError();
   if (err != cudaSuccess) return check_cuda(err, "decode_prep launch");
   kernel_timer_begin(s);
