@@ -11,7 +11,8 @@
 //     64-token chunks of 64 / PS slots) and flags the chunks every row sees
 //     whole; then, per chunk, it stages the pages' scales in shared memory and
 //     bulk-copies their raw K and V bytes (cp.async.bulk, mbarrier transaction
-//     counts) into a 3-stage ring, running ahead of the converters;
+//     counts; one lane per slot and plane) into a 3-stage ring, running ahead
+//     of the converters;
 //   * two converter warpgroups (one 32-channel row segment per thread and
 //     plane) widen the staged rows to f16 tiles, 128-byte swizzled, rows the
 //     slot mask does not select written as zero, over a 3-stage ring: F16 rows
@@ -24,10 +25,12 @@
 //     applies the row masks and the causal comparison of each key's token
 //     position with the row's query position (skipped for chunks seen whole),
 //     multiplies in the slots' score factors, runs the online softmax in the
-//     exp2 domain with lazy O rescaling over two half chunks, and writes P
-//     (f16, times the slots' value factors) back over S;
+//     exp2 domain (S read once per chunk; lazy O rescaling) and writes P (f16,
+//     times the slots' value factors) back over S;
 //   * O += P . V (M = 128, N = 128, K = 64: 4 tcgen05.mma per tile, P the
-//     TMEM A operand, V read MN-major) accumulates in TMEM (fp32).
+//     TMEM A operand, V read MN-major) accumulates in TMEM (fp32).  The MMA
+//     warp issues, per chunk, P.V of tile 0 and tile 0's next S, then the
+//     same for tile 1, so one tile's softmax overlaps the other's MMAs.
 // TMEM: O 2 x 128 | S/P 2 x 64 | Q 2 x 64 columns (512 allocated, one CTA per SM).
 // Rows that see no key are written as 0.
 //
