@@ -14,9 +14,9 @@
 // exact fp16 integers by exponent-bias tricks, e4m3 codes by cvt.f16x2.e4m3x2,
 // and the per-page (or per-32-channel) scale is applied in fp32 to S and folded
 // into P for V.  The query group of a GQA head is the MMA's N dimension, so G
-// <= 8 query heads share every K/V byte.  The four warps' (m, l, O) are merged
-// in shared memory; with several splits the partials go to the workspace and
-// the LSE merge kernel combines them.
+// <= 8 query heads share every K/V byte.  Each consumer warp writes its own
+// (m, l, O) partial per work item to the workspace (splits x 4 slots per query
+// row) and the LSE merge kernel combines them.
 //
 // Register-fragment index maps (m16n8k16, lane = 4*r + c):
 //   QK, 8-bit / 4-bit pages: k-step kk, thread c holds channels 16kk+4c..+3
