@@ -192,6 +192,11 @@ __device__ __forceinline__ uint32_t e4m3x2_f16x2(uint32_t v16) {
   asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(r) : "h"(h));
   return r;
 }
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 __device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
   const __half2 h = __floats2half2_rn(lo, hi);
   return *reinterpret_cast<const uint32_t*>(&h);
@@ -830,8 +835,9 @@ __global__ void __launch_bounds__(kThreads, IAK_MIN_BLOCKS)
           oacc[mt][0] *= al0; oacc[mt][1] *= al1; oacc[mt][2] *= al0; oacc[mt][3] *= al1;
         }
       }
-      const float p0 = exp2f(sc[0] - m_run[0]), p1 = exp2f(sc[1] - m_run[1]);
-      const float p2 = exp2f(sc[2] - m_run[0]), p3 = exp2f(sc[3] - m_run[1]);
+      // hardware exp2 (arguments <= kLazyLog2; results below 2^-126 flush to 0, far below fp16's range)
+      const float p0 = ex2_approx(sc[0] - m_run[0]), p1 = ex2_approx(sc[1] - m_run[1]);
+      const float p2 = ex2_approx(sc[2] - m_run[0]), p3 = ex2_approx(sc[3] - m_run[1]);
       l_run[0] += p0 + p2;
       l_run[1] += p1 + p3;
       // ---------------- O^T += V^T P^T
