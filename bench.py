@@ -234,11 +234,11 @@ class ClockSampler:
 
 
 # DRAM bytes (read + write) of one decode_mma_kernel launch from an ncu capture of a
-# smaller batch of the same workload (profiles/decode_mma_c2_b4.md), and the units
-# (sequences) that capture processed.  Traffic grows in proportion to the sequences
+# smaller batch of the same workload (--set full, batch 4), and the units (sequences)
+# that capture processed.  Traffic grows in proportion to the sequences
 # decoded, so it is scaled to the benched batch.
 NCU_TRAFFIC = {"c2": {"bytes": 179_515_392, "batch": 4, "algorithmic": 174_640_384,
-                      "source": "profiles/decode_mma_c2_b4.md"}}
+                      "source": "ncu --set full capture of decode_mma_kernel, C2 at batch 4"}}
 
 
 def ncu_traffic(workload_name, batch, nbytes):

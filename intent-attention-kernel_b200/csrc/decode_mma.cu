@@ -61,14 +61,15 @@ constexpr int kVOff = 4096;
 constexpr int kResOff = 1024;       // INT4 residual plane inside a K or V region
 constexpr int kScaleOff = 8192;
 constexpr long long kWaitCycles = 4000000000LL;  // ~2 s at boost clock, then give up
-#ifndef IAK_PRODUCER_LANES
-#define IAK_PRODUCER_LANES 4
-#endif
 #ifndef IAK_F16_ONE_BOX
 #define IAK_F16_ONE_BOX 1
 #endif
 constexpr float kLazyLog2 = 8.f;                  // rescale O only when the max grows by > 2^8
-constexpr int kProducerLanes = IAK_PRODUCER_LANES; // producer lanes issuing TMA for consecutive pages
+// Producer lanes issuing TMA for consecutive pages: two for page scales (measured at C2: 2 lanes
+// 4868 GB/s, 4 lanes 4710, 8 lanes 4597, 1 lane 3935), four for group32 pages, which add two to
+// four scale-row copies per page (C3: 4 lanes 2374 GB/s, 2 lanes 2284, 8 lanes 2298).
+template <bool GROUP>
+constexpr int producer_lanes() { return GROUP ? 4 : 2; }
 // F16 pages at D = 128: one TMA box of 32 half-rows (token-major, 256-byte
 // token rows) instead of two 64-channel boxes
 constexpr bool kF16OneBox = IAK_F16_ONE_BOX != 0;
@@ -588,6 +589,7 @@ __global__ void __launch_bounds__(kThreads, IAK_MIN_BLOCKS)
       const int n_pad = (n + kStages - 1) & ~(kStages - 1);
       const int32_t* pid_s = reinterpret_cast<const int32_t*>(ib + ItemLayout::pid);
       const uint8_t* fmt_s = reinterpret_cast<const uint8_t*>(ib + ItemLayout::fmt);
+      constexpr int kProducerLanes = producer_lanes<GROUP>();
       if (lane < kProducerLanes) {
         for (int i = lane; i < n_pad; i += kProducerLanes) {
           const int gi = ctr + i;
