@@ -136,6 +136,11 @@ def test_prefill_and_kv_write_args_rejected_on_the_host():
     pools.page_size, pools.head_dim = 16, 40
     assert L.iak_prefill(ctypes.byref(pools), ctypes.byref(a), None) == N.IAK_ERR_UNSUPPORTED   # head_dim
     pools.head_dim = 128
+    # the tensor-core kernel takes a positive scale only; asked for by name, it refuses others
+    a.kernel, a.sm_scale = N.KERNEL_TENSOR, -0.1
+    assert L.iak_prefill(ctypes.byref(pools), ctypes.byref(a), None) == N.IAK_ERR_UNSUPPORTED
+    assert b"positive sm_scale" in L.iak_last_error()
+    a.kernel = N.KERNEL_AUTO
     ap = N.AppendArgs()
     ap.batch, ap.num_table_heads, ap.num_new = 2, 1, 1
     assert L.iak_append_tokens(ctypes.byref(pools), ctypes.byref(ap), None) == N.IAK_ERR_INVALID_ARG
