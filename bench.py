@@ -120,6 +120,17 @@ def n_scales(mode: str, D: int) -> int:
     return {"page": 1, "group32": D // 32, "channel": D}[mode]
 
 
+L2_BYTES = 126 * 2 ** 20          # B200 L2
+
+
+def l2_note(nbytes: int, what: str) -> str:
+    """The config's statement on L2 for inputs that are not flushed between timed steps."""
+    if nbytes > L2_BYTES:
+        return f"inputs larger than L2 ({nbytes / 1e9:.2f} GB of {what} per step)"
+    return (f"inputs smaller than L2 ({nbytes / 1e6:.1f} MB of {what} per step), not flushed between steps: "
+            "a latency-bound case")
+
+
 def step_bytes(w: dict, fmt: np.ndarray) -> int:
     ns = n_scales(w["scale_mode"], w["D"])
     per_unit = sum(page_bytes(int(f), w["PS"], w["D"], ns) for f in fmt)
@@ -460,7 +471,7 @@ def run_gpu(args):
                        "selected_pages_per_seq_head_per_gpu": int(ids.size),
                        "format_mix": w["mix"], "scale_mode": w["scale_mode"],
                        "selected_kv_bytes_per_step_per_gpu": nbytes,
-                       "l2": f"inputs larger than L2 ({nbytes / 1e9:.2f} GB of selected KV per step)",
+                       "l2": l2_note(nbytes, "selected KV"),
                        "timing": ("one CUDA graph of all timed steps, replayed once after a warm-up replay"
                                   if use_graph else "eager launches"),
                        "parallelism": (f"sp{world} (each sequence's selected pages cut into {world} ranges; partial "
@@ -763,7 +774,7 @@ def run_gpu_mla(args):
                        "selected_pages_per_seq": n_sel, "bf16_pages_per_seq": int((tags_sel == 0).sum()),
                        "fp8_pages_per_seq": int((tags_sel == 1).sum()),
                        "selected_kv_bytes_per_step_per_gpu": nbytes, "flops_per_step_per_gpu": flops,
-                       "l2": f"inputs larger than L2 ({nbytes / 1e9:.2f} GB of selected latents per step)",
+                       "l2": l2_note(nbytes, "selected latents"),
                        "parallelism": f"dp{world} (batch shards, no collective on the data path)"},
             "roofline": {"bound": "tensor", "achieved": round(tflops, 1), "peak": tc_peak, "unit": "TFLOP/s",
                          "frac": round(tflops / tc_peak, 4), "traffic": None, "kernel": "mla_tc_kernel",
@@ -1055,9 +1066,24 @@ def run_prefill(args):
         paged_prefill(q_, pool, table, counts, tags, tag_map, q_positions=qp, causal=True, bases=bases, out=out,
                       kernel="tensor")
 
+    # the selected KV (kv_bytes) and q fit in L2: every timed step starts from a flushed L2 (a write
+    # larger than L2 between steps, outside the step's own CUDA events)
+    ns = n_scales(w["scale_mode"], D)
+    kv_bytes = sum(page_bytes(int(f), PS, D, ns) for f in fmt) * B * Hkv
+    flush = torch.empty(2 * L2_BYTES, dtype=torch.uint8, device=device)
+
+    def timed(fn, n):
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n)]
+        for a, b in evs:
+            flush.zero_()
+            a.record()
+            fn()
+            b.record()
+        torch.cuda.synchronize()
+        return sum(a.elapsed_time(b) for a, b in evs) / n
+
     step()
     torch.cuda.synchronize()
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(0) as clocks:
         t_probe = time.perf_counter()
         while len(clocks.rows) < 3 and time.perf_counter() - t_probe < 3.0:
@@ -1068,12 +1094,7 @@ def run_prefill(args):
             step()
         torch.cuda.synchronize()
         with KernelTimer(args.steps) as ktimer:
-            ev0.record()
-            for _ in range(args.steps):
-                step()
-            ev1.record()
-            torch.cuda.synchronize()
-    t_ms = ev0.elapsed_time(ev1) / args.steps
+            t_ms = timed(step, args.steps)
     kernel_ms = ktimer.total_ms / max(1, ktimer.launches)
     q_host = q.cpu().pin_memory()
     out_host = torch.empty(out.shape, dtype=out.dtype).pin_memory()
@@ -1087,13 +1108,7 @@ def run_prefill(args):
     for _ in range(args.warmup):
         e2e_step()
     torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(args.steps):
-        e2e_step()
-    e1.record()
-    torch.cuda.synchronize()
-    e2e_ms = e0.elapsed_time(e1) / args.steps
+    e2e_ms = timed(e2e_step, args.steps)
     peak, peak_kind = measured_tensor_peak()
     tf = flops / (kernel_ms * 1e-3) / 1e12
     rec = {"metric": PREFILL_METRIC, "value": round(flops / (t_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
@@ -1104,8 +1119,10 @@ def run_prefill(args):
            "config": {"workload": PREFILL["name"], "batch": B, "query_tokens": M, "q_heads": Hq, "kv_heads": Hkv,
                       "head_dim": D, "ctx": T, "page_size": PS, "selected_pages_per_seq_head": int(ids.size),
                       "format_mix": w["mix"], "visible_pairs_per_q_head": pairs, "useful_flops_per_step": flops,
-                      "l2": "selected KV (2.1 GB) larger than L2",
-                      "timing": "eager launches, CUDA events around the timed steps"},
+                      "selected_kv_bytes_per_step": kv_bytes,
+                      "l2": f"L2 flushed before every timed step (a {2 * L2_BYTES >> 20} MB write): the selected KV "
+                            f"({kv_bytes / 1e6:.0f} MB) and q ({q.numel() * 2 / 1e6:.0f} MB) fit in L2",
+                      "timing": "eager launches, CUDA events around each timed step"},
            "roofline": {"bound": "tensor", "achieved": round(tf, 1), "peak": peak, "unit": "TFLOP/s",
                         "frac": round(tf / peak, 4), "traffic": None, "kernel": "prefill_tc_kernel<16>",
                         "kernel_ms": round(kernel_ms, 4),
