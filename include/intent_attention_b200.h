@@ -199,7 +199,9 @@ typedef struct iak_mla_args {
    * instead of `out` */
   float* partial_m; float* partial_l; float* partial_acc;
   int32_t num_splits;             /* 0 = choose automatically                                 */
-  int32_t kernel;                 /* IAK_KERNEL_*: auto, generic (CUDA cores), tensor (tcgen05) */
+  int32_t kernel;                 /* IAK_KERNEL_*: auto, generic (CUDA cores), tensor (tcgen05: d_qk 576,
+                                     d_v 512, <= 128 heads, page_size % 64 == 0, bf16 / f16 q and
+                                     dense pages, sm_scale > 0) */
 } iak_mla_args;
 
 int iak_mla_workspace_size(const iak_mla_args* args, size_t* bytes);
@@ -494,7 +496,9 @@ typedef struct iak_prefill_args {
   int64_t rm_stride_b;
   const void* page_tags; int32_t tag_bytes; uint8_t tag_map[16]; uint8_t tag_default;
   float sm_scale;
-  int32_t kernel;               /* IAK_KERNEL_AUTO / GENERIC / TENSOR             */
+  int32_t kernel;               /* IAK_KERNEL_AUTO / GENERIC / TENSOR: the tensor-core kernel takes
+                                   head_dim 128, page_size 8..64, table_width <= 1024, 16-byte aligned
+                                   pools and sm_scale > 0; TENSOR on other calls -> IAK_ERR_UNSUPPORTED */
 } iak_prefill_args;
 int iak_prefill(const iak_page_pools* pools, const iak_prefill_args* args, void* stream);
 
