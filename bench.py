@@ -244,22 +244,30 @@ class ClockSampler:
                 "window": "nvidia-smi every 100 ms over the load window ending with the timed region"}
 
 
-# DRAM bytes (read + write) of one decode_mma_kernel launch from an ncu capture of a
-# smaller batch of the same workload (--set full, batch 4), and the units (sequences)
-# that capture processed.  Traffic grows in proportion to the sequences
-# decoded, so it is scaled to the benched batch.
-NCU_TRAFFIC = {"c2": {"bytes": 179_515_392, "batch": 4, "algorithmic": 174_640_384,
-                      "source": "ncu --set full capture of decode_mma_kernel, C2 at batch 4"}}
+# DRAM bytes (read + write) of one launch of the workload's hot kernel from an ncu capture
+# (--set full) of the same workload at the batch given, and the units (sequences) that
+# capture processed.  Traffic grows in proportion to the sequences processed, so it is
+# scaled to the benched batch.
+NCU_TRAFFIC = {"c2": {"bytes": 179_515_392, "batch": 4,
+                      "source": "ncu --set full capture of decode_mma_kernel, C2 at batch 4"},
+               "c4": {"bytes": 58_652_672, "batch": 8,
+                      "source": "ncu --set full capture of mla_tc_kernel, C4 at batch 8"},
+               "prefill": {"bytes": 140_648_704, "batch": 2,
+                           "source": "ncu --set full capture of prefill_tc_kernel<16>, the prefill workload"}}
 
 
 def ncu_traffic(workload_name, batch, nbytes):
+    """DRAM bytes of one launch at this batch and a note on where they come from; nbytes = the
+    algorithmic bytes of one launch (None: the workload's roofline unit is not bytes)."""
     rec = NCU_TRAFFIC.get(workload_name)
     if rec is None:
         return None, "null (no ncu capture of this workload)"
     scaled = rec["bytes"] * batch / rec["batch"]
-    return int(scaled), (f"dram__bytes_read.sum + dram__bytes_write.sum of one launch at batch {rec['batch']} "
-                         f"({rec['source']}), scaled x{batch / rec['batch']:g} to this batch; "
-                         f"{scaled / nbytes:.3f}x the algorithmic bytes")
+    note = (f"dram__bytes_read.sum + dram__bytes_write.sum of one launch at batch {rec['batch']} "
+            f"({rec['source']}), scaled x{batch / rec['batch']:g} to this batch")
+    if nbytes:
+        note += f"; {scaled / nbytes:.3f}x the algorithmic bytes"
+    return int(scaled), note
 
 
 def measured_hbm_peak():
@@ -777,7 +785,8 @@ def run_gpu_mla(args):
                        "l2": l2_note(nbytes, "selected latents"),
                        "parallelism": f"dp{world} (batch shards, no collective on the data path)"},
             "roofline": {"bound": "tensor", "achieved": round(tflops, 1), "peak": tc_peak, "unit": "TFLOP/s",
-                         "frac": round(tflops / tc_peak, 4), "traffic": None, "kernel": "mla_tc_kernel",
+                         "frac": round(tflops / tc_peak, 4), "traffic": ncu_traffic("c4", w["B"], nbytes)[0],
+                         "traffic_note": ncu_traffic("c4", w["B"], nbytes)[1], "kernel": "mla_tc_kernel",
                          "kernel_us": round(kernel_ms * 1e3, 2),
                          "hbm": {"achieved": round(kernel_gbs, 1), "peak": hbm_peak, "unit": "GB/s",
                                  "frac": round(kernel_gbs / hbm_peak, 4)},
@@ -1124,7 +1133,8 @@ def run_prefill(args):
                             f"({kv_bytes / 1e6:.0f} MB) and q ({q.numel() * 2 / 1e6:.0f} MB) fit in L2",
                       "timing": "eager launches, CUDA events around each timed step"},
            "roofline": {"bound": "tensor", "achieved": round(tf, 1), "peak": peak, "unit": "TFLOP/s",
-                        "frac": round(tf / peak, 4), "traffic": None, "kernel": "prefill_tc_kernel<16>",
+                        "frac": round(tf / peak, 4), "traffic": ncu_traffic("prefill", B, None)[0],
+                        "traffic_note": ncu_traffic("prefill", B, None)[1], "kernel": "prefill_tc_kernel<16>",
                         "kernel_ms": round(kernel_ms, 4),
                         "note": f"peak = {peak_kind} dense bf16 cuBLAS burst; achieved = useful FLOPs (4 x head_dim "
                                 "per visible (query, key) pair per q head) / the kernel's CUDA-event time"},

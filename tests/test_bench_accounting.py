@@ -43,3 +43,13 @@ def test_l2_statement_follows_the_input_size():
     assert bench.l2_note(2 * bench.L2_BYTES, "selected KV").startswith("inputs larger than L2")
     small = bench.l2_note(1_820_992, "selected KV")
     assert small.startswith("inputs smaller than L2") and "not flushed" in small
+
+
+def test_ncu_traffic_scales_with_the_batch():
+    t, note = bench.ncu_traffic("c2", 32, 1_397_123_072)
+    assert t == 179_515_392 * 8 and "1.028x the algorithmic bytes" in note
+    t, note = bench.ncu_traffic("c4", 64, 438_860_288)
+    assert t == 58_652_672 * 8 and "1.069x" in note
+    t, note = bench.ncu_traffic("prefill", 2, None)
+    assert t == 140_648_704 and "algorithmic" not in note
+    assert bench.ncu_traffic("c3", 64, 1) == (None, "null (no ncu capture of this workload)")
