@@ -474,6 +474,11 @@ def paged_prefill(q: torch.Tensor, pool: PagePool, page_table: torch.Tensor, pag
     position <= ``q_positions[b, m]`` (default m).  ``page_positions`` [B, Ht, W]
     (int32) gives the position of row 0 of each slot's page directly instead.
     Rows that see no key are 0.
+
+    ``kernel``: "auto" runs the tcgen05 kernel when it applies (head_dim 128,
+    page_size 8..64, at most 1024 table slots, 16-byte aligned pools, a
+    positive ``sm_scale``) and the CUDA-core kernel otherwise; "tensor" raises
+    on calls outside those bounds; "generic" always runs the CUDA-core kernel.
     """
     _require_cuda(q, "q")
     if q.dim() != 4:
