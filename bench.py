@@ -72,9 +72,12 @@ def workload(name: str) -> dict:
                     mix={"F16": 0.1, "FP8": 0.3, "INT8": 0.3, "INT4": 0.3}, scale_mode="page", q_std=1.0,
                     outliers=0.0, seed=1005)
     if name == "c1":
+        # formats by position: tokens 0-127 (system) FP16, 128-1023 (retrieved) INT8,
+        # 1024-1279 (tool output) not selected, 1280-1439 (recent) FP16
         return dict(name="C1 CPU-runnable MHA decode", B=1, Hq=8, Hkv=8, D=64, T=1440, PS=16,
                     head_tokens=128, tail_tokens=160, attend_block_pages=56, select_pages=74,
-                    mix={"F16": 0.5, "INT8": 0.5}, scale_mode="page", q_std=1.0, outliers=0.0, seed=1001)
+                    mix={"F16": 0.5, "INT8": 0.5}, scale_mode="page", q_std=1.0, outliers=0.0, seed=1001,
+                    format_by_token=[(0, 128, "F16"), (128, 1024, "INT8"), (1280, 1440, "F16")])
     raise SystemExit(f"unknown workload {name}")
 
 
@@ -101,6 +104,13 @@ def select_pages(w: dict):
     meta = routing_to_kernel_metadata(router.route_layout(BlockLayout(blocks), T), PS)
     ids = np.asarray(meta["selected_page_ids"], dtype=np.int32)
     n = ids.size
+    if "format_by_token" in w:
+        fmt = np.zeros(n, np.uint8)
+        for t0, t1, name in w["format_by_token"]:
+            fmt[(ids * PS >= t0) & (ids * PS < t1)] = FMT_CODE[name]
+        if (fmt == 0).any():
+            raise SystemExit("a selected page has no format in format_by_token")
+        return ids, fmt
     names = list(w["mix"].keys())
     counts = [int(round(w["mix"][k] * n)) for k in names]
     counts[-1] = n - sum(counts[:-1])
@@ -141,56 +151,118 @@ def step_bytes(w: dict, fmt: np.ndarray) -> int:
 #  CPU (reference algorithm) timing on a bounded sample
 # --------------------------------------------------------------------------- #
 
-def cpu_reference_step(w: dict, ids: np.ndarray, fmt: np.ndarray, budget_s: float = 12.0, max_units: int = 64):
-    """Time the numpy oracle decode over sampled (b, kv head) units; extrapolate
-    to the full step.  Returns (seconds per full step, units timed, cores)."""
-    import concurrent.futures as cf
-    from oracle import decode as odec
-    from oracle import quant as oq
-    cores = len(os.sched_getaffinity(0))
-    D, PS, G = w["D"], w["PS"], w["Hq"] // w["Hkv"]
-    n = ids.size
-    rng = np.random.default_rng(w["seed"] + 7)
-    tag_map = {1: "F16", 2: "FP8", 3: "INT8", 4: "INT4", 5: "INT4R"}
+class CpuDecodeSample:
+    """The numpy oracle's decode (the reference algorithm restated, pinned to the
+    reference's own outputs by the tests) of (sequence, kv head) units of a
+    workload, on the host cores.  Four distinct units of the workload's page
+    count and format mix are built once and cycled."""
 
-    def build_unit():
-        k = rng.standard_normal((n, PS, D)).astype(np.float32)
-        v = rng.standard_normal((n, PS, D)).astype(np.float32)
-        pools = {"k_f16": k.astype(np.float16), "v_f16": v.astype(np.float16)}
-        sc = {}
-        for plane, x in (("k", k), ("v", v)):
-            if any(f in (2, 3, 4, 5) for f in fmt):
-                r8 = oq.quantize_pages(x, "INT8", w["scale_mode"])
-                pools[f"{plane}_i8"] = r8["codes"]
-                sc[f"{plane}_scale"] = r8["scale"]
-                pools[f"{plane}_fp8"] = oq.f32_to_e4m3(x / oq.expand_scales(r8["scale"], w["scale_mode"], D))
-                r4 = oq.quantize_pages(x, "INT4_RESIDUAL", w["scale_mode"])
-                pools[f"{plane}_i4"] = oq.pack_int4(r4["codes"])
-                pools[f"{plane}_i4r"] = oq.pack_int4(r4["res_codes"])
-                sc[f"{plane}_res_scale"] = r4["res_scale"]
-        q = rng.standard_normal((G, D)).astype(np.float32) * w["q_std"]
-        return q, pools, sc
+    def __init__(self, w: dict, ids: np.ndarray, fmt: np.ndarray):
+        from oracle import quant as oq
+        self.w, self.fmt = w, fmt
+        self.cores = len(os.sched_getaffinity(0))
+        D, PS, G = w["D"], w["PS"], w["Hq"] // w["Hkv"]
+        n = ids.size
+        rng = np.random.default_rng(w["seed"] + 7)
+        self.units_total = w["B"] * w["Hkv"]
+        self.bytes_per_unit = step_bytes(w, fmt) / self.units_total
 
-    units_total = w["B"] * w["Hkv"]
-    data = [build_unit() for _ in range(min(4, units_total))]
-    tags = fmt.astype(np.int64)
-    pids = np.arange(n)
+        def build_unit():
+            k = rng.standard_normal((n, PS, D)).astype(np.float32)
+            v = rng.standard_normal((n, PS, D)).astype(np.float32)
+            pools = {"k_f16": k.astype(np.float16), "v_f16": v.astype(np.float16)}
+            sc = {}
+            for plane, x in (("k", k), ("v", v)):
+                if any(f in (2, 3, 4, 5) for f in fmt):
+                    r8 = oq.quantize_pages(x, "INT8", w["scale_mode"])
+                    pools[f"{plane}_i8"] = r8["codes"]
+                    sc[f"{plane}_scale"] = r8["scale"]
+                    pools[f"{plane}_fp8"] = oq.f32_to_e4m3(x / oq.expand_scales(r8["scale"], w["scale_mode"], D))
+                    r4 = oq.quantize_pages(x, "INT4_RESIDUAL", w["scale_mode"])
+                    pools[f"{plane}_i4"] = oq.pack_int4(r4["codes"])
+                    pools[f"{plane}_i4r"] = oq.pack_int4(r4["res_codes"])
+                    sc[f"{plane}_res_scale"] = r4["res_scale"]
+            q = rng.standard_normal((G, D)).astype(np.float32) * w["q_std"]
+            return q, pools, sc
 
-    def one(i):
-        q, pools, sc = data[i % len(data)]
-        return odec.unit_partial(q, pids, tags, tag_map, "SKIP", pools, sc, w["scale_mode"], 1.0 / math.sqrt(D))
+        self.data = [build_unit() for _ in range(min(4, self.units_total))]
+        self.tags = fmt.astype(np.int64)
+        self.pids = np.arange(n)
 
-    # numpy's BLAS uses every core for the matmuls; a thread pool overlaps the
-    # per-unit gather / dequantisation work across cores as well
-    done = 0
-    t0 = time.perf_counter()
-    with cf.ThreadPoolExecutor(max_workers=cores) as ex:
-        while done < min(units_total, max_units) and time.perf_counter() - t0 < budget_s:
-            batch = min(cores, units_total - done)
-            list(ex.map(one, range(done, done + batch)))
-            done += batch
-    dt = time.perf_counter() - t0
-    return dt * units_total / done, done, cores
+    def _one(self, i):
+        from oracle import decode as odec
+        q, pools, sc = self.data[i % len(self.data)]
+        return odec.unit_partial(q, self.pids, self.tags, {1: "F16", 2: "FP8", 3: "INT8", 4: "INT4", 5: "INT4R"},
+                                 "SKIP", pools, sc, self.w["scale_mode"], 1.0 / math.sqrt(self.w["D"]))
+
+    def run_for(self, budget_s: float, max_units: int = 0):
+        """Decode whole waves of one unit per core until ``budget_s`` has passed
+        (at least one wave, at most ``max_units`` units when given).  Returns
+        (seconds, units decoded); nothing is extrapolated."""
+        import concurrent.futures as cf
+        # numpy's BLAS uses every core for the matmuls; a thread pool overlaps the
+        # per-unit gather / dequantisation work across cores as well
+        limit = max_units or 1 << 30
+        done = 0
+        t0 = time.perf_counter()
+        with cf.ThreadPoolExecutor(max_workers=self.cores) as ex:
+            while done < limit and (done == 0 or time.perf_counter() - t0 < budget_s):
+                batch = min(self.cores, limit - done)
+                list(ex.map(self._one, range(done, done + batch)))
+                done += batch
+        return time.perf_counter() - t0, done
+
+
+def cpu_baseline_record(sample: CpuDecodeSample, budget_s: float) -> dict:
+    """The ``cpu_baseline`` object: the numpy port's selected-KV rate on a bounded sample."""
+    sec, units = sample.run_for(budget_s)
+    return {"value": round(units * sample.bytes_per_unit / sec / 1e9, 4), "unit": "GB/s", "cores": sample.cores,
+            "kind": "port", "seconds": round(sec, 3), "units_timed": units, "units_per_step": sample.units_total,
+            "sample": f"{units} of the step's {sample.units_total} (sequence, kv head) units decoded by the numpy "
+                      f"oracle on {sample.cores} host threads in {sec:.2f} s; value = their selected-KV bytes / "
+                      "that time"}
+
+
+REFERENCE_TIMING = os.path.join(ROOT, "oracle", "reference_cpu_timing.json")
+
+
+def reference_cpu_record(workload_name: str):
+    """The reference's own CPU decode paths (fused_selected_quant_decode_reference and
+    intent_quant_attention_reference) timed on C2-shaped samples by
+    oracle/time_reference_cpu.py in the build container (the reference is pure Python
+    and is not installed on the GPU box), or None for other workloads."""
+    if workload_name != "c2":
+        return None
+    try:
+        with open(REFERENCE_TIMING) as f:
+            t = json.load(f)
+    except (OSError, ValueError):
+        return None
+    fr = t["fused_selected_quant_decode_reference"]
+    return {"value": fr["value_gbs"], "unit": "GB/s", "cores": t["cores"], "kind": "reference",
+            "seconds_per_step": fr["seconds_per_step"], "sample": fr["sample"],
+            "oracle_path_value": t["intent_quant_attention_reference"]["value_gbs"],
+            "oracle_path_sample": t["intent_quant_attention_reference"]["sample"],
+            "measured_on": t["measured_on"], "source": "oracle/reference_cpu_timing.json"}
+
+
+def workload_config(w: dict, n_sel_total: int, n_sel_rank: int, world: int, seq_shard: bool, nbytes_rank: int,
+                    exchange: str) -> dict:
+    """The ``config`` object both arms print for a decode workload."""
+    return {"workload": w["name"], "batch_per_gpu": w["B"], "global_batch": w["B"] * (1 if seq_shard else world),
+            "q_heads": w["Hq"], "kv_heads": w["Hkv"], "head_dim": w["D"], "ctx": w["T"],
+            "page_size": w["PS"], "selected_pages_per_seq_head": n_sel_total,
+            "selected_pages_per_seq_head_per_gpu": n_sel_rank,
+            "format_mix": ({f"tokens {a}-{b - 1}": f for a, b, f in w["format_by_token"]}
+                           if "format_by_token" in w else w["mix"]),
+            "scale_mode": w["scale_mode"], "selected_kv_bytes_per_step_per_gpu": nbytes_rank,
+            "l2": l2_note(nbytes_rank, "selected KV"),
+            "parallelism": (f"sp{world} (each sequence's selected pages cut into {world} ranges; partial "
+                            "(m, l, acc) blocks exchanged "
+                            + ("by NVLink peer stores with epoch flags (CUDA IPC)" if exchange == "p2p"
+                               else "with one NCCL all-gather")
+                            + ", LSE-merged on every rank)")
+            if seq_shard else f"dp{world} (batch shards, no collective on the data path)"}
 
 
 # --------------------------------------------------------------------------- #
@@ -473,21 +545,9 @@ def run_gpu(args):
             "warmup": args.warmup, "ms_per_step": round(t_ms, 5), "us_per_step": round(t_ms * 1e3, 2),
             "higher_is_better": True, "scaling": "strong" if seq_shard else "weak", "vs_baseline": None, "dtype": "fp16/fp8/int8 pages, fp32 acc",
             "data": "synthetic (seeded N(0,1) K/V with 1% x8 outliers, bf16 Q)",
-            "config": {"workload": w["name"], "batch_per_gpu": w["B"], "global_batch": w["B"] * (1 if seq_shard else world),
-                       "q_heads": w["Hq"], "kv_heads": w["Hkv"], "head_dim": w["D"], "ctx": w["T"],
-                       "page_size": w["PS"], "selected_pages_per_seq_head": n_sel_total,
-                       "selected_pages_per_seq_head_per_gpu": int(ids.size),
-                       "format_mix": w["mix"], "scale_mode": w["scale_mode"],
-                       "selected_kv_bytes_per_step_per_gpu": nbytes,
-                       "l2": l2_note(nbytes, "selected KV"),
-                       "timing": ("one CUDA graph of all timed steps, replayed once after a warm-up replay"
-                                  if use_graph else "eager launches"),
-                       "parallelism": (f"sp{world} (each sequence's selected pages cut into {world} ranges; partial "
-                                       "(m, l, acc) blocks exchanged "
-                                       + ("by NVLink peer stores with epoch flags (CUDA IPC)" if args.exchange == "p2p"
-                                          else "with one NCCL all-gather")
-                                       + ", LSE-merged on every rank)")
-                       if seq_shard else f"dp{world} (batch shards, no collective on the data path)"},
+            "config": workload_config(w, n_sel_total, int(ids.size), world, seq_shard, nbytes, args.exchange),
+            "timing": ("one CUDA graph of all timed steps, replayed once after a warm-up replay"
+                       if use_graph else "eager launches"),
             "roofline": {"bound": "hbm", "achieved": round(kernel_gbs, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(kernel_gbs / peak, 4), "traffic": traffic,
                          "kernel": "decode_mma_kernel", "kernel_us": round(kernel_ms * 1e3, 2),
@@ -505,11 +565,10 @@ def run_gpu(args):
             "clocks": clocks.summary(),
         }
         if world == 1 and not args.no_cpu_baseline:
-            sec, units, cores = cpu_reference_step(w, ids, fmt, budget_s=args.cpu_budget)
-            rec["cpu_baseline"] = {"value": round(nbytes / sec / 1e9, 4), "unit": "GB/s", "cores": cores,
-                                   "kind": "port", "seconds_per_step": round(sec, 3),
-                                   "sample": f"{units} of {w['B'] * w['Hkv']} (sequence, kv-head) units timed with the "
-                                             "numpy oracle decode, extrapolated linearly to the full step"}
+            rec["cpu_baseline"] = cpu_baseline_record(CpuDecodeSample(w, ids, fmt), args.cpu_budget)
+            ref_rec = reference_cpu_record(args.workload)
+            if ref_rec is not None:
+                rec["cpu_baseline_reference"] = ref_rec
         print(json.dumps(rec), flush=True)
     if decoder is not None:
         if decoder._x is not None:
@@ -522,6 +581,14 @@ def run_gpu(args):
 
 
 def run_reference(args):
+    """The reference arm: the reference algorithm's CPU implementation on the host
+    cores (the numpy port that the tests pin to the reference's own outputs), on
+    the same workload and config as the GPU arm.  Each step decodes a bounded
+    sample of the workload's (sequence, kv head) units, whole waves of one unit
+    per host thread for at least ``--ref-step-s`` seconds; ``value`` is the
+    sample's selected-KV bytes / its measured time and ``ms_per_step`` the
+    sample's measured time (nothing is extrapolated).  Under torchrun rank 0
+    alone runs."""
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -529,25 +596,42 @@ def run_reference(args):
     if args.workload == "c4":
         return run_reference_mla(args, world)
     w = workload(args.workload)
+    if args.batch:
+        w["B"] = args.batch
     ids, fmt = select_pages(w)
-    nbytes = step_bytes(w, fmt)
-    vals = []
-    cores = units = None
+    n_sel_total = int(ids.size)
+    seq_shard = args.workload == "c5" and world > 1
+    ids_r, fmt_r = ids, fmt
+    if seq_shard:
+        from intent_attention.split_kv import shard_bounds
+        a, b = shard_bounds(ids.size, 0, world)
+        ids_r, fmt_r = ids[a:b], fmt[a:b]
+        w["name"] = "C5 long-context decode, sequence-sharded split-KV"
+    sample = CpuDecodeSample(w, ids, fmt)
+    rates, secs, units = [], [], []
     for i in range(args.warmup + args.steps):
-        sec, units, cores = cpu_reference_step(w, ids, fmt, budget_s=args.cpu_budget / max(1, args.steps),
-                                               max_units=64)
+        sec, n = sample.run_for(args.ref_step_s)
         if i >= args.warmup:
-            vals.append(sec)
-    sec = statistics.median(vals)
-    v = nbytes / sec / 1e9
+            rates.append(n * sample.bytes_per_unit / sec)
+            secs.append(sec)
+            units.append(n)
+    v = statistics.median(rates) / 1e9
     rec = {"impl": "reference", "metric": METRIC, "value": round(v, 4), "unit": "GB/s", "n_gpus": world,
-           "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(sec * 1e3, 3),
-           "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32 (numpy)",
-           "data": "synthetic", "config": {"workload": w["name"], "batch": w["B"], "q_heads": w["Hq"],
-                                           "kv_heads": w["Hkv"], "head_dim": w["D"], "ctx": w["T"]},
-           "cpu_baseline": {"value": round(v, 4), "unit": "GB/s", "cores": cores, "kind": "port",
-                            "sample": f"{units} (sequence, kv-head) units per step, extrapolated to the full step"},
+           "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(statistics.median(secs) * 1e3, 3),
+           "higher_is_better": True, "scaling": "strong" if seq_shard else "weak", "vs_baseline": None,
+           "dtype": "fp32 dequantisation, fp64 attention (numpy)", "data": "synthetic",
+           "config": workload_config(w, n_sel_total, int(ids_r.size), world, seq_shard, step_bytes(w, fmt_r),
+                                     args.exchange),
+           "step": (f"a sample of {int(statistics.median(units))} of the step's {sample.units_total} (sequence, kv "
+                    "head) units (median over steps) decoded on the host cores; ms_per_step is the sample's "
+                    "measured time"),
+           "cpu_baseline": {"value": round(v, 4), "unit": "GB/s", "cores": sample.cores, "kind": "port",
+                            "sample": f"whole waves of {sample.cores} (sequence, kv head) units per step, at least "
+                                      f"{args.ref_step_s} s each, numpy oracle decode of the workload's pages"},
            "e2e": {"value": round(v, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    ref_rec = reference_cpu_record(args.workload)
+    if ref_rec is not None:
+        rec["cpu_baseline_reference"] = ref_rec
     print(json.dumps(rec), flush=True)
 
 
@@ -616,56 +700,78 @@ def build_mla_workload(w: dict, ids: np.ndarray, tags_sel: np.ndarray, device, r
     return dense, fp8, scale, tags, table, q
 
 
-def cpu_mla_step(w: dict, ids: np.ndarray, tags_sel: np.ndarray, budget_s: float = 12.0, max_seqs: int = 16):
-    """Time the numpy oracle's per-head MLA decode over sampled sequences and
-    extrapolate to the batch.  Returns (seconds per step, sequences timed, cores)."""
-    import concurrent.futures as cf
-    from oracle import mla as omla
-    from oracle import quant as oq
-    cores = len(os.sched_getaffinity(0))
-    PS, Dqk, Dv, H = w["PS"], w["Dqk"], w["Dv"], w["H"]
-    n = ids.size
-    rng = np.random.default_rng(w["seed"] + 7)
-    lat = rng.standard_normal((n, PS, Dqk)).astype(np.float32)
-    scale = np.maximum(np.abs(lat).reshape(n, -1).max(1) / 127.0, 1e-8).astype(np.float32)
-    pools = {"bf16": lat, "fp8": oq.f32_to_e4m3(lat / scale[:, None, None])}
-    q = rng.standard_normal((1, H, Dqk)).astype(np.float32)
-    table = np.arange(n)[None, :]
-    tags = tags_sel.astype(np.int64)
+class CpuMlaSample:
+    """The numpy oracle's per-head MLA decode of whole sequences of the C4
+    workload on the host cores (one sequence's latents built once, reused)."""
 
-    def one(_):
-        return omla.mla_paged_decode(q, table, None, tags, pools, scale, Dv, 1.0 / math.sqrt(Dqk))
+    def __init__(self, w: dict, ids: np.ndarray, tags_sel: np.ndarray):
+        from oracle import quant as oq
+        self.w = w
+        self.cores = len(os.sched_getaffinity(0))
+        PS, Dqk, H = w["PS"], w["Dqk"], w["H"]
+        n = ids.size
+        rng = np.random.default_rng(w["seed"] + 7)
+        lat = rng.standard_normal((n, PS, Dqk)).astype(np.float32)
+        self.scale = np.maximum(np.abs(lat).reshape(n, -1).max(1) / 127.0, 1e-8).astype(np.float32)
+        self.pools = {"bf16": lat, "fp8": oq.f32_to_e4m3(lat / self.scale[:, None, None])}
+        self.q = rng.standard_normal((1, H, Dqk)).astype(np.float32)
+        self.table = np.arange(n)[None, :]
+        self.tags = tags_sel.astype(np.int64)
+        self.bytes_per_seq = mla_bytes_flops(w, tags_sel)[0] / w["B"]
 
-    done = 0
-    t0 = time.perf_counter()
-    with cf.ThreadPoolExecutor(max_workers=cores) as ex:
-        while done < min(w["B"], max_seqs) and time.perf_counter() - t0 < budget_s:
-            k = min(cores, w["B"] - done)
-            list(ex.map(one, range(k)))
-            done += k
-    dt = time.perf_counter() - t0
-    return dt * w["B"] / done, done, cores
+    def _one(self, _):
+        from oracle import mla as omla
+        return omla.mla_paged_decode(self.q, self.table, None, self.tags, self.pools, self.scale, self.w["Dv"],
+                                     1.0 / math.sqrt(self.w["Dqk"]))
+
+    def run_for(self, budget_s: float):
+        """Whole waves of one sequence per core until ``budget_s`` has passed (at
+        least one wave).  Returns (seconds, sequences decoded)."""
+        import concurrent.futures as cf
+        done = 0
+        t0 = time.perf_counter()
+        with cf.ThreadPoolExecutor(max_workers=self.cores) as ex:
+            while done == 0 or time.perf_counter() - t0 < budget_s:
+                list(ex.map(self._one, range(self.cores)))
+                done += self.cores
+        return time.perf_counter() - t0, done
+
+
+def mla_config(w: dict, ids: np.ndarray, tags_sel: np.ndarray, world: int) -> dict:
+    """The ``config`` object both arms print for the C4 workload."""
+    nbytes, flops = mla_bytes_flops(w, tags_sel)
+    return {"workload": w["name"], "batch_per_gpu": w["B"], "global_batch": w["B"] * world,
+            "q_heads": w["H"], "d_qk": w["Dqk"], "d_v": w["Dv"], "ctx": w["T"], "page_size": w["PS"],
+            "selected_pages_per_seq": int(ids.size), "bf16_pages_per_seq": int((tags_sel == 0).sum()),
+            "fp8_pages_per_seq": int((tags_sel == 1).sum()),
+            "selected_kv_bytes_per_step_per_gpu": nbytes, "flops_per_step_per_gpu": flops,
+            "l2": l2_note(nbytes, "selected latents"),
+            "parallelism": f"dp{world} (batch shards, no collective on the data path)"}
 
 
 def run_reference_mla(args, world):
     w = dict(C4)
+    if args.batch:
+        w["B"] = args.batch
     ids, tags_sel = select_mla_pages(w)
-    nbytes, _ = mla_bytes_flops(w, tags_sel)
-    vals = []
-    seqs = cores = None
+    sample = CpuMlaSample(w, ids, tags_sel)
+    rates, secs, seqs = [], [], []
     for i in range(args.warmup + args.steps):
-        sec, seqs, cores = cpu_mla_step(w, ids, tags_sel, budget_s=args.cpu_budget / max(1, args.steps), max_seqs=4)
+        sec, n = sample.run_for(args.ref_step_s)
         if i >= args.warmup:
-            vals.append(sec)
-    sec = statistics.median(vals)
-    v = nbytes / sec / 1e9
+            rates.append(n * sample.bytes_per_seq / sec)
+            secs.append(sec)
+            seqs.append(n)
+    v = statistics.median(rates) / 1e9
     rec = {"impl": "reference", "metric": METRIC, "value": round(v, 4), "unit": "GB/s", "n_gpus": world,
-           "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(sec * 1e3, 3),
+           "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(statistics.median(secs) * 1e3, 3),
            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp64 (numpy)",
-           "data": "synthetic", "config": {"workload": w["name"], "batch": w["B"], "q_heads": w["H"],
-                                           "d_qk": w["Dqk"], "d_v": w["Dv"], "ctx": w["T"]},
-           "cpu_baseline": {"value": round(v, 4), "unit": "GB/s", "cores": cores, "kind": "port",
-                            "sample": f"{seqs} sequences per step, extrapolated to the full batch"},
+           "data": "synthetic", "config": mla_config(w, ids, tags_sel, world),
+           "step": (f"a sample of {int(statistics.median(seqs))} of the step's {w['B']} sequences (median over "
+                    "steps) decoded on the host cores; ms_per_step is the sample's measured time"),
+           "cpu_baseline": {"value": round(v, 4), "unit": "GB/s", "cores": sample.cores, "kind": "port",
+                            "sample": f"whole waves of {sample.cores} sequences per step, at least "
+                                      f"{args.ref_step_s} s each, numpy oracle per-head MLA decode"},
            "e2e": {"value": round(v, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(rec), flush=True)
 
@@ -777,13 +883,7 @@ def run_gpu_mla(args):
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "bf16/fp8-e4m3 latent pages, f16 tensor-core operands, fp32 acc",
             "data": "synthetic (seeded N(0,1) latents and bf16 Q)",
-            "config": {"workload": w["name"], "batch_per_gpu": w["B"], "global_batch": w["B"] * world,
-                       "q_heads": w["H"], "d_qk": w["Dqk"], "d_v": w["Dv"], "ctx": w["T"], "page_size": w["PS"],
-                       "selected_pages_per_seq": n_sel, "bf16_pages_per_seq": int((tags_sel == 0).sum()),
-                       "fp8_pages_per_seq": int((tags_sel == 1).sum()),
-                       "selected_kv_bytes_per_step_per_gpu": nbytes, "flops_per_step_per_gpu": flops,
-                       "l2": l2_note(nbytes, "selected latents"),
-                       "parallelism": f"dp{world} (batch shards, no collective on the data path)"},
+            "config": mla_config(w, ids, tags_sel, world),
             "roofline": {"bound": "tensor", "achieved": round(tflops, 1), "peak": tc_peak, "unit": "TFLOP/s",
                          "frac": round(tflops / tc_peak, 4), "traffic": ncu_traffic("c4", w["B"], nbytes)[0],
                          "traffic_note": ncu_traffic("c4", w["B"], nbytes)[1], "kernel": "mla_tc_kernel",
@@ -802,11 +902,13 @@ def run_gpu_mla(args):
             "clocks": clocks.summary(),
         }
         if world == 1 and not args.no_cpu_baseline:
-            sec, seqs, cores = cpu_mla_step(w, ids, tags_sel, budget_s=args.cpu_budget)
-            rec["cpu_baseline"] = {"value": round(nbytes / sec / 1e9, 4), "unit": "GB/s", "cores": cores,
-                                   "kind": "port", "seconds_per_step": round(sec, 3),
-                                   "sample": f"{seqs} of {w['B']} sequences timed with the numpy oracle's per-head "
-                                             "MLA decode, extrapolated linearly to the full step"}
+            mla_sample = CpuMlaSample(w, ids, tags_sel)
+            sec, seqs = mla_sample.run_for(args.cpu_budget)
+            rec["cpu_baseline"] = {"value": round(seqs * mla_sample.bytes_per_seq / sec / 1e9, 4), "unit": "GB/s",
+                                   "cores": mla_sample.cores, "kind": "port", "seconds": round(sec, 3),
+                                   "sample": f"{seqs} sequences decoded by the numpy oracle's per-head MLA decode "
+                                             f"on {mla_sample.cores} host threads in {sec:.2f} s; value = their "
+                                             "selected latent bytes / that time"}
         print(json.dumps(rec), flush=True)
     if world > 1:
         dist.barrier()
@@ -1315,11 +1417,19 @@ def main():
     ap.add_argument("--exchange", default="p2p", choices=["p2p", "nccl"],
                     help="C5 on several GPUs: partial blocks over NVLink peer stores or one NCCL all-gather")
     ap.add_argument("--no-graph", action="store_true", help="time eager launches instead of a captured CUDA graph")
-    ap.add_argument("--cpu-budget", type=float, default=12.0)
+    ap.add_argument("--cpu-budget", type=float, default=12.0,
+                    help="seconds of host work for the GPU arm's cpu_baseline sample")
+    ap.add_argument("--ref-step-s", type=float, default=0.5,
+                    help="--impl reference: at least this many seconds of host work per step")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if args.gpus != world:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE is {world}: launch one process per GPU "
+                         f"(python -m torch.distributed.run --nproc-per-node {args.gpus} ... bench.py --gpus "
+                         f"{args.gpus}), or pass --gpus {world}")
     if args.warmup < 3:
-        args.warmup = 3
+        raise SystemExit(f"--warmup {args.warmup}: at least 3 untimed warm-up steps are required")
     if args.workload == "route":
         run_route(args)
     elif args.workload == "append":

@@ -44,7 +44,7 @@
 extern "C" {
 #endif
 
-#define IAK_ABI_VERSION 1
+#define IAK_ABI_VERSION 2
 
 typedef enum iak_status {
   IAK_OK = 0,
@@ -120,13 +120,36 @@ typedef struct iak_decode_args {
   float* partial_m; float* partial_l; float* partial_acc;
   int32_t num_splits;             /* 0 = choose automatically               */
   int32_t kernel;                 /* IAK_KERNEL_*: 0 auto, 1 generic, 2 tensor core */
+  /* Device-side waits.  The tensor-core decode is a pipeline of warps that
+   * wait on one another (page copies, stage release); each wait gives up
+   * after wait_budget_ns nanoseconds (0 = the default of about 2 s), after
+   * which the kernel stops, lets the copies it issued land and, when status
+   * is non-NULL, ORs IAK_STATUS_DECODE_TIMEOUT into *status (device memory;
+   * never cleared by the library, so one word can collect many calls).  The
+   * output of a call that timed out is undefined.  iak_device_status reads
+   * the process-wide counters instead. */
+  uint32_t* status;
+  uint32_t wait_budget_ns;
 } iak_decode_args;
+
+/* bits of iak_decode_args.status */
+enum { IAK_STATUS_DECODE_TIMEOUT = 1 };
 
 /* decode kernel selection (iak_decode_args.kernel) */
 enum { IAK_KERNEL_AUTO = 0, IAK_KERNEL_GENERIC = 1, IAK_KERNEL_TENSOR = 2 };
 
 int iak_version(void);
 const char* iak_last_error(void);
+
+/* Timeout counters of the current device (no counterpart in the reference).
+ * Every kernel warp whose bounded wait gave up adds one to its kernel's
+ * counter: the tensor-core decode (iak_decode / iak_decode_noalloc), the
+ * tcgen05 MLA decode and the tcgen05 prefill.  Copies the three counters to
+ * the non-NULL outputs and, when reset != 0, sets them back to zero.  Waits
+ * for the device (a synchronous copy); returns IAK_ERR_TIMEOUT when any
+ * counter read was non-zero, else IAK_OK. */
+int iak_device_status(uint32_t* decode_timeouts, uint32_t* mla_timeouts, uint32_t* prefill_timeouts,
+                      int32_t reset);
 
 /* Workspace (device bytes) iak_decode needs for these arguments. */
 int iak_decode_workspace_size(const iak_page_pools* pools, const iak_decode_args* args,
@@ -151,7 +174,10 @@ int iak_decode(const iak_page_pools* pools, const iak_decode_args* args,
  * iak_decode_workspace_size exceeds it are rejected with IAK_ERR_WORKSPACE
  * (pass fewer num_splits, or use iak_decode).  The first call on a device
  * looks up the array's device address with that device current, so make that
- * first call before any stream capture.  All calls share the one array and it
+ * first call before any stream capture.  The address is cached per device for
+ * the life of the process and belongs to the device's primary context: do not
+ * use the entry point after cudaDeviceReset of that device, nor with another
+ * driver context current.  All calls share the one array and it
  * keeps the last call's contents (nothing in it needs to start at zero):
  * calls that overlap on the GPU, on any streams, race.  Calls no cudaMalloc,
  * cudaFree or allocating library routine. */

@@ -50,6 +50,20 @@ int device_sm_count() {
   return cache[dev];
 }
 
+int device_clock_khz() {
+  static std::mutex mu;
+  static int cache[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 1965000;
+  std::lock_guard<std::mutex> lock(mu);
+  if (cache[dev] == 0) {
+    int k = 0;
+    if (cudaDeviceGetAttribute(&k, cudaDevAttrClockRate, dev) != cudaSuccess || k <= 0) k = 1965000;
+    cache[dev] = k;
+  }
+  return cache[dev];
+}
+
 // Process-wide kernel timer: event pairs recorded around the main decode launch.
 struct KernelTimer {
   std::mutex mu;
@@ -160,6 +174,10 @@ static int prepare(const iak_page_pools* P, const iak_decode_args* a, DecodePara
   std::memcpy(p->tag_map, a->tag_map, 16); p->tag_default = a->tag_default;
   p->sm_scale = a->sm_scale;
   p->ex_m = a->partial_m; p->ex_l = a->partial_l; p->ex_acc = a->partial_acc;
+  p->status = a->status;
+  p->wait_cycles = a->wait_budget_ns == 0
+                       ? kDefaultWaitCycles
+                       : std::max<long long>(1, static_cast<long long>(a->wait_budget_ns) * device_clock_khz() / 1000000);
   if (p->ex_l && (!p->ex_m || !p->ex_acc)) return fail(IAK_ERR_INVALID_ARG, "partial export needs m, l and acc");
   const int64_t units = static_cast<int64_t>(a->batch) * a->num_table_heads;
   if (a->kernel < 0 || a->kernel > 2) return fail(IAK_ERR_INVALID_ARG, "bad kernel selector %d", a->kernel);
@@ -229,6 +247,21 @@ using namespace iak;
 extern "C" {
 
 int iak_version(void) { return IAK_ABI_VERSION; }
+
+int iak_device_status(uint32_t* decode_timeouts, uint32_t* mla_timeouts, uint32_t* prefill_timeouts,
+                      int32_t reset) {
+  unsigned int v[3] = {0, 0, 0};
+  int st = read_decode_timeouts(&v[0], reset != 0);
+  if (!st) st = read_mla_timeouts(&v[1], reset != 0);
+  if (!st) st = read_prefill_timeouts(&v[2], reset != 0);
+  if (st) return st;
+  if (decode_timeouts) *decode_timeouts = v[0];
+  if (mla_timeouts) *mla_timeouts = v[1];
+  if (prefill_timeouts) *prefill_timeouts = v[2];
+  if (v[0] || v[1] || v[2])
+    return fail(IAK_ERR_TIMEOUT, "device-side waits gave up: decode %u, mla %u, prefill %u warps", v[0], v[1], v[2]);
+  return IAK_OK;
+}
 
 const char* iak_last_error(void) { return g_last_error.c_str(); }
 

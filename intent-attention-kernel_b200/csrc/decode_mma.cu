@@ -60,7 +60,7 @@ constexpr int kStageBytes = 9216;   // K region 4 KB | V region 4 KB | scale row
 constexpr int kVOff = 4096;
 constexpr int kResOff = 1024;       // INT4 residual plane inside a K or V region
 constexpr int kScaleOff = 8192;
-constexpr long long kWaitCycles = 4000000000LL;  // ~2 s at boost clock, then give up
+constexpr long long kWaitCycles = kDefaultWaitCycles;  // budget of the drain waits
 #ifndef IAK_F16_ONE_BOX
 #define IAK_F16_ONE_BOX 1
 #endif
@@ -81,8 +81,10 @@ struct TmaMaps {
 
 // Per-unit query table (built by decode_prep_kernel, bulk-copied per work item):
 // fp16 fragments [D/16][32] uint4 | int8 terms [D/32][32] uint4 | the same in
-// INT4 order | 128 floats: term scales s1[8], s2[8], int4 biases [4][8] x 2.
+// INT4 order | 128 floats: term scales s1[8], s2[8], int4 biases [4][8] x 2,
+// and at kQScF the power-of-two factor of each query head's fp16 fragments.
 constexpr int kQFrag = 0, kQI8 = 4096, kQI4 = 6144, kQSc = 8192, kQTab = 8704;
+constexpr int kQScF = 80;
 
 // One work-item buffer: query table | page ids | 4 scale scalars | formats | meta.
 struct ItemLayout {
@@ -122,13 +124,26 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Bounded wait: false when the phase did not complete within kWaitCycles.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
-  if (mbar_try_wait(bar, parity)) return true;
+__device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait: false when the phase did not complete within `budget` SM cycles.  The
+// budget is checked between a non-blocking test and each (suspending) try_wait, so a
+// budget shorter than a global-memory round trip gives up on any phase that is not
+// already complete.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, long long budget) {
+  if (mbar_test_wait(bar, parity)) return true;
   const long long t0 = clock64();
-  while (!mbar_try_wait(bar, parity))
-    if (clock64() - t0 > kWaitCycles) return false;
-  return true;
+  while (true) {
+    if (clock64() - t0 > budget) return false;
+    if (mbar_try_wait(bar, parity)) return true;
+  }
 }
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
   asm volatile(
@@ -377,6 +392,7 @@ __global__ void __launch_bounds__(256) decode_prep_kernel(const DecodeParams p, 
   __shared__ float qs[8 * D];
   __shared__ int8_t i1s[8 * D], i2s[8 * D];
   __shared__ float qsc[128];
+  __shared__ float qfi[8];
   const int unit = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int b = unit / p.Ht, hk = unit % p.Ht;
   if (tid < 128) qsc[tid] = 0.f;
@@ -392,6 +408,11 @@ __global__ void __launch_bounds__(256) decode_prep_kernel(const DecodeParams p, 
     for (int e = 0; e < E; ++e) am = fmaxf(am, fabsf(q[e]));
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+    // The fp16 fragments hold q / 2^fe with the head's absmax in [2^14, 2^15): bf16 queries
+    // outside fp16's normal range (|q| > 65504, or below 2^-14) still convert exactly, and the
+    // scores of fp16 / e4m3 pages are multiplied back by 2^fe.
+    const int fe = min(max(((__float_as_int(am) >> 23) & 0xFF) - 127 - 14, -126), 126);
+    if (lane == 0) qfi[g] = __int_as_float((127 - fe) << 23);
     const float s1 = am > 0.f ? am / 127.f : 1.f;
     float t1[E], am2 = 0.f;
 #pragma unroll
@@ -423,6 +444,7 @@ __global__ void __launch_bounds__(256) decode_prep_kernel(const DecodeParams p, 
     if (lane == 0) {
       qsc[g] = s1;
       qsc[8 + g] = s2;
+      qsc[kQScF + g] = __int_as_float((fe + 127) << 23);
     }
     if (lane % GL == 0) {
       const int j = lane / GL;
@@ -435,12 +457,13 @@ __global__ void __launch_bounds__(256) decode_prep_kernel(const DecodeParams p, 
   const int r = lane >> 2, c = lane & 3;
   if (warp == 0) {
     const float* qr = qs + r * D;
+    const float fi = qfi[r];
     uint4* qfrag = reinterpret_cast<uint4*>(out + kQFrag);
+    auto h2 = [&](int d) { return pack_f16x2(qr[d] * fi, qr[d + 1] * fi); };
 #pragma unroll
     for (int kk = 0; kk < KT; ++kk) {
       const int b0 = 16 * kk + 2 * c, b1 = 16 * kk + 4 * c;
-      qfrag[kk * 32 + lane] = make_uint4(pack_f16x2(qr[b0], qr[b0 + 1]), pack_f16x2(qr[b0 + 8], qr[b0 + 9]),
-                                         pack_f16x2(qr[b1], qr[b1 + 1]), pack_f16x2(qr[b1 + 2], qr[b1 + 3]));
+      qfrag[kk * 32 + lane] = make_uint4(h2(b0), h2(b0 + 8), h2(b1), h2(b1 + 2));
     }
   } else if (warp == 1) {
     uint4* qi8 = reinterpret_cast<uint4*>(out + kQI8);
@@ -513,20 +536,30 @@ __global__ void __launch_bounds__(kThreads, IAK_MIN_BLOCKS)
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   }
   __syncthreads();
+  // A role whose bounded wait gives up (p.wait_cycles) stops; every wait result is
+  // made warp-uniform first, so the warp's collectives stay converged.  Before the
+  // CTA exits, the lanes that issued bulk / TMA copies wait (with the default budget)
+  // for the copies they issued, so no copy lands in a finished CTA's shared memory.
   bool timed_out = false;
+  const long long budget = p.wait_cycles;
+  auto wait_all = [&](uint32_t bar, uint32_t parity) {
+    return __all_sync(0xffffffffu, mbar_wait(bar, parity, budget));
+  };
 
   if (warp == kPrepWarp) {
     // -------------------------------------------------------------- preparer
     constexpr int kPer = kChunkMax / 32;
+    int last_k[2] = {-1, -1};   // last item whose query table was copied into each buffer
     for (int k = 0, item = blockIdx.x; item < n_items; ++k, item += gridDim.x) {
       const int buf = k & 1;
       char* ib = item_buf(buf);
-      if (k >= 2 && !mbar_wait(iempty_bar(buf), ((k >> 1) - 1) & 1)) {
+      if (k >= 2 && !wait_all(iempty_bar(buf), ((k >> 1) - 1) & 1)) {
         timed_out = true;
         break;
       }
       int unit, split, lo, hi;
       item_range(p, item, unit, split, lo, hi);
+      last_k[buf] = k;
       if (lane == 0) {
         mbar_arrive_expect_tx(ifull_bar(buf), kQTab);
         bulk_load(smem_u32(ib + ItemLayout::qtab), qtab + static_cast<int64_t>(unit) * kQTab, kQTab, ifull_bar(buf));
@@ -575,13 +608,19 @@ __global__ void __launch_bounds__(kThreads, IAK_MIN_BLOCKS)
       __syncwarp();
       if (lane == 0) mbar_arrive(ifull_bar(buf));
     }
+    // drain: the query-table copies this warp issued
+    for (int b2 = 0; b2 < 2; ++b2)
+      if (lane == 0 && last_k[b2] >= 0 && !mbar_wait(ifull_bar(b2), (last_k[b2] >> 1) & 1, kWaitCycles))
+        timed_out = true;
   } else if (warp == kTmaWarp) {
     // -------------------------------------------------------------- TMA producer
-    int ctr = 0;   // pages issued before the current item
+    constexpr int kProducerLanes = producer_lanes<GROUP>();
+    int ctr = 0;        // pages issued before the current item
+    int g_last = -1;    // ring index of the last stage this lane armed
     for (int k = 0, item = blockIdx.x; item < n_items && !timed_out; ++k, item += gridDim.x) {
       const int buf = k & 1;
       const char* ib = item_buf(buf);
-      if (!mbar_wait(ifull_bar(buf), (k >> 1) & 1)) {
+      if (!wait_all(ifull_bar(buf), (k >> 1) & 1)) {
         timed_out = true;
         break;
       }
@@ -589,16 +628,16 @@ __global__ void __launch_bounds__(kThreads, IAK_MIN_BLOCKS)
       const int n_pad = (n + kStages - 1) & ~(kStages - 1);
       const int32_t* pid_s = reinterpret_cast<const int32_t*>(ib + ItemLayout::pid);
       const uint8_t* fmt_s = reinterpret_cast<const uint8_t*>(ib + ItemLayout::fmt);
-      constexpr int kProducerLanes = producer_lanes<GROUP>();
       if (lane < kProducerLanes) {
         for (int i = lane; i < n_pad; i += kProducerLanes) {
           const int gi = ctr + i;
           const int s = gi & (kStages - 1), round = gi / kStages;
           const uint32_t full = full_bar(s);
-          if (round > 0 && !mbar_wait(empty_bar(s), (round - 1) & 1)) {
+          if (round > 0 && !mbar_wait(empty_bar(s), (round - 1) & 1, budget)) {
             timed_out = true;
             break;
           }
+          g_last = gi;
           if (i >= n) {            // padding slot: completes the stage's phase without data
             mbar_arrive(full);
             continue;
@@ -647,9 +686,16 @@ __global__ void __launch_bounds__(kThreads, IAK_MIN_BLOCKS)
           }
         }
       }
-      __syncwarp();
+      timed_out = __any_sync(0xffffffffu, timed_out);
       ctr += n_pad;
     }
+    // drain: a lane arms its stages in ring order with stride kProducerLanes, so its last
+    // kStages / kProducerLanes arms cover each of its stages once (their latest phase)
+    if (lane < kProducerLanes)
+      for (int j = 0; j < kStages / kProducerLanes; ++j) {
+        const int gi = g_last - j * kProducerLanes;
+        if (gi >= 0 && !mbar_wait(full_bar(gi & (kStages - 1)), (gi / kStages) & 1, kWaitCycles)) timed_out = true;
+      }
   } else {
     // -------------------------------------------------------------- consumers
     const float qk_log2 = p.sm_scale * 1.4426950408889634f;
@@ -658,7 +704,7 @@ __global__ void __launch_bounds__(kThreads, IAK_MIN_BLOCKS)
     for (int k = 0, item = blockIdx.x; item < n_items; ++k, item += gridDim.x) {
       const int buf = k & 1;
       const char* ib = item_buf(buf);
-      if (!mbar_wait(ifull_bar(buf), (k >> 1) & 1)) {
+      if (!wait_all(ifull_bar(buf), (k >> 1) & 1)) {
         timed_out = true;
         break;
       }
@@ -682,7 +728,7 @@ __global__ void __launch_bounds__(kThreads, IAK_MIN_BLOCKS)
       for (int i = warp; i < n_pad; i += kConsumerWarps) {
         const int gi = ctr + i;
         const int s = gi & (kStages - 1), round = gi / kStages;
-        if (!mbar_wait(full_bar(s), round & 1)) {
+        if (!wait_all(full_bar(s), round & 1)) {
           timed_out = true;
           break;
         }
@@ -730,10 +776,13 @@ __global__ void __launch_bounds__(kThreads, IAK_MIN_BLOCKS)
       float sc[4] = {0.f, 0.f, 0.f, 0.f};
       const float s1a = qsc[2 * c], s1b = qsc[2 * c + 1], s2a = qsc[8 + 2 * c], s2b = qsc[8 + 2 * c + 1];
       if (fmt == IAK_FMT_F16 || fmt == IAK_FMT_FP8) {
+        // fp16 fragments carry q / 2^fe: the factor 2^fe of each query column comes back here
+        const float qfa = qsc[kQScF + 2 * c], qfb = qsc[kQScF + 2 * c + 1];
         if (!GROUP) {
           const float ks = scal_s[i];
+          const float ka = ks * qfa, kb = ks * qfb;
 #pragma unroll
-          for (int e = 0; e < 4; ++e) sc[e] = (sacc[0][e] + sacc[1][e]) * ks;
+          for (int e = 0; e < 4; ++e) sc[e] = (sacc[0][e] + sacc[1][e]) * ((e & 1) ? kb : ka);
         } else {
           const bool q = fmt != IAK_FMT_F16;
 #pragma unroll
@@ -742,6 +791,8 @@ __global__ void __launch_bounds__(kThreads, IAK_MIN_BLOCKS)
 #pragma unroll
             for (int e = 0; e < 4; ++e) sc[e] = fmaf(sacc[g][e], ks, sc[e]);
           }
+#pragma unroll
+          for (int e = 0; e < 4; ++e) sc[e] *= (e & 1) ? qfb : qfa;
         }
       } else if (fmt == IAK_FMT_INT8) {
         int i1[4] = {0, 0, 0, 0}, i2[4] = {0, 0, 0, 0};
@@ -898,6 +949,7 @@ __global__ void __launch_bounds__(kThreads, IAK_MIN_BLOCKS)
         __syncwarp();
         if (lane == 0) mbar_arrive(empty_bar(s));
       }
+      if (timed_out) break;
       // ---- this warp's partial of the item
 #pragma unroll
       for (int off = 4; off < 32; off <<= 1) {
@@ -929,7 +981,10 @@ __global__ void __launch_bounds__(kThreads, IAK_MIN_BLOCKS)
       ctr += n_pad;
     }
   }
-  if (timed_out) atomicAdd(&g_decode_timeouts, 1u);
+  if (timed_out && lane == 0) {
+    atomicAdd(&g_decode_timeouts, 1u);
+    if (p.status) atomicOr(p.status, static_cast<unsigned int>(IAK_STATUS_DECODE_TIMEOUT));
+  }
 }
 
 // --------------------------------------------------------- tensor maps ---
@@ -1009,6 +1064,19 @@ int cached_map(CUtensorMap* out, const void* base, int kind, int D, int64_t num_
 }
 
 }  // namespace
+
+int read_decode_timeouts(unsigned int* value, bool reset) {
+  unsigned int v = 0;
+  int st = check_cuda(cudaMemcpyFromSymbol(&v, g_decode_timeouts, sizeof(v)), "read decode timeouts");
+  if (st) return st;
+  if (reset && v) {
+    const unsigned int zero = 0;
+    st = check_cuda(cudaMemcpyToSymbol(g_decode_timeouts, &zero, sizeof(zero)), "reset decode timeouts");
+    if (st) return st;
+  }
+  *value = v;
+  return IAK_OK;
+}
 
 bool mma_shape_eligible(const DecodeParams& p) {
   if (p.PS != kPS || (p.D != 64 && p.D != 128)) return false;

@@ -19,6 +19,14 @@ void set_error(const char* fmt, ...);
 int fail(int status, const char* fmt, ...);
 int check_cuda(cudaError_t e, const char* what);
 int device_sm_count();
+// SM clock of the current device in kHz (cached per device)
+int device_clock_khz();
+// timeout counters of each kernel family (defined beside the kernels)
+int read_decode_timeouts(unsigned int* value, bool reset);
+int read_mla_timeouts(unsigned int* value, bool reset);
+int read_prefill_timeouts(unsigned int* value, bool reset);
+// default budget of a bounded device-side wait: about 2 s at the boost clock
+constexpr long long kDefaultWaitCycles = 4000000000LL;
 // kernel timer hooks around the main decode launch (no-ops unless enabled)
 void kernel_timer_begin(cudaStream_t s);
 void kernel_timer_end(cudaStream_t s);
@@ -52,6 +60,8 @@ struct DecodeParams {
   float* ws_m; float* ws_l; float* ws_acc;
   // optional export of final per-row partials (rows = B*Hq)
   float* ex_m; float* ex_l; float* ex_acc;
+  unsigned int* status;   // IAK_STATUS_* bits ORed on a timeout (or NULL)
+  long long wait_cycles;  // budget of each bounded device-side wait, in SM cycles
 };
 
 // Launchers (return IAK_OK or a status; errors recorded with set_error).

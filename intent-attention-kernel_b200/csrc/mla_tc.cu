@@ -45,6 +45,19 @@ namespace iak {
 
 __device__ unsigned int g_mla_timeouts = 0;
 
+int read_mla_timeouts(unsigned int* value, bool reset) {
+  unsigned int v = 0;
+  int st = check_cuda(cudaMemcpyFromSymbol(&v, g_mla_timeouts, sizeof(v)), "read mla timeouts");
+  if (st) return st;
+  if (reset && v) {
+    const unsigned int zero = 0;
+    st = check_cuda(cudaMemcpyToSymbol(g_mla_timeouts, &zero, sizeof(zero)), "reset mla timeouts");
+    if (st) return st;
+  }
+  *value = v;
+  return IAK_OK;
+}
+
 namespace {
 
 using namespace tc;

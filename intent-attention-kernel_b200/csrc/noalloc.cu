@@ -18,7 +18,10 @@ void* g_scratch_ptr[64] = {nullptr};
 
 // Device address of the scratch array on the current device.  Looked up once
 // per device, with that device current; host code cannot use the symbol itself
-// (on the host it names a stand-in, not device memory).
+// (on the host it names a stand-in, not device memory).  The cached address
+// belongs to the device's primary context (the one the CUDA runtime uses): it
+// does not survive cudaDeviceReset of that device, and a call made while a
+// different driver context is current would use the wrong address.
 int scratch_address(void** out) {
   int dev = 0;
   int st = check_cuda(cudaGetDevice(&dev), "cudaGetDevice");

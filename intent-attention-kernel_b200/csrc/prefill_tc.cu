@@ -46,6 +46,19 @@ namespace iak {
 
 __device__ unsigned int g_prefill_timeouts = 0;
 
+int read_prefill_timeouts(unsigned int* value, bool reset) {
+  unsigned int v = 0;
+  int st = check_cuda(cudaMemcpyFromSymbol(&v, g_prefill_timeouts, sizeof(v)), "read prefill timeouts");
+  if (st) return st;
+  if (reset && v) {
+    const unsigned int zero = 0;
+    st = check_cuda(cudaMemcpyToSymbol(g_prefill_timeouts, &zero, sizeof(zero)), "reset prefill timeouts");
+    if (st) return st;
+  }
+  *value = v;
+  return IAK_OK;
+}
+
 namespace {
 
 using namespace tc;

@@ -49,7 +49,11 @@ class DecodeArgs(ctypes.Structure):
         ("sm_scale", ctypes.c_float),
         ("partial_m", c_void_p), ("partial_l", c_void_p), ("partial_acc", c_void_p),
         ("num_splits", c_i32), ("kernel", c_i32),
+        ("status", c_void_p), ("wait_budget_ns", ctypes.c_uint32),
     ]
+
+
+STATUS_DECODE_TIMEOUT = 1
 
 
 class PackArgs(ctypes.Structure):
@@ -164,6 +168,8 @@ class PeerExchange(ctypes.Structure):
 SIGNATURES = {
     "iak_version": (ctypes.c_int, []),
     "iak_last_error": (ctypes.c_char_p, []),
+    "iak_device_status": (ctypes.c_int, [ctypes.POINTER(ctypes.c_uint32), ctypes.POINTER(ctypes.c_uint32),
+                                         ctypes.POINTER(ctypes.c_uint32), c_i32]),
     "iak_decode_workspace_size": (ctypes.c_int, [ctypes.POINTER(PagePools), ctypes.POINTER(DecodeArgs),
                                                  ctypes.POINTER(ctypes.c_size_t)]),
     "iak_decode": (ctypes.c_int, [ctypes.POINTER(PagePools), ctypes.POINTER(DecodeArgs), c_void_p,
@@ -244,6 +250,24 @@ def check(status: int, what: str) -> None:
     if status == IAK_ERR_INVALID_ARG:
         raise ValueError(f"{what}: {msg}")
     raise RuntimeError(f"{what} failed (status {status}): {msg}")
+
+
+def device_status(reset: bool = True) -> dict:
+    """Timeout counters of the current device: warps whose bounded device-side
+    wait gave up in the tensor-core decode, the tcgen05 MLA decode and the
+    tcgen05 prefill since the last reset.  Waits for the device."""
+    v = [ctypes.c_uint32(0) for _ in range(3)]
+    st = lib().iak_device_status(ctypes.byref(v[0]), ctypes.byref(v[1]), ctypes.byref(v[2]), 1 if reset else 0)
+    if st not in (IAK_OK, IAK_ERR_TIMEOUT):
+        check(st, "iak_device_status")
+    return {"decode": v[0].value, "mla": v[1].value, "prefill": v[2].value}
+
+
+def raise_on_timeouts(reset: bool = True) -> None:
+    """RuntimeError if any device-side wait gave up since the last reset."""
+    st = device_status(reset)
+    if any(st.values()):
+        raise RuntimeError(f"device-side waits gave up (warps per kernel family): {st}")
 
 
 class KernelTimer:

@@ -216,7 +216,7 @@ def make_tag_map(mapping: Mapping[int, str]) -> Tuple[int, ...]:
 
 
 def _decode_structs(q, pool, page_table, page_counts, page_tags, tag_map, tag_default, sm_scale, out,
-                    partial, num_splits, kernel="auto"):
+                    partial, num_splits, kernel="auto", status=None, wait_budget_ns=0):
     B, Hq, D = q.shape
     if page_table.dim() != 3 or page_table.shape[0] != B:
         raise ValueError(f"page_table must be [B, Ht, W] with B={B}, got {tuple(page_table.shape)}")
@@ -245,6 +245,12 @@ def _decode_structs(q, pool, page_table, page_counts, page_tags, tag_map, tag_de
         args.partial_m, args.partial_l, args.partial_acc = m.data_ptr(), l.data_ptr(), acc.data_ptr()
     args.num_splits = int(num_splits)
     args.kernel = N.KERNELS[kernel]
+    if status is not None:
+        _require_cuda(status, "status")
+        if status.dtype not in (torch.int32, torch.uint32) or status.numel() < 1:
+            raise ValueError("status must be a 32-bit integer CUDA tensor")
+        args.status = status.data_ptr()
+    args.wait_budget_ns = int(wait_budget_ns)
     return pool.struct(), args
 
 
@@ -253,8 +259,15 @@ def paged_decode(q: torch.Tensor, pool: PagePool, page_table: torch.Tensor, page
                  sm_scale: Optional[float] = None, out: Optional[torch.Tensor] = None,
                  out_dtype: Optional[torch.dtype] = None, num_splits: int = 0,
                  partial: Optional[Tuple[torch.Tensor, torch.Tensor, torch.Tensor]] = None,
-                 kernel: str = "auto") -> torch.Tensor:
+                 kernel: str = "auto", status: Optional[torch.Tensor] = None,
+                 wait_budget_ns: int = 0) -> torch.Tensor:
     """Single-query paged decode over selected pages -> out [B, Hq, D].
+
+    ``status`` (a 32-bit CUDA tensor, optional) collects ``IAK_STATUS_*`` bits:
+    bit 0 is set when a bounded device-side wait of the tensor-core decode gave
+    up (each wait's budget is ``wait_budget_ns`` nanoseconds, 0 = about 2 s); it is never
+    cleared here, and reading it does not stall the launch.  The output of a
+    call that timed out is undefined.
 
     ``tag_map`` (16 IAK_FMT codes, see ``make_tag_map``) translates the
     caller's precision enum; tags outside 0..15 use ``tag_default``.  With
@@ -293,7 +306,7 @@ def paged_decode(q: torch.Tensor, pool: PagePool, page_table: torch.Tensor, page
         if out.shape != q.shape or out.stride(-1) != 1 or out.dtype not in _DT:
             raise ValueError(f"out must be a {tuple(q.shape)} float tensor with a contiguous last dim")
     pools, args = _decode_structs(q, pool, page_table, page_counts, page_tags, tag_map, tag_default, sm_scale,
-                                  out, partial, num_splits, kernel)
+                                  out, partial, num_splits, kernel, status, wait_budget_ns)
     L = N.lib()
     nbytes = ctypes.c_size_t(0)
     N.check(L.iak_decode_workspace_size(ctypes.byref(pools), ctypes.byref(args), ctypes.byref(nbytes)),

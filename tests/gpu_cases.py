@@ -73,3 +73,33 @@ def run_oracle(case, sm_scale=None):
     pools, sc = oracle_pools(case["pool"])
     return odec.paged_decode(case["np_q"], case["np_table"], case["np_counts"], case["np_tags"], ORACLE_FMT, pools,
                              sc, case["scale_mode"], sm_scale=sm_scale, default_fmt="SKIP")
+
+
+POOL_PLANES = ("k_f16", "v_f16", "k_fp8", "v_fp8", "k_i8", "v_i8", "k_i4", "v_i4", "k_i4r", "v_i4r")
+SCALE_PLANES = ("k_scale", "v_scale", "k_res_scale", "v_res_scale")
+
+
+def compact_oracle_view(pool: PagePool, table: torch.Tensor, counts, tags: torch.Tensor):
+    """The oracle's view of only the pages a decode can reach.
+
+    Gathers, on the device, every pool plane and scale row of the distinct valid
+    page ids of ``table`` (slots below ``counts``), copies them to the host and
+    renumbers the table to the compact ids, so that configurations whose pools
+    span millions of pages stay cheap to check.  Returns (np_table, np_counts,
+    np_tags, pools, scales) for ``oracle.decode.paged_decode``.
+    """
+    t = table.long()
+    W = t.shape[-1]
+    if counts is not None:
+        live = torch.arange(W, device=t.device)[None, None, :] < counts.long()[:, :, None]
+        t = torch.where(live, t, torch.full_like(t, -1))
+    t = torch.where((t >= 0) & (t < pool.num_pages), t, torch.full_like(t, -1))
+    uniq = torch.unique(t[t >= 0])
+    compact = torch.searchsorted(uniq, t.clamp(min=0))
+    compact = torch.where(t >= 0, compact, torch.full_like(compact, -1))
+    pools = {n: getattr(pool, n).index_select(0, uniq).cpu().numpy() for n in POOL_PLANES
+             if getattr(pool, n) is not None}
+    scales = {n: getattr(pool, n).index_select(0, uniq).cpu().numpy() for n in SCALE_PLANES
+              if getattr(pool, n) is not None}
+    np_tags = tags.long().index_select(0, uniq).cpu().numpy()
+    return compact.int().cpu().numpy(), None, np_tags, pools, scales

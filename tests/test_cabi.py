@@ -41,7 +41,7 @@ def test_library_exports_all_declared_symbols():
 
 def test_version_and_error_query():
     L = N.lib()
-    assert L.iak_version() == 1
+    assert L.iak_version() == 2
     # a pure host-side validation error: no device call is made
     st = L.iak_merge_partials(None, None, None, 4, 0, 64, None, 0, 64, None)
     assert st == N.IAK_ERR_INVALID_ARG
