@@ -190,12 +190,11 @@ static int prepare(const iak_page_pools* P, const iak_decode_args* a, DecodePara
   const int W = a->table_width;
   int splits = a->num_splits, pps;
   if (p->tensor) {
-    // persistent kernel over (unit, split) items of <= kTensorItemSlots slots;
-    // aim for ~8 items per resident CTA so the static item striding balances
+    // persistent kernel (one CTA per SM) over (unit, split) items of <= kTensorItemSlots slots
     if (splits <= 0) {
-      // Static item striding over ~2 resident CTAs per SM: minimise
+      // Static item striding over the resident CTAs: minimise
       // waves * (slots per item + a fixed per-item cost of ~16 slots).
-      const int64_t ctas = 2LL * device_sm_count();
+      const int64_t ctas = device_sm_count();
       int64_t best = -1, best_cost = 0;
       const int max_s = std::max(1, std::min(W, 256));
       for (int cand = 1; cand <= max_s; ++cand) {
@@ -229,15 +228,32 @@ static int prepare(const iak_page_pools* P, const iak_decode_args* a, DecodePara
   return IAK_OK;
 }
 
+// Tensor-path workspace head: [query tables][unit counters][item counters]
 static size_t qtab_bytes_for(const DecodeParams& p) {
-  return p.tensor ? align_up(static_cast<size_t>(p.B) * p.Ht * kQueryTableBytes, 256) : 0;
+  if (!p.tensor) return 0;
+  const size_t units = static_cast<size_t>(p.B) * p.Ht;
+  return align_up(units * kQueryTableBytes, 256) + align_up(units * 4, 256) +
+         align_up(units * p.num_splits * 4, 256);
 }
 
-// Workspace: [query tables (tensor path)] [m: rows x slots] [l] [acc: rows x slots x D]
+// per-row partial arrays of `slots` slots: [m: rows x slots] [l] [acc: rows x slots x D]
+static size_t partial_bytes(const DecodeParams& p, int slots) {
+  const size_t n = static_cast<size_t>(p.B) * p.Hq * slots;
+  return align_up(n * 4, 256) * 2 + align_up(n * p.D * 4, 256);
+}
+
+// Workspace: [tensor-path head] [level-0 partials: ws_slots per row]
+// [tensor path: level-1 partials, num_splits per row]
 static size_t workspace_bytes_for(const DecodeParams& p) {
   if (!p.tensor && p.num_splits <= 1) return 0;
-  const size_t n = static_cast<size_t>(p.B) * p.Hq * p.ws_slots;
-  return qtab_bytes_for(p) + align_up(n * 4, 256) * 2 + align_up(n * p.D * 4, 256);
+  return qtab_bytes_for(p) + partial_bytes(p, p.ws_slots) + (p.tensor ? partial_bytes(p, p.num_splits) : 0);
+}
+
+static void carve_partials(char* w, const DecodeParams& p, int slots, float** m, float** l, float** acc) {
+  const size_t n = static_cast<size_t>(p.B) * p.Hq * slots;
+  *m = reinterpret_cast<float*>(w);
+  *l = reinterpret_cast<float*>(w + align_up(n * 4, 256));
+  *acc = reinterpret_cast<float*>(w + 2 * align_up(n * 4, 256));
 }
 
 }  // namespace iak
@@ -286,13 +302,18 @@ int iak_decode(const iak_page_pools* pools, const iak_decode_args* args, void* w
     if (!workspace || ws_bytes < need)
       return fail(IAK_ERR_WORKSPACE, "workspace of %zu bytes needed, %zu given", need, workspace ? ws_bytes : 0);
     if (reinterpret_cast<uintptr_t>(workspace) % 256) return fail(IAK_ERR_WORKSPACE, "workspace must be 256-byte aligned");
-    const size_t n = static_cast<size_t>(p.B) * p.Hq * p.ws_slots;
     char* w = static_cast<char*>(workspace);
-    p.ws_qtab = p.tensor ? w : nullptr;
+    if (p.tensor) {
+      const size_t units = static_cast<size_t>(p.B) * p.Ht;
+      p.ws_qtab = w;
+      p.ws_cnt = reinterpret_cast<unsigned int*>(w + align_up(units * kQueryTableBytes, 256));
+      p.ws_icnt = reinterpret_cast<unsigned int*>(w + align_up(units * kQueryTableBytes, 256) +
+                                                  align_up(units * 4, 256));
+    }
     w += qtab_bytes_for(p);
-    p.ws_m = reinterpret_cast<float*>(w);
-    p.ws_l = reinterpret_cast<float*>(w + align_up(n * 4, 256));
-    p.ws_acc = reinterpret_cast<float*>(w + 2 * align_up(n * 4, 256));
+    carve_partials(w, p, p.ws_slots, &p.ws_m, &p.ws_l, &p.ws_acc);
+    w += partial_bytes(p, p.ws_slots);
+    if (p.tensor) carve_partials(w, p, p.num_splits, &p.ws_m1, &p.ws_l1, &p.ws_acc1);
   }
   if (p.W == 0) {
     // nothing selected anywhere: every output row is zero (or an empty partial)
@@ -302,7 +323,8 @@ int iak_decode(const iak_page_pools* pools, const iak_decode_args* args, void* w
   }
   st = p.tensor ? launch_decode_mma(p, *pools, s) : launch_decode_generic(p, s);
   if (st) return st;
-  if (p.ws_slots > 1 || p.tensor) {
+  // the tensor-core decode merges each unit's partials itself (its last consumer warp)
+  if (p.ws_slots > 1 && !p.tensor) {
     st = launch_merge(p.ws_m, p.ws_l, p.ws_acc, static_cast<int64_t>(p.B) * p.Hq, p.ws_slots, p.D, p.out,
                       p.out_dtype, 0, &p, p.ex_m, p.ex_l, p.ex_acc, s);
     if (st) return st;

@@ -44,47 +44,65 @@ __device__ unsigned int g_decode_timeouts = 0;
 namespace {
 
 constexpr int kPS = 16;
-constexpr int kConsumerWarps = 4;
-constexpr int kTmaWarp = kConsumerWarps;          // issues the TMA page loads
-constexpr int kPrepWarp = kConsumerWarps + 1;     // prepares the next work item
-constexpr int kThreads = (kConsumerWarps + 2) * 32;
+// Warp roles of the persistent decode CTA (one CTA per SM, 4 warpgroups):
+// warpgroup 0 = TMA producer warp, preparer warp and two warps that only hand
+// their registers back; warpgroups 1-3 = 12 consumer warps.
+constexpr int kConsumerWarps = 12;
+constexpr int kTmaWarp = 0;                       // issues the TMA page loads
+constexpr int kPrepWarp = 1;                      // prepares the next work item
+constexpr int kFirstConsumerWarp = 4;
+constexpr int kThreads = (kFirstConsumerWarp + kConsumerWarps) * 32;
+constexpr int kRegsLight = 56;                    // setmaxnreg of warpgroup 0
+constexpr int kRegsConsumer = 152;                // setmaxnreg of the consumer warpgroups
+static_assert(kRegsLight * 128 + kRegsConsumer * 32 * kConsumerWarps <= 65536 &&
+                  kThreads * 128 == 65536,
+              "register split must fit the launch's 128 registers per thread");
 constexpr int kChunkMax = 256;                    // table slots per work item
-#ifndef IAK_STAGES
-#define IAK_STAGES 8
-#endif
-#ifndef IAK_MIN_BLOCKS
-#define IAK_MIN_BLOCKS 2
-#endif
-constexpr int kStages = IAK_STAGES;     // power of two, multiple of the consumer warp count
-constexpr int kStageBytes = 9216;   // K region 4 KB | V region 4 KB | scale rows 1 KB
-constexpr int kVOff = 4096;
-constexpr int kResOff = 1024;       // INT4 residual plane inside a K or V region
-constexpr int kScaleOff = 8192;
+// Every consumer warp owns a byte FIFO in shared memory: its pages are laid out
+// back to back (1 KB aligned, so the 128-byte TMA swizzle lines up), wrapping to
+// the FIFO start when a page does not fit before the end.  Producer lane w and
+// consumer warp w walk the same page sequence and compute the same offsets.
+constexpr int kFifoBytes = 16384;
+constexpr int kResOff = 1024;                     // INT4 residual plane inside a K or V region
+constexpr int kDescScaleBytes = 64;               // group scales of one page: k | v | k res | v res
 constexpr long long kWaitCycles = kDefaultWaitCycles;  // budget of the drain waits
-#ifndef IAK_F16_ONE_BOX
-#define IAK_F16_ONE_BOX 1
-#endif
 constexpr float kLazyLog2 = 8.f;                  // rescale O only when the max grows by > 2^8
-// Producer lanes issuing TMA for consecutive pages: two for page scales (measured at C2: 2 lanes
-// 4868 GB/s, 4 lanes 4710, 8 lanes 4597, 1 lane 3935), four for group32 pages, which add two to
-// four scale-row copies per page (C3: 4 lanes 2374 GB/s, 2 lanes 2284, 8 lanes 2298).
+// F16 pages at D = 128: one TMA box of 32 half-rows (token-major, 256-byte token rows)
+constexpr bool kF16OneBox = true;
+// pages in flight per consumer FIFO (one full / empty mbarrier pair each)
 template <bool GROUP>
-constexpr int producer_lanes() { return GROUP ? 4 : 2; }
-// F16 pages at D = 128: one TMA box of 32 half-rows (token-major, 256-byte
-// token rows) instead of two 64-channel boxes
-constexpr bool kF16OneBox = IAK_F16_ONE_BOX != 0;
+constexpr int fifo_desc() { return GROUP ? 6 : 8; }
 
 enum MapIdx { M_KF16 = 0, M_VF16, M_KFP8, M_VFP8, M_KI8, M_VI8, M_KI4, M_VI4, M_KI4R, M_VI4R, M_COUNT };
 struct TmaMaps {
   CUtensorMap m[M_COUNT];
 };
 
+// V region offset of a staged page (= half its footprint): K at 0, V at vo; INT4R
+// keeps its residual planes kResOff into each region.
+template <int D>
+__host__ __device__ __forceinline__ int page_vo(int fmt) {
+  if (fmt == IAK_FMT_F16) return 32 * D;
+  if (fmt == IAK_FMT_INT4R) return 2048;
+  if (fmt == IAK_FMT_INT4) return 1024;
+  return 16 * D < 1024 ? 1024 : 16 * D;   // FP8, INT8
+}
+// place a page of `sz` bytes at FIFO position `head`: returns its start (wrapped
+// to the next FIFO lap when it would cross the end)
+__device__ __forceinline__ uint32_t fifo_place(uint32_t head, uint32_t sz) {
+  const uint32_t o = head & (kFifoBytes - 1);
+  return o + sz > kFifoBytes ? head + (kFifoBytes - o) : head;
+}
+
 // Per-unit query table (built by decode_prep_kernel, bulk-copied per work item):
 // fp16 fragments [D/16][32] uint4 | int8 terms [D/32][32] uint4 | the same in
-// INT4 order | 128 floats: term scales s1[8], s2[8], int4 biases [4][8] x 2,
-// and at kQScF the power-of-two factor of each query head's fp16 fragments.
+// INT4 order | 128 words: term scales s1[8], s2[8] (floats); at kQB1 / kQB2 the
+// int32 offsets -8 * sum(i1) / -8 * sum(i2) of each 32-channel block and query
+// head ([block][head]), at kQB1T / kQB2T the same over all channels, which start
+// the INT4 integer-MMA accumulators so that the +8 of the offset-binary codes
+// cancels exactly; at kQScF the power-of-two factor of each head's fp16 fragments.
 constexpr int kQFrag = 0, kQI8 = 4096, kQI4 = 6144, kQSc = 8192, kQTab = 8704;
-constexpr int kQScF = 80;
+constexpr int kQB1 = 16, kQB2 = 48, kQScF = 80, kQB1T = 88, kQB2T = 96;
 
 // One work-item buffer: query table | page ids | 4 scale scalars | formats | meta.
 struct ItemLayout {
@@ -96,10 +114,16 @@ struct ItemLayout {
   static constexpr int bytes = (meta + 16 + 127) / 128 * 128;
 };
 
+template <bool GROUP>
 struct SmemLayout {
-  static constexpr int items = kStages * kStageBytes;              // two ItemLayout buffers
-  static constexpr int bars = items + 2 * ItemLayout::bytes;       // full[S], empty[S], ifull[2], iempty[2]
-  static constexpr int total = bars + (2 * kStages + 4) * 8;
+  static constexpr int desc = fifo_desc<GROUP>();
+  static constexpr int fifo = 0;                                        // [kConsumerWarps][kFifoBytes]
+  static constexpr int items = kConsumerWarps * kFifoBytes;             // two ItemLayout buffers
+  static constexpr int dscale = items + 2 * ItemLayout::bytes;          // [warp][desc][64] (group scales)
+  static constexpr int bars = dscale + (GROUP ? kConsumerWarps * desc * kDescScaleBytes : 0);
+  // full[w][d], empty[w][d], ilist[2], ifull[2], iempty[2]
+  static constexpr int total = bars + (2 * kConsumerWarps * desc + 6) * 8;
+  static_assert(total + 1024 <= 232448, "shared memory of the persistent decode CTA");
 };
 
 // ----------------------------------------------------------------- PTX ---
@@ -195,6 +219,11 @@ __device__ __forceinline__ uint32_t lop_and_or(uint32_t a, uint32_t mask, uint32
 __device__ __forceinline__ uint32_t hsub2(uint32_t a, uint32_t b) {
   uint32_t r;
   asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+__device__ __forceinline__ uint32_t hmul2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
   return r;
 }
 __device__ __forceinline__ uint32_t hfma2(uint32_t a, uint32_t b, uint32_t c) {
@@ -395,7 +424,13 @@ __global__ void __launch_bounds__(256) decode_prep_kernel(const DecodeParams p, 
   __shared__ float qfi[8];
   const int unit = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int b = unit / p.Ht, hk = unit % p.Ht;
+  // the decode kernel may start now (programmatic dependent launch); it waits for
+  // this grid before it reads a query table or touches a merge counter
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   if (tid < 128) qsc[tid] = 0.f;
+  // merge counters of this unit and of its items start at zero on every call
+  if (tid == 0) p.ws_cnt[unit] = 0u;
+  for (int s = tid; s < p.num_splits; s += blockDim.x) p.ws_icnt[static_cast<int64_t>(unit) * p.num_splits + s] = 0u;
   {
     // warp g quantises query head g of the group (zeros past G): q = s1 * i1 + s2 * i2
     const int g = warp;
@@ -434,22 +469,31 @@ __global__ void __launch_bounds__(256) decode_prep_kernel(const DecodeParams p, 
       sum1 += static_cast<int>(t1[e]);
       sum2 += static_cast<int>(t2);
     }
-    // sums of the terms over each 32-channel block (they undo the INT4 +8 offset)
+    // sums of the terms over each 32-channel block and over all channels (they undo the
+    // INT4 +8 offset)
+    int tot1 = sum1, tot2 = sum2;
 #pragma unroll
     for (int o = 1; o < GL; o <<= 1) {
       sum1 += __shfl_xor_sync(0xffffffffu, sum1, o);
       sum2 += __shfl_xor_sync(0xffffffffu, sum2, o);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      tot1 += __shfl_xor_sync(0xffffffffu, tot1, o);
+      tot2 += __shfl_xor_sync(0xffffffffu, tot2, o);
     }
     __syncthreads();                   // qsc zeroed
     if (lane == 0) {
       qsc[g] = s1;
       qsc[8 + g] = s2;
       qsc[kQScF + g] = __int_as_float((fe + 127) << 23);
+      qsc[kQB1T + g] = __int_as_float(-8 * tot1);
+      qsc[kQB2T + g] = __int_as_float(-8 * tot2);
     }
     if (lane % GL == 0) {
       const int j = lane / GL;
-      qsc[16 + j * 8 + g] = static_cast<float>(sum1);
-      qsc[48 + j * 8 + g] = static_cast<float>(sum2);
+      qsc[kQB1 + j * 8 + g] = __int_as_float(-8 * sum1);
+      qsc[kQB2 + j * 8 + g] = __int_as_float(-8 * sum2);
     }
   }
   __syncthreads();
@@ -503,35 +547,93 @@ __device__ __forceinline__ void item_range(const DecodeParams& p, int item, int&
   hi = min(lo + p.pages_per_split, count);
 }
 
-// Persistent split-KV decode.  CTA c processes work items c, c + gridDim.x, ...
-// (item = (unit, split) of <= kChunkMax table slots).  Warp kPrepWarp fills
-// one of two item buffers (query table by bulk copy, compacted page list)
-// ahead of use; warp kTmaWarp streams every item's pages through the stage
-// ring without draining between items; each consumer warp writes its own
-// (m, l, acc) partial per item, merged afterwards by merge_kernel.
+// One warp merges S partials (m natural-log max, l, acc[D]; m / l at stride 1, acc
+// rows at stride D) into (M, L, A): the recurrence of the reference's decode loop
+// (fused_selected_quant_decode.py:323-332) applied across partials.  Lane t owns
+// channels t * D/32 .. t * D/32 + D/32 - 1.  Reads bypass L1 (other SMs wrote them).
+template <int D>
+__device__ __forceinline__ void warp_merge(const float* m, const float* l, const float* acc, int S, int lane,
+                                           float& M, float& L, float (&A)[D / 32]) {
+  constexpr int C = D / 32;
+  float mx = -INFINITY;
+  for (int s = lane; s < S; s += 32)
+    if (__ldcg(l + s) > 0.f) mx = fmaxf(mx, __ldcg(m + s));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  float lsum = 0.f;
+#pragma unroll
+  for (int j = 0; j < C; ++j) A[j] = 0.f;
+  for (int s0 = 0; s0 < S; s0 += 32) {
+    const int s = s0 + lane;
+    float w = 0.f;
+    if (s < S && mx != -INFINITY) {
+      const float ls = __ldcg(l + s);
+      if (ls > 0.f) {
+        w = expf(__ldcg(m + s) - mx);
+        lsum = fmaf(ls, w, lsum);
+      }
+    }
+    const int n = min(32, S - s0);
+    for (int k = 0; k < n; ++k) {
+      const float wk = __shfl_sync(0xffffffffu, w, k);
+      if (wk == 0.f) continue;                       // warp-uniform
+      const float* a = acc + static_cast<int64_t>(s0 + k) * D + lane * C;
+      if constexpr (C == 4) {
+        const float4 v = __ldcg(reinterpret_cast<const float4*>(a));
+        A[0] = fmaf(wk, v.x, A[0]); A[1] = fmaf(wk, v.y, A[1]); A[2] = fmaf(wk, v.z, A[2]); A[3] = fmaf(wk, v.w, A[3]);
+      } else {
+        const float2 v = __ldcg(reinterpret_cast<const float2*>(a));
+        A[0] = fmaf(wk, v.x, A[0]); A[1] = fmaf(wk, v.y, A[1]);
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, o);
+  M = mx;
+  L = lsum;
+}
+
+// Persistent split-KV decode, one CTA per SM.  CTA c processes work items c,
+// c + gridDim.x, ... (item = (unit, split) of <= kChunkMax table slots).  The
+// preparer fills one of two item buffers ahead of use (compacted page list,
+// scales, query table by bulk copy); the TMA warp streams every item's pages
+// into the consumer FIFOs (lane w feeds consumer warp w; page i of an item goes
+// to warp i % kConsumerWarps) without draining between items; each consumer warp
+// writes its (m, l, acc) partial per item.  The last consumer warp of an item
+// merges the item's partials, and the last item merger of a unit merges the
+// unit's items into the output (or the exported partial block): no merge launch.
 template <int D, bool GROUP>
-__global__ void __launch_bounds__(kThreads, IAK_MIN_BLOCKS)
+__global__ void __launch_bounds__(kThreads, 1)
     decode_mma_kernel(const DecodeParams p, const __grid_constant__ TmaMaps maps, const char* __restrict__ qtab,
                       int n_items) {
   constexpr int KT = D / 16;   // k-steps of QK, m-tiles of PV
   constexpr int NG = GROUP ? D / 32 : 1;
+  constexpr int ND = fifo_desc<GROUP>();
+  using SL = SmemLayout<GROUP>;
   extern __shared__ __align__(1024) char smem_raw[];
   char* smem = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SmemLayout::bars);   // full | empty | ifull | iempty
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SL::bars);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int r = lane >> 2, c = lane & 3;
-  auto full_bar = [&](int s) { return smem_u32(&bars[s]); };
-  auto empty_bar = [&](int s) { return smem_u32(&bars[kStages + s]); };
-  auto ifull_bar = [&](int buf) { return smem_u32(&bars[2 * kStages + buf]); };
-  auto iempty_bar = [&](int buf) { return smem_u32(&bars[2 * kStages + 2 + buf]); };
-  auto item_buf = [&](int buf) { return smem + SmemLayout::items + buf * ItemLayout::bytes; };
+  auto full_bar = [&](int w, int d) { return smem_u32(&bars[w * ND + d]); };
+  auto empty_bar = [&](int w, int d) { return smem_u32(&bars[(kConsumerWarps + w) * ND + d]); };
+  auto ilist_bar = [&](int buf) { return smem_u32(&bars[2 * kConsumerWarps * ND + buf]); };
+  auto ifull_bar = [&](int buf) { return smem_u32(&bars[2 * kConsumerWarps * ND + 2 + buf]); };
+  auto iempty_bar = [&](int buf) { return smem_u32(&bars[2 * kConsumerWarps * ND + 4 + buf]); };
+  auto item_buf = [&](int buf) { return smem + SL::items + buf * ItemLayout::bytes; };
+  auto dscale = [&](int w, int d) { return smem + SL::dscale + (w * ND + d) * kDescScaleBytes; };
 
   if (tid == 0) {
-    for (int s = 0; s < 2 * kStages; ++s) mbar_init(smem_u32(&bars[s]), 1);
-    // item-ready: the preparer's arrive.expect_tx (query-table bytes) + its
-    // arrive after the page list is written; item-free: one per consumer warp
-    for (int s = 0; s < 2; ++s) mbar_init(ifull_bar(s), 2);
-    for (int s = 0; s < 2; ++s) mbar_init(iempty_bar(s), kConsumerWarps);
+    for (int i = 0; i < 2 * kConsumerWarps * ND; ++i) mbar_init(smem_u32(&bars[i]), 1);
+    // list-ready: the preparer's arrive; item-ready: its arrive after the page list +
+    // its arrive.expect_tx of the query-table bytes; item-free: one per consumer warp
+    // item-free: one arrive per consumer warp and per TMA feeder lane (a lane must have
+    // read the item's page count before its buffer is reused)
+    for (int b2 = 0; b2 < 2; ++b2) {
+      mbar_init(ilist_bar(b2), 1);
+      mbar_init(ifull_bar(b2), 2);
+      mbar_init(iempty_bar(b2), 2 * kConsumerWarps);
+    }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   }
@@ -546,6 +648,7 @@ __global__ void __launch_bounds__(kThreads, IAK_MIN_BLOCKS)
     return __all_sync(0xffffffffu, mbar_wait(bar, parity, budget));
   };
 
+  if (warp < kFirstConsumerWarp) asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;\n" ::"n"(kRegsLight));
   if (warp == kPrepWarp) {
     // -------------------------------------------------------------- preparer
     constexpr int kPer = kChunkMax / 32;
@@ -559,11 +662,6 @@ __global__ void __launch_bounds__(kThreads, IAK_MIN_BLOCKS)
       }
       int unit, split, lo, hi;
       item_range(p, item, unit, split, lo, hi);
-      last_k[buf] = k;
-      if (lane == 0) {
-        mbar_arrive_expect_tx(ifull_bar(buf), kQTab);
-        bulk_load(smem_u32(ib + ItemLayout::qtab), qtab + static_cast<int64_t>(unit) * kQTab, kQTab, ifull_bar(buf));
-      }
       const int bb = unit / p.Ht, hk = unit - bb * p.Ht;
       const int32_t* table = p.pt + bb * p.pt_sb + hk * p.pt_sh;
       int32_t* pid_s = reinterpret_cast<int32_t*>(ib + ItemLayout::pid);
@@ -606,7 +704,18 @@ __global__ void __launch_bounds__(kThreads, IAK_MIN_BLOCKS)
         meta[2] = split;
       }
       __syncwarp();
-      if (lane == 0) mbar_arrive(ifull_bar(buf));
+      if (lane == 0) {
+        mbar_arrive(ilist_bar(buf));
+        mbar_arrive(ifull_bar(buf));
+      }
+      // the query tables come from the preparation kernel, which may still be
+      // running (programmatic dependent launch): wait for it before the first copy
+      if (k == 0) asm volatile("griddepcontrol.wait;" ::: "memory");
+      last_k[buf] = k;
+      if (lane == 0) {
+        mbar_arrive_expect_tx(ifull_bar(buf), kQTab);
+        bulk_load(smem_u32(ib + ItemLayout::qtab), qtab + static_cast<int64_t>(unit) * kQTab, kQTab, ifull_bar(buf));
+      }
     }
     // drain: the query-table copies this warp issued
     for (int b2 = 0; b2 < 2; ++b2)
@@ -614,93 +723,131 @@ __global__ void __launch_bounds__(kThreads, IAK_MIN_BLOCKS)
         timed_out = true;
   } else if (warp == kTmaWarp) {
     // -------------------------------------------------------------- TMA producer
-    constexpr int kProducerLanes = producer_lanes<GROUP>();
-    int ctr = 0;        // pages issued before the current item
-    int g_last = -1;    // ring index of the last stage this lane armed
-    for (int k = 0, item = blockIdx.x; item < n_items && !timed_out; ++k, item += gridDim.x) {
-      const int buf = k & 1;
-      const char* ib = item_buf(buf);
-      if (!wait_all(ifull_bar(buf), (k >> 1) & 1)) {
-        timed_out = true;
-        break;
+    // Lane w (< kConsumerWarps) feeds consumer warp w's FIFO.  The lanes advance
+    // independently through the items: a converged polling loop in which every lane
+    // makes whatever progress its FIFO allows (non-blocking barrier tests), and the
+    // warp naps briefly when no lane could move.
+    const int cw = lane;
+    const bool feeder = lane < kConsumerWarps;
+    int k = 0, item = blockIdx.x;        // this lane's current item
+    bool have = false;                   // its page list is ready
+    int n = 0, i = 0;                    // pages of the item, next page index
+    int kw = 0, kt = 0;                  // pages issued to the FIFO, oldest not yet released
+    uint32_t head = 0, tail = 0;         // FIFO byte positions (monotonic, wrapping)
+    uint32_t ends[ND];                   // end position of each in-flight descriptor's page
+#pragma unroll
+    for (int d = 0; d < ND; ++d) ends[d] = 0;
+    const char* ib = nullptr;
+    long long t_idle = clock64();
+    while (true) {
+      bool active = feeder && item < n_items;
+      bool moved = false;
+      if (active && !have) {
+        if (mbar_test_wait(ilist_bar(k & 1), (k >> 1) & 1)) {
+          ib = item_buf(k & 1);
+          n = reinterpret_cast<const int*>(ib + ItemLayout::meta)[0];
+          i = cw;
+          have = true;
+          moved = true;
+        }
       }
-      const int n = reinterpret_cast<const int*>(ib + ItemLayout::meta)[0];
-      const int n_pad = (n + kStages - 1) & ~(kStages - 1);
-      const int32_t* pid_s = reinterpret_cast<const int32_t*>(ib + ItemLayout::pid);
-      const uint8_t* fmt_s = reinterpret_cast<const uint8_t*>(ib + ItemLayout::fmt);
-      if (lane < kProducerLanes) {
-        for (int i = lane; i < n_pad; i += kProducerLanes) {
-          const int gi = ctr + i;
-          const int s = gi & (kStages - 1), round = gi / kStages;
-          const uint32_t full = full_bar(s);
-          if (round > 0 && !mbar_wait(empty_bar(s), (round - 1) & 1, budget)) {
-            timed_out = true;
-            break;
+      if (active && have) {
+        if (i >= n) {
+          mbar_arrive(iempty_bar(k & 1));
+          have = false;
+          ++k;
+          item += gridDim.x;
+          moved = true;
+        } else {
+          // pages the consumer has released free their descriptors and bytes
+          while (kt < kw && mbar_test_wait(empty_bar(cw, kt % ND), (kt / ND) & 1)) {
+            const int dt = kt % ND;
+#pragma unroll
+            for (int d = 0; d < ND; ++d)
+              if (d == dt) tail = ends[d];
+            ++kt;
           }
-          g_last = gi;
-          if (i >= n) {            // padding slot: completes the stage's phase without data
-            mbar_arrive(full);
-            continue;
-          }
-          const int fmt = fmt_s[i], pid = pid_s[i];
-          const uint32_t st = smem_u32(smem + s * kStageBytes);
-          uint32_t bytes;
-          if (fmt == IAK_FMT_F16) bytes = 2 * kPS * D * 2;
-          else if (fmt == IAK_FMT_INT4) bytes = 2 * kPS * D / 2;
-          else bytes = 2 * kPS * D;   // FP8, INT8, INT4R (two half-size planes)
-          if (GROUP && fmt != IAK_FMT_F16) bytes += (fmt == IAK_FMT_INT4R ? 4 : 2) * NG * 4;
-          mbar_arrive_expect_tx(full, bytes);
-          if (fmt == IAK_FMT_F16) {
-            if constexpr (D == 128 && kF16OneBox) {
-              tma_load_2d(st, &maps.m[M_KF16], 0, pid * kPS * 2, full);
-              tma_load_2d(st + kVOff, &maps.m[M_VF16], 0, pid * kPS * 2, full);
-            } else {
-              tma_load_2d(st, &maps.m[M_KF16], 0, pid * kPS, full);
-              tma_load_2d(st + kVOff, &maps.m[M_VF16], 0, pid * kPS, full);
+          const int fmt = reinterpret_cast<const uint8_t*>(ib + ItemLayout::fmt)[i];
+          const uint32_t vo = page_vo<D>(fmt);
+          const uint32_t pos = fifo_place(head, 2 * vo);
+          if (kw - kt < ND && pos + 2 * vo - tail <= kFifoBytes) {
+            const int pid = reinterpret_cast<const int32_t*>(ib + ItemLayout::pid)[i];
+            const int d = kw % ND;
+            const uint32_t full = full_bar(cw, d);
+            const uint32_t st = smem_u32(smem + SL::fifo + cw * kFifoBytes + (pos & (kFifoBytes - 1)));
+            uint32_t bytes;
+            if (fmt == IAK_FMT_F16) bytes = 2 * kPS * D * 2;
+            else if (fmt == IAK_FMT_INT4) bytes = 2 * kPS * D / 2;
+            else bytes = 2 * kPS * D;   // FP8, INT8, INT4R (two half-size planes)
+            if (GROUP && fmt != IAK_FMT_F16) bytes += (fmt == IAK_FMT_INT4R ? 4 : 2) * NG * 4;
+            mbar_arrive_expect_tx(full, bytes);
+            if (fmt == IAK_FMT_F16) {
               if constexpr (D == 128) {
-                tma_load_2d(st + 2048, &maps.m[M_KF16], 64, pid * kPS, full);
-                tma_load_2d(st + kVOff + 2048, &maps.m[M_VF16], 64, pid * kPS, full);
+                tma_load_2d(st, &maps.m[M_KF16], 0, pid * kPS * 2, full);
+                tma_load_2d(st + vo, &maps.m[M_VF16], 0, pid * kPS * 2, full);
+              } else {
+                tma_load_2d(st, &maps.m[M_KF16], 0, pid * kPS, full);
+                tma_load_2d(st + vo, &maps.m[M_VF16], 0, pid * kPS, full);
+              }
+            } else if (fmt == IAK_FMT_FP8 || fmt == IAK_FMT_INT8) {
+              const int y = pid * (kPS * D / 128);   // 128-byte lines of 8-bit token rows
+              const int mk = fmt == IAK_FMT_FP8 ? M_KFP8 : M_KI8;
+              tma_load_2d(st, &maps.m[mk], 0, y, full);
+              tma_load_2d(st + vo, &maps.m[mk + 1], 0, y, full);
+            } else {
+              const int y = pid * (kPS * D / 256);   // 128-byte lines of packed int4 token rows
+              tma_load_2d(st, &maps.m[M_KI4], 0, y, full);
+              tma_load_2d(st + vo, &maps.m[M_VI4], 0, y, full);
+              if (fmt == IAK_FMT_INT4R) {
+                tma_load_2d(st + kResOff, &maps.m[M_KI4R], 0, y, full);
+                tma_load_2d(st + vo + kResOff, &maps.m[M_VI4R], 0, y, full);
               }
             }
-          } else if (fmt == IAK_FMT_FP8 || fmt == IAK_FMT_INT8) {
-            const int y = pid * (kPS * D / 128);   // 128-byte lines of 8-bit token rows
-            const int mk = fmt == IAK_FMT_FP8 ? M_KFP8 : M_KI8;
-            tma_load_2d(st, &maps.m[mk], 0, y, full);
-            tma_load_2d(st + kVOff, &maps.m[mk + 1], 0, y, full);
-          } else {
-            const int y = pid * (kPS * D / 256);   // 128-byte lines of packed int4 token rows
-            tma_load_2d(st, &maps.m[M_KI4], 0, y, full);
-            tma_load_2d(st + kVOff, &maps.m[M_VI4], 0, y, full);
-            if (fmt == IAK_FMT_INT4R) {
-              tma_load_2d(st + kResOff, &maps.m[M_KI4R], 0, y, full);
-              tma_load_2d(st + kVOff + kResOff, &maps.m[M_VI4R], 0, y, full);
+            if (GROUP && fmt != IAK_FMT_F16) {
+              const uint32_t sc = smem_u32(dscale(cw, d));
+              bulk_load(sc, p.k_scale + static_cast<int64_t>(pid) * NG, NG * 4, full);
+              bulk_load(sc + 16, p.v_scale + static_cast<int64_t>(pid) * NG, NG * 4, full);
+              if (fmt == IAK_FMT_INT4R) {
+                bulk_load(sc + 32, p.k_rscale + static_cast<int64_t>(pid) * NG, NG * 4, full);
+                bulk_load(sc + 48, p.v_rscale + static_cast<int64_t>(pid) * NG, NG * 4, full);
+              }
             }
-          }
-          if (GROUP && fmt != IAK_FMT_F16) {
-            bulk_load(st + kScaleOff, p.k_scale + static_cast<int64_t>(pid) * NG, NG * 4, full);
-            bulk_load(st + kScaleOff + 16 * 4, p.v_scale + static_cast<int64_t>(pid) * NG, NG * 4, full);
-            if (fmt == IAK_FMT_INT4R) {
-              bulk_load(st + kScaleOff + 32 * 4, p.k_rscale + static_cast<int64_t>(pid) * NG, NG * 4, full);
-              bulk_load(st + kScaleOff + 48 * 4, p.v_rscale + static_cast<int64_t>(pid) * NG, NG * 4, full);
-            }
+#pragma unroll
+            for (int dd = 0; dd < ND; ++dd)
+              if (dd == d) ends[dd] = pos + 2 * vo;
+            head = pos + 2 * vo;
+            ++kw;
+            i += kConsumerWarps;
+            moved = true;
           }
         }
       }
-      timed_out = __any_sync(0xffffffffu, timed_out);
-      ctr += n_pad;
-    }
-    // drain: a lane arms its stages in ring order with stride kProducerLanes, so its last
-    // kStages / kProducerLanes arms cover each of its stages once (their latest phase)
-    if (lane < kProducerLanes)
-      for (int j = 0; j < kStages / kProducerLanes; ++j) {
-        const int gi = g_last - j * kProducerLanes;
-        if (gi >= 0 && !mbar_wait(full_bar(gi & (kStages - 1)), (gi / kStages) & 1, kWaitCycles)) timed_out = true;
+      if (!__any_sync(0xffffffffu, active)) break;
+      if (__any_sync(0xffffffffu, moved)) {
+        t_idle = clock64();
+      } else {
+        if (clock64() - t_idle > budget) {
+          timed_out = true;
+          break;
+        }
+        __nanosleep(64);
       }
-  } else {
+    }
+    // drain: the latest phase of every descriptor this lane armed
+    if (feeder)
+      for (int j = kw - 1; j >= 0 && j >= kw - ND; --j)
+        if (!mbar_wait(full_bar(cw, j % ND), (j / ND) & 1, kWaitCycles)) timed_out = true;
+    timed_out = __any_sync(0xffffffffu, timed_out);
+  } else if (warp >= kFirstConsumerWarp) {
     // -------------------------------------------------------------- consumers
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;\n" ::"n"(kRegsConsumer));
+    asm volatile("griddepcontrol.wait;" ::: "memory");   // the counters the preparation kernel zeroed
+    const int cw = warp - kFirstConsumerWarp;
     const float qk_log2 = p.sm_scale * 1.4426950408889634f;
-    const int S = p.num_splits * kConsumerWarps;   // partial slots per query row
-    int ctr = 0;
+    const int S0 = p.num_splits * kConsumerWarps;   // level-0 partial slots per query row
+    const char* fifo = smem + SL::fifo + cw * kFifoBytes;
+    int kw = 0;                                     // pages this FIFO has delivered
+    uint32_t head = 0;                              // its byte position (the producer's, replayed)
     for (int k = 0, item = blockIdx.x; item < n_items; ++k, item += gridDim.x) {
       const int buf = k & 1;
       const char* ib = item_buf(buf);
@@ -720,250 +867,258 @@ __global__ void __launch_bounds__(kThreads, IAK_MIN_BLOCKS)
       float oacc[KT][4];
 #pragma unroll
       for (int mt = 0; mt < KT; ++mt) oacc[mt][0] = oacc[mt][1] = oacc[mt][2] = oacc[mt][3] = 0.f;
-      // Every item occupies a multiple of kStages ring slots (the tail is
-      // padding), so stage s is always filled by TMA lane s % kProducerLanes and
-      // drained by consumer warp s % kConsumerWarps, one phase at a time: a
-      // parity wait can never be two phases ahead of its barrier.
-      const int n_pad = (n_valid + kStages - 1) & ~(kStages - 1);
-      for (int i = warp; i < n_pad; i += kConsumerWarps) {
-        const int gi = ctr + i;
-        const int s = gi & (kStages - 1), round = gi / kStages;
-        if (!wait_all(full_bar(s), round & 1)) {
+      for (int i = cw; i < n_valid; i += kConsumerWarps) {
+        const int fmt = fmt_s[i];
+        const uint32_t vo = page_vo<D>(fmt);
+        const uint32_t pos = fifo_place(head, 2 * vo);
+        head = pos + 2 * vo;
+        const int d = kw % ND;
+        if (!wait_all(full_bar(cw, d), (kw / ND) & 1)) {
           timed_out = true;
           break;
         }
-        if (i >= n_valid) {
-          __syncwarp();
-          if (lane == 0) mbar_arrive(empty_bar(s));
-          continue;
-        }
-      const char* st = smem + s * kStageBytes;
-      const uint32_t st_u32 = smem_u32(st);
-      const int fmt = fmt_s[i];
-      const float* gsc = reinterpret_cast<const float*>(st + kScaleOff);
-      // ---------------- S^T = K Q^T
-      // accumulator of k-step kk: its 32-channel group (group scales) or its
-      // parity (two independent MMA chains per page)
-      constexpr int NA = GROUP ? NG : 2;
-      float sacc[NA][4];
-#pragma unroll
-      for (int g = 0; g < NA; ++g)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) sacc[g][e] = 0.f;
-      if (fmt == IAK_FMT_F16) {
-#pragma unroll
-        for (int kk = 0; kk < KT; ++kk) {
-          uint32_t a[4];
-          k_frag_f16<D>(st_u32, lane, kk, a);
-          const uint4 qf = qfrag[kk * 32 + lane];
-          mma16816(sacc[GROUP ? kk / 2 : (kk & 1)], a[0], a[1], a[2], a[3], qf.x, qf.y);
-        }
-      } else if (fmt == IAK_FMT_FP8) {
-#pragma unroll
-        for (int kk = 0; kk < KT; kk += 2) {
-          uint32_t x[4];
-          ldsm_rows(st_u32, D, lane, kk, x);
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
+        const char* pg = fifo + (pos & (kFifoBytes - 1));
+        const uint32_t pg_u32 = smem_u32(pg);
+        const float* gsc = reinterpret_cast<const float*>(dscale(cw, d));
+        // ---------------- S^T = K Q^T
+        // accumulator of k-step kk: its 32-channel group (group scales) or its
+        // parity (two independent MMA chains per page)
+        constexpr int NA = GROUP ? NG : 2;
+        float sacc[NA][4];
+  #pragma unroll
+        for (int g = 0; g < NA; ++g)
+  #pragma unroll
+          for (int e = 0; e < 4; ++e) sacc[g][e] = 0.f;
+        if (fmt == IAK_FMT_F16) {
+  #pragma unroll
+          for (int kk = 0; kk < KT; ++kk) {
             uint32_t a[4];
-            k_frag_8bit_from(x[2 * h], x[2 * h + 1], true, a);
-            const uint4 qf = qfrag[(kk + h) * 32 + lane];
-            mma16816(sacc[GROUP ? (kk + h) / 2 : h], a[0], a[1], a[2], a[3], qf.z, qf.w);
+            k_frag_f16<D>(pg_u32, lane, kk, a);
+            const uint4 qf = qfrag[kk * 32 + lane];
+            mma16816(sacc[GROUP ? kk / 2 : (kk & 1)], a[0], a[1], a[2], a[3], qf.x, qf.y);
           }
-        }
-      }
-      // ---------------- scores (times the K scale; INT8 / INT4 on the integer tensor path)
-      float sc[4] = {0.f, 0.f, 0.f, 0.f};
-      const float s1a = qsc[2 * c], s1b = qsc[2 * c + 1], s2a = qsc[8 + 2 * c], s2b = qsc[8 + 2 * c + 1];
-      if (fmt == IAK_FMT_F16 || fmt == IAK_FMT_FP8) {
-        // fp16 fragments carry q / 2^fe: the factor 2^fe of each query column comes back here
-        const float qfa = qsc[kQScF + 2 * c], qfb = qsc[kQScF + 2 * c + 1];
-        if (!GROUP) {
-          const float ks = scal_s[i];
-          const float ka = ks * qfa, kb = ks * qfb;
-#pragma unroll
-          for (int e = 0; e < 4; ++e) sc[e] = (sacc[0][e] + sacc[1][e]) * ((e & 1) ? kb : ka);
-        } else {
-          const bool q = fmt != IAK_FMT_F16;
-#pragma unroll
-          for (int g = 0; g < NA; ++g) {
-            const float ks = q ? gsc[g] : 1.f;
-#pragma unroll
-            for (int e = 0; e < 4; ++e) sc[e] = fmaf(sacc[g][e], ks, sc[e]);
-          }
-#pragma unroll
-          for (int e = 0; e < 4; ++e) sc[e] *= (e & 1) ? qfb : qfa;
-        }
-      } else if (fmt == IAK_FMT_INT8) {
-        int i1[4] = {0, 0, 0, 0}, i2[4] = {0, 0, 0, 0};
-#pragma unroll
-        for (int j = 0; j < D / 32; ++j) {
-          uint32_t x[4];
-          ldsm_rows(st_u32, D, lane, 2 * j, x);
-          const uint4 qi = qi8[j * 32 + lane];
-          imma_s8(i1, x, qi.x, qi.y);
-          imma_s8(i2, x, qi.z, qi.w);
-          if (GROUP) {
-            const float ks = gsc[j];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              sc[e] = fmaf(ks, fmaf((e & 1) ? s1b : s1a, static_cast<float>(i1[e]),
-                                    ((e & 1) ? s2b : s2a) * static_cast<float>(i2[e])), sc[e]);
-              i1[e] = i2[e] = 0;
+        } else if (fmt == IAK_FMT_FP8) {
+  #pragma unroll
+          for (int kk = 0; kk < KT; kk += 2) {
+            uint32_t x[4];
+            ldsm_rows(pg_u32, D, lane, kk, x);
+  #pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              uint32_t a[4];
+              k_frag_8bit_from(x[2 * h], x[2 * h + 1], true, a);
+              const uint4 qf = qfrag[(kk + h) * 32 + lane];
+              mma16816(sacc[GROUP ? (kk + h) / 2 : h], a[0], a[1], a[2], a[3], qf.z, qf.w);
             }
           }
         }
-        if (!GROUP) {
-          const float ks = scal_s[i];
-#pragma unroll
-          for (int e = 0; e < 4; ++e)
-            sc[e] = ks * fmaf((e & 1) ? s1b : s1a, static_cast<float>(i1[e]),
-                              ((e & 1) ? s2b : s2a) * static_cast<float>(i2[e]));
-        }
-      } else {
-        // INT4 / INT4R: nibbles -> bytes (code + 8) on the u8 x s8 path; the +8
-        // offset is removed exactly with the per-group sums of the q terms
-        const int nplanes = fmt == IAK_FMT_INT4R ? 2 : 1;
-        for (int pl = 0; pl < nplanes; ++pl) {
+        // ---------------- scores (times the K scale; INT8 / INT4 on the integer tensor path)
+        float sc[4] = {0.f, 0.f, 0.f, 0.f};
+        const float s1a = qsc[2 * c], s1b = qsc[2 * c + 1], s2a = qsc[8 + 2 * c], s2b = qsc[8 + 2 * c + 1];
+        if (fmt == IAK_FMT_F16 || fmt == IAK_FMT_FP8) {
+          // fp16 fragments carry q / 2^fe: the factor 2^fe of each query column comes back here
+          const float qfa = qsc[kQScF + 2 * c], qfb = qsc[kQScF + 2 * c + 1];
+          if (!GROUP) {
+            const float ks = scal_s[i];
+            const float ka = ks * qfa, kb = ks * qfb;
+  #pragma unroll
+            for (int e = 0; e < 4; ++e) sc[e] = (sacc[0][e] + sacc[1][e]) * ((e & 1) ? kb : ka);
+          } else {
+            const bool q = fmt != IAK_FMT_F16;
+  #pragma unroll
+            for (int g = 0; g < NA; ++g) {
+              const float ks = q ? gsc[g] : 1.f;
+  #pragma unroll
+              for (int e = 0; e < 4; ++e) sc[e] = fmaf(sacc[g][e], ks, sc[e]);
+            }
+  #pragma unroll
+            for (int e = 0; e < 4; ++e) sc[e] *= (e & 1) ? qfb : qfa;
+          }
+        } else if (fmt == IAK_FMT_INT8) {
           int i1[4] = {0, 0, 0, 0}, i2[4] = {0, 0, 0, 0};
-          float bias1a = 0.f, bias1b = 0.f, bias2a = 0.f, bias2b = 0.f;
-#pragma unroll
-          for (int jj = 0; jj < D / 64; ++jj) {
+  #pragma unroll
+          for (int j = 0; j < D / 32; ++j) {
             uint32_t x[4];
-            ldsm_rows(st_u32 + pl * kResOff, D / 2, lane, 2 * jj, x);
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-              const int j = 2 * jj + h;
-              const uint32_t a[4] = {x[2 * h] & 0x0F0F0F0Fu, x[2 * h + 1] & 0x0F0F0F0Fu,
-                                     (x[2 * h] >> 4) & 0x0F0F0F0Fu, (x[2 * h + 1] >> 4) & 0x0F0F0F0Fu};
-              const uint4 qi = qi4[j * 32 + lane];
-              imma_u8(i1, a, qi.x, qi.y);
-              imma_u8(i2, a, qi.z, qi.w);
-              const float b1a = qsc[16 + j * 8 + 2 * c], b1b = qsc[16 + j * 8 + 2 * c + 1];
-              const float b2a = qsc[48 + j * 8 + 2 * c], b2b = qsc[48 + j * 8 + 2 * c + 1];
-              if (GROUP) {
-                const float ks = gsc[32 * pl + j];
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                  const float t1 = static_cast<float>(i1[e]) - 8.f * ((e & 1) ? b1b : b1a);
-                  const float t2 = static_cast<float>(i2[e]) - 8.f * ((e & 1) ? b2b : b2a);
-                  sc[e] = fmaf(ks, fmaf((e & 1) ? s1b : s1a, t1, ((e & 1) ? s2b : s2a) * t2), sc[e]);
-                  i1[e] = i2[e] = 0;
-                }
-              } else {
-                bias1a += b1a; bias1b += b1b; bias2a += b2a; bias2b += b2b;
+            ldsm_rows(pg_u32, D, lane, 2 * j, x);
+            const uint4 qi = qi8[j * 32 + lane];
+            imma_s8(i1, x, qi.x, qi.y);
+            imma_s8(i2, x, qi.z, qi.w);
+            if (GROUP) {
+              const float ks = gsc[j];
+  #pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                sc[e] = fmaf(ks, fmaf((e & 1) ? s1b : s1a, static_cast<float>(i1[e]),
+                                      ((e & 1) ? s2b : s2a) * static_cast<float>(i2[e])), sc[e]);
+                i1[e] = i2[e] = 0;
               }
             }
           }
           if (!GROUP) {
-            const float ks = scal_s[(pl == 0 ? 0 : 2) * kChunkMax + i];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const float t1 = static_cast<float>(i1[e]) - 8.f * ((e & 1) ? bias1b : bias1a);
-              const float t2 = static_cast<float>(i2[e]) - 8.f * ((e & 1) ? bias2b : bias2a);
-              sc[e] = fmaf(ks, fmaf((e & 1) ? s1b : s1a, t1, ((e & 1) ? s2b : s2a) * t2), sc[e]);
+            const float ks = scal_s[i];
+  #pragma unroll
+            for (int e = 0; e < 4; ++e)
+              sc[e] = ks * fmaf((e & 1) ? s1b : s1a, static_cast<float>(i1[e]),
+                                ((e & 1) ? s2b : s2a) * static_cast<float>(i2[e]));
+          }
+        } else {
+          // INT4 / INT4R: nibbles -> bytes (code + 8) on the u8 x s8 path; the
+          // accumulators start at -8 * sum(q term) of their channels, so the +8
+          // offset cancels exactly in the integer sums
+          const int nplanes = fmt == IAK_FMT_INT4R ? 2 : 1;
+          const int2* qbi = reinterpret_cast<const int2*>(qsc);   // [word / 2]
+          for (int pl = 0; pl < nplanes; ++pl) {
+            int i1[4], i2[4];
+            if (!GROUP) {
+              const int2 b1 = qbi[(kQB1T >> 1) + c], b2 = qbi[(kQB2T >> 1) + c];
+              i1[0] = i1[2] = b1.x; i1[1] = i1[3] = b1.y;
+              i2[0] = i2[2] = b2.x; i2[1] = i2[3] = b2.y;
+            }
+  #pragma unroll
+            for (int jj = 0; jj < D / 64; ++jj) {
+              uint32_t x[4];
+              ldsm_rows(pg_u32 + pl * kResOff, D / 2, lane, 2 * jj, x);
+  #pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                const int j = 2 * jj + h;
+                const uint32_t a[4] = {x[2 * h] & 0x0F0F0F0Fu, x[2 * h + 1] & 0x0F0F0F0Fu,
+                                       (x[2 * h] >> 4) & 0x0F0F0F0Fu, (x[2 * h + 1] >> 4) & 0x0F0F0F0Fu};
+                const uint4 qi = qi4[j * 32 + lane];
+                if (GROUP) {
+                  const int2 b1 = qbi[((kQB1 + 8 * j) >> 1) + c], b2 = qbi[((kQB2 + 8 * j) >> 1) + c];
+                  i1[0] = i1[2] = b1.x; i1[1] = i1[3] = b1.y;
+                  i2[0] = i2[2] = b2.x; i2[1] = i2[3] = b2.y;
+                }
+                imma_u8(i1, a, qi.x, qi.y);
+                imma_u8(i2, a, qi.z, qi.w);
+                if (GROUP) {
+                  const float ks = gsc[8 * pl + j];
+  #pragma unroll
+                  for (int e = 0; e < 4; ++e)
+                    sc[e] = fmaf(ks, fmaf((e & 1) ? s1b : s1a, static_cast<float>(i1[e]),
+                                          ((e & 1) ? s2b : s2a) * static_cast<float>(i2[e])), sc[e]);
+                }
+              }
+            }
+            if (!GROUP) {
+              const float ks = scal_s[(pl == 0 ? 0 : 2) * kChunkMax + i];
+  #pragma unroll
+              for (int e = 0; e < 4; ++e)
+                sc[e] = fmaf(ks, fmaf((e & 1) ? s1b : s1a, static_cast<float>(i1[e]),
+                                      ((e & 1) ? s2b : s2a) * static_cast<float>(i2[e])), sc[e]);
             }
           }
         }
-      }
-#pragma unroll
-      for (int e = 0; e < 4; ++e) sc[e] *= qk_log2;
-      // ---------------- online softmax (log2 domain)
-      float pm0 = fmaxf(sc[0], sc[2]), pm1 = fmaxf(sc[1], sc[3]);
-#pragma unroll
-      for (int off = 4; off < 32; off <<= 1) {
-        pm0 = fmaxf(pm0, __shfl_xor_sync(0xffffffffu, pm0, off));
-        pm1 = fmaxf(pm1, __shfl_xor_sync(0xffffffffu, pm1, off));
-      }
-      // Lazy rescaling: the running max only moves (and O, l are rescaled)
-      // when some query's page max exceeds it by more than kLazyLog2; until
-      // then p <= 2^kLazyLog2, far inside fp16 / fp32 range.  Warp-uniform.
-      if (__any_sync(0xffffffffu, pm0 > m_run[0] + kLazyLog2 || pm1 > m_run[1] + kLazyLog2)) {
-        const float mn0 = fmaxf(m_run[0], pm0), mn1 = fmaxf(m_run[1], pm1);
-        const float al0 = exp2f(m_run[0] - mn0), al1 = exp2f(m_run[1] - mn1);
-        m_run[0] = mn0; m_run[1] = mn1;
-        l_run[0] *= al0; l_run[1] *= al1;
-#pragma unroll
-        for (int mt = 0; mt < KT; ++mt) {
-          oacc[mt][0] *= al0; oacc[mt][1] *= al1; oacc[mt][2] *= al0; oacc[mt][3] *= al1;
+  #pragma unroll
+        for (int e = 0; e < 4; ++e) sc[e] *= qk_log2;
+        // ---------------- online softmax (log2 domain)
+        float pm0 = fmaxf(sc[0], sc[2]), pm1 = fmaxf(sc[1], sc[3]);
+  #pragma unroll
+        for (int off = 4; off < 32; off <<= 1) {
+          pm0 = fmaxf(pm0, __shfl_xor_sync(0xffffffffu, pm0, off));
+          pm1 = fmaxf(pm1, __shfl_xor_sync(0xffffffffu, pm1, off));
         }
-      }
-      // hardware exp2 (arguments <= kLazyLog2; results below 2^-126 flush to 0, far below fp16's range)
-      const float p0 = ex2_approx(sc[0] - m_run[0]), p1 = ex2_approx(sc[1] - m_run[1]);
-      const float p2 = ex2_approx(sc[2] - m_run[0]), p3 = ex2_approx(sc[3] - m_run[1]);
-      l_run[0] += p0 + p2;
-      l_run[1] += p1 + p3;
-      // ---------------- O^T += V^T P^T
-      uint32_t vh[2][D / 64][8];
-      if (!GROUP) {
-        // per-page V scale folded into P
-        const float vs = scal_s[kChunkMax + i];
-        const uint32_t pb0 = movm_t(pack_f16x2(p0 * vs, p1 * vs));
-        const uint32_t pb1 = movm_t(pack_f16x2(p2 * vs, p3 * vs));
-        if (fmt == IAK_FMT_F16) v_table_f16<D>(st + kVOff, r, c, vh);
-        else if (fmt == IAK_FMT_FP8 || fmt == IAK_FMT_INT8) v_table_8bit<D>(st + kVOff, r, c, fmt == IAK_FMT_FP8, vh);
-        else v_table_int4<D>(st + kVOff, r, c, vh);
-#pragma unroll
-        for (int mt = 0; mt < KT; ++mt) {
-          uint32_t a0, a1, a2, a3;
-          pv_afrag<D>(vh, mt, a0, a1, a2, a3);
-          mma16816(oacc[mt], a0, a1, a2, a3, pb0, pb1);
+        // Lazy rescaling: the running max only moves (and O, l are rescaled)
+        // when some query's page max exceeds it by more than kLazyLog2; until
+        // then p <= 2^kLazyLog2, far inside fp16 / fp32 range.  Warp-uniform.
+        if (__any_sync(0xffffffffu, pm0 > m_run[0] + kLazyLog2 || pm1 > m_run[1] + kLazyLog2)) {
+          const float mn0 = fmaxf(m_run[0], pm0), mn1 = fmaxf(m_run[1], pm1);
+          const float al0 = exp2f(m_run[0] - mn0), al1 = exp2f(m_run[1] - mn1);
+          m_run[0] = mn0; m_run[1] = mn1;
+          l_run[0] *= al0; l_run[1] *= al1;
+  #pragma unroll
+          for (int mt = 0; mt < KT; ++mt) {
+            oacc[mt][0] *= al0; oacc[mt][1] *= al1; oacc[mt][2] *= al0; oacc[mt][3] *= al1;
+          }
         }
-        if (fmt == IAK_FMT_INT4R) {
-          const float vrs = scal_s[3 * kChunkMax + i];
-          const uint32_t rb0 = movm_t(pack_f16x2(p0 * vrs, p1 * vrs));
-          const uint32_t rb1 = movm_t(pack_f16x2(p2 * vrs, p3 * vrs));
-          v_table_int4<D>(st + kVOff + kResOff, r, c, vh);
-#pragma unroll
+        // hardware exp2 (arguments <= kLazyLog2; results below 2^-126 flush to 0, far below fp16's range)
+        const float p0 = ex2_approx(sc[0] - m_run[0]), p1 = ex2_approx(sc[1] - m_run[1]);
+        const float p2 = ex2_approx(sc[2] - m_run[0]), p3 = ex2_approx(sc[3] - m_run[1]);
+        l_run[0] += p0 + p2;
+        l_run[1] += p1 + p3;
+        // ---------------- O^T += V^T P^T
+        uint32_t vh[2][D / 64][8];
+        if (!GROUP) {
+          // per-page V scale folded into P
+          const float vs = scal_s[kChunkMax + i];
+          const uint32_t pb0 = movm_t(pack_f16x2(p0 * vs, p1 * vs));
+          const uint32_t pb1 = movm_t(pack_f16x2(p2 * vs, p3 * vs));
+          if (fmt == IAK_FMT_F16) v_table_f16<D>(pg + vo, r, c, vh);
+          else if (fmt == IAK_FMT_FP8 || fmt == IAK_FMT_INT8) v_table_8bit<D>(pg + vo, r, c, fmt == IAK_FMT_FP8, vh);
+          else v_table_int4<D>(pg + vo, r, c, vh);
+  #pragma unroll
           for (int mt = 0; mt < KT; ++mt) {
             uint32_t a0, a1, a2, a3;
             pv_afrag<D>(vh, mt, a0, a1, a2, a3);
-            mma16816(oacc[mt], a0, a1, a2, a3, rb0, rb1);
+            mma16816(oacc[mt], a0, a1, a2, a3, pb0, pb1);
+          }
+          if (fmt == IAK_FMT_INT4R) {
+            const float vrs = scal_s[3 * kChunkMax + i];
+            const uint32_t rb0 = movm_t(pack_f16x2(p0 * vrs, p1 * vrs));
+            const uint32_t rb1 = movm_t(pack_f16x2(p2 * vrs, p3 * vrs));
+            v_table_int4<D>(pg + vo + kResOff, r, c, vh);
+  #pragma unroll
+            for (int mt = 0; mt < KT; ++mt) {
+              uint32_t a0, a1, a2, a3;
+              pv_afrag<D>(vh, mt, a0, a1, a2, a3);
+              mma16816(oacc[mt], a0, a1, a2, a3, rb0, rb1);
+            }
+          }
+        } else {
+          // per-32-channel V scales.  The page's largest V scale rides on P (as a page
+          // scale does); each group's ratio to it (<= 1) multiplies the V fragments in
+          // fp16.  Rows r of the lane's PV fragments are group gA, rows r + 8 group gB.
+          const int gA = pv_word<D>(r, 0) >> 2, gB = pv_word<D>(r, D / 64 - 1) >> 2;
+          const bool q = fmt != IAK_FMT_F16;
+          const int nplanes = fmt == IAK_FMT_INT4R ? 2 : 1;
+          for (int pl = 0; pl < nplanes; ++pl) {
+            const char* vt = pg + vo + pl * kResOff;
+            if (fmt == IAK_FMT_F16) v_table_f16<D>(vt, r, c, vh);
+            else if (fmt == IAK_FMT_FP8 || fmt == IAK_FMT_INT8) v_table_8bit<D>(vt, r, c, fmt == IAK_FMT_FP8, vh);
+            else v_table_int4<D>(vt, r, c, vh);
+            float vmax = 1.f;
+            if (q) {
+              const float* vsc = gsc + (pl == 0 ? 4 : 12);
+              vmax = vsc[0];
+  #pragma unroll
+              for (int g = 1; g < NG; ++g) vmax = fmaxf(vmax, vsc[g]);
+              const float inv = __frcp_rn(vmax);
+              const uint32_t rA = pack_f16x2(vsc[gA] * inv, vsc[gA] * inv);
+              const uint32_t rB = pack_f16x2(vsc[gB] * inv, vsc[gB] * inv);
+  #pragma unroll
+              for (int tp = 0; tp < 2; ++tp)
+  #pragma unroll
+                for (int n = 0; n < 8; ++n) {
+                  vh[tp][0][n] = hmul2(vh[tp][0][n], rA);
+                  vh[tp][D / 64 - 1][n] = hmul2(vh[tp][D / 64 - 1][n], rB);
+                }
+            }
+            const uint32_t pb0 = movm_t(pack_f16x2(p0 * vmax, p1 * vmax));
+            const uint32_t pb1 = movm_t(pack_f16x2(p2 * vmax, p3 * vmax));
+  #pragma unroll
+            for (int mt = 0; mt < KT; ++mt) {
+              uint32_t a0, a1, a2, a3;
+              pv_afrag<D>(vh, mt, a0, a1, a2, a3);
+              mma16816(oacc[mt], a0, a1, a2, a3, pb0, pb1);
+            }
           }
         }
-      } else {
-        // per-32-channel V scales: rows r use group gA, rows r+8 group gB
-        const uint32_t pb0 = movm_t(pack_f16x2(p0, p1));
-        const uint32_t pb1 = movm_t(pack_f16x2(p2, p3));
-        const int gA = pv_word<D>(r, 0) >> 2, gB = pv_word<D>(r, D / 64 - 1) >> 2;
-        const bool q = fmt != IAK_FMT_F16;
-        const int nplanes = fmt == IAK_FMT_INT4R ? 2 : 1;
-        for (int pl = 0; pl < nplanes; ++pl) {
-          const float* vsc = gsc + (pl == 0 ? 16 : 48);
-          const float sA = q ? vsc[gA] : 1.f, sB = q ? vsc[gB] : 1.f;
-          const char* vt = st + kVOff + pl * kResOff;
-          if (fmt == IAK_FMT_F16) v_table_f16<D>(vt, r, c, vh);
-          else if (fmt == IAK_FMT_FP8 || fmt == IAK_FMT_INT8) v_table_8bit<D>(vt, r, c, fmt == IAK_FMT_FP8, vh);
-          else v_table_int4<D>(vt, r, c, vh);
-#pragma unroll
-          for (int mt = 0; mt < KT; ++mt) {
-            uint32_t a0, a1, a2, a3;
-            pv_afrag<D>(vh, mt, a0, a1, a2, a3);
-            float t[4] = {0.f, 0.f, 0.f, 0.f};
-            mma16816(t, a0, a1, a2, a3, pb0, pb1);
-            oacc[mt][0] = fmaf(t[0], sA, oacc[mt][0]); oacc[mt][1] = fmaf(t[1], sA, oacc[mt][1]);
-            oacc[mt][2] = fmaf(t[2], sB, oacc[mt][2]); oacc[mt][3] = fmaf(t[3], sB, oacc[mt][3]);
-          }
-        }
-      }
         __syncwarp();
-        if (lane == 0) mbar_arrive(empty_bar(s));
+        if (lane == 0) mbar_arrive(empty_bar(cw, d));
+        ++kw;
       }
       if (timed_out) break;
-      // ---- this warp's partial of the item
+      // ---- this warp's partial of the item (level 0)
 #pragma unroll
       for (int off = 4; off < 32; off <<= 1) {
         l_run[0] += __shfl_xor_sync(0xffffffffu, l_run[0], off);
         l_run[1] += __shfl_xor_sync(0xffffffffu, l_run[1], off);
       }
       const int bb = unit / p.Ht, hk = unit - bb * p.Ht;
-      const int slot = split * kConsumerWarps + warp;
+      const int64_t row0 = static_cast<int64_t>(bb) * p.Hq + hk * p.G;
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         const int g = 2 * c + h;
         if (g < p.G) {
-          const int64_t row = static_cast<int64_t>(bb) * p.Hq + hk * p.G + g;
-          const int64_t wi = row * S + slot;
+          const int64_t wi = (row0 + g) * S0 + split * kConsumerWarps + cw;
           if (r == 0) {
             p.ws_m[wi] = l_run[h] > 0.f ? m_run[h] * 0.6931471805599453f : -INFINITY;  // natural-log max
             p.ws_l[wi] = l_run[h];
@@ -976,9 +1131,56 @@ __global__ void __launch_bounds__(kThreads, IAK_MIN_BLOCKS)
           }
         }
       }
+      __threadfence();
       __syncwarp();
       if (lane == 0) mbar_arrive(iempty_bar(buf));
-      ctr += n_pad;
+      // ---- the item's last warp merges its kConsumerWarps partials (level 1); the
+      // unit's last item merger merges the unit's splits into the output (level 2)
+      const int item_id = unit * p.num_splits + split;
+      unsigned last = 0;
+      if (lane == 0) last = atomicAdd(&p.ws_icnt[item_id], 1u) == kConsumerWarps - 1;
+      if (__shfl_sync(0xffffffffu, last, 0)) {
+        __threadfence();
+        for (int g = 0; g < p.G; ++g) {
+          const int64_t row = row0 + g;
+          const int64_t w0 = row * S0 + split * kConsumerWarps;
+          float M, L, A[D / 32];
+          warp_merge<D>(p.ws_m + w0, p.ws_l + w0, p.ws_acc + w0 * D, kConsumerWarps, lane, M, L, A);
+          const int64_t w1 = row * p.num_splits + split;
+          if (lane == 0) {
+            p.ws_m1[w1] = M;
+            p.ws_l1[w1] = L;
+          }
+#pragma unroll
+          for (int j = 0; j < D / 32; ++j) p.ws_acc1[w1 * D + lane * (D / 32) + j] = A[j];
+        }
+        __threadfence();
+        __syncwarp();
+        unsigned ulast = 0;
+        if (lane == 0) ulast = atomicAdd(&p.ws_cnt[unit], 1u) == static_cast<unsigned>(p.num_splits) - 1;
+        if (__shfl_sync(0xffffffffu, ulast, 0)) {
+          __threadfence();
+          for (int g = 0; g < p.G; ++g) {
+            const int64_t row = row0 + g;
+            const int64_t w1 = row * p.num_splits;
+            float M, L, A[D / 32];
+            warp_merge<D>(p.ws_m1 + w1, p.ws_l1 + w1, p.ws_acc1 + w1 * D, p.num_splits, lane, M, L, A);
+            if (p.ex_l) {
+              if (lane == 0) {
+                p.ex_m[row] = M;
+                p.ex_l[row] = L;
+              }
+#pragma unroll
+              for (int j = 0; j < D / 32; ++j) p.ex_acc[row * D + lane * (D / 32) + j] = A[j];
+            } else {
+              const int64_t off = static_cast<int64_t>(bb) * p.o_sb + static_cast<int64_t>(hk * p.G + g) * p.o_sh;
+              const float inv = L > 0.f ? 1.f / L : 0.f;
+#pragma unroll
+              for (int j = 0; j < D / 32; ++j) store_from_float(p.out, p.out_dtype, off + lane * (D / 32) + j, A[j] * inv);
+            }
+          }
+        }
+      }
     }
   }
   if (timed_out && lane == 0) {
@@ -1088,7 +1290,7 @@ bool mma_shape_eligible(const DecodeParams& p) {
 
 template <int D, bool GROUP>
 static int launch_persistent(const DecodeParams& p, const TmaMaps& maps, int n_items, cudaStream_t s) {
-  const size_t smem = SmemLayout::total + 1024;
+  const size_t smem = SmemLayout<GROUP>::total + 1024;
   auto kern = decode_mma_kernel<D, GROUP>;
   // the smem attribute and occupancy are per (device, instantiation): look them up once
   static std::mutex mu;
@@ -1113,9 +1315,21 @@ static int launch_persistent(const DecodeParams& p, const TmaMaps& maps, int n_i
   decode_prep_kernel<D><<<p.B * p.Ht, 256, 0, s>>>(p, p.ws_qtab);
   err = cudaGetLastError();
   if (err != cudaSuccess) return check_cuda(err, "decode_prep launch");
+  // Programmatic dependent launch: the decode CTAs start while the query tables are
+  // still being built, stream their first pages, and wait (griddepcontrol.wait) only
+  // before they read a query table or a merge counter.
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(ctas));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
   kernel_timer_begin(s);
-  kern<<<ctas, kThreads, smem, s>>>(p, maps, p.ws_qtab, n_items);
-  err = cudaGetLastError();
+  err = cudaLaunchKernelEx(&cfg, kern, p, maps, static_cast<const char*>(p.ws_qtab), n_items);
   kernel_timer_end(s);
   return check_cuda(err, "decode_mma launch");
 }

@@ -56,6 +56,11 @@ struct DecodeParams {
   int tensor;    // 1: the tensor-core path runs (per-warp partial slots, query tables)
   int ws_slots;  // partial slots per query row in the workspace
   char* ws_qtab; // per-unit query tables (tensor path)
+  // tensor path, zeroed by the prep kernel on every call: per-unit count of merged
+  // items, per-item count of consumer warps done
+  unsigned int* ws_cnt; unsigned int* ws_icnt;
+  // tensor path: per-item merged partials [row][split] (level 1 of the in-kernel merge)
+  float* ws_m1; float* ws_l1; float* ws_acc1;
   // split partials, [unit][split][g] and [unit][split][g][D]
   float* ws_m; float* ws_l; float* ws_acc;
   // optional export of final per-row partials (rows = B*Hq)
@@ -70,7 +75,7 @@ int launch_decode_mma(const DecodeParams& p, const iak_page_pools& pools, cudaSt
 bool mma_shape_eligible(const DecodeParams& p);
 constexpr int kQueryTableBytes = 8704;   // per-unit query table of the tensor path
 constexpr int kTensorItemSlots = 256;    // max table slots per tensor-path work item
-constexpr int kTensorConsumerWarps = 4;  // partial slots per work item
+constexpr int kTensorConsumerWarps = 12; // partial slots per work item
 int launch_merge(const float* m, const float* l, const float* acc, int64_t rows, int splits, int D,
                  void* out, int out_dtype, int64_t out_row_stride,
                  const DecodeParams* rowmap, float* ex_m, float* ex_l, float* ex_acc, cudaStream_t s);
