@@ -307,6 +307,19 @@ typedef struct iak_peer_exchange {
 } iak_peer_exchange;
 
 int iak_exchange_area_bytes(int32_t world, int64_t rows, int32_t head_dim, size_t* bytes);
+
+/* Decode fused with the push (no counterpart in the reference): the same decode
+ * as iak_decode on the tensor-core path, but each query row's merged partial
+ * (m, l, acc) is stored by the decode kernel itself into slot x->rank of every
+ * rank's receive array (plain stores over NVLink), and the last work unit to
+ * finish raises this rank's flag in every area and advances the epoch.  Use it
+ * in place of steps 1-2 above (decode into the staging block, then
+ * iak_exchange_push); step 3 (iak_exchange_merge) is unchanged.  args->out and
+ * args->partial_* are not used (partial_* must be NULL); x->rows must be
+ * batch * num_q_heads and x->head_dim the pools' head_dim.  Allocates nothing,
+ * synchronises nothing; IAK_ERR_UNSUPPORTED outside the tensor-core shapes. */
+int iak_decode_exchange(const iak_page_pools* pools, const iak_decode_args* args, const iak_peer_exchange* x,
+                        void* workspace, size_t workspace_bytes, void* stream);
 /* Address of the staging block inside an exchange area. */
 float* iak_exchange_staging_ptr(void* area, int32_t world, int64_t rows, int32_t head_dim);
 int iak_exchange_push(const iak_peer_exchange* x, void* stream);

@@ -140,7 +140,6 @@ static int prepare(const iak_page_pools* P, const iak_decode_args* a, DecodePara
   const bool any_work = a->batch > 0 && a->table_width > 0;
   if (any_work) {
     if (!a->q || !a->page_table || !a->page_tags) return fail(IAK_ERR_INVALID_ARG, "q/page_table/page_tags is NULL");
-    if (!a->out && !a->partial_l) return fail(IAK_ERR_INVALID_ARG, "out is NULL");
     struct { int fmt; const void* k; const void* v; const char* name; } need[] = {
         {IAK_FMT_F16, P->k_f16, P->v_f16, "f16"},   {IAK_FMT_FP8, P->k_fp8, P->v_fp8, "fp8"},
         {IAK_FMT_INT8, P->k_i8, P->v_i8, "int8"},    {IAK_FMT_INT4, P->k_i4, P->v_i4, "int4"},
@@ -190,11 +189,11 @@ static int prepare(const iak_page_pools* P, const iak_decode_args* a, DecodePara
   const int W = a->table_width;
   int splits = a->num_splits, pps;
   if (p->tensor) {
-    // persistent kernel (one CTA per SM) over (unit, split) items of <= kTensorItemSlots slots
+    // persistent kernel (two CTAs per SM) over (unit, split) items of <= kTensorItemSlots slots
     if (splits <= 0) {
       // Static item striding over the resident CTAs: minimise
       // waves * (slots per item + a fixed per-item cost of ~16 slots).
-      const int64_t ctas = device_sm_count();
+      const int64_t ctas = 2LL * device_sm_count();
       int64_t best = -1, best_cost = 0;
       const int max_s = std::max(1, std::min(W, 256));
       for (int cand = 1; cand <= max_s; ++cand) {
@@ -228,12 +227,11 @@ static int prepare(const iak_page_pools* P, const iak_decode_args* a, DecodePara
   return IAK_OK;
 }
 
-// Tensor-path workspace head: [query tables][unit counters][item counters]
+// Tensor-path workspace head: [query tables][unit counters + the launch's done counter]
 static size_t qtab_bytes_for(const DecodeParams& p) {
   if (!p.tensor) return 0;
   const size_t units = static_cast<size_t>(p.B) * p.Ht;
-  return align_up(units * kQueryTableBytes, 256) + align_up(units * 4, 256) +
-         align_up(units * p.num_splits * 4, 256);
+  return align_up(units * kQueryTableBytes, 256) + align_up((units + 1) * 4, 256);
 }
 
 // per-row partial arrays of `slots` slots: [m: rows x slots] [l] [acc: rows x slots x D]
@@ -242,11 +240,12 @@ static size_t partial_bytes(const DecodeParams& p, int slots) {
   return align_up(n * 4, 256) * 2 + align_up(n * p.D * 4, 256);
 }
 
-// Workspace: [tensor-path head] [level-0 partials: ws_slots per row]
-// [tensor path: level-1 partials, num_splits per row]
+// Workspace: tensor path [head] [per-split partials: num_splits per row] (the partials of
+// the consumer warps of a work item are merged in shared memory); CUDA-core path
+// [per-split partials: ws_slots per row] when it splits the page lists
 static size_t workspace_bytes_for(const DecodeParams& p) {
-  if (!p.tensor && p.num_splits <= 1) return 0;
-  return qtab_bytes_for(p) + partial_bytes(p, p.ws_slots) + (p.tensor ? partial_bytes(p, p.num_splits) : 0);
+  if (p.tensor) return qtab_bytes_for(p) + partial_bytes(p, p.num_splits);
+  return p.num_splits <= 1 ? 0 : partial_bytes(p, p.ws_slots);
 }
 
 static void carve_partials(char* w, const DecodeParams& p, int slots, float** m, float** l, float** acc) {
@@ -290,11 +289,35 @@ int iak_decode_workspace_size(const iak_page_pools* pools, const iak_decode_args
   return IAK_OK;
 }
 
-int iak_decode(const iak_page_pools* pools, const iak_decode_args* args, void* workspace, size_t ws_bytes,
-               void* stream) {
+}  // extern "C"
+
+// iak_decode, or with x != NULL iak_decode_exchange (fused peer stores of the rows)
+static int decode_impl(const iak_page_pools* pools, const iak_decode_args* args, void* workspace, size_t ws_bytes,
+                       void* stream, const iak_peer_exchange* x) {
   DecodeParams p;
   int st = prepare(pools, args, &p);
   if (st) return st;
+  if (!x && p.B > 0 && p.W > 0 && !args->out && !args->partial_l) return fail(IAK_ERR_INVALID_ARG, "out is NULL");
+  if (x) {
+    if (!p.tensor)
+      return fail(IAK_ERR_UNSUPPORTED, "the fused exchange runs on the tensor-core decode (page_size 16, head_dim "
+                  "64/128, fp16/bf16 q, page or group32 scales)");
+    if (args->partial_l) return fail(IAK_ERR_INVALID_ARG, "the fused exchange writes the partials itself (partial_* must be NULL)");
+    if (x->world < 1 || x->world > IAK_MAX_PEERS || x->rank < 0 || x->rank >= x->world)
+      return fail(IAK_ERR_INVALID_ARG, "bad exchange rank %d / world %d", x->rank, x->world);
+    if (x->rows != static_cast<int64_t>(p.B) * p.Hq || x->head_dim != p.D)
+      return fail(IAK_ERR_INVALID_ARG, "exchange blocks are %lld rows x %d, the decode has %lld x %d",
+                  static_cast<long long>(x->rows), x->head_dim, static_cast<long long>(p.B) * p.Hq, p.D);
+    for (int r = 0; r < x->world; ++r) {
+      if (!x->areas[r] || reinterpret_cast<uintptr_t>(x->areas[r]) % 256)
+        return fail(IAK_ERR_INVALID_ARG, "exchange area of rank %d is NULL or not 256-byte aligned", r);
+      p.x_areas[r] = static_cast<float*>(x->areas[r]);
+    }
+    p.x_world = x->world;
+    p.x_rank = x->rank;
+    p.x_bs = exchange_block_stride(x->rows, x->head_dim);
+    p.x_flags_off = static_cast<int64_t>(exchange_flags_offset(x->world, x->rows, x->head_dim));
+  }
   if (p.B == 0) return IAK_OK;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const size_t need = workspace_bytes_for(p);
@@ -307,15 +330,13 @@ int iak_decode(const iak_page_pools* pools, const iak_decode_args* args, void* w
       const size_t units = static_cast<size_t>(p.B) * p.Ht;
       p.ws_qtab = w;
       p.ws_cnt = reinterpret_cast<unsigned int*>(w + align_up(units * kQueryTableBytes, 256));
-      p.ws_icnt = reinterpret_cast<unsigned int*>(w + align_up(units * kQueryTableBytes, 256) +
-                                                  align_up(units * 4, 256));
+      p.ws_done = p.ws_cnt + units;
     }
     w += qtab_bytes_for(p);
-    carve_partials(w, p, p.ws_slots, &p.ws_m, &p.ws_l, &p.ws_acc);
-    w += partial_bytes(p, p.ws_slots);
     if (p.tensor) carve_partials(w, p, p.num_splits, &p.ws_m1, &p.ws_l1, &p.ws_acc1);
+    else carve_partials(w, p, p.ws_slots, &p.ws_m, &p.ws_l, &p.ws_acc);
   }
-  if (p.W == 0) {
+  if (p.W == 0 && !x) {
     // nothing selected anywhere: every output row is zero (or an empty partial)
     DecodeParams z = p;
     z.num_splits = 1; z.pages_per_split = 1; z.tensor = 0; z.ws_slots = 1;
@@ -330,6 +351,19 @@ int iak_decode(const iak_page_pools* pools, const iak_decode_args* args, void* w
     if (st) return st;
   }
   return IAK_OK;
+}
+
+extern "C" {
+
+int iak_decode(const iak_page_pools* pools, const iak_decode_args* args, void* workspace, size_t ws_bytes,
+               void* stream) {
+  return decode_impl(pools, args, workspace, ws_bytes, stream, nullptr);
+}
+
+int iak_decode_exchange(const iak_page_pools* pools, const iak_decode_args* args, const iak_peer_exchange* x,
+                        void* workspace, size_t ws_bytes, void* stream) {
+  if (!x) return fail(IAK_ERR_INVALID_ARG, "null exchange descriptor");
+  return decode_impl(pools, args, workspace, ws_bytes, stream, x);
 }
 
 int iak_kernel_timer_enable(int32_t max_launches) {

@@ -44,55 +44,40 @@ __device__ unsigned int g_decode_timeouts = 0;
 namespace {
 
 constexpr int kPS = 16;
-// Warp roles of the persistent decode CTA (one CTA per SM, 4 warpgroups):
-// warpgroup 0 = TMA producer warp, preparer warp and two warps that only hand
-// their registers back; warpgroups 1-3 = 12 consumer warps.
-constexpr int kConsumerWarps = 12;
-constexpr int kTmaWarp = 0;                       // issues the TMA page loads
-constexpr int kPrepWarp = 1;                      // prepares the next work item
-constexpr int kFirstConsumerWarp = 4;
+// Warp roles of the persistent decode CTA (two CTAs per SM): warp 0 prepares the
+// next work item, warp 1 issues the TMA page loads, warps 2-5 consume the pages.
+// Measured alternatives, all correct and all slower at C2 / C3 / C5: one CTA per SM
+// with 12 consumer warps (setmaxnreg 56 / 152) fed by one or three producer warps,
+// by the consumers themselves (TMA, bulk or cp.async copies) through per-warp byte
+// FIFOs, or from a 24-stage ring (C2 394-466 us against 275 us for this layout).
+constexpr int kConsumerWarps = 4;
+constexpr int kPrepWarp = 0;                      // prepares the next work item
+constexpr int kProducerWarps = 1;                 // warp 1 issues the TMA page loads
+constexpr int kFirstConsumerWarp = 2;
 constexpr int kThreads = (kFirstConsumerWarp + kConsumerWarps) * 32;
-constexpr int kRegsLight = 56;                    // setmaxnreg of warpgroup 0
-constexpr int kRegsConsumer = 152;                // setmaxnreg of the consumer warpgroups
-static_assert(kRegsLight * 128 + kRegsConsumer * 32 * kConsumerWarps <= 65536 &&
-                  kThreads * 128 == 65536,
-              "register split must fit the launch's 128 registers per thread");
+constexpr int kCtasPerSm = 2;
 constexpr int kChunkMax = 256;                    // table slots per work item
-// Every consumer warp owns a byte FIFO in shared memory: its pages are laid out
-// back to back (1 KB aligned, so the 128-byte TMA swizzle lines up), wrapping to
-// the FIFO start when a page does not fit before the end.  Producer lane w and
-// consumer warp w walk the same page sequence and compute the same offsets.
-constexpr int kFifoBytes = 16384;
+// Stage ring: stage s is filled by producer lane s % P and drained by consumer warp
+// s % kConsumerWarps; items are padded to whole rings so the mapping never shifts.
+constexpr int kStages = 8;                        // two per consumer warp
+constexpr int kStageBytes = 8192;                 // K region 4 KB | V region 4 KB
+constexpr int kVOff = 4096;
 constexpr int kResOff = 1024;                     // INT4 residual plane inside a K or V region
-constexpr int kDescScaleBytes = 64;               // group scales of one page: k | v | k res | v res
+constexpr int kStageScaleBytes = 64;              // group scales of a stage: k | v | k res | v res
 constexpr long long kWaitCycles = kDefaultWaitCycles;  // budget of the drain waits
 constexpr float kLazyLog2 = 8.f;                  // rescale O only when the max grows by > 2^8
 // F16 pages at D = 128: one TMA box of 32 half-rows (token-major, 256-byte token rows)
 constexpr bool kF16OneBox = true;
-// pages in flight per consumer FIFO (one full / empty mbarrier pair each)
+// issuing lanes per producer warp: two for page scales, four for group32 pages, which add
+// two to four scale-row copies per page (measured on the two-CTA predecessor of this
+// kernel at C2: 2 lanes 4868 GB/s, 4 lanes 4710, 1 lane 3935; at C3: 4 lanes 2374, 2 lanes 2284)
 template <bool GROUP>
-constexpr int fifo_desc() { return GROUP ? 6 : 8; }
+constexpr int lanes_per_producer() { return GROUP ? 4 : 2; }
 
 enum MapIdx { M_KF16 = 0, M_VF16, M_KFP8, M_VFP8, M_KI8, M_VI8, M_KI4, M_VI4, M_KI4R, M_VI4R, M_COUNT };
 struct TmaMaps {
   CUtensorMap m[M_COUNT];
 };
-
-// V region offset of a staged page (= half its footprint): K at 0, V at vo; INT4R
-// keeps its residual planes kResOff into each region.
-template <int D>
-__host__ __device__ __forceinline__ int page_vo(int fmt) {
-  if (fmt == IAK_FMT_F16) return 32 * D;
-  if (fmt == IAK_FMT_INT4R) return 2048;
-  if (fmt == IAK_FMT_INT4) return 1024;
-  return 16 * D < 1024 ? 1024 : 16 * D;   // FP8, INT8
-}
-// place a page of `sz` bytes at FIFO position `head`: returns its start (wrapped
-// to the next FIFO lap when it would cross the end)
-__device__ __forceinline__ uint32_t fifo_place(uint32_t head, uint32_t sz) {
-  const uint32_t o = head & (kFifoBytes - 1);
-  return o + sz > kFifoBytes ? head + (kFifoBytes - o) : head;
-}
 
 // Per-unit query table (built by decode_prep_kernel, bulk-copied per work item):
 // fp16 fragments [D/16][32] uint4 | int8 terms [D/32][32] uint4 | the same in
@@ -114,16 +99,19 @@ struct ItemLayout {
   static constexpr int bytes = (meta + 16 + 127) / 128 * 128;
 };
 
-template <bool GROUP>
+// Merge area: each consumer warp's (acc[D], m, l) per query head of the item, read by
+// the preparer when the item is finished.  Sized for head_dim 128 and 8 query heads.
+constexpr int kMergeRow = 128 + 2;                // floats per (warp, head): acc | m | l
+constexpr int kMergeFloats = kConsumerWarps * 8 * kMergeRow;
+
 struct SmemLayout {
-  static constexpr int desc = fifo_desc<GROUP>();
-  static constexpr int fifo = 0;                                        // [kConsumerWarps][kFifoBytes]
-  static constexpr int items = kConsumerWarps * kFifoBytes;             // two ItemLayout buffers
-  static constexpr int dscale = items + 2 * ItemLayout::bytes;          // [warp][desc][64] (group scales)
-  static constexpr int bars = dscale + (GROUP ? kConsumerWarps * desc * kDescScaleBytes : 0);
-  // full[w][d], empty[w][d], ilist[2], ifull[2], iempty[2]
-  static constexpr int total = bars + (2 * kConsumerWarps * desc + 6) * 8;
-  static_assert(total + 1024 <= 232448, "shared memory of the persistent decode CTA");
+  static constexpr int stages = 0;                                      // [kStages][kStageBytes]
+  static constexpr int scales = kStages * kStageBytes;                  // [kStages][64] group scales
+  static constexpr int items = scales + kStages * kStageScaleBytes;     // two ItemLayout buffers
+  static constexpr int merge = items + 2 * ItemLayout::bytes;           // [warp][head][kMergeRow] floats
+  static constexpr int bars = merge + kMergeFloats * 4;                 // full[S], empty[S], ilist[2], ifull[2], iempty[2], mfree
+  static constexpr int total = bars + (2 * kStages + 7) * 8;
+  static_assert(total + 1024 <= 116736, "two persistent decode CTAs per SM");
 };
 
 // ----------------------------------------------------------------- PTX ---
@@ -220,6 +208,9 @@ __device__ __forceinline__ uint32_t hsub2(uint32_t a, uint32_t b) {
   uint32_t r;
   asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
   return r;
+}
+__device__ __forceinline__ void st_release_sys(uint32_t* ptr, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(ptr), "r"(v) : "memory");
 }
 __device__ __forceinline__ uint32_t hmul2(uint32_t a, uint32_t b) {
   uint32_t r;
@@ -428,9 +419,9 @@ __global__ void __launch_bounds__(256) decode_prep_kernel(const DecodeParams p, 
   // this grid before it reads a query table or touches a merge counter
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   if (tid < 128) qsc[tid] = 0.f;
-  // merge counters of this unit and of its items start at zero on every call
+  // merge counters start at zero on every call
   if (tid == 0) p.ws_cnt[unit] = 0u;
-  for (int s = tid; s < p.num_splits; s += blockDim.x) p.ws_icnt[static_cast<int64_t>(unit) * p.num_splits + s] = 0u;
+  if (tid == 0 && unit == 0) *p.ws_done = 0u;
   {
     // warp g quantises query head g of the group (zeros past G): q = s1 * i1 + s2 * i2
     const int g = warp;
@@ -550,40 +541,57 @@ __device__ __forceinline__ void item_range(const DecodeParams& p, int item, int&
 // One warp merges S partials (m natural-log max, l, acc[D]; m / l at stride 1, acc
 // rows at stride D) into (M, L, A): the recurrence of the reference's decode loop
 // (fused_selected_quant_decode.py:323-332) applied across partials.  Lane t owns
-// channels t * D/32 .. t * D/32 + D/32 - 1.  Reads bypass L1 (other SMs wrote them).
+// channels t * D/32 .. t * D/32 + D/32 - 1.  Reads bypass L1 (other SMs wrote them)
+// and are batched (all m / l, then the accumulator rows eight at a time) so that the
+// merge costs a few L2 round trips, not one per partial.
 template <int D>
 __device__ __forceinline__ void warp_merge(const float* m, const float* l, const float* acc, int S, int lane,
                                            float& M, float& L, float (&A)[D / 32]) {
   constexpr int C = D / 32;
-  float mx = -INFINITY;
-  for (int s = lane; s < S; s += 32)
-    if (__ldcg(l + s) > 0.f) mx = fmaxf(mx, __ldcg(m + s));
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-  float lsum = 0.f;
+  float mx = -INFINITY, lsum = 0.f;
 #pragma unroll
   for (int j = 0; j < C; ++j) A[j] = 0.f;
   for (int s0 = 0; s0 < S; s0 += 32) {
     const int s = s0 + lane;
-    float w = 0.f;
-    if (s < S && mx != -INFINITY) {
-      const float ls = __ldcg(l + s);
-      if (ls > 0.f) {
-        w = expf(__ldcg(m + s) - mx);
-        lsum = fmaf(ls, w, lsum);
-      }
+    const float ls = s < S ? __ldcg(l + s) : 0.f;
+    const float ms = s < S ? __ldcg(m + s) : -INFINITY;
+    float cm = ls > 0.f ? ms : -INFINITY;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, o));
+    // rescale what earlier chunks accumulated to the new running max
+    const float mnew = fmaxf(mx, cm);
+    if (mnew != -INFINITY && mnew > mx && mx != -INFINITY) {
+      const float a = expf(mx - mnew);
+      lsum *= a;
+#pragma unroll
+      for (int j = 0; j < C; ++j) A[j] *= a;
     }
+    mx = mnew;
+    const float w = (ls > 0.f && mx != -INFINITY) ? expf(ms - mx) : 0.f;
+    lsum = fmaf(ls, w, lsum);
     const int n = min(32, S - s0);
-    for (int k = 0; k < n; ++k) {
-      const float wk = __shfl_sync(0xffffffffu, w, k);
-      if (wk == 0.f) continue;                       // warp-uniform
-      const float* a = acc + static_cast<int64_t>(s0 + k) * D + lane * C;
-      if constexpr (C == 4) {
-        const float4 v = __ldcg(reinterpret_cast<const float4*>(a));
-        A[0] = fmaf(wk, v.x, A[0]); A[1] = fmaf(wk, v.y, A[1]); A[2] = fmaf(wk, v.z, A[2]); A[3] = fmaf(wk, v.w, A[3]);
-      } else {
-        const float2 v = __ldcg(reinterpret_cast<const float2*>(a));
-        A[0] = fmaf(wk, v.x, A[0]); A[1] = fmaf(wk, v.y, A[1]);
+    for (int k0 = 0; k0 < n; k0 += 8) {
+      float v[8][C];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        if (k0 + u < n) {
+          const float* a = acc + static_cast<int64_t>(s0 + k0 + u) * D + lane * C;
+          if constexpr (C == 4) {
+            const float4 x = __ldcg(reinterpret_cast<const float4*>(a));
+            v[u][0] = x.x; v[u][1] = x.y; v[u][2] = x.z; v[u][3] = x.w;
+          } else {
+            const float2 x = __ldcg(reinterpret_cast<const float2*>(a));
+            v[u][0] = x.x; v[u][1] = x.y;
+          }
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const float wk = __shfl_sync(0xffffffffu, w, (k0 + u) & 31);
+        if (k0 + u < n && wk != 0.f) {
+#pragma unroll
+          for (int j = 0; j < C; ++j) A[j] = fmaf(wk, v[u][j], A[j]);
+        }
       }
     }
   }
@@ -603,37 +611,40 @@ __device__ __forceinline__ void warp_merge(const float* m, const float* l, const
 // merges the item's partials, and the last item merger of a unit merges the
 // unit's items into the output (or the exported partial block): no merge launch.
 template <int D, bool GROUP>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, kCtasPerSm)
     decode_mma_kernel(const DecodeParams p, const __grid_constant__ TmaMaps maps, const char* __restrict__ qtab,
                       int n_items) {
   constexpr int KT = D / 16;   // k-steps of QK, m-tiles of PV
   constexpr int NG = GROUP ? D / 32 : 1;
-  constexpr int ND = fifo_desc<GROUP>();
-  using SL = SmemLayout<GROUP>;
+  constexpr int LPW = lanes_per_producer<GROUP>();
+  constexpr int kProducerLanes = kProducerWarps * LPW;
+  static_assert(kStages % kProducerLanes == 0 && kStages % kConsumerWarps == 0, "stage ring mapping");
+  using SL = SmemLayout;
   extern __shared__ __align__(1024) char smem_raw[];
   char* smem = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SL::bars);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int r = lane >> 2, c = lane & 3;
-  auto full_bar = [&](int w, int d) { return smem_u32(&bars[w * ND + d]); };
-  auto empty_bar = [&](int w, int d) { return smem_u32(&bars[(kConsumerWarps + w) * ND + d]); };
-  auto ilist_bar = [&](int buf) { return smem_u32(&bars[2 * kConsumerWarps * ND + buf]); };
-  auto ifull_bar = [&](int buf) { return smem_u32(&bars[2 * kConsumerWarps * ND + 2 + buf]); };
-  auto iempty_bar = [&](int buf) { return smem_u32(&bars[2 * kConsumerWarps * ND + 4 + buf]); };
+  auto full_bar = [&](int st) { return smem_u32(&bars[st]); };
+  auto empty_bar = [&](int st) { return smem_u32(&bars[kStages + st]); };
+  auto ilist_bar = [&](int buf) { return smem_u32(&bars[2 * kStages + buf]); };
+  auto ifull_bar = [&](int buf) { return smem_u32(&bars[2 * kStages + 2 + buf]); };
+  auto iempty_bar = [&](int buf) { return smem_u32(&bars[2 * kStages + 4 + buf]); };
+  const uint32_t mfree_bar = smem_u32(&bars[2 * kStages + 6]);   // the preparer has read the merge area
+  float* merge_area = reinterpret_cast<float*>(smem + SL::merge);
   auto item_buf = [&](int buf) { return smem + SL::items + buf * ItemLayout::bytes; };
-  auto dscale = [&](int w, int d) { return smem + SL::dscale + (w * ND + d) * kDescScaleBytes; };
+  auto stage_scales = [&](int st) { return smem + SL::scales + st * kStageScaleBytes; };
 
   if (tid == 0) {
-    for (int i = 0; i < 2 * kConsumerWarps * ND; ++i) mbar_init(smem_u32(&bars[i]), 1);
+    for (int i = 0; i < 2 * kStages; ++i) mbar_init(smem_u32(&bars[i]), 1);
     // list-ready: the preparer's arrive; item-ready: its arrive after the page list +
     // its arrive.expect_tx of the query-table bytes; item-free: one per consumer warp
-    // item-free: one arrive per consumer warp and per TMA feeder lane (a lane must have
-    // read the item's page count before its buffer is reused)
     for (int b2 = 0; b2 < 2; ++b2) {
       mbar_init(ilist_bar(b2), 1);
       mbar_init(ifull_bar(b2), 2);
-      mbar_init(iempty_bar(b2), 2 * kConsumerWarps);
+      mbar_init(iempty_bar(b2), kConsumerWarps);
     }
+    mbar_init(mfree_bar, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   }
@@ -648,17 +659,126 @@ __global__ void __launch_bounds__(kThreads, 1)
     return __all_sync(0xffffffffu, mbar_wait(bar, parity, budget));
   };
 
-  if (warp < kFirstConsumerWarp) asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;\n" ::"n"(kRegsLight));
   if (warp == kPrepWarp) {
     // -------------------------------------------------------------- preparer
     constexpr int kPer = kChunkMax / 32;
+    // Merge of a finished item (all its consumer warps have written their level-0
+    // partials and arrived on its item-free barrier): the kConsumerWarps partials ->
+    // the item's level-1 slot; the unit's last merged item merges the unit's splits into
+    // the output (level 2).  Done here, off the consumers and the stage ring.
+    auto merge_item = [&](int item_done) {
+      const int unit = item_done / p.num_splits, split = item_done - unit * p.num_splits;
+      const int bb = unit / p.Ht, hk = unit - bb * p.Ht;
+      const int64_t row0 = static_cast<int64_t>(bb) * p.Hq + hk * p.G;
+      for (int g = 0; g < p.G; ++g) {
+        const int64_t row = row0 + g;
+        float M = -INFINITY, L = 0.f, A[D / 32], wt[kConsumerWarps];
+#pragma unroll
+        for (int w = 0; w < kConsumerWarps; ++w) {
+          const float* mr = merge_area + (w * 8 + g) * kMergeRow;
+          if (mr[129] > 0.f) M = fmaxf(M, mr[128]);
+        }
+#pragma unroll
+        for (int w = 0; w < kConsumerWarps; ++w) {
+          const float* mr = merge_area + (w * 8 + g) * kMergeRow;
+          wt[w] = (mr[129] > 0.f && M != -INFINITY) ? expf(mr[128] - M) : 0.f;
+          L = fmaf(mr[129], wt[w], L);
+        }
+#pragma unroll
+        for (int j = 0; j < D / 32; ++j) {
+          float a = 0.f;
+#pragma unroll
+          for (int w = 0; w < kConsumerWarps; ++w)
+            if (wt[w] != 0.f) a = fmaf(wt[w], merge_area[(w * 8 + g) * kMergeRow + lane * (D / 32) + j], a);
+          A[j] = a;
+        }
+        const int64_t w1 = row * p.num_splits + split;
+        if (lane == 0) {
+          p.ws_m1[w1] = M;
+          p.ws_l1[w1] = L;
+        }
+#pragma unroll
+        for (int j = 0; j < D / 32; ++j) p.ws_acc1[w1 * D + lane * (D / 32) + j] = A[j];
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(mfree_bar);          // the consumers may write the next item's partials
+      __threadfence();
+      __syncwarp();
+      unsigned ulast = 0;
+      if (lane == 0) ulast = atomicAdd(&p.ws_cnt[unit], 1u) == static_cast<unsigned>(p.num_splits) - 1;
+      if (__shfl_sync(0xffffffffu, ulast, 0)) {
+        __threadfence();
+        // fused exchange: the epoch this launch publishes (the merge that follows on
+        // every rank reads the receive array of its parity)
+        uint32_t epoch = 0;
+        if (p.x_world > 0)
+          epoch = *reinterpret_cast<const volatile uint32_t*>(
+                      reinterpret_cast<const char*>(p.x_areas[p.x_rank]) + p.x_flags_off +
+                      (2 * p.x_world + 2) * sizeof(uint32_t)) + 1u;
+        const int64_t xrows = static_cast<int64_t>(p.B) * p.Hq;
+        for (int g = 0; g < p.G; ++g) {
+          const int64_t row = row0 + g;
+          const int64_t w1 = row * p.num_splits;
+          float M, L, A[D / 32];
+          warp_merge<D>(p.ws_m1 + w1, p.ws_l1 + w1, p.ws_acc1 + w1 * D, p.num_splits, lane, M, L, A);
+          if (p.x_world > 0) {
+            // the row's partial straight into slot x_rank of every rank's receive array
+            for (int rk = 0; rk < p.x_world; ++rk) {
+              float* blk = p.x_areas[rk] + static_cast<int64_t>((epoch & 1u) * p.x_world + p.x_rank) * p.x_bs;
+              if (lane == 0) {
+                blk[row] = M;
+                blk[xrows + row] = L;
+              }
+#pragma unroll
+              for (int j = 0; j < D / 32; ++j) blk[2 * xrows + row * D + lane * (D / 32) + j] = A[j];
+            }
+          } else if (p.ex_l) {
+            if (lane == 0) {
+              p.ex_m[row] = M;
+              p.ex_l[row] = L;
+            }
+#pragma unroll
+            for (int j = 0; j < D / 32; ++j) p.ex_acc[row * D + lane * (D / 32) + j] = A[j];
+          } else {
+            const int64_t off = static_cast<int64_t>(bb) * p.o_sb + static_cast<int64_t>(hk * p.G + g) * p.o_sh;
+            const float inv = L > 0.f ? 1.f / L : 0.f;
+#pragma unroll
+            for (int j = 0; j < D / 32; ++j) store_from_float(p.out, p.out_dtype, off + lane * (D / 32) + j, A[j] * inv);
+          }
+        }
+        if (p.x_world > 0) {
+          // once every unit of this launch has stored its rows, raise this rank's flag
+          // (the epoch) in every area, then advance the epoch
+          __threadfence_system();
+          __syncwarp();
+          unsigned dlast = 0;
+          if (lane == 0) dlast = atomicAdd(p.ws_done, 1u) == static_cast<unsigned>(p.B * p.Ht) - 1;
+          if (__shfl_sync(0xffffffffu, dlast, 0)) {
+            __threadfence_system();
+            if (lane < p.x_world)
+              st_release_sys(reinterpret_cast<uint32_t*>(reinterpret_cast<char*>(p.x_areas[lane]) + p.x_flags_off) +
+                                 (epoch & 1u) * p.x_world + p.x_rank,
+                             epoch);
+            __syncwarp();
+            if (lane == 0)
+              *reinterpret_cast<volatile uint32_t*>(reinterpret_cast<char*>(p.x_areas[p.x_rank]) + p.x_flags_off +
+                                                    (2 * p.x_world + 2) * sizeof(uint32_t)) = epoch;
+          }
+        }
+      }
+    };
     int last_k[2] = {-1, -1};   // last item whose query table was copied into each buffer
+    const int n_mine = blockIdx.x < n_items ? (n_items - 1 - blockIdx.x) / gridDim.x + 1 : 0;
     for (int k = 0, item = blockIdx.x; item < n_items; ++k, item += gridDim.x) {
       const int buf = k & 1;
       char* ib = item_buf(buf);
-      if (k >= 2 && !wait_all(iempty_bar(buf), ((k >> 1) - 1) & 1)) {
-        timed_out = true;
-        break;
+      if (k >= 2) {
+        // item k - 2 is finished: merge it, then reuse its buffer
+        if (!wait_all(iempty_bar(buf), ((k >> 1) - 1) & 1)) {
+          timed_out = true;
+          break;
+        }
+        merge_item(item - 2 * gridDim.x);
       }
       int unit, split, lo, hi;
       item_range(p, item, unit, split, lo, hi);
@@ -717,137 +837,109 @@ __global__ void __launch_bounds__(kThreads, 1)
         bulk_load(smem_u32(ib + ItemLayout::qtab), qtab + static_cast<int64_t>(unit) * kQTab, kQTab, ifull_bar(buf));
       }
     }
+    // the items whose merge the loop has not reached: this CTA's last two
+    for (int j = max(0, n_mine - 2); j < n_mine && !timed_out; ++j) {
+      if (!wait_all(iempty_bar(j & 1), (j >> 1) & 1)) {
+        timed_out = true;
+        break;
+      }
+      merge_item(blockIdx.x + j * gridDim.x);
+    }
     // drain: the query-table copies this warp issued
     for (int b2 = 0; b2 < 2; ++b2)
       if (lane == 0 && last_k[b2] >= 0 && !mbar_wait(ifull_bar(b2), (last_k[b2] >> 1) & 1, kWaitCycles))
         timed_out = true;
-  } else if (warp == kTmaWarp) {
-    // -------------------------------------------------------------- TMA producer
-    // Lane w (< kConsumerWarps) feeds consumer warp w's FIFO.  The lanes advance
-    // independently through the items: a converged polling loop in which every lane
-    // makes whatever progress its FIFO allows (non-blocking barrier tests), and the
-    // warp naps briefly when no lane could move.
-    const int cw = lane;
-    const bool feeder = lane < kConsumerWarps;
-    int k = 0, item = blockIdx.x;        // this lane's current item
-    bool have = false;                   // its page list is ready
-    int n = 0, i = 0;                    // pages of the item, next page index
-    int kw = 0, kt = 0;                  // pages issued to the FIFO, oldest not yet released
-    uint32_t head = 0, tail = 0;         // FIFO byte positions (monotonic, wrapping)
-    uint32_t ends[ND];                   // end position of each in-flight descriptor's page
-#pragma unroll
-    for (int d = 0; d < ND; ++d) ends[d] = 0;
-    const char* ib = nullptr;
-    long long t_idle = clock64();
-    while (true) {
-      bool active = feeder && item < n_items;
-      bool moved = false;
-      if (active && !have) {
-        if (mbar_test_wait(ilist_bar(k & 1), (k >> 1) & 1)) {
-          ib = item_buf(k & 1);
-          n = reinterpret_cast<const int*>(ib + ItemLayout::meta)[0];
-          i = cw;
-          have = true;
-          moved = true;
-        }
+  } else if (warp < kFirstConsumerWarp) {
+    // -------------------------------------------------------------- TMA producers
+    // Lane l < LPW of producer warp j is producer lane (j - 1) * LPW + l; it fills the
+    // stages s = producer lane (mod kProducerLanes) of every item, in ring order.
+    const int pl = (warp - 1) * LPW + lane;
+    int ctr = 0;        // ring slots used by the items before the current one
+    int g_last = -1;    // ring index of the last stage this lane armed
+    for (int k = 0, item = blockIdx.x; item < n_items && !timed_out; ++k, item += gridDim.x) {
+      const int buf = k & 1;
+      const char* ib = item_buf(buf);
+      if (!wait_all(ilist_bar(buf), (k >> 1) & 1)) {
+        timed_out = true;
+        break;
       }
-      if (active && have) {
-        if (i >= n) {
-          mbar_arrive(iempty_bar(k & 1));
-          have = false;
-          ++k;
-          item += gridDim.x;
-          moved = true;
-        } else {
-          // pages the consumer has released free their descriptors and bytes
-          while (kt < kw && mbar_test_wait(empty_bar(cw, kt % ND), (kt / ND) & 1)) {
-            const int dt = kt % ND;
-#pragma unroll
-            for (int d = 0; d < ND; ++d)
-              if (d == dt) tail = ends[d];
-            ++kt;
+      const int n = reinterpret_cast<const int*>(ib + ItemLayout::meta)[0];
+      const int n_pad = (n + kStages - 1) / kStages * kStages;
+      const int32_t* pid_s = reinterpret_cast<const int32_t*>(ib + ItemLayout::pid);
+      const uint8_t* fmt_s = reinterpret_cast<const uint8_t*>(ib + ItemLayout::fmt);
+      if (lane < LPW) {
+        for (int i = pl; i < n_pad; i += kProducerLanes) {
+          const int gi = ctr + i;
+          const int st = gi % kStages, round = gi / kStages;
+          const uint32_t full = full_bar(st);
+          if (round > 0 && !mbar_wait(empty_bar(st), (round - 1) & 1, budget)) {
+            timed_out = true;
+            break;
           }
-          const int fmt = reinterpret_cast<const uint8_t*>(ib + ItemLayout::fmt)[i];
-          const uint32_t vo = page_vo<D>(fmt);
-          const uint32_t pos = fifo_place(head, 2 * vo);
-          if (kw - kt < ND && pos + 2 * vo - tail <= kFifoBytes) {
-            const int pid = reinterpret_cast<const int32_t*>(ib + ItemLayout::pid)[i];
-            const int d = kw % ND;
-            const uint32_t full = full_bar(cw, d);
-            const uint32_t st = smem_u32(smem + SL::fifo + cw * kFifoBytes + (pos & (kFifoBytes - 1)));
-            uint32_t bytes;
-            if (fmt == IAK_FMT_F16) bytes = 2 * kPS * D * 2;
-            else if (fmt == IAK_FMT_INT4) bytes = 2 * kPS * D / 2;
-            else bytes = 2 * kPS * D;   // FP8, INT8, INT4R (two half-size planes)
-            if (GROUP && fmt != IAK_FMT_F16) bytes += (fmt == IAK_FMT_INT4R ? 4 : 2) * NG * 4;
-            mbar_arrive_expect_tx(full, bytes);
-            if (fmt == IAK_FMT_F16) {
-              if constexpr (D == 128) {
-                tma_load_2d(st, &maps.m[M_KF16], 0, pid * kPS * 2, full);
-                tma_load_2d(st + vo, &maps.m[M_VF16], 0, pid * kPS * 2, full);
-              } else {
-                tma_load_2d(st, &maps.m[M_KF16], 0, pid * kPS, full);
-                tma_load_2d(st + vo, &maps.m[M_VF16], 0, pid * kPS, full);
-              }
-            } else if (fmt == IAK_FMT_FP8 || fmt == IAK_FMT_INT8) {
-              const int y = pid * (kPS * D / 128);   // 128-byte lines of 8-bit token rows
-              const int mk = fmt == IAK_FMT_FP8 ? M_KFP8 : M_KI8;
-              tma_load_2d(st, &maps.m[mk], 0, y, full);
-              tma_load_2d(st + vo, &maps.m[mk + 1], 0, y, full);
+          g_last = gi;
+          if (i >= n) {            // padding slot: completes the stage's phase without data
+            mbar_arrive(full);
+            continue;
+          }
+          const int fmt = fmt_s[i], pid = pid_s[i];
+          const uint32_t sa = smem_u32(smem + SL::stages + st * kStageBytes);
+          uint32_t bytes;
+          if (fmt == IAK_FMT_F16) bytes = 2 * kPS * D * 2;
+          else if (fmt == IAK_FMT_INT4) bytes = 2 * kPS * D / 2;
+          else bytes = 2 * kPS * D;   // FP8, INT8, INT4R (two half-size planes)
+          if (GROUP && fmt != IAK_FMT_F16) bytes += (fmt == IAK_FMT_INT4R ? 4 : 2) * NG * 4;
+          mbar_arrive_expect_tx(full, bytes);
+          if (fmt == IAK_FMT_F16) {
+            if constexpr (D == 128 && kF16OneBox) {
+              tma_load_2d(sa, &maps.m[M_KF16], 0, pid * kPS * 2, full);
+              tma_load_2d(sa + kVOff, &maps.m[M_VF16], 0, pid * kPS * 2, full);
             } else {
-              const int y = pid * (kPS * D / 256);   // 128-byte lines of packed int4 token rows
-              tma_load_2d(st, &maps.m[M_KI4], 0, y, full);
-              tma_load_2d(st + vo, &maps.m[M_VI4], 0, y, full);
-              if (fmt == IAK_FMT_INT4R) {
-                tma_load_2d(st + kResOff, &maps.m[M_KI4R], 0, y, full);
-                tma_load_2d(st + vo + kResOff, &maps.m[M_VI4R], 0, y, full);
-              }
+              tma_load_2d(sa, &maps.m[M_KF16], 0, pid * kPS, full);
+              tma_load_2d(sa + kVOff, &maps.m[M_VF16], 0, pid * kPS, full);
             }
-            if (GROUP && fmt != IAK_FMT_F16) {
-              const uint32_t sc = smem_u32(dscale(cw, d));
-              bulk_load(sc, p.k_scale + static_cast<int64_t>(pid) * NG, NG * 4, full);
-              bulk_load(sc + 16, p.v_scale + static_cast<int64_t>(pid) * NG, NG * 4, full);
-              if (fmt == IAK_FMT_INT4R) {
-                bulk_load(sc + 32, p.k_rscale + static_cast<int64_t>(pid) * NG, NG * 4, full);
-                bulk_load(sc + 48, p.v_rscale + static_cast<int64_t>(pid) * NG, NG * 4, full);
-              }
+          } else if (fmt == IAK_FMT_FP8 || fmt == IAK_FMT_INT8) {
+            const int y = pid * (kPS * D / 128);   // 128-byte lines of 8-bit token rows
+            const int mk = fmt == IAK_FMT_FP8 ? M_KFP8 : M_KI8;
+            tma_load_2d(sa, &maps.m[mk], 0, y, full);
+            tma_load_2d(sa + kVOff, &maps.m[mk + 1], 0, y, full);
+          } else {
+            const int y = pid * (kPS * D / 256);   // 128-byte lines of packed int4 token rows
+            tma_load_2d(sa, &maps.m[M_KI4], 0, y, full);
+            tma_load_2d(sa + kVOff, &maps.m[M_VI4], 0, y, full);
+            if (fmt == IAK_FMT_INT4R) {
+              tma_load_2d(sa + kResOff, &maps.m[M_KI4R], 0, y, full);
+              tma_load_2d(sa + kVOff + kResOff, &maps.m[M_VI4R], 0, y, full);
             }
-#pragma unroll
-            for (int dd = 0; dd < ND; ++dd)
-              if (dd == d) ends[dd] = pos + 2 * vo;
-            head = pos + 2 * vo;
-            ++kw;
-            i += kConsumerWarps;
-            moved = true;
+          }
+          if (GROUP && fmt != IAK_FMT_F16) {
+            const uint32_t sc = smem_u32(stage_scales(st));
+            bulk_load(sc, p.k_scale + static_cast<int64_t>(pid) * NG, NG * 4, full);
+            bulk_load(sc + 16, p.v_scale + static_cast<int64_t>(pid) * NG, NG * 4, full);
+            if (fmt == IAK_FMT_INT4R) {
+              bulk_load(sc + 32, p.k_rscale + static_cast<int64_t>(pid) * NG, NG * 4, full);
+              bulk_load(sc + 48, p.v_rscale + static_cast<int64_t>(pid) * NG, NG * 4, full);
+            }
           }
         }
       }
-      if (!__any_sync(0xffffffffu, active)) break;
-      if (__any_sync(0xffffffffu, moved)) {
-        t_idle = clock64();
-      } else {
-        if (clock64() - t_idle > budget) {
-          timed_out = true;
-          break;
-        }
-        __nanosleep(64);
-      }
+      timed_out = __any_sync(0xffffffffu, timed_out);
+      ctr += n_pad;
     }
-    // drain: the latest phase of every descriptor this lane armed
-    if (feeder)
-      for (int j = kw - 1; j >= 0 && j >= kw - ND; --j)
-        if (!mbar_wait(full_bar(cw, j % ND), (j / ND) & 1, kWaitCycles)) timed_out = true;
+    // drain: a lane arms its stages in ring order with stride kProducerLanes, so its last
+    // kStages / kProducerLanes arms cover each of its stages once (their latest phase)
+    if (lane < LPW)
+      for (int j = 0; j < kStages / kProducerLanes; ++j) {
+        const int gi = g_last - j * kProducerLanes;
+        if (gi >= 0 && !mbar_wait(full_bar(gi % kStages), (gi / kStages) & 1, kWaitCycles)) timed_out = true;
+      }
     timed_out = __any_sync(0xffffffffu, timed_out);
-  } else if (warp >= kFirstConsumerWarp) {
+  } else {
     // -------------------------------------------------------------- consumers
-    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;\n" ::"n"(kRegsConsumer));
     asm volatile("griddepcontrol.wait;" ::: "memory");   // the counters the preparation kernel zeroed
     const int cw = warp - kFirstConsumerWarp;
     const float qk_log2 = p.sm_scale * 1.4426950408889634f;
-    const int S0 = p.num_splits * kConsumerWarps;   // level-0 partial slots per query row
-    const char* fifo = smem + SL::fifo + cw * kFifoBytes;
-    int kw = 0;                                     // pages this FIFO has delivered
-    uint32_t head = 0;                              // its byte position (the producer's, replayed)
+    constexpr uint32_t vo = kVOff;
+    int ctr = 0;
     for (int k = 0, item = blockIdx.x; item < n_items; ++k, item += gridDim.x) {
       const int buf = k & 1;
       const char* ib = item_buf(buf);
@@ -867,19 +959,26 @@ __global__ void __launch_bounds__(kThreads, 1)
       float oacc[KT][4];
 #pragma unroll
       for (int mt = 0; mt < KT; ++mt) oacc[mt][0] = oacc[mt][1] = oacc[mt][2] = oacc[mt][3] = 0.f;
-      for (int i = cw; i < n_valid; i += kConsumerWarps) {
-        const int fmt = fmt_s[i];
-        const uint32_t vo = page_vo<D>(fmt);
-        const uint32_t pos = fifo_place(head, 2 * vo);
-        head = pos + 2 * vo;
-        const int d = kw % ND;
-        if (!wait_all(full_bar(cw, d), (kw / ND) & 1)) {
+      // Every item occupies a whole number of rings (the tail is padding), so stage s is
+      // always filled by producer lane s % kProducerLanes and drained by consumer warp
+      // s % kConsumerWarps, one phase at a time.
+      const int n_pad = (n_valid + kStages - 1) / kStages * kStages;
+      for (int i = cw; i < n_pad; i += kConsumerWarps) {
+        const int gi = ctr + i;
+        const int st = gi % kStages, round = gi / kStages;
+        if (!wait_all(full_bar(st), round & 1)) {
           timed_out = true;
           break;
         }
-        const char* pg = fifo + (pos & (kFifoBytes - 1));
+        if (i >= n_valid) {
+          __syncwarp();
+          if (lane == 0) mbar_arrive(empty_bar(st));
+          continue;
+        }
+        const int fmt = fmt_s[i];
+        const char* pg = smem + SL::stages + st * kStageBytes;
         const uint32_t pg_u32 = smem_u32(pg);
-        const float* gsc = reinterpret_cast<const float*>(dscale(cw, d));
+        const float* gsc = reinterpret_cast<const float*>(stage_scales(st));
         // ---------------- S^T = K Q^T
         // accumulator of k-step kk: its 32-channel group (group scales) or its
         // parity (two independent MMA chains per page)
@@ -1102,85 +1201,39 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         __syncwarp();
-        if (lane == 0) mbar_arrive(empty_bar(cw, d));
-        ++kw;
+        if (lane == 0) mbar_arrive(empty_bar(st));
       }
       if (timed_out) break;
-      // ---- this warp's partial of the item (level 0)
+      // ---- this warp's partial of the item, into the CTA's merge area once the preparer
+      // has merged the previous item out of it
 #pragma unroll
       for (int off = 4; off < 32; off <<= 1) {
         l_run[0] += __shfl_xor_sync(0xffffffffu, l_run[0], off);
         l_run[1] += __shfl_xor_sync(0xffffffffu, l_run[1], off);
       }
-      const int bb = unit / p.Ht, hk = unit - bb * p.Ht;
-      const int64_t row0 = static_cast<int64_t>(bb) * p.Hq + hk * p.G;
+      if (k >= 1 && !wait_all(mfree_bar, (k - 1) & 1)) {
+        timed_out = true;
+        break;
+      }
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         const int g = 2 * c + h;
         if (g < p.G) {
-          const int64_t wi = (row0 + g) * S0 + split * kConsumerWarps + cw;
+          float* mr = merge_area + (cw * 8 + g) * kMergeRow;
           if (r == 0) {
-            p.ws_m[wi] = l_run[h] > 0.f ? m_run[h] * 0.6931471805599453f : -INFINITY;  // natural-log max
-            p.ws_l[wi] = l_run[h];
+            mr[128] = l_run[h] > 0.f ? m_run[h] * 0.6931471805599453f : -INFINITY;  // natural-log max
+            mr[129] = l_run[h];
           }
-          float* acc = p.ws_acc + wi * D;
 #pragma unroll
           for (int mt = 0; mt < KT; ++mt) {
-            acc[pv_channel<D>(mt, r)] = oacc[mt][h];
-            acc[pv_channel<D>(mt, r + 8)] = oacc[mt][2 + h];
+            mr[pv_channel<D>(mt, r)] = oacc[mt][h];
+            mr[pv_channel<D>(mt, r + 8)] = oacc[mt][2 + h];
           }
         }
       }
-      __threadfence();
       __syncwarp();
       if (lane == 0) mbar_arrive(iempty_bar(buf));
-      // ---- the item's last warp merges its kConsumerWarps partials (level 1); the
-      // unit's last item merger merges the unit's splits into the output (level 2)
-      const int item_id = unit * p.num_splits + split;
-      unsigned last = 0;
-      if (lane == 0) last = atomicAdd(&p.ws_icnt[item_id], 1u) == kConsumerWarps - 1;
-      if (__shfl_sync(0xffffffffu, last, 0)) {
-        __threadfence();
-        for (int g = 0; g < p.G; ++g) {
-          const int64_t row = row0 + g;
-          const int64_t w0 = row * S0 + split * kConsumerWarps;
-          float M, L, A[D / 32];
-          warp_merge<D>(p.ws_m + w0, p.ws_l + w0, p.ws_acc + w0 * D, kConsumerWarps, lane, M, L, A);
-          const int64_t w1 = row * p.num_splits + split;
-          if (lane == 0) {
-            p.ws_m1[w1] = M;
-            p.ws_l1[w1] = L;
-          }
-#pragma unroll
-          for (int j = 0; j < D / 32; ++j) p.ws_acc1[w1 * D + lane * (D / 32) + j] = A[j];
-        }
-        __threadfence();
-        __syncwarp();
-        unsigned ulast = 0;
-        if (lane == 0) ulast = atomicAdd(&p.ws_cnt[unit], 1u) == static_cast<unsigned>(p.num_splits) - 1;
-        if (__shfl_sync(0xffffffffu, ulast, 0)) {
-          __threadfence();
-          for (int g = 0; g < p.G; ++g) {
-            const int64_t row = row0 + g;
-            const int64_t w1 = row * p.num_splits;
-            float M, L, A[D / 32];
-            warp_merge<D>(p.ws_m1 + w1, p.ws_l1 + w1, p.ws_acc1 + w1 * D, p.num_splits, lane, M, L, A);
-            if (p.ex_l) {
-              if (lane == 0) {
-                p.ex_m[row] = M;
-                p.ex_l[row] = L;
-              }
-#pragma unroll
-              for (int j = 0; j < D / 32; ++j) p.ex_acc[row * D + lane * (D / 32) + j] = A[j];
-            } else {
-              const int64_t off = static_cast<int64_t>(bb) * p.o_sb + static_cast<int64_t>(hk * p.G + g) * p.o_sh;
-              const float inv = L > 0.f ? 1.f / L : 0.f;
-#pragma unroll
-              for (int j = 0; j < D / 32; ++j) store_from_float(p.out, p.out_dtype, off + lane * (D / 32) + j, A[j] * inv);
-            }
-          }
-        }
-      }
+      ctr += n_pad;
     }
   }
   if (timed_out && lane == 0) {
@@ -1290,7 +1343,7 @@ bool mma_shape_eligible(const DecodeParams& p) {
 
 template <int D, bool GROUP>
 static int launch_persistent(const DecodeParams& p, const TmaMaps& maps, int n_items, cudaStream_t s) {
-  const size_t smem = SmemLayout<GROUP>::total + 1024;
+  const size_t smem = SmemLayout::total + 1024;
   auto kern = decode_mma_kernel<D, GROUP>;
   // the smem attribute and occupancy are per (device, instantiation): look them up once
   static std::mutex mu;

@@ -24,15 +24,12 @@ namespace {
 
 constexpr int kPushThreads = 256;
 
-__host__ __device__ inline int64_t block_stride(int64_t rows, int D) {
-  const int64_t bf = rows * (static_cast<int64_t>(D) + 2);
-  return (bf + 63) / 64 * 64;
-}
+__host__ __device__ inline int64_t block_stride(int64_t rows, int D) { return exchange_block_stride(rows, D); }
 __host__ __device__ inline size_t staging_offset(int world, int64_t rows, int D) {
-  return static_cast<size_t>(2) * world * block_stride(rows, D) * sizeof(float);
+  return exchange_staging_offset(world, rows, D);
 }
 __host__ __device__ inline size_t flags_offset(int world, int64_t rows, int D) {
-  return staging_offset(world, rows, D) + block_stride(rows, D) * sizeof(float);
+  return exchange_flags_offset(world, rows, D);
 }
 
 struct PushParams {
@@ -90,32 +87,36 @@ __global__ void __launch_bounds__(kPushThreads) push_kernel(const PushParams p) 
   }
 }
 
-// One thread waits (bounded by timeout_ns of wall time) for every sender's flag of the
-// current epoch (the one this rank's push just published).
-__global__ void wait_kernel(const uint32_t* flags, int world, uint32_t* status, uint64_t timeout_ns) {
-  if (threadIdx.x != 0) return;
-  const uint32_t epoch = *reinterpret_cast<const volatile uint32_t*>(flags + 2 * world + 2);
-  const uint32_t* f = flags + (epoch & 1u) * world;
-  const uint64_t t0 = global_ns();
-  for (int r = 0; r < world; ++r) {
-    unsigned ns = 64;
-    while (ld_acquire_sys(f + r) != epoch) {
-      if (global_ns() - t0 > timeout_ns) {
-        if (status) atomicExch(status, 1u);
-        return;
-      }
-      __nanosleep(ns);
-      if (ns < 1024) ns <<= 1;
-    }
-  }
-}
-
-// LSE merge of the W blocks of the current parity into out (one CTA per row).
+// Bounded wait (timeout_ns of wall time) by thread 0 for every sender's flag of the
+// current epoch (the one this rank just published), then the LSE merge of the W
+// blocks of that parity into out, one CTA per row.  A CTA whose wait runs out sets
+// *status and merges whatever arrived.
 __global__ void exchange_merge_kernel(const float* area, const uint32_t* flags, int world, int64_t rows, int D,
-                                      int64_t bs, void* out, int out_dtype, int64_t out_row_stride) {
+                                      int64_t bs, void* out, int out_dtype, int64_t out_row_stride,
+                                      uint32_t* status, uint64_t timeout_ns) {
   extern __shared__ float w_s[];
   __shared__ float stat[2];
   const uint32_t epoch = *reinterpret_cast<const volatile uint32_t*>(flags + 2 * world + 2);
+  const uint32_t* f = flags + (epoch & 1u) * world;
+  if (threadIdx.x == 0) {
+    const uint64_t t0 = global_ns();
+    bool late = false;
+    for (int r = 0; r < world && !late; ++r) {
+      unsigned ns = 32;
+      while (ld_acquire_sys(f + r) != epoch) {
+        if (global_ns() - t0 > timeout_ns) {
+          late = true;
+          if (status) atomicExch(status, 1u);
+          break;
+        }
+        __nanosleep(ns);
+        if (ns < 512) ns <<= 1;
+      }
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x < world) (void)ld_acquire_sys(f + threadIdx.x);   // acquire for every reading warp
+  __syncthreads();
   const float* blocks = area + static_cast<int64_t>(epoch & 1u) * world * bs;
   for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
     if (threadIdx.x < 32) {
@@ -214,13 +215,11 @@ int iak_exchange_merge(const iak_peer_exchange* x, void* out, int32_t out_dtype,
   const float* own = static_cast<const float*>(x->areas[x->rank]);
   const uint32_t* flags = reinterpret_cast<const uint32_t*>(reinterpret_cast<const char*>(own) +
                                                            flags_offset(x->world, x->rows, x->head_dim));
-  wait_kernel<<<1, 32, 0, s>>>(flags, x->world, status, static_cast<uint64_t>(timeout_us) * 1000ull);
-  st = check_cuda(cudaGetLastError(), "exchange wait launch");
-  if (st) return st;
   const int threads = x->head_dim >= 128 ? 128 : (x->head_dim >= 64 ? 64 : 32);
   const int64_t blocks = std::min<int64_t>(x->rows, 65535LL * 8);
   exchange_merge_kernel<<<static_cast<unsigned>(blocks), threads, x->world * sizeof(float), s>>>(
-      own, flags, x->world, x->rows, x->head_dim, block_stride(x->rows, x->head_dim), out, out_dtype, out_row_stride);
+      own, flags, x->world, x->rows, x->head_dim, block_stride(x->rows, x->head_dim), out, out_dtype, out_row_stride,
+      status, static_cast<uint64_t>(timeout_us) * 1000ull);
   return check_cuda(cudaGetLastError(), "exchange merge launch");
 }
 

@@ -27,6 +27,24 @@ int read_mla_timeouts(unsigned int* value, bool reset);
 int read_prefill_timeouts(unsigned int* value, bool reset);
 // default budget of a bounded device-side wait: about 2 s at the boost clock
 constexpr long long kDefaultWaitCycles = 4000000000LL;
+
+// Exchange area of one rank (device memory of its GPU), for world W and block size
+// rows * (head_dim + 2) floats padded to BS (a multiple of 64 floats):
+//   float  blocks[2][W][BS]      receive arrays, one per parity
+//   float  staging[BS]           this rank's partial block
+//   uint32 flags[2][W]           arrival epoch of each sender, per parity
+//   uint32 push_count[2]         CTAs of this rank's push kernel that finished
+//   uint32 epoch                 last epoch this rank published
+__host__ __device__ inline int64_t exchange_block_stride(int64_t rows, int D) {
+  const int64_t bf = rows * (static_cast<int64_t>(D) + 2);
+  return (bf + 63) / 64 * 64;
+}
+__host__ __device__ inline size_t exchange_staging_offset(int world, int64_t rows, int D) {
+  return static_cast<size_t>(2) * world * exchange_block_stride(rows, D) * sizeof(float);
+}
+__host__ __device__ inline size_t exchange_flags_offset(int world, int64_t rows, int D) {
+  return exchange_staging_offset(world, rows, D) + exchange_block_stride(rows, D) * sizeof(float);
+}
 // kernel timer hooks around the main decode launch (no-ops unless enabled)
 void kernel_timer_begin(cudaStream_t s);
 void kernel_timer_end(cudaStream_t s);
@@ -56,11 +74,18 @@ struct DecodeParams {
   int tensor;    // 1: the tensor-core path runs (per-warp partial slots, query tables)
   int ws_slots;  // partial slots per query row in the workspace
   char* ws_qtab; // per-unit query tables (tensor path)
-  // tensor path, zeroed by the prep kernel on every call: per-unit count of merged
-  // items, per-item count of consumer warps done
-  unsigned int* ws_cnt; unsigned int* ws_icnt;
+  // tensor path, zeroed by the prep kernel on every call: per-unit count of merged items
+  unsigned int* ws_cnt;
   // tensor path: per-item merged partials [row][split] (level 1 of the in-kernel merge)
   float* ws_m1; float* ws_l1; float* ws_acc1;
+  // fused peer exchange (iak_decode_exchange; x_world = 0 otherwise): each row's merged
+  // partial goes straight into slot x_rank of every rank's receive array, and the
+  // last unit to finish raises this rank's flag in every area
+  float* x_areas[IAK_MAX_PEERS];
+  int x_world, x_rank;
+  int64_t x_bs;                 // partial-block stride in floats
+  int64_t x_flags_off;          // byte offset of the flags inside an area
+  unsigned int* ws_done;        // units merged by this launch (tensor path, zeroed by the prep kernel)
   // split partials, [unit][split][g] and [unit][split][g][D]
   float* ws_m; float* ws_l; float* ws_acc;
   // optional export of final per-row partials (rows = B*Hq)
@@ -75,7 +100,7 @@ int launch_decode_mma(const DecodeParams& p, const iak_page_pools& pools, cudaSt
 bool mma_shape_eligible(const DecodeParams& p);
 constexpr int kQueryTableBytes = 8704;   // per-unit query table of the tensor path
 constexpr int kTensorItemSlots = 256;    // max table slots per tensor-path work item
-constexpr int kTensorConsumerWarps = 12; // partial slots per work item
+constexpr int kTensorConsumerWarps = 4;  // partial slots per work item
 int launch_merge(const float* m, const float* l, const float* acc, int64_t rows, int splits, int D,
                  void* out, int out_dtype, int64_t out_row_stride,
                  const DecodeParams* rowmap, float* ex_m, float* ex_l, float* ex_acc, cudaStream_t s);

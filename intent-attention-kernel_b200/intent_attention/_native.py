@@ -183,6 +183,8 @@ SIGNATURES = {
     "iak_prefill": (ctypes.c_int, [ctypes.POINTER(PagePools), ctypes.POINTER(PrefillArgs), c_void_p]),
     "iak_quantize_pages": (ctypes.c_int, [ctypes.POINTER(QuantArgs), c_void_p]),
     "iak_decode_noalloc": (ctypes.c_int, [ctypes.POINTER(PagePools), ctypes.POINTER(DecodeArgs), c_void_p]),
+    "iak_decode_exchange": (ctypes.c_int, [ctypes.POINTER(PagePools), ctypes.POINTER(DecodeArgs),
+                                           ctypes.POINTER(PeerExchange), c_void_p, ctypes.c_size_t, c_void_p]),
     "iak_merge_partial_blocks": (ctypes.c_int, [c_void_p, c_i32, c_i64, c_i32, c_void_p, c_i32, c_i64, c_void_p]),
     "iak_mla_workspace_size": (ctypes.c_int, [ctypes.POINTER(MlaArgs), ctypes.POINTER(ctypes.c_size_t)]),
     "iak_mla_decode": (ctypes.c_int, [ctypes.POINTER(MlaArgs), c_void_p, ctypes.c_size_t, c_void_p]),

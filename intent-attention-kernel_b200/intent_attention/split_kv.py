@@ -29,7 +29,7 @@ from typing import Optional, Sequence, Tuple
 import torch
 
 from . import _native as N
-from .paged import PagePool, _DT, _require_cuda, _stream, paged_decode
+from .paged import PagePool, _DT, _decode_structs, _require_cuda, _stream, _workspace, paged_decode
 
 
 def shard_bounds(n: int, rank: int, world: int) -> Tuple[int, int]:
@@ -99,6 +99,32 @@ def decode_partial_block(q: torch.Tensor, pool: PagePool, page_table: torch.Tens
     paged_decode(q, pool, page_table, page_counts, page_tags, tag_map, tag_default, sm_scale,
                  partial=block_views(block, rows, D), num_splits=num_splits, kernel=kernel)
     return block
+
+
+def decode_exchange(q: torch.Tensor, pool: PagePool, page_table: torch.Tensor, page_counts: Optional[torch.Tensor],
+                    page_tags: torch.Tensor, tag_map: Sequence[int], x: "PeerExchange",
+                    tag_default: int = N.FMT_SKIP, sm_scale: Optional[float] = None, num_splits: int = 0) -> None:
+    """Decode this rank's pages with the push fused in (``iak_decode_exchange``): the
+    decode kernel stores every query row's partial into slot ``x.rank`` of every
+    rank's receive array and raises this rank's flags; ``x.merge(out)`` follows."""
+    import ctypes
+    _require_cuda(q, "q")
+    if q.dim() != 3 or q.stride(-1) != 1:
+        raise ValueError("q must be a [B, Hq, D] tensor with a contiguous last dim")
+    if page_table.dtype != torch.int32 or page_table.stride(-1) != 1:
+        page_table = page_table.to(torch.int32).contiguous()
+    if page_counts is not None and (page_counts.dtype != torch.int32 or page_counts.stride(-1) != 1):
+        page_counts = page_counts.to(torch.int32).contiguous()
+    pools, args = _decode_structs(q, pool, page_table, page_counts, page_tags, tag_map, tag_default, sm_scale,
+                                  None, None, num_splits, "tensor")
+    L = N.lib()
+    nbytes = ctypes.c_size_t(0)
+    N.check(L.iak_decode_workspace_size(ctypes.byref(pools), ctypes.byref(args), ctypes.byref(nbytes)),
+            "iak_decode_workspace_size")
+    ws = _workspace(q.device, nbytes.value)
+    N.check(L.iak_decode_exchange(ctypes.byref(pools), ctypes.byref(args), ctypes.byref(x.x),
+                                  None if ws is None else ws.data_ptr(), 0 if ws is None else ws.numel(),
+                                  _stream(q.device)), "iak_decode_exchange")
 
 
 def merge_partial_blocks(blocks: torch.Tensor, rows: int, head_dim: int,
@@ -265,11 +291,18 @@ class SequenceShardedDecoder:
         if out is None:
             out = torch.empty(q.shape, dtype=q.dtype, device=q.device)
         if self.transport == "p2p":
-            # decode into this rank's slot, store it into every peer over NVLink, bounded wait + merge
             x = self.peer_exchange(rows, D, q.device)
-            decode_partial_block(q, pool, local_table, local_counts, page_tags, tag_map, tag_default, sm_scale,
-                                 block=x.staging, num_splits=num_splits, kernel=kernel)
-            x.push()
+            if kernel != "generic" and pool.page_size == 16 and D in (64, 128) and q.dtype != torch.float32 \
+                    and pool.scale_mode != "channel" and (pool.scale_mode == "page" or D == 128):
+                # the decode kernel stores each row's partial into every rank's receive slot over
+                # NVLink and raises this rank's flags itself; one bounded-wait + merge launch follows
+                decode_exchange(q, pool, local_table, local_counts, page_tags, tag_map, x, tag_default, sm_scale,
+                                num_splits)
+            else:
+                # decode into this rank's staging block, then push it to every rank
+                decode_partial_block(q, pool, local_table, local_counts, page_tags, tag_map, tag_default, sm_scale,
+                                     block=x.staging, num_splits=num_splits, kernel=kernel)
+                x.push()
             return x.merge(out)
         send, recv = self._buffers(rows, D, q.device)
         decode_partial_block(q, pool, local_table, local_counts, page_tags, tag_map, tag_default, sm_scale,
