@@ -385,22 +385,30 @@ def build_gpu_workload(w: dict, ids: np.ndarray, fmt: np.ndarray, device, rank: 
     return pool, table.contiguous(), counts, tags, q
 
 
-def run_gpu(args):
-    from intent_attention._native import KernelTimer
+class _NoClocks:
+    rows = ()
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        return False
+
+    def summary(self):
+        return None
+
+
+def measure_decode(args, wl_name, world, rank, local, device, clocks_on=True):
+    """Build one decode workload on this rank and time it (device step, the decode
+    kernel alone, and end to end through the public API); times are max over ranks.
+    Returns the numbers the JSON line is made of."""
     import torch
     import torch.distributed as dist
+    from intent_attention._native import KernelTimer
     from intent_attention import paged_decode
-    from intent_attention.paged import make_tag_map, reserve_workspace
+    from intent_attention.paged import make_tag_map
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    device = torch.device("cuda", local)
-    if world > 1:
-        from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
-    w = workload(args.workload)
+    w = workload(wl_name)
     if args.batch:
         w["B"] = args.batch
     ids, fmt = select_pages(w)
@@ -408,7 +416,7 @@ def run_gpu(args):
     # C5 on several GPUs shards every sequence's selected pages by sequence range
     # (strong scaling, one all-gather of partial blocks per step); the other
     # workloads shard the batch (weak scaling, no collective on the data path)
-    seq_shard = args.workload == "c5" and world > 1
+    seq_shard = wl_name == "c5" and world > 1
     nbytes_total = step_bytes(w, fmt) * (1 if seq_shard else world)
     if seq_shard:
         from intent_attention.split_kv import SequenceShardedDecoder, shard_bounds
@@ -438,13 +446,13 @@ def run_gpu(args):
     step()
     torch.cuda.synchronize(device)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clocks:
+    with (ClockSampler(local) if clocks_on else _NoClocks()) as clocks:
         # nvidia-smi needs ~0.5 s to start sampling: keep the GPU under the same
         # load until samples arrive, so the clock record covers the load window
         # that ends with the timed region.  Every rank runs the same number of
         # probe rounds (steps may hold a collective).
         t_probe = time.perf_counter()
-        while True:
+        while clocks_on:
             for _ in range(20):
                 step()
             torch.cuda.synchronize(device)
@@ -545,13 +553,51 @@ def run_gpu(args):
 
     # tensor-core path (forced above, so an ineligible shape fails loudly): query-table preparation
     # and the persistent decode kernel, which merges its partials itself
-    # + for sequence shards: the block merge (NCCL), or push + bounded wait + block merge (peer stores)
-    launches_per_step = 2 + ((3 if args.exchange == "p2p" else 1) if seq_shard else 0)
+    # + for sequence shards: the block merge after NCCL's all-gather, or (peer stores, issued by the
+    # decode kernel itself) one bounded-wait + block-merge kernel
+    launches_per_step = 2 + (1 if seq_shard else 0)
     if world > 1:
         t = torch.tensor([kernel_ms], device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         kernel_ms = float(t.item())
 
+    if decoder is not None:
+        if decoder._x is not None:
+            decoder._x.check()
+        if world > 1:
+            dist.barrier()
+        decoder.close()
+    return dict(w=w, ids=ids, fmt=fmt, n_sel_total=n_sel_total, seq_shard=seq_shard, nbytes=nbytes,
+                nbytes_total=nbytes_total, t_ms=t_ms, kernel_ms=kernel_ms, e2e_ms=e2e_ms, h2d=h2d, d2h=d2h,
+                use_graph=use_graph, clocks=clocks.summary(), launches_per_step=launches_per_step)
+
+
+def run_gpu(args):
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
+    m = measure_decode(args, args.workload, world, rank, local, device)
+    # The sequence-sharded C5 step beside the default C2 line: the same run (and, for the
+    # driver's 1-8 GPU scaling run, every N) also times C5 cut by sequence over the ranks
+    # (strong scaling; unsharded on one GPU).
+    c5 = None
+    if args.workload == "c2" and not args.no_c5_strong:
+        torch.cuda.empty_cache()
+        import copy
+        a5 = copy.copy(args)
+        a5.workload, a5.batch, a5.exchange = "c5", 0, "p2p"
+        c5 = measure_decode(a5, "c5", world, rank, local, device, clocks_on=False)
+        torch.cuda.empty_cache()
+    w, ids, fmt, n_sel_total, seq_shard = m["w"], m["ids"], m["fmt"], m["n_sel_total"], m["seq_shard"]
+    nbytes, nbytes_total, t_ms, kernel_ms, e2e_ms = m["nbytes"], m["nbytes_total"], m["t_ms"], m["kernel_ms"], m["e2e_ms"]
+    h2d, d2h, use_graph, launches_per_step = m["h2d"], m["d2h"], m["use_graph"], m["launches_per_step"]
     if rank == 0:
         peak, peak_kind = measured_hbm_peak()
         gbs = nbytes / (t_ms * 1e-3) / 1e9
@@ -581,19 +627,32 @@ def run_gpu(args):
                             "intent_attention.paged_decode") +
                            " with pinned host q / page table / counts in, output out"},
             "gpu_launches": launches_per_step * args.steps,
-            "clocks": clocks.summary(),
+            "clocks": m["clocks"],
         }
         if world == 1 and not args.no_cpu_baseline:
             rec["cpu_baseline"] = cpu_baseline_record(CpuDecodeSample(w, ids, fmt), args.cpu_budget)
             ref_rec = reference_cpu_record(args.workload)
             if ref_rec is not None:
                 rec["cpu_baseline_reference"] = ref_rec
+        if c5 is not None:
+            c5_peak = measured_hbm_peak()[0]
+            rec["c5_strong"] = {
+                "workload": "C5 long-context decode (batch 8, 32 q / 8 kv heads, 512k ctx, 8192 selected pages "
+                            "per (sequence, kv head))" + (f", cut by sequence over {world} GPUs" if world > 1 else
+                                                          ", one GPU"),
+                "scaling": "strong" if world > 1 else "single GPU",
+                "value": round(c5["nbytes_total"] / (c5["t_ms"] * 1e-3) / 1e9, 2), "unit": "GB/s",
+                "us_per_step": round(c5["t_ms"] * 1e3, 2), "kernel_us": round(c5["kernel_ms"] * 1e3, 2),
+                "kernel_frac": round(c5["nbytes"] / (c5["kernel_ms"] * 1e-3) / 1e9 / c5_peak, 4),
+                "selected_kv_bytes_per_step": c5["nbytes_total"], "selected_kv_bytes_per_gpu": c5["nbytes"],
+                "e2e": {"value": round(c5["nbytes_total"] / (c5["e2e_ms"] * 1e-3) / 1e9, 2), "unit": "GB/s",
+                        "ms_per_step": round(c5["e2e_ms"], 5)},
+                "exchange": ("partial (m, l, acc) rows stored by the decode kernel into every rank's receive "
+                             "slot over NVLink, flags raised by its last unit, one bounded-wait + merge kernel"
+                             if world > 1 else "none"),
+                "gpu_launches_per_step": c5["launches_per_step"],
+                "timing": "one CUDA graph of all timed steps, max over ranks"}
         print(json.dumps(rec), flush=True)
-    if decoder is not None:
-        if decoder._x is not None:
-            decoder._x.check()
-        dist.barrier()
-        decoder.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -1441,6 +1500,8 @@ def main():
     ap.add_argument("--ref-step-s", type=float, default=0.5,
                     help="--impl reference: at least this many seconds of host work per step")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-c5-strong", action="store_true",
+                    help="default workload: skip the sequence-sharded C5 measurement added to the line")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if args.gpus != world:

@@ -123,3 +123,61 @@ def test_p2p_merge_wait_times_out_with_status_when_a_peer_never_arrives():
         assert float((torch.ones(4, device="cuda") * 2).sum().item()) == 8.0
     finally:
         L.iak_ipc_free(area.value)
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_fused_exchange_emulated_ranks_two_steps(world):
+    """iak_decode_exchange: the decode kernel stores each row's partial into every
+    rank's receive slot and raises its flag; iak_exchange_merge then merges.  One GPU
+    emulates `world` ranks with one exchange area each.  Every rank's decode is launched
+    (and completes, in stream order) before any merge, so no kernel waits on another
+    that is still running: the merges find every flag already raised.  Two steps cover
+    both parities of the receive arrays."""
+    import ctypes
+    from intent_attention import _native as N
+    from intent_attention.split_kv import decode_exchange
+    L = N.lib()
+    case = make_case(960 + world, B=2, Hq=16, Ht=4, W=90, NP=900, formats=("F16", "FP8", "INT8", "INT4"))
+    B, Hq, D = case["q"].shape
+    rows = B * Hq
+    nbytes = ctypes.c_size_t(0)
+    N.check(L.iak_exchange_area_bytes(world, rows, D, ctypes.byref(nbytes)), "area bytes")
+    areas = []
+    for _ in range(world):
+        a, h = ctypes.c_void_p(0), (ctypes.c_uint8 * 64)()
+        N.check(L.iak_ipc_alloc(nbytes.value, ctypes.byref(a), h), "alloc")
+        areas.append(a.value)
+
+    class _X:       # the attribute decode_exchange reads
+        pass
+
+    try:
+        xs = []
+        for r in range(world):
+            x = N.PeerExchange()
+            for j, a in enumerate(areas):
+                x.areas[j] = a
+            x.rank, x.world, x.rows, x.head_dim = r, world, rows, D
+            holder = _X()
+            holder.x = x
+            xs.append(holder)
+        ref = run_oracle(case)
+        status = torch.zeros(1, dtype=torch.int32, device="cuda")
+        s = torch.cuda.current_stream().cuda_stream
+        for step in range(2):
+            q = case["q"] if step == 0 else (case["q"].float() * 0.5).to(case["q"].dtype)
+            ref_q = ref if step == 0 else run_oracle(dict(case, np_q=q.float().cpu().numpy()))
+            for r in range(world):
+                t_r, c_r = shard_page_lists(case["table"], case["counts"], r, world)
+                decode_exchange(q, case["pool"], t_r, c_r, case["tags"], tag_map_for(case["formats"]), xs[r])
+            for r in range(world):
+                out = torch.full((rows, D), float("nan"), device="cuda")
+                N.check(L.iak_exchange_merge(ctypes.byref(xs[r].x), out.data_ptr(), N.DT_F32, D, status.data_ptr(),
+                                             2_000_000, s), "merge")
+                torch.cuda.synchronize()
+                np.testing.assert_allclose(out.view(B, Hq, D).cpu().numpy(), ref_q, atol=ATOL, rtol=RTOL)
+        assert int(status.item()) == 0
+    finally:
+        torch.cuda.synchronize()
+        for a in areas:
+            L.iak_ipc_free(a)
