@@ -320,23 +320,28 @@ class ClockSampler:
 # (--set full) of the same workload at the batch given, and the units (sequences) that
 # capture processed.  Traffic grows in proportion to the sequences processed, so it is
 # scaled to the benched batch.
-NCU_TRAFFIC = {"c2": {"bytes": 179_515_392, "batch": 4,
-                      "source": "ncu --set full capture of decode_mma_kernel, C2 at batch 4"},
+NCU_TRAFFIC = {"c2": {"bytes": 355_285_504, "batch": 8,
+                      "source": "ncu --set full capture of decode_mma_kernel, C2 at batch 8"},
+               "c3": {"bytes": 142_325_760, "batch": 8,
+                      "source": "ncu --set full capture of decode_mma_kernel, C3 at batch 8"},
+               "c5": {"bytes": 261_581_312, "batch": 1,
+                      "source": "ncu --set full capture of decode_mma_kernel, C5 at batch 1"},
                "c4": {"bytes": 58_652_672, "batch": 8,
                       "source": "ncu --set full capture of mla_tc_kernel, C4 at batch 8"},
                "prefill": {"bytes": 140_648_704, "batch": 2,
                            "source": "ncu --set full capture of prefill_tc_kernel<16>, the prefill workload"}}
 
 
-def ncu_traffic(workload_name, batch, nbytes):
+def ncu_traffic(workload_name, batch, nbytes, shards=1):
     """DRAM bytes of one launch at this batch and a note on where they come from; nbytes = the
-    algorithmic bytes of one launch (None: the workload's roofline unit is not bytes)."""
+    algorithmic bytes of one launch (None: the workload's roofline unit is not bytes); shards =
+    the ranks a sequence-sharded launch shares the pages with."""
     rec = NCU_TRAFFIC.get(workload_name)
     if rec is None:
         return None, "null (no ncu capture of this workload)"
-    scaled = rec["bytes"] * batch / rec["batch"]
+    scaled = rec["bytes"] * batch / rec["batch"] / shards
     note = (f"dram__bytes_read.sum + dram__bytes_write.sum of one launch at batch {rec['batch']} "
-            f"({rec['source']}), scaled x{batch / rec['batch']:g} to this batch")
+            f"({rec['source']}), scaled x{batch / rec['batch'] / shards:g} to this launch")
     if nbytes:
         note += f"; {scaled / nbytes:.3f}x the algorithmic bytes"
     return int(scaled), note
@@ -603,7 +608,7 @@ def run_gpu(args):
         gbs = nbytes / (t_ms * 1e-3) / 1e9
         kernel_gbs = nbytes / (kernel_ms * 1e-3) / 1e9
         value = nbytes_total / (t_ms * 1e-3) / 1e9
-        traffic, traffic_note = ncu_traffic(args.workload, w["B"], nbytes)
+        traffic, traffic_note = ncu_traffic(args.workload, w["B"], nbytes, world if seq_shard else 1)
         rec = {
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(t_ms, 5), "us_per_step": round(t_ms * 1e3, 2),

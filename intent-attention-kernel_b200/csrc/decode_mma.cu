@@ -1,10 +1,13 @@
 // Tensor-core split-KV paged decode for sm_100a.
 //
-// One CTA = one (sequence, page-table head) unit x one contiguous range of its
-// page table (a KV split).  Warp 4 is the producer: one lane gathers every
+// A persistent kernel, two CTAs per SM, walks a list of work items; an item is
+// one (sequence, page-table head) unit x one contiguous range of its page table
+// (a KV split).  Per CTA: warp 0 (the preparer) compacts the next item's page
+// list and bulk-copies its query table, warp 1 (the producer) gathers every
 // selected page with TMA tensor copies (128-byte swizzle, no multicast) into a
-// ring of shared-memory stages guarded by mbarriers.  Warps 0-3 consume the
-// stages round-robin; each warp owns one 16-token page at a time and runs
+// ring of shared-memory stages guarded by mbarriers, and warps 2-5 consume the
+// stages round-robin; each consumer warp owns one 16-token page at a time and
+// runs
 //
 //   S^T[16 tok x 8 q] = K[16 x D] . Q^T        (mma.sync m16n8k16, fp16 -> fp32)
 //   online softmax over tokens (exp2 domain, running max per query head)
@@ -14,9 +17,12 @@
 // exact fp16 integers by exponent-bias tricks, e4m3 codes by cvt.f16x2.e4m3x2,
 // and the per-page (or per-32-channel) scale is applied in fp32 to S and folded
 // into P for V.  The query group of a GQA head is the MMA's N dimension, so G
-// <= 8 query heads share every K/V byte.  Each consumer warp writes its own
-// (m, l, O) partial per work item to the workspace (splits x 4 slots per query
-// row) and the LSE merge kernel combines them.
+// <= 8 query heads share every K/V byte.  At the end of an item each consumer
+// warp leaves its (m, l, O) partial in a shared-memory merge area; the
+// preparer merges the four into the item's partial in the workspace, and the
+// last item of a unit to finish (a counter per unit) merges the unit's splits
+// into the output row, the caller's partial export, or every peer's exchange
+// slot, so no merge launch follows.
 //
 // Register-fragment index maps (m16n8k16, lane = 4*r + c):
 //   QK, 8-bit / 4-bit pages: k-step kk, thread c holds channels 16kk+4c..+3
