@@ -55,7 +55,9 @@ constexpr int kPS = 16;
 // Measured alternatives, all correct and all slower at C2 / C3 / C5: one CTA per SM
 // with 12 consumer warps (setmaxnreg 56 / 152) fed by one or three producer warps,
 // by the consumers themselves (TMA, bulk or cp.async copies) through per-warp byte
-// FIFOs, or from a 24-stage ring (C2 394-466 us against 275 us for this layout).
+// FIFOs, or from a 24-stage ring (C2 394-466 us against 275 us for this layout); and
+// bulk L2 prefetches of the pages 16 or 32 slots ahead of the copies (C2 370 us against
+// 283: the prefetches queue on the same TMA unit as the stage copies).
 constexpr int kConsumerWarps = 4;
 constexpr int kPrepWarp = 0;                      // prepares the next work item
 constexpr int kProducerWarps = 1;                 // warp 1 issues the TMA page loads
@@ -87,7 +89,7 @@ struct TmaMaps {
 
 // Per-unit query table (built by decode_prep_kernel, bulk-copied per work item):
 // fp16 fragments [D/16][32] uint4 | int8 terms [D/32][32] uint4 | the same in
-// INT4 order | 128 words: term scales s1[8], s2[8] (floats); at kQB1 / kQB2 the
+// INT4 order | 128 words: term scales s1[8], s2[8] = s1 / 256 (floats); at kQB1 / kQB2 the
 // int32 offsets -8 * sum(i1) / -8 * sum(i2) of each 32-channel block and query
 // head ([block][head]), at kQB1T / kQB2T the same over all channels, which start
 // the INT4 integer-MMA accumulators so that the +8 of the offset-binary codes
@@ -446,15 +448,13 @@ __global__ void __launch_bounds__(256) decode_prep_kernel(const DecodeParams p, 
     const int fe = min(max(((__float_as_int(am) >> 23) & 0xFF) - 127 - 14, -126), 126);
     if (lane == 0) qfi[g] = __int_as_float((127 - fe) << 23);
     const float s1 = am > 0.f ? am / 127.f : 1.f;
-    float t1[E], am2 = 0.f;
+    // s2 = s1 / 256 exactly (the residual q - s1 * i1 is at most s1 / 2, i.e. 128 steps of s2):
+    // the integer paths then combine the two terms' sums as 256 * I1 + I2 in int32 and apply
+    // one scale, s2
+    const float s2 = s1 * (1.f / 256.f);
+    float t1[E];
 #pragma unroll
-    for (int e = 0; e < E; ++e) {
-      t1[e] = fminf(fmaxf(rintf(q[e] / s1), -127.f), 127.f);
-      am2 = fmaxf(am2, fabsf(q[e] - t1[e] * s1));
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) am2 = fmaxf(am2, __shfl_xor_sync(0xffffffffu, am2, o));
-    const float s2 = am2 > 0.f ? am2 / 127.f : 1.f;
+    for (int e = 0; e < E; ++e) t1[e] = fminf(fmaxf(rintf(q[e] / s1), -127.f), 127.f);
     int sum1 = 0, sum2 = 0;
 #pragma unroll
     for (int e = 0; e < E; ++e) {
@@ -1018,7 +1018,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         }
         // ---------------- scores (times the K scale; INT8 / INT4 on the integer tensor path)
         float sc[4] = {0.f, 0.f, 0.f, 0.f};
-        const float s1a = qsc[2 * c], s1b = qsc[2 * c + 1], s2a = qsc[8 + 2 * c], s2b = qsc[8 + 2 * c + 1];
+        const float s2a = qsc[8 + 2 * c], s2b = qsc[8 + 2 * c + 1];
         if (fmt == IAK_FMT_F16 || fmt == IAK_FMT_FP8) {
           // fp16 fragments carry q / 2^fe: the factor 2^fe of each query column comes back here
           const float qfa = qsc[kQScF + 2 * c], qfb = qsc[kQScF + 2 * c + 1];
@@ -1039,6 +1039,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
             for (int e = 0; e < 4; ++e) sc[e] *= (e & 1) ? qfb : qfa;
           }
         } else if (fmt == IAK_FMT_INT8) {
+          // q = s2 * (256 * i1 + i2): one int32 combine and one scale per score
           int i1[4] = {0, 0, 0, 0}, i2[4] = {0, 0, 0, 0};
   #pragma unroll
           for (int j = 0; j < D / 32; ++j) {
@@ -1051,18 +1052,19 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
               const float ks = gsc[j];
   #pragma unroll
               for (int e = 0; e < 4; ++e) {
-                sc[e] = fmaf(ks, fmaf((e & 1) ? s1b : s1a, static_cast<float>(i1[e]),
-                                      ((e & 1) ? s2b : s2a) * static_cast<float>(i2[e])), sc[e]);
+                sc[e] = fmaf(ks, static_cast<float>(i1[e] * 256 + i2[e]), sc[e]);
                 i1[e] = i2[e] = 0;
               }
             }
           }
-          if (!GROUP) {
-            const float ks = scal_s[i];
+          if (GROUP) {
   #pragma unroll
-            for (int e = 0; e < 4; ++e)
-              sc[e] = ks * fmaf((e & 1) ? s1b : s1a, static_cast<float>(i1[e]),
-                                ((e & 1) ? s2b : s2a) * static_cast<float>(i2[e]));
+            for (int e = 0; e < 4; ++e) sc[e] *= (e & 1) ? s2b : s2a;
+          } else {
+            const float ks = scal_s[i];
+            const float ka = ks * s2a, kb = ks * s2b;
+  #pragma unroll
+            for (int e = 0; e < 4; ++e) sc[e] = static_cast<float>(i1[e] * 256 + i2[e]) * ((e & 1) ? kb : ka);
           }
         } else {
           // INT4 / INT4R: nibbles -> bytes (code + 8) on the u8 x s8 path; the
@@ -1097,20 +1099,18 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
                 if (GROUP) {
                   const float ks = gsc[8 * pl + j];
   #pragma unroll
-                  for (int e = 0; e < 4; ++e)
-                    sc[e] = fmaf(ks, fmaf((e & 1) ? s1b : s1a, static_cast<float>(i1[e]),
-                                          ((e & 1) ? s2b : s2a) * static_cast<float>(i2[e])), sc[e]);
+                  for (int e = 0; e < 4; ++e) sc[e] = fmaf(ks, static_cast<float>(i1[e] * 256 + i2[e]), sc[e]);
                 }
               }
             }
             if (!GROUP) {
               const float ks = scal_s[(pl == 0 ? 0 : 2) * kChunkMax + i];
   #pragma unroll
-              for (int e = 0; e < 4; ++e)
-                sc[e] = fmaf(ks, fmaf((e & 1) ? s1b : s1a, static_cast<float>(i1[e]),
-                                      ((e & 1) ? s2b : s2a) * static_cast<float>(i2[e])), sc[e]);
+              for (int e = 0; e < 4; ++e) sc[e] = fmaf(ks, static_cast<float>(i1[e] * 256 + i2[e]), sc[e]);
             }
           }
+  #pragma unroll
+          for (int e = 0; e < 4; ++e) sc[e] *= (e & 1) ? s2b : s2a;
         }
   #pragma unroll
         for (int e = 0; e < 4; ++e) sc[e] *= qk_log2;

@@ -3,33 +3,39 @@
 // heads per sequence, latent pages of a multiple of 64 tokens, dense BF16 /
 // F16 or FP8-e4m3 (per-page scale) pages.
 //
-// One CTA = one work item (sequence b, page range `split`, value half h):
-//   * the 128 head rows are the M = 128 rows of every MMA.  Q is f16: its
-//     channels [0, 256) sit in TMEM (A operand of the TS-form MMA), channels
-//     [256, 576) in shared memory (K-major, 128-byte swizzle);
-//   * latents are consumed in 64-token chunks of nine 64-channel k-blocks.
-//     A converter warpgroup loads each k-block from global memory (the
-//     producer warp bulk-prefetches chunks into L2 a few chunks ahead),
-//     converts it to f16 x 2^-8 in registers (FP8 by integer bit placement,
-//     exact; dense by one multiply, exact above the f16 subnormal range) and
-//     stores it once, swizzled, into
-//     shared memory: the 5 k-blocks outside this CTA's value half go to a
-//     9-slot ring released as soon as S has read them, the 4 value k-blocks
-//     to a double-buffered set held until P.V has read them;
-//   * S = Q . C^T: M=128, N=64 tokens, K=576 (36 tcgen05.mma; N = 64 keeps
-//     the MMA above the per-instruction floor that makes N <= 32 slow),
-//     fp32 in TMEM, two S buffers.  The softmax warpgroup owns one TMEM lane
-//     (= one head) per thread, so the online softmax needs no cross-thread
-//     reduction; P (f16) is written back over S and is the TMEM A operand of
-//     O_h += P . C[:, h*256 : h*256+256] (M=128, N=256, K=64 in 4 MMAs, the
-//     value k-blocks read MN-major), O_h fp32 in TMEM;
+// One work item (sequence b, page range `split`) runs on a cluster of two
+// CTAs on two SMs, which split the latent channels between them:
+//   * CTA 0 owns latent channels [0, 256), CTA 1 channels [256, 512) and the
+//     64 rope channels [512, 576).  Each CTA converts only its own channels of
+//     every latent row, computes the partial scores S_c = Q_c . C_c^T over
+//     them, and accumulates the value half O_c += P . C[:, 256c : 256c+256];
+//   * the 128 head rows are the M = 128 rows of every MMA; Q_c's 256 latent
+//     channels sit in TMEM (the A operand of the TS-form MMA), the rope
+//     channels of CTA 1 in shared memory (K-major, 128-byte swizzle);
+//   * latents are consumed in 64-token chunks.  A converter warpgroup loads
+//     the CTA's k-blocks (64 channels each) of a chunk from global memory,
+//     one chunk ahead in registers (the chunk after next is bulk-prefetched
+//     into L2 a few chunks ahead), converts them to f16 x 2^-8 (FP8 by integer
+//     bit placement, exact; dense by one multiply) and stores them swizzled
+//     into one of three chunk sets;
+//   * S_c: M=128, N=64 tokens, K=256 or 320, fp32 in TMEM, two S buffers.  The
+//     softmax warpgroup owns one TMEM lane (= one head) per thread.  Each
+//     thread reads its row of S_c and writes it into a local staging block;
+//     each warp then sends its 32 rows (8 KB) into the other CTA's shared
+//     memory with one bulk copy (distributed shared memory, no multicast) whose
+//     bytes complete the receiving CTA's mbarrier, waits for the other CTA's
+//     rows and adds the two; the otherwise idle page-list warp tells the other
+//     CTA when the block has been read (a cluster-scope release that stays off
+//     the softmax's path).  Both CTAs
+//     add the same two fp32 numbers (a + b == b + a), so they hold identical
+//     scores, maxima, P and l without further exchange.  P (f16) is written
+//     back over S and is the TMEM A operand of O_c += P . C_c (M=128, N=256,
+//     K=64 in 4 MMAs, the value k-blocks read MN-major), O_c fp32 in TMEM;
 //   * FP8 latents stay codes: the page scale multiplies the scores and P (so
 //     O accumulates code x scale x weight); l sums unscaled weights;
 //   * the O accumulator is rescaled lazily (only when a row max grows by
 //     more than 2^8), in TMEM.
-// TMEM: O_h 256 | S/P 2 x 64 | Q 128 columns (512 allocated: one CTA per SM).
-// The two value halves of a (b, split) each compute S: TMEM cannot hold a
-// 128 x 512 fp32 accumulator next to S.
+// TMEM: O_c 256 | S/P 2 x 64 | Q_c 128 columns (512 allocated: one CTA per SM).
 //
 // Reference: triton_mla_decode.py:155-186 (_mla_decode_cpu) per query row,
 // restated per head; rows without pages give 0.
@@ -63,20 +69,19 @@ namespace {
 using namespace tc;
 
 constexpr int kDqk = 576, kDv = 512, kHalf = kDv / 2, kRows = 128, kChunk = 64;
-constexpr int kKBlocks = kDqk / 64;                 // 64-channel k-blocks (128-byte swizzle atoms)
-constexpr int kVBlocks = kHalf / 64;                // k-blocks of one value half
-constexpr int kKOnly = kKBlocks - kVBlocks;         // k-blocks only S reads
-constexpr int kKSlots = 9;                          // ring slots for them (more than one chunk)
+constexpr int kValBlocks = kHalf / 64;              // 64-channel k-blocks of one value half (and of Q_c in TMEM)
+constexpr int kMaxBlocks = kValBlocks + 1;          // CTA 1 adds the rope block
+constexpr int kSets = 3;                            // chunk sets in flight
 constexpr int kPrefetchAhead = 4;                   // chunks prefetched into L2 ahead of the converters
-constexpr int kQTmemDims = 256;                     // Q channels [0, 256) live in TMEM (A operand)
-constexpr int kQTmemCols = kQTmemDims / 2;          // two f16 per 32-bit column
-constexpr int kQSmemKb0 = kQTmemDims / 64;          // first Q k-block kept in shared memory
-constexpr int kQSmemKbs = kKBlocks - kQSmemKb0;     // 5 blocks: channels [256, 576)
+constexpr int kQTmemCols = kHalf / 2;               // Q_c: 256 f16 channels, two per 32-bit column
 constexpr int kKbQ = kRows * 128;                   // bytes of one Q k-block (128 rows x 128 B)
 constexpr int kKb = kChunk * 128;                   // bytes of one f16 latent k-block (64 rows x 128 B)
+constexpr int kSetBytes = kMaxBlocks * kKb;
+constexpr int kXRow = kChunk * 4;                   // one head's fp32 partial scores of a chunk
+constexpr int kXBuf = kRows * kXRow;
 constexpr int kMaxItemPages = 512;
-constexpr int kThreads = 320;                       // softmax wg | converter wg | prefetch warp | MMA warp
-constexpr int kConvWarp0 = 4, kPrefWarp = 8, kMmaWarp = 9;
+constexpr int kThreads = 320;                       // softmax wg | converter wg | page-list warp | MMA warp
+constexpr int kConvWarp0 = 4, kListWarp = 8, kMmaWarp = 9;
 constexpr int kSBuf = 2;
 constexpr int kOCol = 0, kSCol = kHalf, kQCol = kSCol + kSBuf * kChunk, kTmemCols = 512;
 static_assert(kQCol + kQTmemCols <= kTmemCols, "TMEM budget");
@@ -85,23 +90,25 @@ constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 
 enum {
-  B_VCONV = 0,                    // value set: converters -> MMA (f16 k-blocks stored)
-  B_VEMPTY = B_VCONV + 2,         // value set: MMA commit after P.V -> converters
-  B_KCONV = B_VEMPTY + 2,         // ring slot: converters -> MMA
-  B_KEMPTY = B_KCONV + kKSlots,   // ring slot: MMA commit after S -> converters
-  B_SFULL = B_KEMPTY + kKSlots,   // MMA commit -> softmax (S ready)
+  B_SETFULL = 0,                  // chunk set: converters -> MMA (f16 k-blocks stored)
+  B_SETEMPTY = B_SETFULL + kSets, // chunk set: MMA commit after P.V -> converters
+  B_SFULL = B_SETEMPTY + kSets,   // MMA commit -> softmax (S_c ready)
   B_PFULL = B_SFULL + kSBuf,      // softmax -> MMA (P written, O rescaled)
   B_PVDONE = B_PFULL + kSBuf,     // MMA commit -> softmax / MMA (P.V done: O current, S/P buffer free)
-  B_DONE = B_PVDONE + kSBuf,      // MMA commit -> MMA (all MMAs retired)
-  B_QREADY,                       // softmax warps -> MMA: Q channels stored in TMEM
+  B_XFULL = B_PVDONE + kSBuf,     // the other CTA's bulk copies (32 KB per chunk) -> this CTA's softmax
+  B_XEMPTY,                       // the other CTA's page-list warp -> this CTA: it has read what this CTA sent
+  B_XREAD,                        // this CTA's softmax -> its page-list warp: received block read
+  B_DONE,                         // MMA commit -> MMA (all MMAs retired)
+  B_QREADY,                       // softmax warps -> MMA: Q_c stored in TMEM
   B_COUNT
 };
 
 struct Smem {
-  static constexpr int q = 0;                                       // Q k-blocks 4..8
-  static constexpr int vset = q + kQSmemKbs * kKbQ;                 // 2 x 4 value k-blocks
-  static constexpr int kring = vset + 2 * kVBlocks * kKb;           // 9 ring k-blocks
-  static constexpr int pid = kring + kKSlots * kKb;
+  static constexpr int q = 0;                                       // Q rope k-block (CTA 1)
+  static constexpr int sets = q + kKbQ;                             // [kSets][kMaxBlocks] latent k-blocks
+  static constexpr int xstage = sets + kSets * kSetBytes;           // [kRows][kXRow]: this CTA's S rows, sent
+  static constexpr int xbuf = xstage + kXBuf;                       // [kRows][kXRow]: the other CTA's S rows
+  static constexpr int pid = xbuf + kXBuf;
   static constexpr int pscale = pid + kMaxItemPages * 4;
   static constexpr int pfmt = pscale + kMaxItemPages * 4;
   static constexpr int bars = pfmt + kMaxItemPages;
@@ -109,7 +116,7 @@ struct Smem {
   static constexpr int nvalid = tmem + 4;
   static constexpr int total = nvalid + 12;
 };
-static_assert(Smem::vset % 1024 == 0 && Smem::kring % 1024 == 0, "1024-byte alignment");
+static_assert(Smem::sets % 1024 == 0 && kSetBytes % 1024 == 0, "1024-byte alignment");
 static_assert(Smem::bars % 8 == 0, "mbarriers need 8-byte alignment");
 static_assert(Smem::total + 1024 <= 232448, "shared memory budget");
 
@@ -144,13 +151,21 @@ __device__ __forceinline__ uint4 to_f16x8(uint4 x, bool bf) {
   return bf ? make_uint4(bf16x2_to_f16x2(x.x), bf16x2_to_f16x2(x.y), bf16x2_to_f16x2(x.z), bf16x2_to_f16x2(x.w)) : x;
 }
 
-// ---------------------------------------------------------------- kernel ---
-// k-block order of a chunk: the blocks outside this CTA's value half ascending (ring), then the value half.
-__device__ __forceinline__ int chunk_kb(int half, int i) {
-  if (i >= kKOnly) return half * kVBlocks + (i - kKOnly);
-  return i < half * kVBlocks ? i : i + kVBlocks;
+// Byte offset of 16-byte chunk q (0..15) of head row r in an exchange buffer (XOR swizzle: the 32
+// rows of a warp spread over all banks).
+__device__ __forceinline__ uint32_t xoff(int r, int q) {
+  return static_cast<uint32_t>(r * kXRow + ((q ^ (r & 15)) << 4));
 }
 
+// The converters' work comes in loads of two 16-byte words per k-block per thread: one whole
+// chunk of an FP8 page (64 rows x 64 codes per k-block), or half of a chunk of a dense page
+// (32 rows x 64 channels per k-block).
+struct LoadUnit {
+  int chunk;     // chunk index, -1 when past the end
+  int half;      // dense pages: which 32 rows
+};
+
+// ---------------------------------------------------------------- kernel ---
 __global__ void __launch_bounds__(kThreads, 1) mla_tc_kernel(const MlaParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
@@ -159,9 +174,12 @@ __global__ void __launch_bounds__(kThreads, 1) mla_tc_kernel(const MlaParams p) 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
   const int S = p.num_splits;
-  const int half = blockIdx.x & 1;
+  const int cta = static_cast<int>(cluster_ctarank());   // which channels this CTA owns
+  const int peer = cta ^ 1;
   const int split = (blockIdx.x >> 1) % S;
   const int b = (blockIdx.x >> 1) / S;
+  const int nblk = cta ? kMaxBlocks : kValBlocks;          // k-blocks this CTA converts per chunk
+  const int kb0 = cta * kValBlocks;                        // its first latent k-block
 
   int32_t* s_pid = reinterpret_cast<int32_t*>(sm + Smem::pid);
   float* s_scale = reinterpret_cast<float*>(sm + Smem::pscale);
@@ -169,30 +187,30 @@ __global__ void __launch_bounds__(kThreads, 1) mla_tc_kernel(const MlaParams p) 
   volatile uint32_t* s_tmem = reinterpret_cast<volatile uint32_t*>(sm + Smem::tmem);
   volatile int* s_nvalid = reinterpret_cast<volatile int*>(sm + Smem::nvalid);
   auto bar = [&](int i) -> uint32_t { return sbase + Smem::bars + 8u * static_cast<uint32_t>(i); };
-  // byte offsets (from sbase) of the f16 k-block slots
-  auto vslot = [&](int set, int i) -> uint32_t { return Smem::vset + (set * kVBlocks + i) * kKb; };
-  auto kslot = [&](int slot) -> uint32_t { return Smem::kring + slot * kKb; };
+  // byte offset (from sbase) of k-block i of chunk set s
+  auto blk = [&](int s, int i) -> uint32_t { return Smem::sets + s * kSetBytes + i * kKb; };
   const bool q_bf16 = p.q_dtype == IAK_DT_BF16;
   const uint16_t* qrow0 = static_cast<const uint16_t*>(p.q) + b * p.q_sb;
 
   if (tid == 0) {
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(bar(B_VCONV + i), 128);
-      mbar_init(bar(B_VEMPTY + i), 1);
-    }
-    for (int i = 0; i < kKSlots; ++i) {
-      mbar_init(bar(B_KCONV + i), 128);
-      mbar_init(bar(B_KEMPTY + i), 1);
+    for (int i = 0; i < kSets; ++i) {
+      mbar_init(bar(B_SETFULL + i), 128);
+      mbar_init(bar(B_SETEMPTY + i), 1);
     }
     for (int k = 0; k < kSBuf; ++k) {
       mbar_init(bar(B_SFULL + k), 1);
       mbar_init(bar(B_PFULL + k), 128);
       mbar_init(bar(B_PVDONE + k), 1);
     }
+    mbar_init(bar(B_XFULL), 1);
+    mbar_init(bar(B_XEMPTY), 1);
+    mbar_init(bar(B_XREAD), 128);
     mbar_init(bar(B_DONE), 1);
     mbar_init(bar(B_QREADY), 128);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    // the receive block expects the other CTA's rows of chunk 0
+    mbar_arrive_expect_tx(bar(B_XFULL), kXBuf);
   }
   if (warp == kMmaWarp) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(sbase + Smem::tmem),
@@ -200,8 +218,9 @@ __global__ void __launch_bounds__(kThreads, 1) mla_tc_kernel(const MlaParams p) 
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
-  if (warp == kPrefWarp) {
-    // compact this item's slice of the page table (valid ids of dense / FP8 pages, in order) with page scales
+  if (warp == kListWarp) {
+    // compact this item's slice of the page table (valid ids of dense / FP8 pages, in order) with
+    // page scales; both CTAs of the pair derive the same list from the same table
     const int n_tab = p.pc ? min(max(p.pc[b], 0), p.W) : p.W;
     const int lo = split * p.pages_per_split, hi = min(n_tab, lo + p.pages_per_split);
     const int32_t* table = p.pt + static_cast<int64_t>(b) * p.pt_sb;
@@ -225,22 +244,21 @@ __global__ void __launch_bounds__(kThreads, 1) mla_tc_kernel(const MlaParams p) 
     }
     if (lane == 0) *s_nvalid = cnt;
   }
-  if (warp >= kConvWarp0 && warp < kPrefWarp) {
-    // Q channels [256, 576) as f16 in the K-major 128-byte-swizzled layout; rows >= H are zero
+  if (cta == 1 && warp >= kConvWarp0 && warp < kListWarp) {
+    // Q rope channels [512, 576) as f16 in the K-major 128-byte-swizzled layout; rows >= H are zero
     const int ct = tid - kConvWarp0 * 32;
-    constexpr int kChunks = kQSmemKbs * 8;   // 16-byte chunks per row kept in shared memory
-#pragma unroll 8
-    for (int i = 0; i < kRows * kChunks / 128; ++i) {
-      const int u = ct + 128 * i, r = u / kChunks, c = u % kChunks;
+#pragma unroll
+    for (int i = 0; i < kRows * 8 / 128; ++i) {
+      const int u = ct + 128 * i, r = u >> 3, c = u & 7;
       uint4 v = make_uint4(0u, 0u, 0u, 0u);
-      if (r < p.H)
-        v = to_f16x8(*reinterpret_cast<const uint4*>(qrow0 + r * p.q_sh + kQTmemDims + c * 8), q_bf16);
-      *reinterpret_cast<uint4*>(sm + Smem::q + (c >> 3) * kKbQ + swz(r, c & 7)) = v;
+      if (r < p.H) v = to_f16x8(*reinterpret_cast<const uint4*>(qrow0 + r * p.q_sh + 2 * kHalf + c * 8), q_bf16);
+      *reinterpret_cast<uint4*>(sm + Smem::q + swz(r, c)) = v;
     }
     fence_proxy_async();
   }
   tc_fence_before();
-  __syncthreads();
+  // every barrier of both CTAs is initialised before either CTA arrives on the other's
+  cluster_sync();
   tc_fence_after();
   const uint32_t tmem = *s_tmem;
   const int n_valid = *s_nvalid;
@@ -252,182 +270,182 @@ __global__ void __launch_bounds__(kThreads, 1) mla_tc_kernel(const MlaParams p) 
     return static_cast<int64_t>(s_pid[j / cpp]) * p.PS + (j % cpp) * kChunk;
   };
 
-  if (warp == kPrefWarp) {
-    // ---------------------------------------------------------------- L2 prefetch, paced by the converters
-    if (lane == 0) {
-      auto prefetch_chunk = [&](int j) {
-        const int64_t row0 = chunk_row0(j);
-        if (s_fmt[j / cpp] == IAK_MLA_FP8)
-          prefetch_l2(p.fp8 + row0 * kDqk, kChunk * kDqk);
-        else
-          prefetch_l2(static_cast<const uint16_t*>(p.dense) + row0 * kDqk, kChunk * kDqk * 2);
-      };
-      for (int j = 0; j < kPrefetchAhead && j < T; ++j) prefetch_chunk(j);
-      for (int j = 0; j + kPrefetchAhead < T; ++j) {
-        // chunk j's value set is stored: the converters have moved past it
-        if (!mbar_wait_sleep(bar(B_VCONV + (j & 1)), (j >> 1) & 1)) { timed_out = true; break; }
-        prefetch_chunk(j + kPrefetchAhead);
+  if (warp == kListWarp) {
+    // ---------------------------------------------------------------- exchange-buffer release
+    // once this CTA's softmax has read the row block the other CTA sent for chunk j, tell the other
+    // CTA (it sends chunk j + 1 into the same block, and reuses its staging block)
+    const uint32_t xempty_remote = mapa_shared(bar(B_XEMPTY), static_cast<uint32_t>(peer));
+    for (int j = 0; j + 1 < T; ++j) {
+      if (!__all_sync(0xffffffffu, mbar_wait_sleep(bar(B_XREAD), j & 1))) {
+        timed_out = true;
+        break;
       }
+      if (lane == 0) {
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        mbar_arrive_cluster(xempty_remote);
+      }
+      __syncwarp();
     }
-  } else if (warp >= kConvWarp0 && warp < kPrefWarp) {
+    if (lane != 0) timed_out = false;           // counted once
+  } else if (warp >= kConvWarp0 && warp < kListWarp) {
     // ---------------------------------------------------------------- converters: global -> f16 -> shared
     const int ct = tid - kConvWarp0 * 32;
     const bool dense_bf16 = p.dense_dtype == IAK_DT_BF16;
-    // FP8: one 16-byte load = 16 codes of a row = two f16 chunks; 256 loads per k-block (2 per thread)
-    // dense: one 16-byte load = one f16 chunk; 512 loads per k-block (4 per thread)
-    auto load_fp8 = [&](const uint8_t* rows, int kb, uint4 (&x)[2]) {
-#pragma unroll
-      for (int i = 0; i < 2; ++i) {
-        const int u = ct + 128 * i, r = u >> 2, q = u & 3;
-        x[i] = *reinterpret_cast<const uint4*>(rows + r * kDqk + kb * 64 + q * 16);
-      }
+    auto prefetch_chunk = [&](int j) {
+      const int64_t row0 = chunk_row0(j);
+      if (s_fmt[j / cpp] == IAK_MLA_FP8)
+        prefetch_l2(p.fp8 + row0 * kDqk, kChunk * kDqk);
+      else
+        prefetch_l2(static_cast<const uint16_t*>(p.dense) + row0 * kDqk, kChunk * kDqk * 2);
     };
-    auto store_fp8 = [&](uint32_t off, const uint4 (&x)[2]) {
-#pragma unroll
-      for (int i = 0; i < 2; ++i) {
-        const int u = ct + 128 * i, r = u >> 2, q = u & 3;
-        const uint32_t w[4] = {x[i].x, x[i].y, x[i].z, x[i].w};
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          uint4 v;
-          e4m3x4_to_f16(w[2 * h], v.x, v.y);
-          e4m3x4_to_f16(w[2 * h + 1], v.z, v.w);
-          *reinterpret_cast<uint4*>(sm + off + swz(r, 2 * q + h)) = v;
-        }
-      }
+    // the two CTAs of the pair prefetch alternate chunks (each prefetch covers whole rows)
+    if (ct == 0)
+      for (int j = cta; j < kPrefetchAhead && j < T; j += 2) prefetch_chunk(j);
+    auto next_unit = [&](LoadUnit u) -> LoadUnit {
+      if (u.chunk < 0) return u;
+      if (s_fmt[u.chunk / cpp] != IAK_MLA_FP8 && u.half == 0) return LoadUnit{u.chunk, 1};
+      return u.chunk + 1 < T ? LoadUnit{u.chunk + 1, 0} : LoadUnit{-1, 0};
     };
-    auto load_dense = [&](const uint16_t* rows, int kb, uint4 (&x)[4]) {
+    // FP8 unit: thread words t = 0, 1 of k-block i are row (ct + 128t) / 4, 16-code segment (ct + 128t) % 4.
+    // Dense half h: row 32h + (ct + 128t) / 8, 8-channel segment (ct + 128t) % 8.
+    auto load_unit = [&](LoadUnit u, uint4 (&x)[kMaxBlocks][2]) {
+      if (u.chunk < 0) return;
+      const int64_t row0 = chunk_row0(u.chunk);
+      if (s_fmt[u.chunk / cpp] == IAK_MLA_FP8) {
+        const uint8_t* rows = p.fp8 + row0 * kDqk + kb0 * 64;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int u = ct + 128 * i, r = u >> 3, c = u & 7;
-        x[i] = *reinterpret_cast<const uint4*>(rows + r * kDqk + kb * 64 + c * 8);
-      }
-    };
-    auto store_dense = [&](uint32_t off, const uint4 (&x)[4]) {
+        for (int i = 0; i < kMaxBlocks; ++i)
+          if (i < nblk) {
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int u = ct + 128 * i, r = u >> 3, c = u & 7;
-        const uint4 y = x[i];
-        *reinterpret_cast<uint4*>(sm + off + swz(r, c)) =
-            dense_bf16 ? make_uint4(bf16x2_to_f16x2(y.x, kTileScale), bf16x2_to_f16x2(y.y, kTileScale),
-                                    bf16x2_to_f16x2(y.z, kTileScale), bf16x2_to_f16x2(y.w, kTileScale))
-                       : make_uint4(f16x2_tile_scale(y.x), f16x2_tile_scale(y.y), f16x2_tile_scale(y.z),
-                                    f16x2_tile_scale(y.w));
-      }
-    };
-    // Per chunk: issue the global loads of every k-block first (FP8: all nine; dense: the five ring
-    // blocks, then the four value blocks), then wait for each destination slot and store.
-    int ring_c = 0;     // ring slot uses so far (5 per chunk)
-    for (int j = 0; j < T && !timed_out; ++j) {
-      const int vs = j & 1;
-      const int pg = j / cpp;
-      const bool fp8 = s_fmt[pg] == IAK_MLA_FP8;
-      const int64_t row0 = static_cast<int64_t>(s_pid[pg]) * p.PS + (j - pg * cpp) * kChunk;
-      auto ring_store = [&](int i, auto&& store) -> bool {
-        const int c = ring_c + i, ks = c % kKSlots;
-        if (c >= kKSlots && !mbar_wait_sleep(bar(B_KEMPTY + ks), ((c / kKSlots) - 1) & 1)) return false;
-        store(kslot(ks));
-        fence_proxy_async();
-        mbar_arrive(bar(B_KCONV + ks));
-        return true;
-      };
-      bool ok = true;
-      if (fp8) {
-        const uint8_t* rows = p.fp8 + row0 * kDqk;
-        uint4 x[kKBlocks][2];
-#pragma unroll
-        for (int i = 0; i < kKBlocks; ++i) load_fp8(rows, chunk_kb(half, i), x[i]);
-#pragma unroll
-        for (int i = 0; i < kKOnly; ++i)
-          if (ok) ok = ring_store(i, [&](uint32_t off) { store_fp8(off, x[i]); });
-        if (ok && j >= 2) ok = mbar_wait_sleep(bar(B_VEMPTY + vs), ((j >> 1) - 1) & 1);
-        if (ok) {
-#pragma unroll
-          for (int i = 0; i < kVBlocks; ++i) store_fp8(vslot(vs, i), x[kKOnly + i]);
-        }
-      } else {
-        const uint16_t* rows = static_cast<const uint16_t*>(p.dense) + row0 * kDqk;
-        {
-          uint4 x[kKOnly][4];
-#pragma unroll
-          for (int i = 0; i < kKOnly; ++i) load_dense(rows, chunk_kb(half, i), x[i]);
-#pragma unroll
-          for (int i = 0; i < kKOnly; ++i)
-            if (ok) ok = ring_store(i, [&](uint32_t off) { store_dense(off, x[i]); });
-        }
-        if (ok) {
-          uint4 x[kVBlocks][4];
-#pragma unroll
-          for (int i = 0; i < kVBlocks; ++i) load_dense(rows, chunk_kb(half, kKOnly + i), x[i]);
-          if (j >= 2) ok = mbar_wait_sleep(bar(B_VEMPTY + vs), ((j >> 1) - 1) & 1);
-          if (ok) {
-#pragma unroll
-            for (int i = 0; i < kVBlocks; ++i) store_dense(vslot(vs, i), x[i]);
+            for (int t = 0; t < 2; ++t) {
+              const int w = ct + 128 * t;
+              x[i][t] = *reinterpret_cast<const uint4*>(rows + (w >> 2) * kDqk + i * 64 + (w & 3) * 16);
+            }
           }
-        }
+      } else {
+        const uint16_t* rows = static_cast<const uint16_t*>(p.dense) + (row0 + 32 * u.half) * kDqk + kb0 * 64;
+#pragma unroll
+        for (int i = 0; i < kMaxBlocks; ++i)
+          if (i < nblk) {
+#pragma unroll
+            for (int t = 0; t < 2; ++t) {
+              const int w = ct + 128 * t;
+              x[i][t] = *reinterpret_cast<const uint4*>(rows + (w >> 3) * kDqk + i * 64 + (w & 7) * 8);
+            }
+          }
       }
-      if (!ok) { timed_out = true; break; }
-      fence_proxy_async();
-      mbar_arrive(bar(B_VCONV + vs));
-      ring_c += kKOnly;
+    };
+    // store one unit into chunk set s
+    auto store_unit = [&](LoadUnit u, int s, const uint4 (&x)[kMaxBlocks][2]) {
+      if (s_fmt[u.chunk / cpp] == IAK_MLA_FP8) {
+#pragma unroll
+        for (int i = 0; i < kMaxBlocks; ++i)
+          if (i < nblk) {
+#pragma unroll
+            for (int t = 0; t < 2; ++t) {
+              const int w = ct + 128 * t, r = w >> 2, q = w & 3;
+              const uint32_t wd[4] = {x[i][t].x, x[i][t].y, x[i][t].z, x[i][t].w};
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                uint4 v;
+                e4m3x4_to_f16(wd[2 * h], v.x, v.y);
+                e4m3x4_to_f16(wd[2 * h + 1], v.z, v.w);
+                *reinterpret_cast<uint4*>(sm + blk(s, i) + swz(r, 2 * q + h)) = v;
+              }
+            }
+          }
+      } else {
+#pragma unroll
+        for (int i = 0; i < kMaxBlocks; ++i)
+          if (i < nblk) {
+#pragma unroll
+            for (int t = 0; t < 2; ++t) {
+              const int w = ct + 128 * t, r = 32 * u.half + (w >> 3), c = w & 7;
+              const uint4 y = x[i][t];
+              *reinterpret_cast<uint4*>(sm + blk(s, i) + swz(r, c)) =
+                  dense_bf16 ? make_uint4(bf16x2_to_f16x2(y.x, kTileScale), bf16x2_to_f16x2(y.y, kTileScale),
+                                          bf16x2_to_f16x2(y.z, kTileScale), bf16x2_to_f16x2(y.w, kTileScale))
+                             : make_uint4(f16x2_tile_scale(y.x), f16x2_tile_scale(y.y), f16x2_tile_scale(y.z),
+                                          f16x2_tile_scale(y.w));
+            }
+          }
+      }
+    };
+    // Process one unit whose words are in x: wait for its set at the chunk's first unit, store,
+    // and publish the set at the chunk's last unit.
+    auto process = [&](LoadUnit u, LoadUnit nxt, const uint4 (&x)[kMaxBlocks][2]) -> bool {
+      const int j = u.chunk, s = j % kSets;
+      if (u.half == 0) {
+        if (ct == 0 && j + kPrefetchAhead < T && ((j + kPrefetchAhead) & 1) == cta) prefetch_chunk(j + kPrefetchAhead);
+        if (j >= kSets && !mbar_wait_sleep(bar(B_SETEMPTY + s), ((j / kSets) - 1) & 1)) return false;
+      }
+      store_unit(u, s, x);
+      if (nxt.chunk != j) {
+        fence_proxy_async();
+        mbar_arrive(bar(B_SETFULL + s));
+      }
+      return true;
+    };
+    // Two register sets in turn: the loads of the next unit are in flight while this one is stored.
+    uint4 xa[kMaxBlocks][2], xb[kMaxBlocks][2];
+    LoadUnit cur = T > 0 ? LoadUnit{0, 0} : LoadUnit{-1, 0};
+    load_unit(cur, xa);
+    while (cur.chunk >= 0) {
+      LoadUnit nxt = next_unit(cur);
+      load_unit(nxt, xb);
+      if (!process(cur, nxt, xa)) { timed_out = true; break; }
+      cur = nxt;
+      if (cur.chunk < 0) break;
+      nxt = next_unit(cur);
+      load_unit(nxt, xa);
+      if (!process(cur, nxt, xb)) { timed_out = true; break; }
+      cur = nxt;
     }
   } else if (warp == kMmaWarp) {
     // ---------------------------------------------------------------- MMA issuer
     // The whole warp runs the loop and polls every barrier; one elected lane issues the MMAs and
     // their commits, so the operands stay warp-uniform.
     {
-      constexpr uint32_t kIdS = idesc_f16(kRows, kChunk, 0, 0);  // S = Q . C^T
-      constexpr uint32_t kIdPV = idesc_f16(kRows, kHalf, 0, 1);  // O += P . C (value blocks read MN-major)
-      const uint64_t q_desc0 = sw128_desc(sbase + Smem::q, 16, 1024);
+      constexpr uint32_t kIdS = idesc_f16(kRows, kChunk, 0, 0);  // S_c = Q_c . C_c^T
+      constexpr uint32_t kIdPV = idesc_f16(kRows, kHalf, 0, 1);  // O_c += P . C_c (value blocks read MN-major)
+      const uint64_t q_rope_desc = sw128_desc(sbase + Smem::q, 16, 1024);
       auto wait = [&](int b, uint32_t parity) -> bool { return __all_sync(0xffffffffu, mbar_wait(bar(b), parity)); };
-      // S MMAs over one k-block: A = Q block kb (TMEM for kb < 4, else shared), B = the latent block
-      auto s_block = [&](uint32_t d, int kb, uint32_t blk_off, bool first) {
-        const uint64_t bd = sw128_desc(sbase + blk_off, 16, 1024);
-#pragma unroll
-        for (int t = 0; t < 4; ++t) {
-          const uint32_t acc = (first && t == 0) ? 0u : 1u;
-          if (kb < kQSmemKb0)
-            mma_ts(d, tmem + kQCol + kb * 32 + t * 8, bd + (t * 2), kIdS, acc);
-          else
-            mma_ss(d, q_desc0 + (((kb - kQSmemKb0) * kKbQ + t * 32) >> 4), bd + (t * 2), kIdS, acc);
-        }
-      };
       if (!wait(B_QREADY, 0)) timed_out = true;
       auto issue_s = [&](int j) -> bool {
-        const int k = j & 1, vs = j & 1;
+        const int k = j & 1, s = j % kSets;
         if (j >= kSBuf && !wait(B_PVDONE + k, ((j >> 1) - 1) & 1)) return false;
-        const uint32_t d = tmem + kSCol + k * kChunk;
-        for (int i = 0; i < kKOnly; ++i) {
-          const int c = kKOnly * j + i, ks = c % kKSlots;
-          if (!wait(B_KCONV + ks, (c / kKSlots) & 1)) return false;
-          tc_fence_after();
-          if (elect_one()) {
-            s_block(d, chunk_kb(half, i), kslot(ks), i == 0);
-            mma_commit(bar(B_KEMPTY + ks));
-          }
-          __syncwarp();
-        }
-        if (!wait(B_VCONV + vs, (j >> 1) & 1)) return false;
+        if (!wait(B_SETFULL + s, (j / kSets) & 1)) return false;
         tc_fence_after();
+        const uint32_t d = tmem + kSCol + k * kChunk;
         if (elect_one()) {
-          for (int i = 0; i < kVBlocks; ++i) s_block(d, chunk_kb(half, kKOnly + i), vslot(vs, i), false);
+          for (int i = 0; i < nblk; ++i) {
+            const uint64_t bd = sw128_desc(sbase + blk(s, i), 16, 1024);
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+              const uint32_t acc = (i == 0 && t == 0) ? 0u : 1u;
+              if (i < kValBlocks)
+                mma_ts(d, tmem + kQCol + i * 32 + t * 8, bd + (t * 2), kIdS, acc);
+              else
+                mma_ss(d, q_rope_desc + ((t * 32) >> 4), bd + (t * 2), kIdS, acc);
+            }
+          }
           mma_commit(bar(B_SFULL + k));
         }
         __syncwarp();
         return true;
       };
       auto issue_pv = [&](int j) -> bool {
-        const int k = j & 1, vs = j & 1;
+        const int k = j & 1, s = j % kSets;
         if (!wait(B_PFULL + k, (j >> 1) & 1)) return false;
         tc_fence_after();
-        const uint64_t bd = sw128_desc(sbase + vslot(vs, 0), kKb, 1024);
+        const uint64_t bd = sw128_desc(sbase + blk(s, 0), kKb, 1024);
         if (elect_one()) {
 #pragma unroll
           for (int t = 0; t < kChunk / 16; ++t)
             mma_ts(tmem + kOCol, tmem + kSCol + k * kChunk + t * 8, bd + ((t * 2048) >> 4), kIdPV,
                    (j > 0 || t > 0) ? 1u : 0u);
           mma_commit(bar(B_PVDONE + k));
-          mma_commit(bar(B_VEMPTY + vs));
+          mma_commit(bar(B_SETEMPTY + s));
         }
         __syncwarp();
         return true;
@@ -443,13 +461,13 @@ __global__ void __launch_bounds__(kThreads, 1) mla_tc_kernel(const MlaParams p) 
       if (!wait(B_DONE, 0)) timed_out = true;
       if (lane != 0) timed_out = false;           // counted once
     }
-  } else {
+  } else if (warp < kConvWarp0) {
     // ---------------------------------------------------------------- softmax (warps 0-3, one head row per thread)
     const int r = tid;                                   // TMEM lane = head row
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(warp * 32) << 16);
     {
-      // Q channels [0, 256) of this row into TMEM columns kQCol.. (f16 pairs), the A operand of S
-      const uint16_t* qr = qrow0 + r * p.q_sh;
+      // Q_c (latent channels [256c, 256c + 256)) of this row into TMEM columns kQCol.. (f16 pairs)
+      const uint16_t* qr = qrow0 + r * p.q_sh + cta * kHalf;
 #pragma unroll 1
       for (int c = 0; c < kQTmemCols / 32; ++c) {
         uint32_t v[32];
@@ -465,42 +483,76 @@ __global__ void __launch_bounds__(kThreads, 1) mla_tc_kernel(const MlaParams p) 
       tc_fence_before();
       mbar_arrive(bar(B_QREADY));
     }
+    // the other CTA's receive block and its barrier; this warp's 32 rows of the blocks
+    const uint32_t x_remote = mapa_shared(sbase + Smem::xbuf, static_cast<uint32_t>(peer)) + warp * 32 * kXRow;
+    const uint32_t xfull_remote = mapa_shared(bar(B_XFULL), static_cast<uint32_t>(peer));
+    const uint32_t x_stage = sbase + Smem::xstage + warp * 32 * kXRow;
     const float base_scale = p.sm_scale * kLog2e / kTileScale;
     float m_used = -INFINITY, l = 0.f;
     for (int j = 0; j < T && !timed_out; ++j) {
       const int k = j & 1;
-      // warp-uniform outcome: the TMEM loads below are warp-collective
       // one lane polls; the outcome is broadcast (warp-uniform: the TMEM loads below are warp-collective)
       bool ok = true;
       if (lane == 0) ok = mbar_wait(bar(B_SFULL + k), (j >> 1) & 1);
       if (!__shfl_sync(0xffffffffu, ok, 0)) { timed_out = true; break; }
       tc_fence_after();
+      uint32_t sr[2][32];
+      tmem_ld32(lane_addr + kSCol + k * kChunk, sr[0]);
+      tmem_ld32(lane_addr + kSCol + k * kChunk + 32, sr[1]);
+      tmem_wait_ld();
+      // ---- exchange the partial rows with the other CTA.  Its receive block (and this CTA's staging
+      // block, which the last bulk copy read) are free once its page-list warp has reported the
+      // read of chunk j - 1.
+      if (j >= 1 && !__all_sync(0xffffffffu, mbar_wait_cluster(bar(B_XEMPTY), (j - 1) & 1))) {
+        timed_out = true;
+        break;
+      }
+#pragma unroll
+      for (int q = 0; q < kChunk / 4; ++q) {
+        const int h = q >> 3, c = (q & 7) * 4;
+        *reinterpret_cast<uint4*>(sm + Smem::xstage + xoff(r, q)) = make_uint4(sr[h][c], sr[h][c + 1], sr[h][c + 2], sr[h][c + 3]);
+      }
+      fence_proxy_async();
+      __syncwarp();
+      if (lane == 0) bulk_copy_to_cluster(x_remote, x_stage, 32 * kXRow, xfull_remote);
+      if (!__all_sync(0xffffffffu, mbar_wait_cluster(bar(B_XFULL), j & 1))) {
+        timed_out = true;
+        break;
+      }
+      // the receive block expects the other CTA's rows of chunk j + 1 (sent only after this CTA's
+      // read of chunk j is reported, so they land in the next phase)
+      if (r == 0 && j + 1 < T) mbar_arrive_expect_tx(bar(B_XFULL), kXBuf);
       // FP8 latents hold codes: the page scale multiplies the scores (key side)
       // and P (value side); l stays in unscaled softmax weights
       const float vs = s_scale[j / cpp];
       const float sc = base_scale * vs;
-      float x[kChunk], tmax = -INFINITY;
+      float x[kChunk], tmax;
       {
-        uint32_t sr[2][32];
-        tmem_ld32(lane_addr + kSCol + k * kChunk, sr[0]);
-        tmem_ld32(lane_addr + kSCol + k * kChunk + 32, sr[1]);
-        tmem_wait_ld();
+        const uint8_t* xl = sm + Smem::xbuf;
         float ma = -INFINITY, mb = -INFINITY;
 #pragma unroll
-        for (int i = 0; i < kChunk; ++i) {
-          x[i] = __uint_as_float(sr[i >> 5][i & 31]);
-          if (i & 1) mb = fmaxf(mb, x[i]);
-          else ma = fmaxf(ma, x[i]);
+        for (int q = 0; q < kChunk / 4; ++q) {
+          const uint4 o = *reinterpret_cast<const uint4*>(xl + xoff(r, q));
+          const int h = q >> 3, c = (q & 7) * 4;
+          // own + other: the other CTA adds the same two numbers in the other order (identical sums)
+          x[4 * q] = __uint_as_float(sr[h][c]) + __uint_as_float(o.x);
+          x[4 * q + 1] = __uint_as_float(sr[h][c + 1]) + __uint_as_float(o.y);
+          x[4 * q + 2] = __uint_as_float(sr[h][c + 2]) + __uint_as_float(o.z);
+          x[4 * q + 3] = __uint_as_float(sr[h][c + 3]) + __uint_as_float(o.w);
+          ma = fmaxf(ma, fmaxf(x[4 * q], x[4 * q + 2]));
+          mb = fmaxf(mb, fmaxf(x[4 * q + 1], x[4 * q + 3]));
         }
         // sc > 0: the max of the scaled scores is the scaled max
         tmax = fmaxf(ma, mb) * sc;
       }
+      // the received block has been read (the page-list warp forwards this to the other CTA)
+      mbar_arrive(bar(B_XREAD));
       if (j == 0) {
         m_used = tmax;
       } else {
         const bool need = tmax > m_used + kLazyLog2;
         if (__any_sync(0xffffffffu, need)) {
-          // rescale O_h in TMEM: every earlier P.V must have landed
+          // rescale O_c in TMEM: every earlier P.V must have landed
           if (!__all_sync(0xffffffffu, mbar_wait_sleep(bar(B_PVDONE + ((j - 1) & 1)), ((j - 1) >> 1) & 1))) {
             timed_out = true;
             break;
@@ -555,13 +607,13 @@ __global__ void __launch_bounds__(kThreads, 1) mla_tc_kernel(const MlaParams p) 
     float* acc_dst = nullptr;
     if (S > 1) {
       const int64_t wi = row * S + split;
-      if (row_ok && half == 0) {
+      if (row_ok && cta == 0) {
         p.ws_m[wi] = have ? m_nat : -INFINITY;
         p.ws_l[wi] = have ? l : 0.f;
       }
       acc_dst = p.ws_acc + wi * p.Dv;
     } else if (p.ex_l) {
-      if (row_ok && half == 0) {
+      if (row_ok && cta == 0) {
         p.ex_m[row] = have ? m_nat : -INFINITY;
         p.ex_l[row] = have ? l : 0.f;
       }
@@ -578,7 +630,7 @@ __global__ void __launch_bounds__(kThreads, 1) mla_tc_kernel(const MlaParams p) 
         for (int i = 0; i < 32; ++i) o[i] = 0u;
       }
       if (!row_ok) continue;
-      const int d0 = half * kHalf + c * 32;
+      const int d0 = cta * kHalf + c * 32;
       if (acc_dst) {
 #pragma unroll
         for (int i = 0; i < 32; i += 4)
@@ -600,6 +652,9 @@ __global__ void __launch_bounds__(kThreads, 1) mla_tc_kernel(const MlaParams p) 
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
   }
   if (timed_out) atomicAdd(&g_mla_timeouts, 1u);
+  __syncwarp();
+  // neither CTA leaves while the other may still store into its shared memory or arrive on its barriers
+  cluster_sync();
 }
 
 }  // namespace
@@ -619,7 +674,7 @@ bool mla_tc_eligible(const MlaParams& p) {
   return true;
 }
 
-// Items = batch x splits x 2 value halves, one CTA each, one CTA per SM:
+// Items = batch x splits, each a cluster of two CTAs (one per SM):
 // pick the split count minimising waves x (pages per item + a fixed cost
 // of about four pages for the Q staging and pipeline fill).
 void plan_mla_tc(MlaParams* p, int requested) {
@@ -662,9 +717,22 @@ int launch_mla_tc(const MlaParams& p, cudaStream_t s) {
       if (dev >= 0 && dev < 64) attr_set[dev] = true;
     }
   }
+  // one cluster of two CTAs (on two SMs) per work item
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(items));
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
   kernel_timer_begin(s);
-  mla_tc_kernel<<<static_cast<unsigned>(items), kThreads, smem, s>>>(p);
-  err = cudaGetLastError();
+  err = cudaLaunchKernelEx(&cfg, mla_tc_kernel, p);
+  if (err == cudaSuccess) err = cudaGetLastError();
   kernel_timer_end(s);
   return check_cuda(err, "mla_tc launch");
 }

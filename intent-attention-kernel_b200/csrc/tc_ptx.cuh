@@ -149,5 +149,66 @@ __device__ __forceinline__ void e4m3x4_to_f16(uint32_t w, uint32_t& lo, uint32_t
   lo = e4m3_pair_bits(__byte_perm(w, 0u, 0x4140));
   hi = e4m3_pair_bits(__byte_perm(w, 0u, 0x4342));
 }
+
+// ------------------------------------------------------------- thread-block clusters ---
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// All threads of every CTA of the cluster (memory ordered at cluster scope).
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// The shared::cluster address of the same shared-memory offset in CTA `rank` of this cluster.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+// Plain store of 16 bytes into another CTA's shared memory (distributed shared memory).
+__device__ __forceinline__ void st_cluster_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.shared::cluster.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d)
+               : "memory");
+}
+// Asynchronous store of 16 bytes into another CTA's shared memory; on arrival it completes 16
+// bytes of transactions on that CTA's mbarrier (both addresses shared::cluster, from mapa).
+__device__ __forceinline__ void st_async_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d,
+                                            uint32_t remote_bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(addr),
+               "r"(a), "r"(b), "r"(c), "r"(d), "r"(remote_bar)
+               : "memory");
+}
+// Bulk copy of `bytes` (a multiple of 16) from this CTA's shared memory (src, 16-byte aligned) into
+// another CTA's (dst, shared::cluster from mapa), completing `bytes` transactions on that CTA's
+// mbarrier (remote_bar, shared::cluster).  Plain (non-multicast) form.
+__device__ __forceinline__ void bulk_copy_to_cluster(uint32_t dst, uint32_t src, uint32_t bytes, uint32_t remote_bar) {
+  asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "r"(src), "r"(bytes), "r"(remote_bar)
+               : "memory");
+}
+// Arrive on an mbarrier of another CTA of the cluster, releasing this thread's earlier writes
+// (and ordering its earlier reads) at cluster scope.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait_acq_cluster(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait with cluster-scope acquire: for phases completed by another CTA's arrivals.
+__device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity) {
+  if (mbar_try_wait_acq_cluster(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (!mbar_try_wait_acq_cluster(bar, parity))
+    if (clock64() - t0 > kTcWaitCycles) return false;
+  return true;
+}
 }  // namespace tc
 }  // namespace iak

@@ -20,6 +20,9 @@ probabilities, the fp16 query fragments of the FP16 / FP8 path) with inputs
 the random N(0, 1) cases never produce.
 """
 
+import json
+import os
+
 import numpy as np
 import pytest
 import torch
@@ -35,11 +38,25 @@ pytestmark = pytest.mark.gpu
 ATOL, RTOL = 2e-3, 1e-2
 ORACLE_FMT = {1: "F16", 2: "FP8", 3: "INT8", 4: "INT4", 5: "INT4R"}
 _BUILT = {}
+# worst errors per configuration; written as JSON to $IAK_PARITY_REPORT (when set) after the module
+_REPORT = {}
 
 
-def _close(got, ref, atol=ATOL, rtol=RTOL):
+def _close(got, ref, atol=ATOL, rtol=RTOL, key=None):
     got = got.float().cpu().numpy() if isinstance(got, torch.Tensor) else got
+    if key is not None:
+        err = np.abs(got.astype(np.float64) - ref)
+        _REPORT[key] = {"max_abs": float(err.max()), "max_abs_over_max_ref": float(err.max() / np.abs(ref).max()),
+                        "max_rel_where_ref_above_atol": float(np.max((err / np.abs(ref))[np.abs(ref) > atol], initial=0.0)),
+                        "elements": int(ref.size), "atol": atol, "rtol": rtol}
     np.testing.assert_allclose(got, ref, atol=atol, rtol=rtol)
+
+
+def teardown_module(module):
+    path = os.environ.get("IAK_PARITY_REPORT")
+    if path and _REPORT:
+        with open(path, "w") as f:
+            json.dump(_REPORT, f, indent=1)
 
 
 def _config(name, batch):
@@ -75,7 +92,7 @@ def test_c1_config_shape():
     w, ids, fmt = cfg[:3]
     assert ids.size == 74 and set(np.unique(fmt)) == {1, 3}
     assert (fmt[(ids >= 8) & (ids < 64)] == 3).all() and (fmt[(ids < 8) | (ids >= 80)] == 1).all()
-    _close(_decode(cfg), cfg[-1])
+    _close(_decode(cfg), cfg[-1], key="C1")
 
 
 @pytest.mark.parametrize("batch", [1, 2])
@@ -86,7 +103,7 @@ def test_c2_config_shape(batch):
     w, ids, fmt = cfg[:3]
     assert ids.size == 1024 and w["Hq"] == 32 and w["Hkv"] == 8 and cfg[7].dtype == torch.bfloat16
     assert np.bincount(fmt, minlength=6)[[1, 2, 3]].tolist() == [307, 410, 307]
-    _close(_decode(cfg), cfg[-1])
+    _close(_decode(cfg), cfg[-1], key=f"C2 batch {batch}")
 
 
 def test_c3_config_shape():
@@ -96,7 +113,7 @@ def test_c3_config_shape():
     w, ids, fmt = cfg[:3]
     assert ids.size == 512 and w["Hq"] // w["Hkv"] == 8 and w["scale_mode"] == "group32"
     assert np.bincount(fmt, minlength=6)[[1, 4, 5]].tolist() == [102, 205, 205]
-    _close(_decode(cfg), cfg[-1])
+    _close(_decode(cfg), cfg[-1], key="C3")
 
 
 def test_c5_config_shape():
@@ -105,7 +122,7 @@ def test_c5_config_shape():
     cfg = _config("c5", 1)
     w, ids, fmt = cfg[:3]
     assert ids.size == 8192 and w["T"] == 524288
-    _close(_decode(cfg), cfg[-1])
+    _close(_decode(cfg), cfg[-1], key="C5")
 
 
 def test_c5_config_shape_eight_shards_merged():
@@ -120,7 +137,7 @@ def test_c5_config_shape_eight_shards_merged():
         t_r, c_r = shard_page_lists(table, counts, r, world)
         decode_partial_block(q, pool, t_r, c_r, tags, tag_map, block=blocks.view(world, -1)[r], kernel="tensor")
     out = merge_partial_blocks(blocks, rows, D).view(B, Hq, D)
-    _close(out, ref)
+    _close(out, ref, key="C5 as 8 sequence shards")
 
 
 @pytest.mark.parametrize("splits", [1, 5])
@@ -154,7 +171,7 @@ def test_c4_config_shape():
              "fp8": fp8.index_select(0, uniq).cpu().numpy()}
     ref = omla.mla_paged_decode(q.float().cpu().numpy(), ct, None, tags.long().index_select(0, uniq).cpu().numpy(),
                                 pools, scale.index_select(0, uniq).cpu().numpy(), w["Dv"], sm)
-    _close(out, ref)
+    _close(out, ref, key="C4")
 
 
 # ------------------------------------------------------------------ stress cases
