@@ -5,20 +5,20 @@
 //
 // One work item (sequence b, page range `split`) runs on a cluster of two
 // CTAs on two SMs, which split the latent channels between them:
-//   * CTA 0 owns latent channels [0, 256), CTA 1 channels [256, 512) and the
-//     64 rope channels [512, 576).  Each CTA converts only its own channels of
+//   * CTA 0 owns latent channels [0, 256) and rope channels [512, 544), CTA 1
+//     channels [256, 512) and [544, 576).  Each CTA converts only its own channels of
 //     every latent row, computes the partial scores S_c = Q_c . C_c^T over
 //     them, and accumulates the value half O_c += P . C[:, 256c : 256c+256];
 //   * the 128 head rows are the M = 128 rows of every MMA; Q_c's 256 latent
 //     channels sit in TMEM (the A operand of the TS-form MMA), the rope
-//     channels of CTA 1 in shared memory (K-major, 128-byte swizzle);
+//     channels in shared memory (K-major, 128-byte swizzle);
 //   * latents are consumed in 64-token chunks.  A converter warpgroup loads
 //     the CTA's k-blocks (64 channels each) of a chunk from global memory,
-//     one chunk ahead in registers (the chunk after next is bulk-prefetched
-//     into L2 a few chunks ahead), converts them to f16 x 2^-8 (FP8 by integer
-//     bit placement, exact; dense by one multiply) and stores them swizzled
-//     into one of three chunk sets;
-//   * S_c: M=128, N=64 tokens, K=256 or 320, fp32 in TMEM, two S buffers.  The
+//     one chunk ahead in registers (chunks are bulk-prefetched into L2 a few
+//     chunks ahead), converts them to f16 x 2^-8 (FP8 by the hardware e4m3x2
+//     conversion and a multiply, exact; dense by one multiply) and stores them
+//     swizzled into one of three chunk sets;
+//   * S_c: M=128, N=64 tokens, K=288 (18 MMAs), fp32 in TMEM, two S buffers.  The
 //     softmax warpgroup owns one TMEM lane (= one head) per thread.  Each
 //     thread reads its row of S_c and writes it into a local staging block;
 //     each warp then sends its 32 rows (8 KB) into the other CTA's shared
@@ -36,6 +36,14 @@
 //   * the O accumulator is rescaled lazily (only when a row max grows by
 //     more than 2^8), in TMEM.
 // TMEM: O_c 256 | S/P 2 x 64 | Q_c 128 columns (512 allocated: one CTA per SM).
+//
+// Measured at the C4 shape (batch 64, 154 pages, per launch): this kernel 398 us.
+// One CTA per value half computing the whole S (no exchange, twice the S MMAs and
+// conversions): 519 us with its converters loading a chunk at once, 499 us with a
+// two-chunk ring, 815-1060 us with loads pipelined one unit or eight jobs ahead
+// in registers (each use then waits on loads issued after it).  Exchanging the
+// partial scores with per-thread st.async stores instead of per-warp bulk copies:
+// 504 us; with plain remote stores and cluster-scope release arrivals: 695 us.
 //
 // Reference: triton_mla_decode.py:155-186 (_mla_decode_cpu) per query row,
 // restated per head; rows without pages give 0.
@@ -70,7 +78,8 @@ using namespace tc;
 
 constexpr int kDqk = 576, kDv = 512, kHalf = kDv / 2, kRows = 128, kChunk = 64;
 constexpr int kValBlocks = kHalf / 64;              // 64-channel k-blocks of one value half (and of Q_c in TMEM)
-constexpr int kMaxBlocks = kValBlocks + 1;          // CTA 1 adds the rope block
+constexpr int kMaxBlocks = kValBlocks + 1;          // + the rope block (each CTA fills its 32 channels)
+constexpr int kRopeHalf = 32;                       // rope channels per CTA
 constexpr int kSets = 3;                            // chunk sets in flight
 constexpr int kPrefetchAhead = 4;                   // chunks prefetched into L2 ahead of the converters
 constexpr int kQTmemCols = kHalf / 2;               // Q_c: 256 f16 channels, two per 32-bit column
@@ -104,7 +113,7 @@ enum {
 };
 
 struct Smem {
-  static constexpr int q = 0;                                       // Q rope k-block (CTA 1)
+  static constexpr int q = 0;                                       // Q rope k-block
   static constexpr int sets = q + kKbQ;                             // [kSets][kMaxBlocks] latent k-blocks
   static constexpr int xstage = sets + kSets * kSetBytes;           // [kRows][kXRow]: this CTA's S rows, sent
   static constexpr int xbuf = xstage + kXBuf;                       // [kRows][kXRow]: the other CTA's S rows
@@ -121,10 +130,7 @@ static_assert(Smem::bars % 8 == 0, "mbarriers need 8-byte alignment");
 static_assert(Smem::total + 1024 <= 232448, "shared memory budget");
 
 // Latent tiles are stored in shared memory as f16 holding value * 2^-8 (kTileScale):
-// * an e4m3 code s.eeee.mmm placed as the f16 bit pattern s.0eeee.mmm0000000 is
-//   exactly code * 2^-8 for every finite code, normals and subnormals alike (e4m3
-//   bias 7, f16 bias 15, both keep an implicit 1 above 0 and the same subnormal
-//   scaling), so FP8 k-blocks need only integer ops, no conversion instructions;
+// * FP8 codes: hardware e4m3x2 -> f16x2 conversion, then times 2^-8 (both exact);
 // * dense rows are multiplied by 2^-8 on the way (exact above the f16 subnormal
 //   range, 2^-24 absolute resolution below it).
 // The 2^8 is restored in the score scale and in the final normalisation.
@@ -178,8 +184,8 @@ __global__ void __launch_bounds__(kThreads, 1) mla_tc_kernel(const MlaParams p) 
   const int peer = cta ^ 1;
   const int split = (blockIdx.x >> 1) % S;
   const int b = (blockIdx.x >> 1) / S;
-  const int nblk = cta ? kMaxBlocks : kValBlocks;          // k-blocks this CTA converts per chunk
   const int kb0 = cta * kValBlocks;                        // its first latent k-block
+  const int rope0 = 2 * kHalf + cta * kRopeHalf;           // its first rope channel
 
   int32_t* s_pid = reinterpret_cast<int32_t*>(sm + Smem::pid);
   float* s_scale = reinterpret_cast<float*>(sm + Smem::pscale);
@@ -244,7 +250,7 @@ __global__ void __launch_bounds__(kThreads, 1) mla_tc_kernel(const MlaParams p) 
     }
     if (lane == 0) *s_nvalid = cnt;
   }
-  if (cta == 1 && warp >= kConvWarp0 && warp < kListWarp) {
+  if (warp >= kConvWarp0 && warp < kListWarp) {
     // Q rope channels [512, 576) as f16 in the K-major 128-byte-swizzled layout; rows >= H are zero
     const int ct = tid - kConvWarp0 * 32;
 #pragma unroll
@@ -306,69 +312,73 @@ __global__ void __launch_bounds__(kThreads, 1) mla_tc_kernel(const MlaParams p) 
       if (s_fmt[u.chunk / cpp] != IAK_MLA_FP8 && u.half == 0) return LoadUnit{u.chunk, 1};
       return u.chunk + 1 < T ? LoadUnit{u.chunk + 1, 0} : LoadUnit{-1, 0};
     };
-    // FP8 unit: thread words t = 0, 1 of k-block i are row (ct + 128t) / 4, 16-code segment (ct + 128t) % 4.
-    // Dense half h: row 32h + (ct + 128t) / 8, 8-channel segment (ct + 128t) % 8.
+    // FP8 unit: thread words t = 0, 1 of value k-block i are row (ct + 128t) / 4, 16-code segment
+    // (ct + 128t) % 4; of the rope block (word 0 only) row ct / 2, 16-code segment ct % 2 of this
+    // CTA's 32 rope channels.  Dense half h: value words row 32h + (ct + 128t) / 8, 8-channel segment
+    // (ct + 128t) % 8; rope word row 32h + ct / 4, 8-channel segment ct % 4.
     auto load_unit = [&](LoadUnit u, uint4 (&x)[kMaxBlocks][2]) {
       if (u.chunk < 0) return;
       const int64_t row0 = chunk_row0(u.chunk);
       if (s_fmt[u.chunk / cpp] == IAK_MLA_FP8) {
-        const uint8_t* rows = p.fp8 + row0 * kDqk + kb0 * 64;
+        const uint8_t* rows = p.fp8 + row0 * kDqk;
 #pragma unroll
-        for (int i = 0; i < kMaxBlocks; ++i)
-          if (i < nblk) {
+        for (int i = 0; i < kValBlocks; ++i)
 #pragma unroll
-            for (int t = 0; t < 2; ++t) {
-              const int w = ct + 128 * t;
-              x[i][t] = *reinterpret_cast<const uint4*>(rows + (w >> 2) * kDqk + i * 64 + (w & 3) * 16);
-            }
+          for (int t = 0; t < 2; ++t) {
+            const int w = ct + 128 * t;
+            x[i][t] = *reinterpret_cast<const uint4*>(rows + (w >> 2) * kDqk + (kb0 + i) * 64 + (w & 3) * 16);
           }
+        x[kValBlocks][0] = *reinterpret_cast<const uint4*>(rows + (ct >> 1) * kDqk + rope0 + (ct & 1) * 16);
       } else {
-        const uint16_t* rows = static_cast<const uint16_t*>(p.dense) + (row0 + 32 * u.half) * kDqk + kb0 * 64;
+        const uint16_t* rows = static_cast<const uint16_t*>(p.dense) + (row0 + 32 * u.half) * kDqk;
 #pragma unroll
-        for (int i = 0; i < kMaxBlocks; ++i)
-          if (i < nblk) {
+        for (int i = 0; i < kValBlocks; ++i)
 #pragma unroll
-            for (int t = 0; t < 2; ++t) {
-              const int w = ct + 128 * t;
-              x[i][t] = *reinterpret_cast<const uint4*>(rows + (w >> 3) * kDqk + i * 64 + (w & 7) * 8);
-            }
+          for (int t = 0; t < 2; ++t) {
+            const int w = ct + 128 * t;
+            x[i][t] = *reinterpret_cast<const uint4*>(rows + (w >> 3) * kDqk + (kb0 + i) * 64 + (w & 7) * 8);
           }
+        x[kValBlocks][0] = *reinterpret_cast<const uint4*>(rows + (ct >> 2) * kDqk + rope0 + (ct & 3) * 8);
       }
     };
-    // store one unit into chunk set s
+    auto store_fp8 = [&](uint32_t off, int r, int c, const uint4& x) {   // 16 codes -> f16 chunks c, c + 1
+      const uint32_t wd[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        uint4 v;
+        e4m3x4_to_f16_scaled(wd[2 * h], v.x, v.y);
+        e4m3x4_to_f16_scaled(wd[2 * h + 1], v.z, v.w);
+        *reinterpret_cast<uint4*>(sm + off + swz(r, c + h)) = v;
+      }
+    };
+    auto store_dense = [&](uint32_t off, int r, int c, const uint4& y) {   // 8 channels -> f16 chunk c
+      *reinterpret_cast<uint4*>(sm + off + swz(r, c)) =
+          dense_bf16 ? make_uint4(bf16x2_to_f16x2(y.x, kTileScale), bf16x2_to_f16x2(y.y, kTileScale),
+                                  bf16x2_to_f16x2(y.z, kTileScale), bf16x2_to_f16x2(y.w, kTileScale))
+                     : make_uint4(f16x2_tile_scale(y.x), f16x2_tile_scale(y.y), f16x2_tile_scale(y.z),
+                                  f16x2_tile_scale(y.w));
+    };
+    // store one unit into chunk set s (the rope block holds this CTA's 32 channels at their place:
+    // 16-byte chunks 4 * cta .. 4 * cta + 3 of each row)
     auto store_unit = [&](LoadUnit u, int s, const uint4 (&x)[kMaxBlocks][2]) {
       if (s_fmt[u.chunk / cpp] == IAK_MLA_FP8) {
 #pragma unroll
-        for (int i = 0; i < kMaxBlocks; ++i)
-          if (i < nblk) {
+        for (int i = 0; i < kValBlocks; ++i)
 #pragma unroll
-            for (int t = 0; t < 2; ++t) {
-              const int w = ct + 128 * t, r = w >> 2, q = w & 3;
-              const uint32_t wd[4] = {x[i][t].x, x[i][t].y, x[i][t].z, x[i][t].w};
-#pragma unroll
-              for (int h = 0; h < 2; ++h) {
-                uint4 v;
-                e4m3x4_to_f16(wd[2 * h], v.x, v.y);
-                e4m3x4_to_f16(wd[2 * h + 1], v.z, v.w);
-                *reinterpret_cast<uint4*>(sm + blk(s, i) + swz(r, 2 * q + h)) = v;
-              }
-            }
+          for (int t = 0; t < 2; ++t) {
+            const int w = ct + 128 * t;
+            store_fp8(blk(s, i), w >> 2, 2 * (w & 3), x[i][t]);
           }
+        store_fp8(blk(s, kValBlocks), ct >> 1, 4 * cta + 2 * (ct & 1), x[kValBlocks][0]);
       } else {
 #pragma unroll
-        for (int i = 0; i < kMaxBlocks; ++i)
-          if (i < nblk) {
+        for (int i = 0; i < kValBlocks; ++i)
 #pragma unroll
-            for (int t = 0; t < 2; ++t) {
-              const int w = ct + 128 * t, r = 32 * u.half + (w >> 3), c = w & 7;
-              const uint4 y = x[i][t];
-              *reinterpret_cast<uint4*>(sm + blk(s, i) + swz(r, c)) =
-                  dense_bf16 ? make_uint4(bf16x2_to_f16x2(y.x, kTileScale), bf16x2_to_f16x2(y.y, kTileScale),
-                                          bf16x2_to_f16x2(y.z, kTileScale), bf16x2_to_f16x2(y.w, kTileScale))
-                             : make_uint4(f16x2_tile_scale(y.x), f16x2_tile_scale(y.y), f16x2_tile_scale(y.z),
-                                          f16x2_tile_scale(y.w));
-            }
+          for (int t = 0; t < 2; ++t) {
+            const int w = ct + 128 * t;
+            store_dense(blk(s, i), 32 * u.half + (w >> 3), w & 7, x[i][t]);
           }
+        store_dense(blk(s, kValBlocks), 32 * u.half + (ct >> 2), 4 * cta + (ct & 3), x[kValBlocks][0]);
       }
     };
     // Process one unit whose words are in x: wait for its set at the chunk's first unit, store,
@@ -418,16 +428,18 @@ __global__ void __launch_bounds__(kThreads, 1) mla_tc_kernel(const MlaParams p) 
         tc_fence_after();
         const uint32_t d = tmem + kSCol + k * kChunk;
         if (elect_one()) {
-          for (int i = 0; i < nblk; ++i) {
+          for (int i = 0; i < kValBlocks; ++i) {
             const uint64_t bd = sw128_desc(sbase + blk(s, i), 16, 1024);
 #pragma unroll
-            for (int t = 0; t < 4; ++t) {
-              const uint32_t acc = (i == 0 && t == 0) ? 0u : 1u;
-              if (i < kValBlocks)
-                mma_ts(d, tmem + kQCol + i * 32 + t * 8, bd + (t * 2), kIdS, acc);
-              else
-                mma_ss(d, q_rope_desc + ((t * 32) >> 4), bd + (t * 2), kIdS, acc);
-            }
+            for (int t = 0; t < 4; ++t)
+              mma_ts(d, tmem + kQCol + i * 32 + t * 8, bd + (t * 2), kIdS, (i == 0 && t == 0) ? 0u : 1u);
+          }
+          {
+            // this CTA's 32 rope channels: k-steps 2 * cta and 2 * cta + 1 of the rope block
+            const uint64_t bd = sw128_desc(sbase + blk(s, kValBlocks), 16, 1024);
+#pragma unroll
+            for (int t = 2 * cta; t < 2 * cta + 2; ++t)
+              mma_ss(d, q_rope_desc + ((t * 32) >> 4), bd + (t * 2), kIdS, 1u);
           }
           mma_commit(bar(B_SFULL + k));
         }

@@ -3,6 +3,7 @@
 #pragma once
 
 #include <cstdint>
+#include <cuda_fp16.h>
 
 namespace iak {
 namespace tc {
@@ -148,6 +149,21 @@ __device__ __forceinline__ uint32_t e4m3_pair_bits(uint32_t t) {
 __device__ __forceinline__ void e4m3x4_to_f16(uint32_t w, uint32_t& lo, uint32_t& hi) {
   lo = e4m3_pair_bits(__byte_perm(w, 0u, 0x4140));
   hi = e4m3_pair_bits(__byte_perm(w, 0u, 0x4342));
+}
+
+// four e4m3 codes of w -> two f16x2 words of code * 2^-8 (first code in the low half of the first
+// word) with the hardware e4m3x2 conversion (exact: every finite e4m3 value is an f16) and one
+// multiply by 2^-8 per pair (exact: the smallest e4m3 subnormal, 2^-9, times 2^-8 stays above
+// f16's smallest subnormal, 2^-24)
+__device__ __forceinline__ void e4m3x4_to_f16_scaled(uint32_t w, uint32_t& lo, uint32_t& hi) {
+  asm("{\n .reg .b16 a, b;\n mov.b32 {a, b}, %2;\n cvt.rn.f16x2.e4m3x2 %0, a;\n cvt.rn.f16x2.e4m3x2 %1, b;\n}\n"
+      : "=r"(lo), "=r"(hi)
+      : "r"(w));
+  const __half2 k = __float2half2_rn(1.f / 256.f);
+  const __half2 l2 = __hmul2(*reinterpret_cast<const __half2*>(&lo), k);
+  const __half2 h2 = __hmul2(*reinterpret_cast<const __half2*>(&hi), k);
+  lo = *reinterpret_cast<const uint32_t*>(&l2);
+  hi = *reinterpret_cast<const uint32_t*>(&h2);
 }
 
 // ------------------------------------------------------------- thread-block clusters ---
