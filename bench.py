@@ -974,8 +974,9 @@ def run_gpu_mla(args):
                          "hbm": {"achieved": round(kernel_gbs, 1), "peak": hbm_peak, "unit": "GB/s",
                                  "frac": round(kernel_gbs / hbm_peak, 4)},
                          "note": f"peak = {tc_kind} cuBLAS bf16 GEMM (burst); achieved = useful FLOPs per launch "
-                                 "(2*(d_qk+d_v) per head and selected token; the two value halves recompute "
-                                 "Q.C^T, 1.53x the useful tensor work) / CUDA-event kernel time; hbm = selected "
+                                 "(2*(d_qk+d_v) per head and selected token; each work item runs on a pair of "
+                                 "CTAs that split the latent channels, so no FLOP is computed twice) / "
+                                 "CUDA-event kernel time; hbm = selected "
                                  f"latent bytes / the same time vs the {hbm_kind} copy bandwidth"},
             "e2e": {"value": round(nbytes * world / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
                     "ms_per_step": round(e2e_ms, 5), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,

@@ -65,20 +65,26 @@ constexpr int kFirstConsumerWarp = 2;
 constexpr int kThreads = (kFirstConsumerWarp + kConsumerWarps) * 32;
 constexpr int kCtasPerSm = 2;
 constexpr int kChunkMax = 256;                    // table slots per work item
-// Stage ring: stage s is filled by producer lane s % P and drained by consumer warp
-// s % kConsumerWarps; items are padded to whole rings so the mapping never shifts.
-constexpr int kStages = 8;                        // two per consumer warp
-constexpr int kStageBytes = 8192;                 // K region 4 KB | V region 4 KB
-constexpr int kVOff = 4096;
+// Page slots: every consumer warp owns a sub-ring of slots, filled in its own order by
+// the producer lane that feeds it; page i of an item goes to consumer warp
+// i % kConsumerWarps.  With per-page scales a warp has two 8 KB slots, one page each
+// (K 4 KB | V 4 KB).  With group-32 scales it has four 4 KB slots: a D = 128 FP16 page
+// takes two and every other page one (K at 0, V at 2 KB, INT4 residual planes at +1 KB),
+// so a warp has three to four low-bit pages in flight (C3 455 -> 434 us).  The same
+// compact slots for page-scaled pools measured C2 280 -> 308 us and C5 529 -> 545 us:
+// there the consumers, not the pages in flight, are the bound.
+constexpr int kSlots = 16;                        // barrier pairs (four 4 KB slots per warp)
+constexpr int kSlotRegion = 65536;                // shared memory of all slots
 constexpr int kResOff = 1024;                     // INT4 residual plane inside a K or V region
-constexpr int kStageScaleBytes = 64;              // group scales of a stage: k | v | k res | v res
+constexpr int kStageScaleBytes = 64;              // group scales of a slot: k | v | k res | v res
 constexpr long long kWaitCycles = kDefaultWaitCycles;  // budget of the drain waits
 constexpr float kLazyLog2 = 8.f;                  // rescale O only when the max grows by > 2^8
 // F16 pages at D = 128: one TMA box of 32 half-rows (token-major, 256-byte token rows)
 constexpr bool kF16OneBox = true;
-// issuing lanes per producer warp: two for page scales, four for group32 pages, which add
-// two to four scale-row copies per page (measured on the two-CTA predecessor of this
-// kernel at C2: 2 lanes 4868 GB/s, 4 lanes 4710, 1 lane 3935; at C3: 4 lanes 2374, 2 lanes 2284)
+// issuing lanes per producer warp: with group scales one per consumer warp (each lane feeds
+// one sub-ring; two lanes feeding two sub-rings each in page order would block a warp
+// behind a full neighbour), with page scales two (measured at C2 with 8 KB stages: 2 lanes
+// 4868 GB/s, 4 lanes 4710, 1 lane 3935)
 template <bool GROUP>
 constexpr int lanes_per_producer() { return GROUP ? 4 : 2; }
 
@@ -113,12 +119,12 @@ constexpr int kMergeRow = 128 + 2;                // floats per (warp, head): ac
 constexpr int kMergeFloats = kConsumerWarps * 8 * kMergeRow;
 
 struct SmemLayout {
-  static constexpr int stages = 0;                                      // [kStages][kStageBytes]
-  static constexpr int scales = kStages * kStageBytes;                  // [kStages][64] group scales
-  static constexpr int items = scales + kStages * kStageScaleBytes;     // two ItemLayout buffers
+  static constexpr int stages = 0;                                      // the page slots
+  static constexpr int scales = kSlotRegion;                            // [kSlots][64] group scales
+  static constexpr int items = scales + kSlots * kStageScaleBytes;      // two ItemLayout buffers
   static constexpr int merge = items + 2 * ItemLayout::bytes;           // [warp][head][kMergeRow] floats
-  static constexpr int bars = merge + kMergeFloats * 4;                 // full[S], empty[S], ilist[2], ifull[2], iempty[2], mfree
-  static constexpr int total = bars + (2 * kStages + 7) * 8;
+  static constexpr int bars = merge + kMergeFloats * 4;                 // full[16], empty[16], ilist[2], ifull[2], iempty[2], mfree
+  static constexpr int total = bars + (2 * kSlots + 7) * 8;
   static_assert(total + 1024 <= 116736, "two persistent decode CTAs per SM");
 };
 
@@ -623,8 +629,10 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
   constexpr int KT = D / 16;   // k-steps of QK, m-tiles of PV
   constexpr int NG = GROUP ? D / 32 : 1;
   constexpr int LPW = lanes_per_producer<GROUP>();
+  constexpr int SPW = GROUP ? 4 : 2;             // slots per consumer warp
+  constexpr int SB = GROUP ? 4096 : 8192;        // bytes per slot
   constexpr int kProducerLanes = kProducerWarps * LPW;
-  static_assert(kStages % kProducerLanes == 0 && kStages % kConsumerWarps == 0, "stage ring mapping");
+  static_assert(kConsumerWarps == 4 && kConsumerWarps % kProducerLanes == 0, "slot sub-ring mapping");
   using SL = SmemLayout;
   extern __shared__ __align__(1024) char smem_raw[];
   char* smem = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -632,17 +640,20 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int r = lane >> 2, c = lane & 3;
   auto full_bar = [&](int st) { return smem_u32(&bars[st]); };
-  auto empty_bar = [&](int st) { return smem_u32(&bars[kStages + st]); };
-  auto ilist_bar = [&](int buf) { return smem_u32(&bars[2 * kStages + buf]); };
-  auto ifull_bar = [&](int buf) { return smem_u32(&bars[2 * kStages + 2 + buf]); };
-  auto iempty_bar = [&](int buf) { return smem_u32(&bars[2 * kStages + 4 + buf]); };
-  const uint32_t mfree_bar = smem_u32(&bars[2 * kStages + 6]);   // the preparer has read the merge area
+  auto empty_bar = [&](int st) { return smem_u32(&bars[kSlots + st]); };
+  auto ilist_bar = [&](int buf) { return smem_u32(&bars[2 * kSlots + buf]); };
+  auto ifull_bar = [&](int buf) { return smem_u32(&bars[2 * kSlots + 2 + buf]); };
+  auto iempty_bar = [&](int buf) { return smem_u32(&bars[2 * kSlots + 4 + buf]); };
+  const uint32_t mfree_bar = smem_u32(&bars[2 * kSlots + 6]);   // the preparer has read the merge area
+  // slots a page of format fmt takes, and where its V plane starts
+  auto page_slots = [&](int fmt) { return (GROUP && D == 128 && fmt == IAK_FMT_F16) ? 2 : 1; };
+  auto v_off = [&](int fmt) { return (!GROUP || (D == 128 && fmt == IAK_FMT_F16)) ? 4096u : 2048u; };
   float* merge_area = reinterpret_cast<float*>(smem + SL::merge);
   auto item_buf = [&](int buf) { return smem + SL::items + buf * ItemLayout::bytes; };
   auto stage_scales = [&](int st) { return smem + SL::scales + st * kStageScaleBytes; };
 
   if (tid == 0) {
-    for (int i = 0; i < 2 * kStages; ++i) mbar_init(smem_u32(&bars[i]), 1);
+    for (int i = 0; i < 2 * kSlots; ++i) mbar_init(smem_u32(&bars[i]), 1);
     // list-ready: the preparer's arrive; item-ready: its arrive after the page list +
     // its arrive.expect_tx of the query-table bytes; item-free: one per consumer warp
     for (int b2 = 0; b2 < 2; ++b2) {
@@ -857,11 +868,21 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         timed_out = true;
   } else if (warp < kFirstConsumerWarp) {
     // -------------------------------------------------------------- TMA producers
-    // Lane l < LPW of producer warp j is producer lane (j - 1) * LPW + l; it fills the
-    // stages s = producer lane (mod kProducerLanes) of every item, in ring order.
+    // Lane l < LPW of the producer warp handles pages i = l (mod LPW) of every item; page i
+    // goes to consumer warp i % 4, so lane l feeds the sub-rings of warps l, l + LPW, ...
+    // and keeps one slot counter per fed warp (slot u of warp w is sub-ring slot u % 4 in
+    // its round u / 4).  A two-slot page never wraps: if it would start at the last slot,
+    // that slot is skipped (its phase completed without data), which the consumer mirrors.
     const int pl = (warp - 1) * LPW + lane;
-    int ctr = 0;        // ring slots used by the items before the current one
-    int g_last = -1;    // ring index of the last stage this lane armed
+    constexpr int kFed = kConsumerWarps / LPW;
+    int cnt[kFed];
+#pragma unroll
+    for (int t = 0; t < kFed; ++t) cnt[t] = 0;
+    // claim slot u of warp w: wait until its previous round was released
+    auto claim = [&](int w, int u) -> bool {
+      const int st = w * SPW + u % SPW, round = u / SPW;
+      return round == 0 || mbar_wait(empty_bar(st), (round - 1) & 1, budget);
+    };
     for (int k = 0, item = blockIdx.x; item < n_items && !timed_out; ++k, item += gridDim.x) {
       const int buf = k & 1;
       const char* ib = item_buf(buf);
@@ -870,25 +891,26 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         break;
       }
       const int n = reinterpret_cast<const int*>(ib + ItemLayout::meta)[0];
-      const int n_pad = (n + kStages - 1) / kStages * kStages;
       const int32_t* pid_s = reinterpret_cast<const int32_t*>(ib + ItemLayout::pid);
       const uint8_t* fmt_s = reinterpret_cast<const uint8_t*>(ib + ItemLayout::fmt);
       if (lane < LPW) {
-        for (int i = pl; i < n_pad; i += kProducerLanes) {
-          const int gi = ctr + i;
-          const int st = gi % kStages, round = gi / kStages;
-          const uint32_t full = full_bar(st);
-          if (round > 0 && !mbar_wait(empty_bar(st), (round - 1) & 1, budget)) {
-            timed_out = true;
-            break;
-          }
-          g_last = gi;
-          if (i >= n) {            // padding slot: completes the stage's phase without data
-            mbar_arrive(full);
-            continue;
-          }
+        for (int i = pl; i < n; i += kProducerLanes) {
+          const int w = i % kConsumerWarps, t = w / LPW;
           const int fmt = fmt_s[i], pid = pid_s[i];
-          const uint32_t sa = smem_u32(smem + SL::stages + st * kStageBytes);
+          const int ns = page_slots(fmt);
+          int u = cnt[t];
+          if (ns == 2 && u % SPW == SPW - 1) {
+            if (!claim(w, u)) { timed_out = true; break; }
+            mbar_arrive(full_bar(w * SPW + u % SPW));   // skipped slot
+            ++u;
+          }
+          if (!claim(w, u) || (ns == 2 && !claim(w, u + 1))) { timed_out = true; break; }
+          const int st = w * SPW + u % SPW;
+          cnt[t] = u + ns;
+          const uint32_t full = full_bar(st);
+          if (ns == 2) mbar_arrive(full_bar(st + 1));     // the second slot carries no barrier bytes
+          const uint32_t sa = smem_u32(smem + SL::stages + st * SB);
+          const uint32_t vo = v_off(fmt);
           uint32_t bytes;
           if (fmt == IAK_FMT_F16) bytes = 2 * kPS * D * 2;
           else if (fmt == IAK_FMT_INT4) bytes = 2 * kPS * D / 2;
@@ -898,23 +920,23 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
           if (fmt == IAK_FMT_F16) {
             if constexpr (D == 128 && kF16OneBox) {
               tma_load_2d(sa, &maps.m[M_KF16], 0, pid * kPS * 2, full);
-              tma_load_2d(sa + kVOff, &maps.m[M_VF16], 0, pid * kPS * 2, full);
+              tma_load_2d(sa + vo, &maps.m[M_VF16], 0, pid * kPS * 2, full);
             } else {
               tma_load_2d(sa, &maps.m[M_KF16], 0, pid * kPS, full);
-              tma_load_2d(sa + kVOff, &maps.m[M_VF16], 0, pid * kPS, full);
+              tma_load_2d(sa + vo, &maps.m[M_VF16], 0, pid * kPS, full);
             }
           } else if (fmt == IAK_FMT_FP8 || fmt == IAK_FMT_INT8) {
             const int y = pid * (kPS * D / 128);   // 128-byte lines of 8-bit token rows
             const int mk = fmt == IAK_FMT_FP8 ? M_KFP8 : M_KI8;
             tma_load_2d(sa, &maps.m[mk], 0, y, full);
-            tma_load_2d(sa + kVOff, &maps.m[mk + 1], 0, y, full);
+            tma_load_2d(sa + vo, &maps.m[mk + 1], 0, y, full);
           } else {
             const int y = pid * (kPS * D / 256);   // 128-byte lines of packed int4 token rows
             tma_load_2d(sa, &maps.m[M_KI4], 0, y, full);
-            tma_load_2d(sa + kVOff, &maps.m[M_VI4], 0, y, full);
+            tma_load_2d(sa + vo, &maps.m[M_VI4], 0, y, full);
             if (fmt == IAK_FMT_INT4R) {
               tma_load_2d(sa + kResOff, &maps.m[M_KI4R], 0, y, full);
-              tma_load_2d(sa + kVOff + kResOff, &maps.m[M_VI4R], 0, y, full);
+              tma_load_2d(sa + vo + kResOff, &maps.m[M_VI4R], 0, y, full);
             }
           }
           if (GROUP && fmt != IAK_FMT_F16) {
@@ -929,14 +951,15 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         }
       }
       timed_out = __any_sync(0xffffffffu, timed_out);
-      ctr += n_pad;
     }
-    // drain: a lane arms its stages in ring order with stride kProducerLanes, so its last
-    // kStages / kProducerLanes arms cover each of its stages once (their latest phase)
+    // drain: the last round this lane armed on each slot of the sub-rings it feeds
     if (lane < LPW)
-      for (int j = 0; j < kStages / kProducerLanes; ++j) {
-        const int gi = g_last - j * kProducerLanes;
-        if (gi >= 0 && !mbar_wait(full_bar(gi % kStages), (gi / kStages) & 1, kWaitCycles)) timed_out = true;
+#pragma unroll
+      for (int t = 0; t < kFed; ++t) {
+        const int w = pl + t * LPW;
+        for (int u = max(0, cnt[t] - SPW); u < cnt[t]; ++u)
+          if (!mbar_wait(full_bar(w * SPW + u % SPW), (u / SPW) & 1, kWaitCycles))
+            timed_out = true;
       }
     timed_out = __any_sync(0xffffffffu, timed_out);
   } else {
@@ -944,8 +967,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     asm volatile("griddepcontrol.wait;" ::: "memory");   // the counters the preparation kernel zeroed
     const int cw = warp - kFirstConsumerWarp;
     const float qk_log2 = p.sm_scale * 1.4426950408889634f;
-    constexpr uint32_t vo = kVOff;
-    int ctr = 0;
+    int cnt = 0;        // slots of this warp's sub-ring used so far (mirrors the producer lane)
     for (int k = 0, item = blockIdx.x; item < n_items; ++k, item += gridDim.x) {
       const int buf = k & 1;
       const char* ib = item_buf(buf);
@@ -954,7 +976,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         break;
       }
       const int* meta = reinterpret_cast<const int*>(ib + ItemLayout::meta);
-      const int n_valid = meta[0], unit = meta[1], split = meta[2];
+      const int n_valid = meta[0];
       const float* scal_s = reinterpret_cast<const float*>(ib + ItemLayout::scal);
       const uint8_t* fmt_s = reinterpret_cast<const uint8_t*>(ib + ItemLayout::fmt);
       const uint4* qfrag = reinterpret_cast<const uint4*>(ib + kQFrag);
@@ -965,24 +987,31 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
       float oacc[KT][4];
 #pragma unroll
       for (int mt = 0; mt < KT; ++mt) oacc[mt][0] = oacc[mt][1] = oacc[mt][2] = oacc[mt][3] = 0.f;
-      // Every item occupies a whole number of rings (the tail is padding), so stage s is
-      // always filled by producer lane s % kProducerLanes and drained by consumer warp
-      // s % kConsumerWarps, one phase at a time.
-      const int n_pad = (n_valid + kStages - 1) / kStages * kStages;
-      for (int i = cw; i < n_pad; i += kConsumerWarps) {
-        const int gi = ctr + i;
-        const int st = gi % kStages, round = gi / kStages;
-        if (!wait_all(full_bar(st), round & 1)) {
+      // Pages i = cw (mod 4) of the item, from this warp's sub-ring, in order; a skipped slot
+      // (a two-slot page that would wrap) is waited for and released like a page.
+      for (int i = cw; i < n_valid; i += kConsumerWarps) {
+        const int fmt = fmt_s[i];
+        const int ns = page_slots(fmt);
+        int u = cnt;
+        if (ns == 2 && u % SPW == SPW - 1) {
+          const int sk = cw * SPW + SPW - 1;
+          if (!wait_all(full_bar(sk), (u / SPW) & 1)) {
+            timed_out = true;
+            break;
+          }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(empty_bar(sk));
+          ++u;
+        }
+        const int st = cw * SPW + u % SPW;
+        cnt = u + ns;
+        if (!wait_all(full_bar(st), (u / SPW) & 1) ||
+            (ns == 2 && !wait_all(full_bar(st + 1), ((u + 1) / SPW) & 1))) {
           timed_out = true;
           break;
         }
-        if (i >= n_valid) {
-          __syncwarp();
-          if (lane == 0) mbar_arrive(empty_bar(st));
-          continue;
-        }
-        const int fmt = fmt_s[i];
-        const char* pg = smem + SL::stages + st * kStageBytes;
+        const uint32_t vo = v_off(fmt);
+        const char* pg = smem + SL::stages + st * SB;
         const uint32_t pg_u32 = smem_u32(pg);
         const float* gsc = reinterpret_cast<const float*>(stage_scales(st));
         // ---------------- S^T = K Q^T
@@ -1207,7 +1236,10 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
           }
         }
         __syncwarp();
-        if (lane == 0) mbar_arrive(empty_bar(st));
+        if (lane == 0) {
+          mbar_arrive(empty_bar(st));
+          if (ns == 2) mbar_arrive(empty_bar(st + 1));
+        }
       }
       if (timed_out) break;
       // ---- this warp's partial of the item, into the CTA's merge area once the preparer
@@ -1239,7 +1271,6 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(iempty_bar(buf));
-      ctr += n_pad;
     }
   }
   if (timed_out && lane == 0) {
