@@ -320,9 +320,9 @@ class ClockSampler:
 # (--set full) of the same workload at the batch given, and the units (sequences) that
 # capture processed.  Traffic grows in proportion to the sequences processed, so it is
 # scaled to the benched batch.
-NCU_TRAFFIC = {"c2": {"bytes": 355_285_504, "batch": 8,
+NCU_TRAFFIC = {"c2": {"bytes": 359_842_048, "batch": 8,
                       "source": "ncu --set full capture of decode_mma_kernel, C2 at batch 8"},
-               "c3": {"bytes": 142_325_760, "batch": 8,
+               "c3": {"bytes": 144_109_824, "batch": 8,
                       "source": "ncu --set full capture of decode_mma_kernel, C3 at batch 8"},
                "c5": {"bytes": 261_581_312, "batch": 1,
                       "source": "ncu --set full capture of decode_mma_kernel, C5 at batch 1"},
