@@ -324,7 +324,7 @@ NCU_TRAFFIC = {"c2": {"bytes": 359_842_048, "batch": 8,
                       "source": "ncu --set full capture of decode_mma_kernel, C2 at batch 8"},
                "c3": {"bytes": 144_109_824, "batch": 8,
                       "source": "ncu --set full capture of decode_mma_kernel, C3 at batch 8"},
-               "c5": {"bytes": 261_581_312, "batch": 1,
+               "c5": {"bytes": 261_447_680, "batch": 1,
                       "source": "ncu --set full capture of decode_mma_kernel, C5 at batch 1"},
                "c4": {"bytes": 58_652_672, "batch": 8,
                       "source": "ncu --set full capture of mla_tc_kernel, C4 at batch 8"},
@@ -403,6 +403,61 @@ class _NoClocks:
         return None
 
 
+def pipelined_e2e(device, steps, warmup, h2d_pairs, d2h_pairs, run, world=1):
+    """End-to-end steps through the public API with host buffers, as a serving loop runs them:
+    every step copies its inputs from pinned host memory, calls the API and copies its result
+    back.  Two sets of device buffers let step s+1's input copies (one copy stream) and step
+    s-1's result copy (another) run while step s runs on the compute stream; each step's copies
+    stay inside the timed region.  h2d_pairs: [(host, (dev0, dev1))]; d2h_pairs: [((dev0, dev1),
+    (host0, host1))]; run(b) calls the API on buffer set b.  Returns ms per step (max over ranks)."""
+    import torch
+    import torch.distributed as dist
+    compute = torch.cuda.current_stream(device)
+    cin, cout = torch.cuda.Stream(device), torch.cuda.Stream(device)
+    ev = {name: [torch.cuda.Event() for _ in range(2)] for name in ("in", "run", "out")}
+    started = [False, False]
+
+    def one(i):
+        b = i & 1
+        with torch.cuda.stream(cin):
+            if started[b]:
+                cin.wait_event(ev["run"][b])          # step i-2 has read these inputs
+            for host, devs in h2d_pairs:
+                devs[b].copy_(host, non_blocking=True)
+            ev["in"][b].record(cin)
+        compute.wait_event(ev["in"][b])
+        if started[b]:
+            compute.wait_event(ev["out"][b])          # step i-2's result has been copied out
+        run(b)
+        ev["run"][b].record(compute)
+        with torch.cuda.stream(cout):
+            cout.wait_event(ev["run"][b])
+            for devs, hosts in d2h_pairs:
+                hosts[b].copy_(devs[b], non_blocking=True)
+            ev["out"][b].record(cout)
+        started[b] = True
+
+    for i in range(warmup):
+        one(i)
+    torch.cuda.synchronize(device)
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(compute)
+    cin.wait_stream(compute)
+    for i in range(steps):
+        one(warmup + i)
+    compute.wait_stream(cout)
+    e1.record(compute)
+    torch.cuda.synchronize(device)
+    ms = e0.elapsed_time(e1) / steps
+    if world > 1:
+        t = torch.tensor([ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    return ms
+
+
 def measure_decode(args, wl_name, world, rank, local, device, clocks_on=True):
     """Build one decode workload on this rank and time it (device step, the decode
     kernel alone, and end to end through the public API); times are max over ranks.
@@ -434,12 +489,13 @@ def measure_decode(args, wl_name, world, rank, local, device, clocks_on=True):
     out = torch.empty(q.shape, dtype=torch.bfloat16, device=device)
     decoder = SequenceShardedDecoder(transport=args.exchange) if seq_shard else None
 
-    def decode(q_, table_, counts_):
+    def decode(q_, table_, counts_, out_=None):
+        o = out if out_ is None else out_
         if decoder is not None:
-            decoder.decode(q_, pool, table_, counts_, tags, tag_map, 0, out=out, num_splits=args.splits,
+            decoder.decode(q_, pool, table_, counts_, tags, tag_map, 0, out=o, num_splits=args.splits,
                            kernel="tensor")
         else:
-            paged_decode(q_, pool, table_, counts_, tags, tag_map, 0, out=out, num_splits=args.splits,
+            paged_decode(q_, pool, table_, counts_, tags, tag_map, 0, out=o, num_splits=args.splits,
                          kernel="tensor")
 
     def step():
@@ -527,34 +583,17 @@ def measure_decode(args, wl_name, world, rank, local, device, clocks_on=True):
     q_host = q.cpu().pin_memory()
     table_host = table.cpu().pin_memory()
     counts_host = counts.cpu().pin_memory()
-    out_host = torch.empty(out.shape, dtype=out.dtype).pin_memory()
-    q_dev, table_dev, counts_dev = torch.empty_like(q), torch.empty_like(table), torch.empty_like(counts)
+    out_hosts = tuple(torch.empty(out.shape, dtype=out.dtype).pin_memory() for _ in range(2))
+    q_devs = (torch.empty_like(q), torch.empty_like(q))
+    table_devs = (torch.empty_like(table), torch.empty_like(table))
+    counts_devs = (torch.empty_like(counts), torch.empty_like(counts))
+    out_devs = (out, torch.empty_like(out))
     h2d = q_host.numel() * q_host.element_size() + table_host.numel() * 4 + counts_host.numel() * 4
-    d2h = out_host.numel() * out_host.element_size()
-
-    def e2e_step():
-        q_dev.copy_(q_host, non_blocking=True)
-        table_dev.copy_(table_host, non_blocking=True)
-        counts_dev.copy_(counts_host, non_blocking=True)
-        decode(q_dev, table_dev, counts_dev)
-        out_host.copy_(out, non_blocking=True)
-
-    for _ in range(args.warmup):
-        e2e_step()
-    torch.cuda.synchronize(device)
-    if world > 1:
-        dist.barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(args.steps):
-        e2e_step()
-    e1.record()
-    torch.cuda.synchronize(device)
-    e2e_ms = e0.elapsed_time(e1) / args.steps
-    if world > 1:
-        t = torch.tensor([e2e_ms], device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
+    d2h = out.numel() * out.element_size()
+    e2e_ms = pipelined_e2e(device, args.steps, args.warmup,
+                           [(q_host, q_devs), (table_host, table_devs), (counts_host, counts_devs)],
+                           [(out_devs, out_hosts)],
+                           lambda b: decode(q_devs[b], table_devs[b], counts_devs[b], out_devs[b]), world)
 
     # tensor-core path (forced above, so an ineligible shape fails loudly): query-table preparation
     # and the persistent decode kernel, which merges its partials itself
@@ -630,7 +669,8 @@ def run_gpu(args):
                     "ms_per_step": round(e2e_ms, 5), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "api": ("intent_attention.SequenceShardedDecoder.decode" if seq_shard else
                             "intent_attention.paged_decode") +
-                           " with pinned host q / page table / counts in, output out"},
+                           " with pinned host q / page table / counts in, output out; two buffer sets, the "
+                           "next step's input copies and the previous step's output copy on copy streams"},
             "gpu_launches": launches_per_step * args.steps,
             "clocks": m["clocks"],
         }
@@ -890,9 +930,10 @@ def run_gpu_mla(args):
     tag_map = make_mla_tag_map({0: "DENSE", 1: "FP8", 2: "SKIP"})
     out = torch.empty((w["B"], w["H"], w["Dv"]), dtype=torch.bfloat16, device=device)
 
-    def decode(q_, table_):
+    def decode(q_, table_, out_=None):
         mla_paged_decode(q_, table_, None, dense_pages=dense, fp8_pages=fp8, fp8_scale=scale, page_tags=tags,
-                         tag_map=tag_map, d_v=w["Dv"], out=out, num_splits=args.splits, kernel="tensor")
+                         tag_map=tag_map, d_v=w["Dv"], out=out if out_ is None else out_, num_splits=args.splits,
+                         kernel="tensor")
 
     decode(q, table)
     torch.cuda.synchronize(device)
@@ -925,29 +966,13 @@ def run_gpu_mla(args):
     kernel_ms = ktimer.total_ms / max(1, ktimer.launches)
 
     q_host, table_host = q.cpu().pin_memory(), table.cpu().pin_memory()
-    out_host = torch.empty(out.shape, dtype=out.dtype).pin_memory()
-    q_dev, table_dev = torch.empty_like(q), torch.empty_like(table)
+    out_hosts = tuple(torch.empty(out.shape, dtype=out.dtype).pin_memory() for _ in range(2))
+    q_devs, table_devs = (torch.empty_like(q), torch.empty_like(q)), (torch.empty_like(table), torch.empty_like(table))
+    out_devs = (out, torch.empty_like(out))
     h2d = q_host.numel() * q_host.element_size() + table_host.numel() * 4
-    d2h = out_host.numel() * out_host.element_size()
-
-    def e2e_step():
-        q_dev.copy_(q_host, non_blocking=True)
-        table_dev.copy_(table_host, non_blocking=True)
-        decode(q_dev, table_dev)
-        out_host.copy_(out, non_blocking=True)
-
-    for _ in range(args.warmup):
-        e2e_step()
-    torch.cuda.synchronize(device)
-    if world > 1:
-        dist.barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(args.steps):
-        e2e_step()
-    e1.record()
-    torch.cuda.synchronize(device)
-    e2e_ms = e0.elapsed_time(e1) / args.steps
+    d2h = out.numel() * out.element_size()
+    e2e_ms = pipelined_e2e(device, args.steps, args.warmup, [(q_host, q_devs), (table_host, table_devs)],
+                           [(out_devs, out_hosts)], lambda b: decode(q_devs[b], table_devs[b], out_devs[b]), world)
     if world > 1:
         t = torch.tensor([t_ms, kernel_ms, e2e_ms], device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -981,7 +1006,8 @@ def run_gpu_mla(args):
             "e2e": {"value": round(nbytes * world / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
                     "ms_per_step": round(e2e_ms, 5), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "api": "intent_attention.triton_mla_decode.mla_paged_decode with pinned host q / page table "
-                           "in, context out"},
+                           "in, context out; two buffer sets, the next step's input copies and the previous "
+                           "step's output copy on copy streams"},
             "gpu_launches": args.steps,
             "clocks": clocks.summary(),
         }
