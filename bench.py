@@ -483,6 +483,14 @@ def measure_decode(args, wl_name, world, rank, local, device, clocks_on=True):
         a, b = shard_bounds(ids.size, rank, world)
         ids, fmt = ids[a:b], fmt[a:b]
         w["name"] = "C5 long-context decode, sequence-sharded split-KV"
+    if not seq_shard and getattr(args, "shard_of", 0) > 1 and wl_name == "c5":
+        # one rank's share of C5 cut over shard_of GPUs, decoded on this GPU alone (no exchange):
+        # sizes the per-rank decode of the sequence-sharded case on one GPU
+        from intent_attention.split_kv import shard_bounds
+        a, b = shard_bounds(ids.size, 0, args.shard_of)
+        ids, fmt = ids[a:b], fmt[a:b]
+        nbytes_total = step_bytes(w, fmt)
+        w["name"] = f"C5 long-context decode, rank 0's share of {args.shard_of} sequence shards (one GPU, no exchange)"
     nbytes = step_bytes(w, fmt)                     # this rank's selected-KV bytes per step
     pool, table, counts, tags, q = build_gpu_workload(w, ids, fmt, device, 0 if seq_shard else rank)
     tag_map = make_tag_map({c: (f if f in w["mix"] else "SKIP") for f, c in FMT_CODE.items()})
@@ -1524,6 +1532,8 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--splits", type=int, default=0)
     ap.add_argument("--batch", type=int, default=0, help="override the workload's batch (profiling runs)")
+    ap.add_argument("--shard-of", type=int, default=0,
+                    help="c5 on one GPU: decode rank 0's share of the pages cut over this many GPUs (profiling runs)")
     ap.add_argument("--exchange", default="p2p", choices=["p2p", "nccl"],
                     help="C5 on several GPUs: partial blocks over NVLink peer stores or one NCCL all-gather")
     ap.add_argument("--no-graph", action="store_true", help="time eager launches instead of a captured CUDA graph")
