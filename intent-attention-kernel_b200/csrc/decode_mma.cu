@@ -350,6 +350,34 @@ __device__ __forceinline__ void v_table_int4(const char* tile, int r, int c, uin
   }
 }
 
+// INT4_RESIDUAL V with group scales, both planes in one table (D = 128): the base and residual
+// codes of each pair, dequantised and combined as base * rb + residual * rr in f16, with rb / rr
+// the groups' base / residual scales over the page's largest V scale (rows r: rbA / rrA, rows
+// r + 8: rbB / rrB), so the page needs one P.V instead of one per plane.
+__device__ __forceinline__ void v_table_int4r_group(const char* tb, const char* tr, int r, int c, uint32_t rbA,
+                                                    uint32_t rbB, uint32_t rrA, uint32_t rrB,
+                                                    uint32_t (&vh)[2][2][8]) {
+  constexpr int RB = 64;
+#pragma unroll
+  for (int tp = 0; tp < 2; ++tp) {
+    const int t0 = 2 * c + 8 * tp, t1 = t0 + 1;
+#pragma unroll
+    for (int ws = 0; ws < 2; ++ws) {
+      const int w = pv_word<128>(r, ws);
+      const uint32_t rb = ws == 0 ? rbA : rbB, rr = ws == 0 ? rrA : rrB;
+      const uint32_t x0 = lds32(tb, sw128(t0 * RB + 4 * w)), x1 = lds32(tb, sw128(t1 * RB + 4 * w));
+      const uint32_t y0 = lds32(tr, sw128(t0 * RB + 4 * w)), y1 = lds32(tr, sw128(t1 * RB + 4 * w));
+#pragma unroll
+      for (int b = 0; b < 4; ++b) {
+        const uint32_t sel = b | (b << 4) | ((4 + b) << 8) | ((4 + b) << 12);
+        const uint32_t t = __byte_perm(x0, x1, sel), u = __byte_perm(y0, y1, sel);
+        vh[tp][ws][2 * b] = hfma2(i4pair_lo(u), rr, hmul2(i4pair_lo(t), rb));
+        vh[tp][ws][2 * b + 1] = hfma2(i4pair_hi(u), rr, hmul2(i4pair_hi(t), rb));
+      }
+    }
+  }
+}
+
 // shared-memory offset of fp16 channel d (multiple of 4) of token t
 template <int D>
 __device__ __forceinline__ uint32_t f16_off(int t, int d) {
@@ -1202,7 +1230,30 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
           // fp16.  Rows r of the lane's PV fragments are group gA, rows r + 8 group gB.
           const int gA = pv_word<D>(r, 0) >> 2, gB = pv_word<D>(r, D / 64 - 1) >> 2;
           const bool q = fmt != IAK_FMT_F16;
-          const int nplanes = fmt == IAK_FMT_INT4R ? 2 : 1;
+          if constexpr (D == 128) {
+            if (fmt == IAK_FMT_INT4R) {
+              // both planes in one table, one P.V (the scales over the largest of the page's
+              // base and residual V scales, so every ratio is at most 1)
+              const float* vb = gsc + 4;
+              const float* vr = gsc + 12;
+              float vmax = fmaxf(vb[0], vr[0]);
+  #pragma unroll
+              for (int g = 1; g < NG; ++g) vmax = fmaxf(vmax, fmaxf(vb[g], vr[g]));
+              const float inv = __frcp_rn(vmax);
+              v_table_int4r_group(pg + vo, pg + vo + kResOff, r, c, pack_f16x2(vb[gA] * inv, vb[gA] * inv),
+                                  pack_f16x2(vb[gB] * inv, vb[gB] * inv), pack_f16x2(vr[gA] * inv, vr[gA] * inv),
+                                  pack_f16x2(vr[gB] * inv, vr[gB] * inv), vh);
+              const uint32_t pb0 = movm_t(pack_f16x2(p0 * vmax, p1 * vmax));
+              const uint32_t pb1 = movm_t(pack_f16x2(p2 * vmax, p3 * vmax));
+  #pragma unroll
+              for (int mt = 0; mt < KT; ++mt) {
+                uint32_t a0, a1, a2, a3;
+                pv_afrag<D>(vh, mt, a0, a1, a2, a3);
+                mma16816(oacc[mt], a0, a1, a2, a3, pb0, pb1);
+              }
+            }
+          }
+          const int nplanes = (D == 128 && fmt == IAK_FMT_INT4R) ? 0 : 1;
           for (int pl = 0; pl < nplanes; ++pl) {
             const char* vt = pg + vo + pl * kResOff;
             if (fmt == IAK_FMT_F16) v_table_f16<D>(vt, r, c, vh);
