@@ -641,15 +641,16 @@ __device__ __forceinline__ void warp_merge(const float* m, const float* l, const
   L = lsum;
 }
 
-// Persistent split-KV decode, one CTA per SM.  CTA c processes work items c,
-// c + gridDim.x, ... (item = (unit, split) of <= kChunkMax table slots).  The
+// Persistent split-KV decode, kCtasPerSm CTAs per SM.  CTA c processes work items
+// c, c + gridDim.x, ... (item = (unit, split) of <= kChunkMax table slots).  The
 // preparer fills one of two item buffers ahead of use (compacted page list,
 // scales, query table by bulk copy); the TMA warp streams every item's pages
-// into the consumer FIFOs (lane w feeds consumer warp w; page i of an item goes
-// to warp i % kConsumerWarps) without draining between items; each consumer warp
-// writes its (m, l, acc) partial per item.  The last consumer warp of an item
-// merges the item's partials, and the last item merger of a unit merges the
-// unit's items into the output (or the exported partial block): no merge launch.
+// into the consumer warps' slot sub-rings (page i of an item goes to warp
+// i % kConsumerWarps) without draining between items; each consumer warp writes
+// its (m, l, acc) partial of an item into the shared-memory merge area.  The
+// preparer merges the item's partials into the item's workspace slot, and the
+// last item merged of a unit merges the unit's items into the output (or the
+// exported partial block, or every peer's receive slot): no merge launch.
 template <int D, bool GROUP>
 __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     decode_mma_kernel(const DecodeParams p, const __grid_constant__ TmaMaps maps, const char* __restrict__ qtab,
@@ -1173,15 +1174,17 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         for (int e = 0; e < 4; ++e) sc[e] *= qk_log2;
         // ---------------- online softmax (log2 domain)
         float pm0 = fmaxf(sc[0], sc[2]), pm1 = fmaxf(sc[1], sc[3]);
-  #pragma unroll
-        for (int off = 4; off < 32; off <<= 1) {
-          pm0 = fmaxf(pm0, __shfl_xor_sync(0xffffffffu, pm0, off));
-          pm1 = fmaxf(pm1, __shfl_xor_sync(0xffffffffu, pm1, off));
-        }
         // Lazy rescaling: the running max only moves (and O, l are rescaled)
         // when some query's page max exceeds it by more than kLazyLog2; until
         // then p <= 2^kLazyLog2, far inside fp16 / fp32 range.  Warp-uniform.
+        // A lane's own scores decide whether any column max crossed the bound,
+        // so the column maxima are only reduced on the (rare) rescaling pages.
         if (__any_sync(0xffffffffu, pm0 > m_run[0] + kLazyLog2 || pm1 > m_run[1] + kLazyLog2)) {
+  #pragma unroll
+          for (int off = 4; off < 32; off <<= 1) {
+            pm0 = fmaxf(pm0, __shfl_xor_sync(0xffffffffu, pm0, off));
+            pm1 = fmaxf(pm1, __shfl_xor_sync(0xffffffffu, pm1, off));
+          }
           const float mn0 = fmaxf(m_run[0], pm0), mn1 = fmaxf(m_run[1], pm1);
           const float al0 = exp2f(m_run[0] - mn0), al1 = exp2f(m_run[1] - mn1);
           m_run[0] = mn0; m_run[1] = mn1;
