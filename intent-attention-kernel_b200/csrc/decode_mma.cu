@@ -833,33 +833,47 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
       int32_t* pid_s = reinterpret_cast<int32_t*>(ib + ItemLayout::pid);
       float* scal_s = reinterpret_cast<float*>(ib + ItemLayout::scal);
       uint8_t* fmt_s = reinterpret_cast<uint8_t*>(ib + ItemLayout::fmt);
-      // all loads of the item first (three dependent rounds), then compaction
+      // All loads of the item first, in three dependent rounds (the table slice with the
+      // page count, the formats, the page scales), then compaction.  The table loads are
+      // bounded by the table row, not by the page count, so they do not wait for it.
+      const int hw = min(lo + p.pages_per_split, p.W);
       int pids[kPer], fmts[kPer];
 #pragma unroll
       for (int t = 0; t < kPer; ++t) {
         const int j = lo + 32 * t + lane;
-        pids[t] = j < hi ? table[j] : -1;
+        pids[t] = j < hw ? table[j] : -1;
       }
 #pragma unroll
       for (int t = 0; t < kPer; ++t)
+        if (lo + 32 * t + lane >= hi) pids[t] = -1;
+#pragma unroll
+      for (int t = 0; t < kPer; ++t)
         fmts[t] = (pids[t] >= 0 && pids[t] < p.num_pages) ? page_format(p, pids[t]) : IAK_FMT_SKIP;
-      int n = 0;
+      // page scales into registers (issued before the compaction's shared-memory stores,
+      // which loads placed after them would wait for)
+      float ksc[GROUP ? 1 : kPer], vsc[GROUP ? 1 : kPer], krs[GROUP ? 1 : kPer], vrs[GROUP ? 1 : kPer];
+      if constexpr (!GROUP) {
+#pragma unroll
+        for (int t = 0; t < kPer; ++t) {
+          const int fmt = fmts[t], pid = pids[t];
+          const bool q = fmt != IAK_FMT_F16 && fmt != IAK_FMT_SKIP && fmt != IAK_FMT_SPARSE;
+          const bool r4 = fmt == IAK_FMT_INT4R;
+          ksc[t] = q ? __ldg(p.k_scale + pid) : 1.f;
+          vsc[t] = q ? __ldg(p.v_scale + pid) : 1.f;
+          krs[t] = r4 ? __ldg(p.k_rscale + pid) : 0.f;
+          vrs[t] = r4 ? __ldg(p.v_rscale + pid) : 0.f;
+        }
+      }
+      int n = 0, idxs[kPer];
 #pragma unroll
       for (int t = 0; t < kPer; ++t) {
         const int fmt = fmts[t], pid = pids[t];
         const bool valid = fmt != IAK_FMT_SKIP && fmt != IAK_FMT_SPARSE;
         const unsigned bal = __ballot_sync(0xffffffffu, valid);
+        idxs[t] = valid ? n + __popc(bal & ((1u << lane) - 1u)) : -1;
         if (valid) {
-          const int idx = n + __popc(bal & ((1u << lane) - 1u));
-          pid_s[idx] = pid;
-          fmt_s[idx] = static_cast<uint8_t>(fmt);
-          if (!GROUP) {
-            const bool q = fmt != IAK_FMT_F16;
-            scal_s[idx] = q ? p.k_scale[pid] : 1.f;
-            scal_s[kChunkMax + idx] = q ? p.v_scale[pid] : 1.f;
-            scal_s[2 * kChunkMax + idx] = fmt == IAK_FMT_INT4R ? p.k_rscale[pid] : 0.f;
-            scal_s[3 * kChunkMax + idx] = fmt == IAK_FMT_INT4R ? p.v_rscale[pid] : 0.f;
-          }
+          pid_s[idxs[t]] = pid;
+          fmt_s[idxs[t]] = static_cast<uint8_t>(fmt);
         }
         n += __popc(bal);
       }
@@ -870,10 +884,21 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         meta[2] = split;
       }
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(ilist_bar(buf));
-        mbar_arrive(ifull_bar(buf));
+      // the page list is all the producer reads: it may start the item's copies while
+      // the scales land
+      if (lane == 0) mbar_arrive(ilist_bar(buf));
+      if constexpr (!GROUP) {
+#pragma unroll
+        for (int t = 0; t < kPer; ++t)
+          if (idxs[t] >= 0) {
+            scal_s[idxs[t]] = ksc[t];
+            scal_s[kChunkMax + idxs[t]] = vsc[t];
+            scal_s[2 * kChunkMax + idxs[t]] = krs[t];
+            scal_s[3 * kChunkMax + idxs[t]] = vrs[t];
+          }
+        __syncwarp();
       }
+      if (lane == 0) mbar_arrive(ifull_bar(buf));
       // the query tables come from the preparation kernel, which may still be
       // running (programmatic dependent launch): wait for it before the first copy
       if (k == 0) asm volatile("griddepcontrol.wait;" ::: "memory");
