@@ -815,7 +815,18 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     };
     int last_k[2] = {-1, -1};   // last item whose query table was copied into each buffer
     const int n_mine = blockIdx.x < n_items ? (n_items - 1 - blockIdx.x) / gridDim.x + 1 : 0;
-    for (int k = 0, item = blockIdx.x; item < n_items; ++k, item += gridDim.x) {
+    // This CTA's k-th item: items go in waves of gridDim.x, each full wave rotated by k CTAs,
+    // so that a CTA visits different splits of the units (unrotated, a grid that is a multiple
+    // of the split count would hand every CTA the same split of each unit it visits, and the
+    // splits differ in their page formats and so in cost); the partial last wave is not rotated.
+    // The producer and consumers only count turns, which the rotation leaves unchanged.
+    const int nb = static_cast<int>(gridDim.x);
+    auto item_of = [&](int k) {
+      const int base = k * nb;
+      return base + nb <= n_items ? base + (static_cast<int>(blockIdx.x) + k) % nb : base + static_cast<int>(blockIdx.x);
+    };
+    for (int k = 0, turn = blockIdx.x; turn < n_items; ++k, turn += gridDim.x) {
+      const int item = item_of(k);
       const int buf = k & 1;
       char* ib = item_buf(buf);
       if (k >= 2) {
@@ -824,7 +835,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
           timed_out = true;
           break;
         }
-        merge_item(item - 2 * gridDim.x);
+        merge_item(item_of(k - 2));
       }
       int unit, split, lo, hi;
       item_range(p, item, unit, split, lo, hi);
@@ -914,7 +925,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         timed_out = true;
         break;
       }
-      merge_item(blockIdx.x + j * gridDim.x);
+      merge_item(item_of(j));
     }
     // drain: the query-table copies this warp issued
     for (int b2 = 0; b2 < 2; ++b2)
