@@ -81,12 +81,12 @@ constexpr long long kWaitCycles = kDefaultWaitCycles;  // budget of the drain wa
 constexpr float kLazyLog2 = 8.f;                  // rescale O only when the max grows by > 2^8
 // F16 pages at D = 128: one TMA box of 32 half-rows (token-major, 256-byte token rows)
 constexpr bool kF16OneBox = true;
-// issuing lanes per producer warp: with group scales one per consumer warp (each lane feeds
-// one sub-ring; two lanes feeding two sub-rings each in page order would block a warp
-// behind a full neighbour), with page scales two (measured at C2 with 8 KB stages: 2 lanes
-// 4868 GB/s, 4 lanes 4710, 1 lane 3935)
-template <bool GROUP>
-constexpr int lanes_per_producer() { return GROUP ? 4 : 2; }
+// Issuing lanes of the producer warp (a template parameter, LPW): four feed one consumer
+// sub-ring each; two feed two sub-rings each in page order, so that a lane waiting for one
+// warp's slot holds back the other warp's pages.  Group-scaled pools use four; page-scaled
+// pools four when they can hold 4-bit pages (DecodeParams::producer_lanes), else two.
+// Same-box A/B with the per-warp slot rings: four lanes take C5 (30 % INT4 pages) from 519
+// to 499 us and slow C2 (FP16 / FP8 / INT8) from 267.6 to 270 us.
 
 enum MapIdx { M_KF16 = 0, M_VF16, M_KFP8, M_VFP8, M_KI8, M_VI8, M_KI4, M_VI4, M_KI4R, M_VI4R, M_COUNT };
 struct TmaMaps {
@@ -651,13 +651,12 @@ __device__ __forceinline__ void warp_merge(const float* m, const float* l, const
 // preparer merges the item's partials into the item's workspace slot, and the
 // last item merged of a unit merges the unit's items into the output (or the
 // exported partial block, or every peer's receive slot): no merge launch.
-template <int D, bool GROUP>
+template <int D, bool GROUP, int LPW>
 __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     decode_mma_kernel(const DecodeParams p, const __grid_constant__ TmaMaps maps, const char* __restrict__ qtab,
                       int n_items) {
   constexpr int KT = D / 16;   // k-steps of QK, m-tiles of PV
   constexpr int NG = GROUP ? D / 32 : 1;
-  constexpr int LPW = lanes_per_producer<GROUP>();
   constexpr int SPW = GROUP ? 4 : 2;             // slots per consumer warp
   constexpr int SB = GROUP ? 4096 : 8192;        // bytes per slot
   constexpr int kProducerLanes = kProducerWarps * LPW;
@@ -1468,10 +1467,10 @@ bool mma_shape_eligible(const DecodeParams& p) {
   return true;
 }
 
-template <int D, bool GROUP>
+template <int D, bool GROUP, int LPW>
 static int launch_persistent(const DecodeParams& p, const TmaMaps& maps, int n_items, cudaStream_t s) {
   const size_t smem = SmemLayout::total + 1024;
-  auto kern = decode_mma_kernel<D, GROUP>;
+  auto kern = decode_mma_kernel<D, GROUP, LPW>;
   // the smem attribute and occupancy are per (device, instantiation): look them up once
   static std::mutex mu;
   static int per_sm_cache[64] = {0};
@@ -1529,9 +1528,10 @@ int launch_decode_mma(const DecodeParams& p, const iak_page_pools& P, cudaStream
   }
   if (!p.ws_qtab) return fail(IAK_ERR_WORKSPACE, "tensor-core decode needs a workspace");
   const int n_items = p.B * p.Ht * p.num_splits;
-  if (p.D == 128 && p.scale_mode == IAK_SCALE_GROUP32) return launch_persistent<128, true>(p, maps, n_items, s);
-  if (p.D == 128) return launch_persistent<128, false>(p, maps, n_items, s);
-  return launch_persistent<64, false>(p, maps, n_items, s);
+  if (p.D == 128 && p.scale_mode == IAK_SCALE_GROUP32) return launch_persistent<128, true, 4>(p, maps, n_items, s);
+  if (p.D == 128 && p.producer_lanes == 4) return launch_persistent<128, false, 4>(p, maps, n_items, s);
+  if (p.D == 128) return launch_persistent<128, false, 2>(p, maps, n_items, s);
+  return launch_persistent<64, false, 2>(p, maps, n_items, s);
 }
 
 }  // namespace iak
