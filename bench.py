@@ -218,9 +218,9 @@ def cpu_baseline_record(sample: CpuDecodeSample, budget_s: float) -> dict:
     sec, units = sample.run_for(budget_s)
     return {"value": round(units * sample.bytes_per_unit / sec / 1e9, 4), "unit": "GB/s", "cores": sample.cores,
             "kind": "port", "seconds": round(sec, 3), "units_timed": units, "units_per_step": sample.units_total,
-            "sample": f"{units} of the step's {sample.units_total} (sequence, kv head) units decoded by the numpy "
-                      f"oracle on {sample.cores} host threads in {sec:.2f} s; value = their selected-KV bytes / "
-                      "that time"}
+            "sample": f"{units} (sequence, kv head) units of the step's layout (a step has "
+                      f"{sample.units_total}) decoded by the numpy oracle on {sample.cores} host threads in "
+                      f"{sec:.2f} s; value = their selected-KV bytes / that time"}
 
 
 REFERENCE_TIMING = os.path.join(ROOT, "oracle", "reference_cpu_timing.json")
@@ -320,11 +320,11 @@ class ClockSampler:
 # (--set full) of the same workload at the batch given, and the units (sequences) that
 # capture processed.  Traffic grows in proportion to the sequences processed, so it is
 # scaled to the benched batch.
-NCU_TRAFFIC = {"c2": {"bytes": 359_842_048, "batch": 8,
+NCU_TRAFFIC = {"c2": {"bytes": 356_315_904, "batch": 8,
                       "source": "ncu --set full capture of decode_mma_kernel, C2 at batch 8"},
-               "c3": {"bytes": 144_109_824, "batch": 8,
+               "c3": {"bytes": 142_390_528, "batch": 8,
                       "source": "ncu --set full capture of decode_mma_kernel, C3 at batch 8"},
-               "c5": {"bytes": 261_447_680, "batch": 1,
+               "c5": {"bytes": 262_467_328, "batch": 1,
                       "source": "ncu --set full capture of decode_mma_kernel, C5 at batch 1"},
                "c4": {"bytes": 58_652_672, "batch": 8,
                       "source": "ncu --set full capture of mla_tc_kernel, C4 at batch 8"},
