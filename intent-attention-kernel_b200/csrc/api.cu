@@ -177,9 +177,6 @@ static int prepare(const iak_page_pools* P, const iak_decode_args* a, DecodePara
   p->wait_cycles = a->wait_budget_ns == 0
                        ? kDefaultWaitCycles
                        : std::max<long long>(1, static_cast<long long>(a->wait_budget_ns) * device_clock_khz() / 1000000);
-  // four TMA issuing lanes when the pools can hold 4-bit pages (more, smaller pages per byte),
-  // two otherwise (measured: C5 with 30 % INT4 pages 519 -> 499 us with four; C2 267.6 -> 270)
-  p->producer_lanes = (fmt_reachable(a, IAK_FMT_INT4) || fmt_reachable(a, IAK_FMT_INT4R)) ? 4 : 2;
   if (p->ex_l && (!p->ex_m || !p->ex_acc)) return fail(IAK_ERR_INVALID_ARG, "partial export needs m, l and acc");
   const int64_t units = static_cast<int64_t>(a->batch) * a->num_table_heads;
   if (a->kernel < 0 || a->kernel > 2) return fail(IAK_ERR_INVALID_ARG, "bad kernel selector %d", a->kernel);

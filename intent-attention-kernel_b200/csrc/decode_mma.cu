@@ -81,12 +81,11 @@ constexpr long long kWaitCycles = kDefaultWaitCycles;  // budget of the drain wa
 constexpr float kLazyLog2 = 8.f;                  // rescale O only when the max grows by > 2^8
 // F16 pages at D = 128: one TMA box of 32 half-rows (token-major, 256-byte token rows)
 constexpr bool kF16OneBox = true;
-// Issuing lanes of the producer warp (a template parameter, LPW): four feed one consumer
-// sub-ring each; two feed two sub-rings each in page order, so that a lane waiting for one
-// warp's slot holds back the other warp's pages.  Group-scaled pools use four; page-scaled
-// pools four when they can hold 4-bit pages (DecodeParams::producer_lanes), else two.
-// Same-box A/B with the per-warp slot rings: four lanes take C5 (30 % INT4 pages) from 519
-// to 499 us and slow C2 (FP16 / FP8 / INT8) from 267.6 to 270 us.
+// Issuing lanes of the producer warp: one per consumer warp, each feeding that warp's slot
+// sub-ring in its page order.  With two lanes feeding two sub-rings each, a lane waiting for
+// one warp's slot holds back the other warp's pages; once page-scaled slots free their K and
+// V halves separately that coupling costs C2 310 us against 260-264 with four lanes.
+constexpr int kProducerLanes = 4;
 
 enum MapIdx { M_KF16 = 0, M_VF16, M_KFP8, M_VFP8, M_KI8, M_VI8, M_KI4, M_VI4, M_KI4R, M_VI4R, M_COUNT };
 struct TmaMaps {
@@ -651,16 +650,20 @@ __device__ __forceinline__ void warp_merge(const float* m, const float* l, const
 // preparer merges the item's partials into the item's workspace slot, and the
 // last item merged of a unit merges the unit's items into the output (or the
 // exported partial block, or every peer's receive slot): no merge launch.
-template <int D, bool GROUP, int LPW>
+template <int D, bool GROUP>
 __global__ void __launch_bounds__(kThreads, kCtasPerSm)
     decode_mma_kernel(const DecodeParams p, const __grid_constant__ TmaMaps maps, const char* __restrict__ qtab,
                       int n_items) {
   constexpr int KT = D / 16;   // k-steps of QK, m-tiles of PV
   constexpr int NG = GROUP ? D / 32 : 1;
   constexpr int SPW = GROUP ? 4 : 2;             // slots per consumer warp
+  // Page-scaled pools: each 8 KB slot holds one page, K at 0 and V at 4 KB, with a barrier
+  // pair per half, so that the K half is released (and refilled with the page two ahead)
+  // as soon as the page's scores are computed, and the V half after its P.V.
+  constexpr bool SKV = !GROUP;
   constexpr int SB = GROUP ? 4096 : 8192;        // bytes per slot
-  constexpr int kProducerLanes = kProducerWarps * LPW;
-  static_assert(kConsumerWarps == 4 && kConsumerWarps % kProducerLanes == 0, "slot sub-ring mapping");
+  constexpr int LPW = kProducerLanes;
+  static_assert(kConsumerWarps == 4 && kProducerWarps == 1 && kConsumerWarps % LPW == 0, "slot sub-ring mapping");
   using SL = SmemLayout;
   extern __shared__ __align__(1024) char smem_raw[];
   char* smem = reinterpret_cast<char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -943,9 +946,9 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
 #pragma unroll
     for (int t = 0; t < kFed; ++t) cnt[t] = 0;
     // claim slot u of warp w: wait until its previous round was released
-    auto claim = [&](int w, int u) -> bool {
+    auto claim = [&](int w, int u, int part = 0) -> bool {
       const int st = w * SPW + u % SPW, round = u / SPW;
-      return round == 0 || mbar_wait(empty_bar(st), (round - 1) & 1, budget);
+      return round == 0 || mbar_wait(empty_bar(SKV ? 2 * st + part : st), (round - 1) & 1, budget);
     };
     for (int k = 0, item = blockIdx.x; item < n_items && !timed_out; ++k, item += gridDim.x) {
       const int buf = k & 1;
@@ -963,6 +966,40 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
           const int fmt = fmt_s[i], pid = pid_s[i];
           const int ns = page_slots(fmt);
           int u = cnt[t];
+          if constexpr (SKV) {
+            // K half, then V half, each armed with its own bytes
+            if (!claim(w, u, 0)) { timed_out = true; break; }
+            const int st = w * SPW + u % SPW;
+            cnt[t] = u + 1;
+            const uint32_t sa = smem_u32(smem + SL::stages + st * SB);
+            const uint32_t kfull = full_bar(2 * st), vfull = full_bar(2 * st + 1);
+            const uint32_t half = fmt == IAK_FMT_F16 ? kPS * D * 2 : (fmt == IAK_FMT_INT4 ? kPS * D / 2 : kPS * D);
+            mbar_arrive_expect_tx(kfull, half);
+            if (fmt == IAK_FMT_F16) {
+              if constexpr (D == 128 && kF16OneBox) tma_load_2d(sa, &maps.m[M_KF16], 0, pid * kPS * 2, kfull);
+              else tma_load_2d(sa, &maps.m[M_KF16], 0, pid * kPS, kfull);
+            } else if (fmt == IAK_FMT_FP8 || fmt == IAK_FMT_INT8) {
+              tma_load_2d(sa, &maps.m[fmt == IAK_FMT_FP8 ? M_KFP8 : M_KI8], 0, pid * (kPS * D / 128), kfull);
+            } else {
+              const int y = pid * (kPS * D / 256);
+              tma_load_2d(sa, &maps.m[M_KI4], 0, y, kfull);
+              if (fmt == IAK_FMT_INT4R) tma_load_2d(sa + kResOff, &maps.m[M_KI4R], 0, y, kfull);
+            }
+            if (!claim(w, u, 1)) { timed_out = true; break; }
+            const uint32_t va = sa + 4096u;
+            mbar_arrive_expect_tx(vfull, half);
+            if (fmt == IAK_FMT_F16) {
+              if constexpr (D == 128 && kF16OneBox) tma_load_2d(va, &maps.m[M_VF16], 0, pid * kPS * 2, vfull);
+              else tma_load_2d(va, &maps.m[M_VF16], 0, pid * kPS, vfull);
+            } else if (fmt == IAK_FMT_FP8 || fmt == IAK_FMT_INT8) {
+              tma_load_2d(va, &maps.m[fmt == IAK_FMT_FP8 ? M_VFP8 : M_VI8], 0, pid * (kPS * D / 128), vfull);
+            } else {
+              const int y = pid * (kPS * D / 256);
+              tma_load_2d(va, &maps.m[M_VI4], 0, y, vfull);
+              if (fmt == IAK_FMT_INT4R) tma_load_2d(va + kResOff, &maps.m[M_VI4R], 0, y, vfull);
+            }
+            continue;
+          }
           if (ns == 2 && u % SPW == SPW - 1) {
             if (!claim(w, u)) { timed_out = true; break; }
             mbar_arrive(full_bar(w * SPW + u % SPW));   // skipped slot
@@ -1022,8 +1059,10 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
       for (int t = 0; t < kFed; ++t) {
         const int w = pl + t * LPW;
         for (int u = max(0, cnt[t] - SPW); u < cnt[t]; ++u)
-          if (!mbar_wait(full_bar(w * SPW + u % SPW), (u / SPW) & 1, kWaitCycles))
-            timed_out = true;
+          for (int part = 0; part < (SKV ? 2 : 1); ++part)
+            if (!mbar_wait(full_bar(SKV ? 2 * (w * SPW + u % SPW) + part : w * SPW + u % SPW), (u / SPW) & 1,
+                           kWaitCycles))
+              timed_out = true;
       }
     timed_out = __any_sync(0xffffffffu, timed_out);
   } else {
@@ -1069,7 +1108,7 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         }
         const int st = cw * SPW + u % SPW;
         cnt = u + ns;
-        if (!wait_all(full_bar(st), (u / SPW) & 1) ||
+        if (!wait_all(full_bar(SKV ? 2 * st : st), (u / SPW) & 1) ||
             (ns == 2 && !wait_all(full_bar(st + 1), ((u + 1) / SPW) & 1))) {
           timed_out = true;
           break;
@@ -1207,6 +1246,11 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         }
   #pragma unroll
         for (int e = 0; e < 4; ++e) sc[e] *= qk_log2;
+        if constexpr (SKV) {
+          // the page's K half is read: free it for the page two ahead
+          __syncwarp();
+          if (lane == 0) mbar_arrive(empty_bar(2 * st));
+        }
         // ---------------- online softmax (log2 domain)
         float pm0 = fmaxf(sc[0], sc[2]), pm1 = fmaxf(sc[1], sc[3]);
         // Lazy rescaling: the running max only moves (and O, l are rescaled)
@@ -1235,6 +1279,12 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         l_run[0] += p0 + p2;
         l_run[1] += p1 + p3;
         // ---------------- O^T += V^T P^T
+        if constexpr (SKV) {
+          if (!wait_all(full_bar(2 * st + 1), (u / SPW) & 1)) {
+            timed_out = true;
+            break;
+          }
+        }
         uint32_t vh[2][D / 64][8];
         if (!GROUP) {
           // per-page V scale folded into P
@@ -1326,8 +1376,12 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         }
         __syncwarp();
         if (lane == 0) {
-          mbar_arrive(empty_bar(st));
-          if (ns == 2) mbar_arrive(empty_bar(st + 1));
+          if constexpr (SKV) {
+            mbar_arrive(empty_bar(2 * st + 1));
+          } else {
+            mbar_arrive(empty_bar(st));
+            if (ns == 2) mbar_arrive(empty_bar(st + 1));
+          }
         }
       }
       if (timed_out) break;
@@ -1467,10 +1521,10 @@ bool mma_shape_eligible(const DecodeParams& p) {
   return true;
 }
 
-template <int D, bool GROUP, int LPW>
+template <int D, bool GROUP>
 static int launch_persistent(const DecodeParams& p, const TmaMaps& maps, int n_items, cudaStream_t s) {
   const size_t smem = SmemLayout::total + 1024;
-  auto kern = decode_mma_kernel<D, GROUP, LPW>;
+  auto kern = decode_mma_kernel<D, GROUP>;
   // the smem attribute and occupancy are per (device, instantiation): look them up once
   static std::mutex mu;
   static int per_sm_cache[64] = {0};
@@ -1528,10 +1582,9 @@ int launch_decode_mma(const DecodeParams& p, const iak_page_pools& P, cudaStream
   }
   if (!p.ws_qtab) return fail(IAK_ERR_WORKSPACE, "tensor-core decode needs a workspace");
   const int n_items = p.B * p.Ht * p.num_splits;
-  if (p.D == 128 && p.scale_mode == IAK_SCALE_GROUP32) return launch_persistent<128, true, 4>(p, maps, n_items, s);
-  if (p.D == 128 && p.producer_lanes == 4) return launch_persistent<128, false, 4>(p, maps, n_items, s);
-  if (p.D == 128) return launch_persistent<128, false, 2>(p, maps, n_items, s);
-  return launch_persistent<64, false, 2>(p, maps, n_items, s);
+  if (p.D == 128 && p.scale_mode == IAK_SCALE_GROUP32) return launch_persistent<128, true>(p, maps, n_items, s);
+  if (p.D == 128) return launch_persistent<128, false>(p, maps, n_items, s);
+  return launch_persistent<64, false>(p, maps, n_items, s);
 }
 
 }  // namespace iak

@@ -92,7 +92,6 @@ struct DecodeParams {
   float* ex_m; float* ex_l; float* ex_acc;
   unsigned int* status;   // IAK_STATUS_* bits ORed on a timeout (or NULL)
   long long wait_cycles;  // budget of each bounded device-side wait, in SM cycles
-  int producer_lanes;     // TMA issuing lanes of the tensor path's producer warp (2 or 4)
 };
 
 // Launchers (return IAK_OK or a status; errors recorded with set_error).
