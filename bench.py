@@ -320,11 +320,11 @@ class ClockSampler:
 # (--set full) of the same workload at the batch given, and the units (sequences) that
 # capture processed.  Traffic grows in proportion to the sequences processed, so it is
 # scaled to the benched batch.
-NCU_TRAFFIC = {"c2": {"bytes": 356_315_904, "batch": 8,
+NCU_TRAFFIC = {"c2": {"bytes": 356_055_552, "batch": 8,
                       "source": "ncu --set full capture of decode_mma_kernel, C2 at batch 8"},
                "c3": {"bytes": 142_390_528, "batch": 8,
                       "source": "ncu --set full capture of decode_mma_kernel, C3 at batch 8"},
-               "c5": {"bytes": 262_467_328, "batch": 1,
+               "c5": {"bytes": 261_946_112, "batch": 1,
                       "source": "ncu --set full capture of decode_mma_kernel, C5 at batch 1"},
                "c4": {"bytes": 58_652_672, "batch": 8,
                       "source": "ncu --set full capture of mla_tc_kernel, C4 at batch 8"},
