@@ -640,8 +640,9 @@ __device__ __forceinline__ void warp_merge(const float* m, const float* l, const
   L = lsum;
 }
 
-// Persistent split-KV decode, kCtasPerSm CTAs per SM.  CTA c processes work items
-// c, c + gridDim.x, ... (item = (unit, split) of <= kChunkMax table slots).  The
+// Persistent split-KV decode, kCtasPerSm CTAs per SM.  CTA c processes one work item
+// (unit, split) of <= kChunkMax table slots per wave of gridDim.x items (the full waves
+// rotated by the CTA's turn, see item_of).  The
 // preparer fills one of two item buffers ahead of use (compacted page list,
 // scales, query table by bulk copy); the TMA warp streams every item's pages
 // into the consumer warps' slot sub-rings (page i of an item goes to warp
