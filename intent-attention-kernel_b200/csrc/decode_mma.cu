@@ -1109,6 +1109,8 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         }
         const int st = cw * SPW + u % SPW;
         cnt = u + ns;
+        // the page's K (page-scaled pools: the slot's K half; its V half is waited for
+        // before P.V), or the whole page
         if (!wait_all(full_bar(SKV ? 2 * st : st), (u / SPW) & 1) ||
             (ns == 2 && !wait_all(full_bar(st + 1), ((u + 1) / SPW) & 1))) {
           timed_out = true;
